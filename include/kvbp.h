@@ -1,0 +1,179 @@
+/*
+ * kvbp.h -- C ABI of the B200 (sm_100a) capped-KV decode path.
+ *
+ * One decode step of GQA attention over a globally capped KV cache, fused with the
+ * eviction policy's per-slot score update, the structural prefix/suffix protection,
+ * victim selection and the scatter of the new K/V into a free slot.  The reference
+ * (Gpgabriel25/KVCacheBoundaryProtection) has no FFI; these entry points are what its
+ * JAX decode loop would bind through a jax.ffi / XLA custom call.  Each declaration
+ * names the reference code it replaces (paths inside the reference project).
+ *
+ * Conventions
+ *  - Every entry point is stateless and enqueue-only on ``stream`` (a cudaStream_t):
+ *    no host synchronisation, no device allocation.  The caller owns every buffer.
+ *  - Return value: KVBP_OK, or a KVBP_ERR_* code for an argument / shape / launch
+ *    error detected on the host before or at launch; kvbp_last_error() then holds a
+ *    message (thread-local).
+ *  - Problems found on the device are OR-ed into the caller's int32 ``dev_err`` word
+ *    (KVBP_DEV_* bits; may be NULL).  Kernels never trap; every wait is bounded.
+ *  - Tensors are dense row-major; "bf16" means IEEE bfloat16 bit patterns.
+ *  - Slot layout: a sequence's cache holds S slots.  slot_pos[b][s] is the absolute
+ *    position stored in slot s, or -1 when the slot is free.  After step 0 the retained
+ *    prompt positions fill slots 0..R-1 in ascending order; each decode step's new
+ *    position takes the lowest free slot before that step's eviction; victims' slots
+ *    become free.
+ */
+#ifndef KVBP_H
+#define KVBP_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* kvbp_stream_t; /* == cudaStream_t */
+
+#define KVBP_OK 0
+#define KVBP_ERR_ARG 1
+#define KVBP_ERR_UNSUPPORTED 2
+#define KVBP_ERR_CUDA 3
+
+#define KVBP_DEV_NO_FREE_SLOT 1
+#define KVBP_DEV_NAN_SCORE 2
+#define KVBP_DEV_INDEX 4
+#define KVBP_DEV_WAIT_TIMEOUT 8
+#define KVBP_DEV_NO_VALID_SLOT 16
+#define KVBP_DEV_LOG_OVERFLOW 32
+
+/* Policy ids: the reference CLI names (scripts/run_v3_jax.py:145-148, built at
+ * :500-518); "attention-mass" is an alias of "h2o_faithful". */
+#define KVBP_POLICY_LRU 0
+#define KVBP_POLICY_H2O_FAITHFUL 1
+#define KVBP_POLICY_H2O 2
+#define KVBP_POLICY_SNAPKV 3
+#define KVBP_POLICY_SNAPKV_FAITHFUL 4
+#define KVBP_POLICY_ADAKV 5
+#define KVBP_POLICY_QUEST 6
+#define KVBP_POLICY_STREAMINGLLM 7
+
+const char* kvbp_version(void);
+const char* kvbp_last_error(void);
+/* Policy id for a reference policy name, or -1. */
+int kvbp_policy_id(const char* name);
+
+/* Per-sequence eviction state (device pointers).  Arrays are [B][S] except posmap,
+ * which is [B][W]: bit p of sequence b is set while position p is retained. */
+typedef struct kvbp_state {
+  int32_t B, S, W;
+  int32_t* slot_pos;
+  int32_t* insert_step;
+  int32_t* last_access;
+  int32_t* access_count;
+  float* attn;      /* latest per-step score                  (KVBlockMetadata.attention_score) */
+  float* max_attn;  /* running max of per-step scores         (.max_attention_score) */
+  double* cumul;    /* float64 sum of per-step scores         (.cumulative_attention_score) */
+  float* prefill;   /* prefill score                          (.prefill_attention_score) */
+  uint32_t* posmap;
+} kvbp_state;
+
+/* Eviction configuration.  n_prefix / n_suffix are the ProtectedPolicyWrapper sizes
+ * max(4, int(capacity * frac)) (0 when frac == 0), see kvbp_protection_sizes(). */
+typedef struct kvbp_evict_cfg {
+  int32_t capacity;      /* --capacity */
+  int32_t evict_every;   /* --evict-every */
+  int32_t policy;        /* KVBP_POLICY_* */
+  int32_t protect;       /* --protect-prefix-suffix */
+  int32_t n_prefix;
+  int32_t n_suffix;
+  int32_t decode_regime; /* 1: --eviction-regime decode, 0: prefill (evict at step 0 only) */
+} kvbp_evict_cfg;
+
+/* Protection sizes of ProtectedPolicyWrapper (scripts/run_v3_jax.py:119-121). */
+void kvbp_protection_sizes(int32_t capacity, double prefix_frac, double suffix_frac, int32_t* n_prefix,
+                           int32_t* n_suffix);
+
+/* K1 -- decode attention over the slot cache + per-slot eviction score, one layer.
+ * Replaces the GQA einsum/mask/softmax/PV of _attention_layer
+ * (src/counterfact_kv_eviction/jax_inference.py:1018-1050) and the per-key score
+ * reduction (max over heads :1345, over layers :1670-1673).
+ * q [B][Hq][128] bf16; kcache/vcache [B][Hkv][S][128] bf16 (16-byte aligned);
+ * slot_pos [B][S]; out [B][Hq][128] bf16; step_score [B][S] float (non-negative,
+ * updated with max(existing, max over this layer's heads of p)).  Hq/Hkv <= 8. */
+int kvbp_decode_attn_score(kvbp_stream_t stream, int32_t B, int32_t Hq, int32_t Hkv, int32_t head_dim, int32_t S,
+                           const void* q, const void* kcache, const void* vcache, const int32_t* slot_pos, void* out,
+                           float* step_score, int32_t* dev_err);
+
+/* K4 -- QKV epilogue + scatter of the new K/V into its slot.  Replaces the bias add
+ * (jax_inference.py:953-956), q/k RMSNorm (:975-978), RoPE (:621-637,1000-1001) and the
+ * cache write dynamic_update_slice (:1011-1012).  qkv [rows][ldq] bf16 holds the Hq
+ * query heads, then Hkv key heads, then Hkv value heads (128 each); bias may be NULL
+ * (Qwen3), q_norm_w/k_norm_w may be NULL (Qwen2).  Row r belongs to sequence
+ * r / rows_per_seq and is written to slot write_slot[r] (skipped when < 0) of
+ * kcache/vcache [seq][Hkv][S][128].  inv_freq [64] float: RoPE inverse frequencies. */
+int kvbp_qkv_rope_scatter(kvbp_stream_t stream, int32_t rows, int32_t rows_per_seq, int32_t Hq, int32_t Hkv,
+                          int32_t head_dim, int32_t S, const void* qkv, int32_t ldq, const void* bias,
+                          const void* q_norm_w, const void* k_norm_w, float eps, const float* inv_freq,
+                          const int32_t* positions, const int32_t* write_slot, void* q_out, void* kcache,
+                          void* vcache, int32_t* dev_err);
+
+/* K2 -- per-step score update of every retained slot from step_score, then clears
+ * step_score.  Replaces kv_coupled_generator.py:504-516 (attn/max/cumul update, 5 %
+ * relative access threshold, last_access_step / access_count).  seq_step [B] device. */
+int kvbp_score_update(kvbp_stream_t stream, const kvbp_state* st, const int32_t* seq_step, float* step_score,
+                      int32_t* dev_err);
+
+/* K3 -- one decode step's bookkeeping: advances seq_step/next_pos, puts the new
+ * position into the lowest free slot (kv_coupled_generator.py:350-364) and, every
+ * evict_every steps, selects and frees victims: ProtectedPolicyWrapper
+ * (scripts/run_v3_jax.py:113-136) + the policy's composite-key top-k
+ * (policies.py:12-63 and the policy classes) + the hard-capacity guardrail
+ * (kv_coupled_generator.py:549-604).  Outputs cur_pos[b] (position to forward) and
+ * write_slot[b] (its slot, -1 if evicted at this step); appends victims to
+ * evlog [B][evcap] (evcount [B]); logs tokens[b] into token_log[B][log_steps] and the
+ * retained count into retained_log[B][log_steps+1] when those are non-NULL. */
+int kvbp_append_evict(kvbp_stream_t stream, const kvbp_state* st, const kvbp_evict_cfg* cfg, int32_t* seq_step,
+                      int32_t* next_pos, int32_t* cur_pos, int32_t* write_slot, const int32_t* tokens,
+                      int32_t* token_log, int32_t log_steps, int32_t* evlog, int32_t* evcount, int32_t evcap,
+                      int32_t* retained_log, int32_t* dev_err);
+
+/* K3 at step 0 -- victim selection over the P prompt positions after prefill
+ * (kv_coupled_generator.py:229-239 with force_if_over_capacity).  scores [B][P] are the
+ * prefill per-key scores (NULL = zeros, as for LRU).  Writes victim [B][P] flags and the
+ * policy victims, in eviction order, to evlog [B][evcap][0..n).  *n_policy_victims
+ * receives n (identical for every sequence). */
+int kvbp_prefill_select(kvbp_stream_t stream, int32_t B, int32_t P, const kvbp_evict_cfg* cfg, const float* scores,
+                        uint8_t* victim, int32_t* evlog, int32_t evcap, int32_t* n_policy_victims,
+                        int32_t* dev_err);
+
+/* K6 -- step-0 compaction: applies the hard-capacity guardrail, lays the retained prompt
+ * positions into slots 0..R-1, initialises their metadata (kv_coupled_generator.py:179-209)
+ * and gather_src [B][S] (prompt position per slot, -1 = none); resets seq_step to 0,
+ * next_pos to P and clears step_score [B][S]. */
+int kvbp_prefill_compact(kvbp_stream_t stream, const kvbp_state* st, int32_t P, int32_t capacity,
+                         int32_t n_policy_victims, const uint8_t* victim, const float* scores, int32_t* gather_src,
+                         int32_t* evlog, int32_t evcap, int32_t* evcount, int32_t* seq_step, int32_t* next_pos,
+                         int32_t* retained_log, int32_t log_steps, float* step_score, int32_t* dev_err);
+
+/* K6 -- copies prompt K/V rows src [layers][B][Hkv][P][128] into the slot caches
+ * dst [layers][B][Hkv][S][128] following gather_src. */
+int kvbp_gather_kv(kvbp_stream_t stream, const void* src_k, const void* src_v, void* dst_k, void* dst_v,
+                   const int32_t* gather_src, int32_t layers, int32_t B, int32_t Hkv, int32_t P, int32_t S);
+
+/* Dense-step helpers (reference: _forward_jittable, jax_inference.py:1182-1348). */
+/* out[r] = table[ids[r]] (bf16 rows of ``hidden``), jax_inference.py:1208. */
+int kvbp_embed(kvbp_stream_t stream, int32_t rows, int32_t vocab, int32_t hidden, const void* table,
+               const int32_t* ids, void* out, int32_t* dev_err);
+/* h = bf16(h + delta) (delta may be NULL); out = bf16(rms_norm(h) * w), jax_inference.py:609-618. */
+int kvbp_add_rmsnorm(kvbp_stream_t stream, int32_t rows, int32_t hidden, void* h, const void* delta, const void* w,
+                     void* out, float eps);
+/* act = bf16(bf16(g * bf16(sigmoid(g))) * u) for gu = [g | u] rows, jax_inference.py:702-704,1103-1107. */
+int kvbp_silu_mul(kvbp_stream_t stream, int32_t rows, int32_t ffn, const void* gu, void* act);
+/* Greedy sampling: first index of the row maximum (numpy.argmax), kv_coupled_generator.py:344. */
+int kvbp_argmax(kvbp_stream_t stream, int32_t rows, int32_t vocab, int64_t ld, const void* logits, int32_t* out_ids);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KVBP_H */

@@ -1,0 +1,147 @@
+// Shared device helpers for the capped-KV decode kernels (sm_100a).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace kvbp {
+
+// Bits of the caller-provided device error word.  Kernels never trap: they record
+// the condition, skip the offending access and return.
+enum DeviceError : int {
+  kErrNoFreeSlot = 1,     // a new position found no free KV slot
+  kErrNanScore = 2,       // a NaN reached the score / key arithmetic
+  kErrIndex = 4,          // a slot or position index outside its buffer was skipped
+  kErrWaitTimeout = 8,    // a bounded mbarrier wait gave up
+  kErrNoValidSlot = 16,   // attention found no valid slot for a (sequence, kv head)
+  kErrLogOverflow = 32,   // the eviction log is full
+};
+
+__device__ __forceinline__ void set_err(int* err, int bit) {
+  if (err) atomicOr(err, bit);
+}
+
+// bfloat16 round-to-nearest-even of a float32, returned as float32.
+__device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+__device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  uint32_t a = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(lo));
+  uint32_t b = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(hi));
+  return a | (b << 16);
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ---- mbarrier / TMA primitives (inline PTX) -------------------------------------
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait: gives up after ``limit`` polls (each try_wait already blocks for a
+// hardware-defined interval), so a lost transaction can never hang the GPU.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint32_t limit = (1u << 22)) {
+  for (uint32_t i = 0; i < limit; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (i > 64) __nanosleep(64);
+  }
+  return false;
+}
+
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap* m) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
+}
+
+// 2-D tiled TMA load (no multicast) into this CTA's shared memory.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+__device__ __forceinline__ void ldmatrix_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+// D = A(16x16 bf16, row) * B(16x8 bf16, col) + D, float32 accumulate.
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                               uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// ---- order-preserving encodings used by the eviction keys -----------------------
+// float64 -> uint64 whose unsigned order equals the numeric order (-0.0 == +0.0).
+__device__ __forceinline__ uint64_t ord_f64(double x) {
+  if (x == 0.0) x = 0.0;
+  uint64_t b = static_cast<uint64_t>(__double_as_longlong(x));
+  return (b >> 63) ? ~b : (b | 0x8000000000000000ull);
+}
+
+__device__ __forceinline__ uint32_t ord_i32(int v) { return static_cast<uint32_t>(v) ^ 0x80000000u; }
+
+// Code whose unsigned order equals the order of the decimal strings of
+// non-negative integers (Python ``str`` comparison: "100" < "11" < "9", and a
+// prefix sorts first).  Digits map to 1..10 in base 11, right-padded with 0 to
+// ten places; 11^10 < 2^35.
+__device__ __forceinline__ uint64_t lex_code(int pos) {
+  uint32_t v = static_cast<uint32_t>(pos);
+  int digits[10];
+  int n = 0;
+  do {
+    digits[n++] = static_cast<int>(v % 10u);
+    v /= 10u;
+  } while (v && n < 10);
+  uint64_t code = 0;
+#pragma unroll
+  for (int i = 0; i < 10; ++i) code = code * 11ull + (i < n ? static_cast<uint64_t>(digits[n - 1 - i] + 1) : 0ull);
+  return code;
+}
+
+struct Key3 {
+  uint64_t a, b, c;
+};
+
+__device__ __forceinline__ bool key_less(const Key3& x, const Key3& y) {
+  if (x.a != y.a) return x.a < y.a;
+  if (x.b != y.b) return x.b < y.b;
+  return x.c < y.c;
+}
+
+__device__ __forceinline__ Key3 key_max() { return Key3{~0ull, ~0ull, ~0ull}; }
+
+}  // namespace kvbp

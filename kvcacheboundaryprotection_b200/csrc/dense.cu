@@ -1,0 +1,308 @@
+// Per-token kernels around the GEMMs of one decoder step: embedding gather, fused
+// residual-add + RMSNorm, the QKV epilogue (bias, q/k RMSNorm, RoPE, scatter of the
+// new K/V into its cache slot), SwiGLU and greedy argmax.  Rounding points follow
+// src/counterfact_kv_eviction/jax_inference.py (rms_norm :609-618, rotary_embedding
+// :621-637, bias add :953-956, q/k norm :975-978, cache write :1011-1012, silu/mlp
+// :702-704,1089-1107, residual adds :1280,1325, greedy sampling at
+// kv_coupled_generator.py:344).
+#include "common.cuh"
+#include "kvbp_internal.h"
+
+namespace kvbp {
+
+template <typename T>
+__device__ __forceinline__ T warp_sum(T v) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Block-wide float sum; every thread receives the total.  ``red`` holds 32 floats.
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+  v = warp_sum(v);
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float t = lane < nw ? red[lane] : 0.f;
+  t = warp_sum(t);
+  return t;
+}
+
+// ---- embedding gather --------------------------------------------------------------
+__global__ void embed_kernel(const __nv_bfloat16* __restrict__ table, const int* __restrict__ ids, int V, int H,
+                             __nv_bfloat16* __restrict__ out, int* err) {
+  const int r = blockIdx.x;
+  const int id = ids[r];
+  if (id < 0 || id >= V) {
+    set_err(err, kErrIndex);
+    return;
+  }
+  const uint4* src = reinterpret_cast<const uint4*>(table + static_cast<size_t>(id) * H);
+  uint4* dst = reinterpret_cast<uint4*>(out + static_cast<size_t>(r) * H);
+  for (int i = threadIdx.x; i < H / 8; i += blockDim.x) dst[i] = src[i];
+}
+
+// ---- h = bf16(h + delta); out = bf16(rmsnorm(h) * w) ---------------------------------
+__global__ void add_rmsnorm_kernel(__nv_bfloat16* __restrict__ h, const __nv_bfloat16* __restrict__ delta,
+                                   const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ out, int H,
+                                   float eps) {
+  __shared__ float red[32];
+  const size_t r = blockIdx.x;
+  __nv_bfloat16* hr = h + r * H;
+  const __nv_bfloat16* dr = delta ? delta + r * H : nullptr;
+  float ss = 0.f;
+  for (int i = threadIdx.x * 2; i < H; i += blockDim.x * 2) {
+    const uint32_t hv = *reinterpret_cast<const uint32_t*>(hr + i);
+    float x0 = bf16lo(hv), x1 = bf16hi(hv);
+    if (dr) {
+      const uint32_t dv = *reinterpret_cast<const uint32_t*>(dr + i);
+      x0 = bf16r(x0 + bf16lo(dv));
+      x1 = bf16r(x1 + bf16hi(dv));
+      *reinterpret_cast<uint32_t*>(hr + i) = pack_bf16(x0, x1);
+    }
+    ss += x0 * x0 + x1 * x1;
+  }
+  ss = block_sum(ss, red);
+  const float var = ss / static_cast<float>(H);
+  const float inv = 1.0f / sqrtf(var + eps);
+  for (int i = threadIdx.x * 2; i < H; i += blockDim.x * 2) {
+    const uint32_t hv = *reinterpret_cast<const uint32_t*>(hr + i);
+    const uint32_t wv = *reinterpret_cast<const uint32_t*>(w + i);
+    *reinterpret_cast<uint32_t*>(out + r * H + i) =
+        pack_bf16((bf16lo(hv) * inv) * bf16lo(wv), (bf16hi(hv) * inv) * bf16hi(wv));
+  }
+}
+
+// ---- QKV epilogue -----------------------------------------------------------------
+// Block (row, head) of 64 threads; thread i owns the RoPE pair (i, i + 64).
+__global__ void qkv_epilogue_kernel(const __nv_bfloat16* __restrict__ qkv, int ldq,
+                                    const __nv_bfloat16* __restrict__ bias, const __nv_bfloat16* __restrict__ qnw,
+                                    const __nv_bfloat16* __restrict__ knw, float eps,
+                                    const float* __restrict__ inv_freq, const int* __restrict__ positions,
+                                    const int* __restrict__ write_slot, int rows_per_seq, int Hq, int Hkv, int S,
+                                    __nv_bfloat16* __restrict__ q_out, __nv_bfloat16* __restrict__ kcache,
+                                    __nv_bfloat16* __restrict__ vcache, int* err) {
+  __shared__ float red[32];
+  const int r = blockIdx.x, hh = blockIdx.y, i = threadIdx.x;
+  const __nv_bfloat16* src = qkv + static_cast<size_t>(r) * ldq + hh * 128;
+  float x0 = __bfloat162float(src[i]);
+  float x1 = __bfloat162float(src[i + 64]);
+  if (bias) {
+    x0 = bf16r(x0 + __bfloat162float(bias[hh * 128 + i]));
+    x1 = bf16r(x1 + __bfloat162float(bias[hh * 128 + i + 64]));
+  }
+  const bool is_q = hh < Hq, is_k = !is_q && hh < Hq + Hkv;
+  if (is_q || is_k) {
+    const __nv_bfloat16* nw = is_q ? qnw : knw;
+    if (nw) {  // block-uniform branch
+      const float ss = block_sum(x0 * x0 + x1 * x1, red);
+      const float inv = 1.0f / sqrtf(ss / 128.0f + eps);
+      x0 = bf16r((x0 * inv) * __bfloat162float(nw[i]));
+      x1 = bf16r((x1 * inv) * __bfloat162float(nw[i + 64]));
+    }
+    const float ang = static_cast<float>(positions[r]) * inv_freq[i];
+    const float c = bf16r(cosf(ang)), s = bf16r(sinf(ang));
+    const float y0 = bf16r(bf16r(x0 * c) - bf16r(x1 * s));
+    const float y1 = bf16r(bf16r(x1 * c) + bf16r(x0 * s));
+    x0 = y0;
+    x1 = y1;
+  }
+  if (is_q) {
+    __nv_bfloat16* dst = q_out + (static_cast<size_t>(r) * Hq + hh) * 128;
+    dst[i] = __float2bfloat16_rn(x0);
+    dst[i + 64] = __float2bfloat16_rn(x1);
+    return;
+  }
+  const int slot = write_slot[r];
+  if (slot < 0) return;  // position evicted before its forward: nothing to store
+  if (slot >= S) {
+    set_err(err, kErrIndex);
+    return;
+  }
+  const int kvh = is_k ? hh - Hq : hh - Hq - Hkv;
+  const int seq = r / rows_per_seq;
+  __nv_bfloat16* dst = (is_k ? kcache : vcache) + ((static_cast<size_t>(seq) * Hkv + kvh) * S + slot) * 128;
+  dst[i] = __float2bfloat16_rn(x0);
+  dst[i + 64] = __float2bfloat16_rn(x1);
+}
+
+// ---- SwiGLU: act = bf16(bf16(g * bf16(sigmoid(g))) * u) -------------------------------
+__global__ void silu_mul_kernel(const __nv_bfloat16* __restrict__ gu, int F, long long n,
+                                __nv_bfloat16* __restrict__ act) {
+  for (long long e = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) * 2; e < n;
+       e += static_cast<long long>(gridDim.x) * blockDim.x * 2) {
+    const long long r = e / F, c = e % F;
+    const uint32_t gv = *reinterpret_cast<const uint32_t*>(gu + r * 2 * F + c);
+    const uint32_t uv = *reinterpret_cast<const uint32_t*>(gu + r * 2 * F + F + c);
+    float out[2];
+    const float g[2] = {bf16lo(gv), bf16hi(gv)};
+    const float u[2] = {bf16lo(uv), bf16hi(uv)};
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const float sig = bf16r(1.0f / (1.0f + expf(-g[j])));
+      out[j] = bf16r(bf16r(g[j] * sig) * u[j]);
+    }
+    *reinterpret_cast<uint32_t*>(act + r * F + c) = pack_bf16(out[0], out[1]);
+  }
+}
+
+// ---- greedy argmax: first index of the maximum (numpy.argmax semantics) ----------------
+struct ArgBest {
+  float v;
+  int i;
+};
+
+__device__ __forceinline__ bool arg_better(float av, int ai, float bv, int bi) {
+  const bool an = av != av, bn = bv != bv;
+  if (an != bn) return an;  // numpy.argmax returns the first NaN
+  if (an) return ai < bi;
+  return av > bv || (av == bv && ai < bi);
+}
+
+__global__ void argmax_kernel(const __nv_bfloat16* __restrict__ logits, long long ld, int V, int* __restrict__ out) {
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  const int r = blockIdx.x;
+  const __nv_bfloat16* row = logits + r * ld;
+  float bv = -__int_as_float(0x7f800000);
+  int bi = 0x7fffffff;
+  const int nvec = V / 8;
+  for (int j = threadIdx.x; j < nvec; j += blockDim.x) {
+    const uint4 w = reinterpret_cast<const uint4*>(row)[j];
+    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float a = bf16lo(ws[k]), b = bf16hi(ws[k]);
+      const int ia = j * 8 + 2 * k;
+      if (arg_better(a, ia, bv, bi)) bv = a, bi = ia;
+      if (arg_better(b, ia + 1, bv, bi)) bv = b, bi = ia + 1;
+    }
+  }
+  for (int j = nvec * 8 + threadIdx.x; j < V; j += blockDim.x) {
+    const float a = __bfloat162float(row[j]);
+    if (arg_better(a, j, bv, bi)) bv = a, bi = j;
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (arg_better(ov, oi, bv, bi)) bv = ov, bi = oi;
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) sv[warp] = bv, si[warp] = bi;
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = blockDim.x >> 5;
+    bv = lane < nw ? sv[lane] : -__int_as_float(0x7f800000);
+    bi = lane < nw ? si[lane] : 0x7fffffff;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (arg_better(ov, oi, bv, bi)) bv = ov, bi = oi;
+    }
+    if (lane == 0) out[r] = bi;
+  }
+}
+
+// ------------------------------------------------------------------------------------
+static int check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(kStatusCuda, "%s launch: %s", what, cudaGetErrorString(e));
+  return kStatusOk;
+}
+
+int embed(cudaStream_t st, int rows, int V, int H, const void* table, const int* ids, void* out, int* err) {
+  if (!table || !ids || !out) return fail(kStatusArg, "embed: null pointer");
+  if (rows <= 0 || H <= 0 || V <= 0 || H % 8) return fail(kStatusArg, "embed: bad size (H must be a multiple of 8)");
+  embed_kernel<<<rows, 128, 0, st>>>(static_cast<const __nv_bfloat16*>(table), ids, V, H,
+                                     static_cast<__nv_bfloat16*>(out), err);
+  return check_launch("embed");
+}
+
+int add_rmsnorm(cudaStream_t st, int rows, int H, void* h, const void* delta, const void* w, void* out, float eps) {
+  if (!h || !w || !out) return fail(kStatusArg, "add_rmsnorm: null pointer");
+  if (rows <= 0 || H <= 0 || H % 2) return fail(kStatusArg, "add_rmsnorm: bad size");
+  add_rmsnorm_kernel<<<rows, 256, 0, st>>>(static_cast<__nv_bfloat16*>(h), static_cast<const __nv_bfloat16*>(delta),
+                                           static_cast<const __nv_bfloat16*>(w), static_cast<__nv_bfloat16*>(out), H,
+                                           eps);
+  return check_launch("add_rmsnorm");
+}
+
+int qkv_epilogue(cudaStream_t st, int rows, int rows_per_seq, int Hq, int Hkv, int D, int S, const void* qkv, int ldq,
+                 const void* bias, const void* qnw, const void* knw, float eps, const float* inv_freq,
+                 const int* positions, const int* write_slot, void* q_out, void* kcache, void* vcache, int* err) {
+  if (!qkv || !inv_freq || !positions || !write_slot || !q_out || !kcache || !vcache)
+    return fail(kStatusArg, "qkv_epilogue: null pointer");
+  if (D != 128) return fail(kStatusUnsupported, "qkv_epilogue: head_dim %d unsupported (only 128)", D);
+  if (rows <= 0 || rows_per_seq <= 0 || Hq <= 0 || Hkv <= 0 || S <= 0 || ldq < (Hq + 2 * Hkv) * D)
+    return fail(kStatusArg, "qkv_epilogue: bad size");
+  if ((Hq + 2 * Hkv) > 65535) return fail(kStatusArg, "qkv_epilogue: too many heads");
+  dim3 grid(rows, Hq + 2 * Hkv);
+  qkv_epilogue_kernel<<<grid, 64, 0, st>>>(
+      static_cast<const __nv_bfloat16*>(qkv), ldq, static_cast<const __nv_bfloat16*>(bias),
+      static_cast<const __nv_bfloat16*>(qnw), static_cast<const __nv_bfloat16*>(knw), eps, inv_freq, positions,
+      write_slot, rows_per_seq, Hq, Hkv, S, static_cast<__nv_bfloat16*>(q_out), static_cast<__nv_bfloat16*>(kcache),
+      static_cast<__nv_bfloat16*>(vcache), err);
+  return check_launch("qkv_epilogue");
+}
+
+int silu_mul(cudaStream_t st, int rows, int F, const void* gu, void* act) {
+  if (!gu || !act) return fail(kStatusArg, "silu_mul: null pointer");
+  if (rows <= 0 || F <= 0 || F % 2) return fail(kStatusArg, "silu_mul: bad size");
+  const long long n = static_cast<long long>(rows) * F;
+  long long blocks = (n / 2 + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  silu_mul_kernel<<<static_cast<int>(blocks), 256, 0, st>>>(static_cast<const __nv_bfloat16*>(gu), F, n,
+                                                             static_cast<__nv_bfloat16*>(act));
+  return check_launch("silu_mul");
+}
+
+int argmax_rows(cudaStream_t st, int rows, int V, long long ld, const void* logits, int* out) {
+  if (!logits || !out) return fail(kStatusArg, "argmax: null pointer");
+  if (rows <= 0 || V <= 0 || ld < V) return fail(kStatusArg, "argmax: bad size");
+  if ((ld % 8) || (reinterpret_cast<uintptr_t>(logits) & 15))
+    return fail(kStatusArg, "argmax: rows must be 16-byte aligned (ld % 8 == 0)");
+  argmax_kernel<<<rows, 1024, 0, st>>>(static_cast<const __nv_bfloat16*>(logits), ld, V, out);
+  return check_launch("argmax");
+}
+
+}  // namespace kvbp
+
+// ------------------------------------------------------------------------------------
+// C ABI
+// ------------------------------------------------------------------------------------
+#include "../../include/kvbp.h"
+
+extern "C" {
+
+int kvbp_embed(kvbp_stream_t stream, int32_t rows, int32_t vocab, int32_t hidden, const void* table,
+               const int32_t* ids, void* out, int32_t* dev_err) {
+  return kvbp::embed(reinterpret_cast<cudaStream_t>(stream), rows, vocab, hidden, table, ids, out, dev_err);
+}
+
+int kvbp_add_rmsnorm(kvbp_stream_t stream, int32_t rows, int32_t hidden, void* h, const void* delta, const void* w,
+                     void* out, float eps) {
+  return kvbp::add_rmsnorm(reinterpret_cast<cudaStream_t>(stream), rows, hidden, h, delta, w, out, eps);
+}
+
+int kvbp_silu_mul(kvbp_stream_t stream, int32_t rows, int32_t ffn, const void* gu, void* act) {
+  return kvbp::silu_mul(reinterpret_cast<cudaStream_t>(stream), rows, ffn, gu, act);
+}
+
+int kvbp_argmax(kvbp_stream_t stream, int32_t rows, int32_t vocab, int64_t ld, const void* logits, int32_t* out_ids) {
+  return kvbp::argmax_rows(reinterpret_cast<cudaStream_t>(stream), rows, vocab, ld, logits, out_ids);
+}
+
+int kvbp_qkv_rope_scatter(kvbp_stream_t stream, int32_t rows, int32_t rows_per_seq, int32_t Hq, int32_t Hkv,
+                          int32_t head_dim, int32_t S, const void* qkv, int32_t ldq, const void* bias,
+                          const void* q_norm_w, const void* k_norm_w, float eps, const float* inv_freq,
+                          const int32_t* positions, const int32_t* write_slot, void* q_out, void* kcache,
+                          void* vcache, int32_t* dev_err) {
+  return kvbp::qkv_epilogue(reinterpret_cast<cudaStream_t>(stream), rows, rows_per_seq, Hq, Hkv, head_dim, S, qkv,
+                            ldq, bias, q_norm_w, k_norm_w, eps, inv_freq, positions, write_slot, q_out, kcache,
+                            vcache, dev_err);
+}
+
+}  // extern "C"

@@ -1,0 +1,469 @@
+"""Device-resident capped-KV decode engine (B200, sm_100a).
+
+``CappedKVEngine`` owns, for a batch of B sequences decoded in lockstep:
+
+* the decoder weights (bf16; q/k/v and gate/up fused into one matrix each),
+* the slot KV cache ``[L][B][Hkv][S][128]`` bf16 with S = capacity + evict_every
+  (capacity + max_new_tokens under ``--eviction-regime prefill``),
+* the per-slot eviction metadata (``kvbp_state``) and the position bitmap,
+* activation buffers, the eviction / token / retained-count logs.
+
+One decode step is::
+
+    kvbp_append_evict   new position -> lowest free slot; cadence eviction
+    kvbp_embed
+    L x [ kvbp_add_rmsnorm, GEMM qkv, kvbp_qkv_rope_scatter, kvbp_decode_attn_score,
+          GEMM o, kvbp_add_rmsnorm, GEMM gate|up, kvbp_silu_mul, GEMM down ]
+    kvbp_add_rmsnorm (final), GEMM lm_head, kvbp_argmax
+    kvbp_score_update
+
+Every step-dependent value (step counter, positions, slots) lives on the device, so
+one captured CUDA graph replays every step.  The GEMMs are cuBLAS (torch.mm) with
+bf16 output and float32 accumulation; everything else is this package's kernels.
+
+The reference computes the same step in ``KVCoupledQwen35Generator`` (host loop,
+``src/counterfact_kv_eviction/kv_coupled_generator.py:336-516``) around
+``JAXModelAdapter``'s jitted forward (``jax_inference.py:1182-1348,1606-1682``).
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import Dict, List, Optional
+
+import numpy as np
+import torch
+
+from . import capi
+from .capi import EvictCfg, State, check, lib
+from .config import ModelConfig
+
+
+def inv_freq_table(head_dim: int, theta: float) -> np.ndarray:
+    """RoPE inverse frequencies as float32 ops (jax_inference.py:623-624)."""
+    half = head_dim // 2
+    expo = np.arange(0, half, dtype=np.float32) / np.float32(half)
+    return (np.float32(1.0) / (np.float32(theta) ** expo)).astype(np.float32)
+
+
+def scale_bf16(head_dim: int) -> float:
+    return float(torch.tensor(1.0 / math.sqrt(head_dim), dtype=torch.float32).to(torch.bfloat16).item())
+
+
+def _ptr(t: Optional[torch.Tensor]):
+    return None if t is None else t.data_ptr()
+
+
+@dataclass
+class EvictionSpec:
+    """Eviction configuration of the harness (scripts/run_v3_jax.py:141-206)."""
+
+    policy: str = "lru"
+    capacity: int = 256
+    evict_every: int = 8
+    protect: bool = True
+    prefix_frac: float = 0.10
+    suffix_frac: float = 0.10
+    regime: str = "decode"
+    # capacity the protection wrapper sizes its prefix/suffix from (its own ``capacity``
+    # field, run_v3_jax.py:119); None = the eviction capacity
+    protect_capacity: Optional[int] = None
+
+    def sizes(self) -> tuple:
+        if not self.protect:
+            return 0, 0
+        cap = self.capacity if self.protect_capacity is None else self.protect_capacity
+        return capi.protection_sizes(cap, self.prefix_frac, self.suffix_frac)
+
+
+class FusedWeights:
+    """Decoder weights on the device in the engine's layout (bf16): q/k/v stacked into
+    one [(Hq+2Hkv)*128, H] matrix (+ stacked bias), gate/up stacked into [2F, H]."""
+
+    def __init__(self, cfg: ModelConfig, w: Dict[str, torch.Tensor], device: torch.device):
+        c, d, bf = cfg, torch.device(device), torch.bfloat16
+
+        def g(name):
+            return w[name].to(device=d, dtype=bf).contiguous()
+
+        self.cfg = cfg
+        self.embed_w = g("embed")
+        self.lm_w = self.embed_w if c.tie_embed else g("lm_head")
+        self.final_norm = g("final_norm")
+        self.layers = []
+        for i in range(c.n_layers):
+            self.layers.append(
+                {
+                    "in_norm": g(f"l{i}.in_norm"),
+                    "post_norm": g(f"l{i}.post_norm"),
+                    "w_qkv": torch.cat([g(f"l{i}.wq"), g(f"l{i}.wk"), g(f"l{i}.wv")], 0).contiguous(),
+                    "b_qkv": torch.cat([g(f"l{i}.bq"), g(f"l{i}.bk"), g(f"l{i}.bv")], 0).contiguous()
+                    if c.qkv_bias
+                    else None,
+                    "q_norm": g(f"l{i}.q_norm") if c.qk_norm else None,
+                    "k_norm": g(f"l{i}.k_norm") if c.qk_norm else None,
+                    "w_o": g(f"l{i}.wo"),
+                    "w_gu": torch.cat([g(f"l{i}.w_gate"), g(f"l{i}.w_up")], 0).contiguous(),
+                    "w_down": g(f"l{i}.w_down"),
+                }
+            )
+        self.inv_freq = torch.from_numpy(inv_freq_table(c.head_dim, c.rope_theta)).to(d)
+
+    def nbytes(self) -> int:
+        n = self.embed_w.numel() + (0 if self.lm_w is self.embed_w else self.lm_w.numel()) + self.final_norm.numel()
+        for L in self.layers:
+            n += sum(t.numel() for t in L.values() if t is not None)
+        return 2 * n
+
+
+class CappedKVEngine:
+    def __init__(
+        self,
+        cfg: ModelConfig,
+        weights: Dict[str, torch.Tensor],
+        *,
+        batch: int,
+        evict: EvictionSpec,
+        max_prompt_len: int,
+        max_new_tokens: int,
+        device: Optional[torch.device] = None,
+        kv_heads: Optional[List[int]] = None,
+    ):
+        if cfg.head_dim != 128:
+            raise ValueError("only head_dim 128 is supported")
+        if cfg.group > 8:
+            raise ValueError("query group size > 8 is not supported by the decode kernel")
+        if evict.capacity <= 0:
+            raise ValueError("capacity must be > 0")
+        if evict.evict_every <= 0:
+            raise ValueError("evict_every_n_steps must be > 0")
+        if evict.regime not in ("decode", "prefill"):
+            raise ValueError("eviction_regime must be 'decode' or 'prefill'")
+        lib()  # fail loudly when the CUDA library is missing
+        self.dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        if self.dev.type != "cuda":
+            raise ValueError("CappedKVEngine runs on CUDA devices only")
+        torch.backends.cuda.matmul.allow_tf32 = False
+        torch.backends.cuda.matmul.allow_bf16_reduced_precision_reduction = False
+        self.cfg = cfg
+        self.ev = evict
+        self.B = int(batch)
+        self.max_prompt = int(max_prompt_len)
+        self.max_new = int(max_new_tokens)
+        self.policy_id = capi.policy_id(evict.policy)
+        self.n_prefix, self.n_suffix = evict.sizes()
+        C = evict.capacity
+        self.S = C + (evict.evict_every if evict.regime == "decode" else max(1, self.max_new))
+        self.W = (self.max_prompt + self.max_new + 2 + 31) // 32
+        self.evcap = self.max_prompt + self.max_new + 2
+        self._load_weights(weights)
+        self._alloc()
+        self.graph: Optional[torch.cuda.CUDAGraph] = None
+        self.prompt_len = 0
+        self.step = 0
+
+    # ------------------------------------------------------------------ setup
+    def _load_weights(self, w) -> None:
+        fw = w if isinstance(w, FusedWeights) else FusedWeights(self.cfg, w, self.dev)
+        self.fw = fw
+        self.embed_w, self.lm_w, self.final_norm = fw.embed_w, fw.lm_w, fw.final_norm
+        self.layers = fw.layers
+        self.inv_freq = fw.inv_freq
+
+    def _alloc(self) -> None:
+        c, d, B, S = self.cfg, self.dev, self.B, self.S
+        i32, f32, bf = torch.int32, torch.float32, torch.bfloat16
+        L = c.n_layers
+        self.kc = torch.zeros(L, B, c.n_kv_heads, S, c.head_dim, dtype=bf, device=d)
+        self.vc = torch.zeros_like(self.kc)
+        z = lambda *s, dt=i32: torch.zeros(*s, dtype=dt, device=d)  # noqa: E731
+        self.slot_pos = torch.full((B, S), -1, dtype=i32, device=d)
+        self.insert_step = z(B, S)
+        self.last_access = z(B, S)
+        self.access_count = z(B, S)
+        self.attn_s = z(B, S, dt=f32)
+        self.max_attn = z(B, S, dt=f32)
+        self.cumul = z(B, S, dt=torch.float64)
+        self.prefill_s = z(B, S, dt=f32)
+        self.posmap = z(B, self.W, dt=torch.int32)
+        self.step_score = z(B, S, dt=f32)
+        self.seq_step = z(B)
+        self.next_pos = z(B)
+        self.cur_pos = z(B)
+        self.write_slot = z(B)
+        self.tokens = z(B)
+        self.token_log = z(B, max(1, self.max_new))
+        self.retained_log = z(B, self.max_new + 1)
+        self.evlog = z(B, self.evcap)
+        self.evcount = z(B)
+        self.dev_err = z(1)
+        H, F, V = c.hidden, c.ffn, c.vocab
+        self.h = z(B, H, dt=bf)
+        self.x = z(B, H, dt=bf)
+        self.qkv = z(B, c.qkv_dim, dt=bf)
+        self.q = z(B, c.n_heads, c.head_dim, dt=bf)
+        self.attn_out = z(B, c.n_heads * c.head_dim, dt=bf)
+        self.o = z(B, H, dt=bf)
+        self.gu = z(B, 2 * F, dt=bf)
+        self.act = z(B, F, dt=bf)
+        self.dn = z(B, H, dt=bf)
+        self.logits = z(B, V, dt=bf)
+        self._state = State(
+            B, S, self.W,
+            self.slot_pos.data_ptr(), self.insert_step.data_ptr(), self.last_access.data_ptr(),
+            self.access_count.data_ptr(), self.attn_s.data_ptr(), self.max_attn.data_ptr(),
+            self.cumul.data_ptr(), self.prefill_s.data_ptr(), self.posmap.data_ptr(),
+        )
+        self._cfg = EvictCfg(
+            self.ev.capacity, self.ev.evict_every, self.policy_id, int(self.ev.protect), self.n_prefix,
+            self.n_suffix, int(self.ev.regime == "decode"),
+        )
+
+    @property
+    def stream(self) -> int:
+        return torch.cuda.current_stream(self.dev).cuda_stream
+
+    def kv_bytes_per_layer(self) -> int:
+        return self.kc[0].numel() * 2 * 2
+
+    # ------------------------------------------------------------------ prefill
+    def _prefill_attention(self, q, kbuf, vbuf, need_scores, colmax):
+        """Causal prefill attention with the reference's rounding points, on the GPU.
+
+        q [P, Hq, D] bf16; kbuf/vbuf [Hkv, P, D] bf16.  Returns [P, Hq*D] bf16 and folds
+        the per-key max over heads and query rows of the probabilities into ``colmax``
+        (jax_inference.py:1018-1050 with the causal mask :1169-1179, per-key max
+        :1754-1760).  Implemented with cuBLAS/torch ops (bf16 QK^T output, fp32 softmax
+        and fp32 P.V).
+        """
+        c = self.cfg
+        P = q.shape[0]
+        G, D = c.group, c.head_dim
+        out = torch.empty(P, c.n_heads, D, dtype=torch.bfloat16, device=self.dev)
+        scale = torch.tensor(scale_bf16(D), dtype=torch.bfloat16, device=self.dev)
+        R = max(1, min(P, (1 << 27) // max(1, P * G * 4)))
+        cols = torch.arange(P, device=self.dev)
+        for g in range(c.n_kv_heads):
+            K = kbuf[g]
+            V = vbuf[g].float()
+            for r0 in range(0, P, R):
+                r1 = min(P, r0 + R)
+                qg = q[r0:r1, g * G : (g + 1) * G, :].reshape((r1 - r0) * G, D)
+                s = torch.matmul(qg, K[:r1].t())
+                s = (s * scale).float()
+                rows = torch.arange(r0, r1, device=self.dev).repeat_interleave(G)
+                s = s + torch.where(cols[None, :r1] > rows[:, None], -1e9, 0.0)
+                p = torch.softmax(s, dim=-1)
+                out[r0:r1, g * G : (g + 1) * G, :] = (p @ V[:r1]).reshape(r1 - r0, G, D).to(torch.bfloat16)
+                if need_scores:
+                    torch.maximum(colmax[:r1], p.amax(0), out=colmax[:r1])
+        return out.reshape(P, c.n_heads * D)
+
+    def prefill(self, input_ids: torch.Tensor) -> None:
+        """Step 0 for the whole batch: forward the prompts, score positions (non-LRU),
+        evict down to capacity (forced), compact into slots and sample step 1's token."""
+        c, d, st = self.cfg, self.dev, self.stream
+        L = lib()
+        ids = input_ids.to(device=d, dtype=torch.int32).contiguous()
+        B, P = ids.shape
+        if B != self.B:
+            raise ValueError(f"batch {B} != engine batch {self.B}")
+        if P <= 0:
+            raise ValueError("input_ids must be non-empty")
+        if P > self.max_prompt:
+            raise ValueError(f"prompt length {P} > max_prompt_len {self.max_prompt}")
+        need_scores = capi.POLICY_IDS[self.ev.policy] != 0
+        Hkv, D = c.n_kv_heads, c.head_dim
+        pre_k = torch.empty(c.n_layers, B, Hkv, P, D, dtype=torch.bfloat16, device=d)
+        pre_v = torch.empty_like(pre_k)
+        scores = torch.zeros(B, P, dtype=torch.float32, device=d) if need_scores else None
+        positions = torch.arange(P, dtype=torch.int32, device=d)
+        H = c.hidden
+        for b in range(B):
+            h = torch.empty(P, H, dtype=torch.bfloat16, device=d)
+            check(L.kvbp_embed(st, P, c.vocab, H, _ptr(self.embed_w), _ptr(ids[b]), _ptr(h), _ptr(self.dev_err)), "embed")
+            x = torch.empty_like(h)
+            delta = None
+            colmax = torch.zeros(P, dtype=torch.float32, device=d) if need_scores else None
+            for li, Lw in enumerate(self.layers):
+                check(L.kvbp_add_rmsnorm(st, P, H, _ptr(h), _ptr(delta), _ptr(Lw["in_norm"]), _ptr(x), c.eps), "rmsnorm")
+                qkv = torch.mm(x, Lw["w_qkv"].t())
+                q = torch.empty(P, c.n_heads, D, dtype=torch.bfloat16, device=d)
+                kb, vb = pre_k[li, b], pre_v[li, b]
+                check(
+                    L.kvbp_qkv_rope_scatter(
+                        st, P, P, c.n_heads, Hkv, D, P, _ptr(qkv), c.qkv_dim, _ptr(Lw["b_qkv"]), _ptr(Lw["q_norm"]),
+                        _ptr(Lw["k_norm"]), c.eps, _ptr(self.inv_freq), _ptr(positions), _ptr(positions), _ptr(q),
+                        _ptr(kb), _ptr(vb), _ptr(self.dev_err),
+                    ),
+                    "qkv_rope_scatter",
+                )
+                lcol = torch.zeros(P, dtype=torch.float32, device=d) if need_scores else None
+                att = self._prefill_attention(q, kb, vb, need_scores, lcol)
+                if need_scores:
+                    torch.maximum(colmax, lcol, out=colmax)
+                o = torch.mm(att, Lw["w_o"].t())
+                check(L.kvbp_add_rmsnorm(st, P, H, _ptr(h), _ptr(o), _ptr(Lw["post_norm"]), _ptr(x), c.eps), "rmsnorm")
+                gu = torch.mm(x, Lw["w_gu"].t())
+                act = torch.empty(P, c.ffn, dtype=torch.bfloat16, device=d)
+                check(L.kvbp_silu_mul(st, P, c.ffn, _ptr(gu), _ptr(act)), "silu_mul")
+                delta = torch.mm(act, Lw["w_down"].t())
+                del gu, act, qkv, q
+            hl = h[P - 1 : P].contiguous()
+            dl = delta[P - 1 : P].contiguous()
+            xl = torch.empty_like(hl)
+            check(L.kvbp_add_rmsnorm(st, 1, H, _ptr(hl), _ptr(dl), _ptr(self.final_norm), _ptr(xl), c.eps), "rmsnorm")
+            torch.mm(xl, self.lm_w.t(), out=self.logits[b : b + 1])
+            if need_scores:
+                scores[b] = colmax
+        self._select_and_compact(P, scores, pre_k, pre_v)
+        check(L.kvbp_argmax(st, B, c.vocab, c.vocab, _ptr(self.logits), _ptr(self.tokens)), "argmax")
+
+    def _select_and_compact(self, P, scores, pre_k=None, pre_v=None) -> None:
+        L, st = lib(), self.stream
+        victim = torch.zeros(self.B, P, dtype=torch.uint8, device=self.dev)
+        self.evlog.zero_()
+        nvict = capi.C.c_int32()
+        check(
+            L.kvbp_prefill_select(
+                st, self.B, P, capi.C.byref(self._cfg), _ptr(scores), _ptr(victim), _ptr(self.evlog), self.evcap,
+                capi.C.byref(nvict), _ptr(self.dev_err),
+            ),
+            "prefill_select",
+        )
+        self.gather_src = torch.empty(self.B, self.S, dtype=torch.int32, device=self.dev)
+        self.retained_log.zero_()
+        check(
+            L.kvbp_prefill_compact(
+                st, capi.C.byref(self._state), P, self.ev.capacity, nvict.value, _ptr(victim), _ptr(scores),
+                _ptr(self.gather_src), _ptr(self.evlog), self.evcap, _ptr(self.evcount), _ptr(self.seq_step),
+                _ptr(self.next_pos), _ptr(self.retained_log), self.max_new, _ptr(self.step_score), _ptr(self.dev_err),
+            ),
+            "prefill_compact",
+        )
+        if pre_k is not None:
+            c = self.cfg
+            check(
+                L.kvbp_gather_kv(
+                    st, _ptr(pre_k), _ptr(pre_v), _ptr(self.kc), _ptr(self.vc), _ptr(self.gather_src), c.n_layers,
+                    self.B, c.n_kv_heads, P, self.S,
+                ),
+                "gather_kv",
+            )
+        self.prompt_len = P
+        self.step = 0
+        self.n_policy_victims_step0 = nvict.value
+
+    def synthetic_prefill(self, prompt_len: int, seed: int = 0) -> None:
+        """Post-prefill state of ``prompt_len``-token prompts without running the prefill:
+        seeded N(0,1) K/V in every slot, U(0,1) prefill scores through the real step-0
+        selection and compaction kernels, random first tokens.  For decode throughput
+        measurement, where prefill is excluded from the metric."""
+        g = torch.Generator(device=self.dev)
+        g.manual_seed(int(seed))
+        P = int(prompt_len)
+        scores = torch.rand(self.B, P, generator=g, device=self.dev, dtype=torch.float32)
+        need_scores = capi.POLICY_IDS[self.ev.policy] != 0
+        self._select_and_compact(P, scores if need_scores else None)
+        for t in (self.kc, self.vc):
+            for li in range(t.shape[0]):
+                t[li].normal_(generator=g)
+        self.tokens.copy_(torch.randint(0, self.cfg.vocab, (self.B,), generator=g, device=self.dev, dtype=torch.int32))
+
+    # ------------------------------------------------------------------ decode
+    def _append_evict(self) -> None:
+        check(
+            lib().kvbp_append_evict(
+                self.stream, capi.C.byref(self._state), capi.C.byref(self._cfg), _ptr(self.seq_step),
+                _ptr(self.next_pos), _ptr(self.cur_pos), _ptr(self.write_slot), _ptr(self.tokens),
+                _ptr(self.token_log), self.max_new, _ptr(self.evlog), _ptr(self.evcount), self.evcap,
+                _ptr(self.retained_log), _ptr(self.dev_err),
+            ),
+            "append_evict",
+        )
+
+    def _forward(self) -> None:
+        """Forward the token of every sequence at cur_pos, writing its K/V to write_slot."""
+        c, st, L, B = self.cfg, self.stream, lib(), self.B
+        H, D = c.hidden, c.head_dim
+        check(L.kvbp_embed(st, B, c.vocab, H, _ptr(self.embed_w), _ptr(self.tokens), _ptr(self.h), _ptr(self.dev_err)), "embed")
+        delta = None
+        for li, Lw in enumerate(self.layers):
+            check(L.kvbp_add_rmsnorm(st, B, H, _ptr(self.h), _ptr(delta), _ptr(Lw["in_norm"]), _ptr(self.x), c.eps), "rmsnorm")
+            torch.mm(self.x, Lw["w_qkv"].t(), out=self.qkv)
+            check(
+                L.kvbp_qkv_rope_scatter(
+                    st, B, 1, c.n_heads, c.n_kv_heads, D, self.S, _ptr(self.qkv), c.qkv_dim, _ptr(Lw["b_qkv"]),
+                    _ptr(Lw["q_norm"]), _ptr(Lw["k_norm"]), c.eps, _ptr(self.inv_freq), _ptr(self.cur_pos),
+                    _ptr(self.write_slot), _ptr(self.q), _ptr(self.kc[li]), _ptr(self.vc[li]), _ptr(self.dev_err),
+                ),
+                "qkv_rope_scatter",
+            )
+            check(
+                L.kvbp_decode_attn_score(
+                    st, B, c.n_heads, c.n_kv_heads, D, self.S, _ptr(self.q), _ptr(self.kc[li]), _ptr(self.vc[li]),
+                    _ptr(self.slot_pos), _ptr(self.attn_out), _ptr(self.step_score), _ptr(self.dev_err),
+                ),
+                "decode_attn_score",
+            )
+            torch.mm(self.attn_out, Lw["w_o"].t(), out=self.o)
+            check(L.kvbp_add_rmsnorm(st, B, H, _ptr(self.h), _ptr(self.o), _ptr(Lw["post_norm"]), _ptr(self.x), c.eps), "rmsnorm")
+            torch.mm(self.x, Lw["w_gu"].t(), out=self.gu)
+            check(L.kvbp_silu_mul(st, B, c.ffn, _ptr(self.gu), _ptr(self.act)), "silu_mul")
+            torch.mm(self.act, Lw["w_down"].t(), out=self.dn)
+            delta = self.dn
+        check(L.kvbp_add_rmsnorm(st, B, H, _ptr(self.h), _ptr(self.dn), _ptr(self.final_norm), _ptr(self.x), c.eps), "rmsnorm")
+        torch.mm(self.x, self.lm_w.t(), out=self.logits)
+
+    def _sample_and_score(self) -> None:
+        L, st, c = lib(), self.stream, self.cfg
+        check(L.kvbp_argmax(st, self.B, c.vocab, c.vocab, _ptr(self.logits), _ptr(self.tokens)), "argmax")
+        check(L.kvbp_score_update(st, capi.C.byref(self._state), _ptr(self.seq_step), _ptr(self.step_score), _ptr(self.dev_err)), "score_update")
+
+    def decode_step_launches(self, *, forward: bool = True, sample: bool = True) -> None:
+        """Enqueue one decode step (no host synchronisation)."""
+        self._append_evict()
+        if forward:
+            self._forward()
+            if sample:
+                self._sample_and_score()
+            else:
+                check(lib().kvbp_score_update(self.stream, capi.C.byref(self._state), _ptr(self.seq_step), _ptr(self.step_score), _ptr(self.dev_err)), "score_update")
+
+    def capture(self) -> None:
+        """Capture one full decode step (append/evict + forward + sample + score) as a graph."""
+        s = torch.cuda.Stream(self.dev)
+        s.wait_stream(torch.cuda.current_stream(self.dev))
+        # cuBLAS creates its handle and workspace lazily; do that outside the capture
+        with torch.cuda.stream(s):
+            L0 = self.layers[0]
+            for a, w, o in ((self.x, L0["w_qkv"], self.qkv), (self.attn_out, L0["w_o"], self.o),
+                            (self.x, L0["w_gu"], self.gu), (self.act, L0["w_down"], self.dn),
+                            (self.x, self.lm_w, self.logits)):
+                torch.mm(a, w.t(), out=o)
+        s.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(g, stream=s):
+                self.decode_step_launches()
+        torch.cuda.current_stream(self.dev).wait_stream(s)
+        self.graph = g
+
+    def run_step(self, *, use_graph: bool = True) -> None:
+        """One decode step for steps 1..max_new-1 (append/evict, forward, sample, score)."""
+        if use_graph and self.graph is not None:
+            self.graph.replay()
+        else:
+            self.decode_step_launches()
+        self.step += 1
+
+    def final_step(self) -> None:
+        """Step max_new: the sampled token is appended (and evicted at cadence) but not forwarded."""
+        self._append_evict()
+        self.step += 1
+
+    def check_device_errors(self) -> None:
+        word = int(self.dev_err.item())
+        if word:
+            raise capi.KVBPError("device reported: " + "; ".join(capi.decode_dev_errors(word)))

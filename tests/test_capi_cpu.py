@@ -1,0 +1,67 @@
+"""C-ABI library checks that need no GPU: it loads, exports every declared symbol,
+and its host-side validation / pure host helpers behave."""
+
+import ctypes as C
+import os
+import re
+
+import pytest
+
+from kvcacheboundaryprotection_b200 import build, capi
+
+from conftest import REPO
+
+
+def _declared():
+    text = open(os.path.join(REPO, "include", "kvbp.h")).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(kvbp_[a-z0-9_]+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def L():
+    build.build()
+    return capi.lib()
+
+
+def test_exports_every_declared_symbol(L):
+    names = _declared()
+    assert len(names) >= 15
+    for n in names:
+        assert hasattr(L, n), n
+    assert set(names) == set(capi.SIGNATURES), "ctypes signatures out of sync with include/kvbp.h"
+
+
+def test_version_and_policy_ids(L):
+    assert b"sm_100a" in L.kvbp_version()
+    assert capi.policy_id("lru") == 0
+    assert capi.policy_id("attention-mass") == capi.policy_id("h2o_faithful") == 1
+    assert L.kvbp_policy_id(b"random") == -1
+    with pytest.raises(ValueError):
+        capi.policy_id("adakv_faithful")
+
+
+@pytest.mark.parametrize(
+    "cap,pf,sf,expect",
+    [(256, 0.10, 0.10, (25, 25)), (1024, 0.10, 0.10, (102, 102)), (4096, 0.10, 0.10, (409, 409)),
+     (256, 0.05, 0.05, (12, 12)), (8, 0.10, 0.0, (4, 0)), (1000, 0.07, 0.0, (70, 0)), (30, 0.0, 0.5, (0, 15))],
+)
+def test_protection_sizes_match_python(L, cap, pf, sf, expect):
+    py = (max(4, int(cap * pf)) if pf > 0 else 0, max(4, int(cap * sf)) if sf > 0 else 0)
+    assert capi.protection_sizes(cap, pf, sf) == py == expect
+
+
+def test_host_validation_rejects_bad_arguments(L):
+    # null pointers are rejected on the host before any CUDA call
+    st = L.kvbp_decode_attn_score(None, 1, 4, 1, 128, 64, None, None, None, None, None, None, None)
+    assert st == 1 and b"null" in L.kvbp_last_error()
+    st = L.kvbp_decode_attn_score(None, 1, 4, 1, 64, 64, 1, 1, 1, 1, 1, 1, None)
+    assert st == 2  # head_dim 64 unsupported
+    st = L.kvbp_decode_attn_score(None, 1, 18, 2, 128, 64, 16, 16, 16, 16, 16, 16, None)
+    assert st == 2  # group of 9 heads unsupported
+    assert L.kvbp_argmax(None, 1, 100, 50, 16, 16) == 1  # ld < vocab
+    cfg = capi.EvictCfg(0, 8, 0, 1, 25, 25, 1)
+    n = C.c_int32()
+    assert L.kvbp_prefill_select(None, 1, 100, C.byref(cfg), None, 16, 16, 10, C.byref(n), None) == 1
+    with pytest.raises(capi.KVBPError):
+        capi.check(L.kvbp_embed(None, 1, 10, 12, 16, 16, 16, None), "embed")

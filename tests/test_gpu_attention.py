@@ -1,0 +1,140 @@
+"""K1 decode attention + per-slot score vs. a plain PyTorch fp32 reference of the same op.
+
+The reference op (jax_inference.py:1018-1050): s = bf16(bf16(q.k) * bf16(1/sqrt(128))),
+float32 softmax over the valid slots, out = bf16(p @ float32(V)); per-slot score =
+max over the group's heads of p, max-accumulated into step_score.
+
+Tolerances: q.k is accumulated in fp32 in a different order (tensor-core mma vs. the
+fp32 GEMM), so a logit can land on the neighbouring bfloat16 value; such slots move
+their probabilities by <= 2^-8 relative.  We require
+  * out:   max |diff| <= 1.6e-2 and >= 97 % of elements bit-identical,
+  * score: rel diff <= 1e-5 on >= 97 % of slots and <= 2e-2 everywhere.
+"""
+
+import math
+
+import pytest
+import torch
+
+from kvcacheboundaryprotection_b200 import build, capi
+
+pytestmark = pytest.mark.gpu
+
+SCALE = float(torch.tensor(1.0 / math.sqrt(128)).to(torch.bfloat16))
+
+
+def torch_reference(q, kc, vc, slot_pos):
+    B, Hq, D = q.shape
+    Hkv, S = kc.shape[1], kc.shape[2]
+    G = Hq // Hkv
+    out = torch.zeros(B, Hq, D, dtype=torch.float32, device=q.device)
+    score = torch.zeros(B, S, dtype=torch.float32, device=q.device)
+    for b in range(B):
+        valid = slot_pos[b] >= 0
+        for g in range(Hkv):
+            K = kc[b, g].float()
+            V = vc[b, g].float()
+            qg = q[b, g * G : (g + 1) * G].float()
+            s = (qg @ K.t()).to(torch.bfloat16).float()
+            s = (s * SCALE).to(torch.bfloat16).float()
+            s = torch.where(valid[None, :], s, torch.tensor(float("-inf"), device=q.device))
+            p = torch.softmax(s, dim=-1)
+            out[b, g * G : (g + 1) * G] = (p @ V).to(torch.bfloat16).float()
+            score[b] = torch.maximum(score[b], p.max(0).values)
+    return out, score
+
+
+def run_kernel(q, kc, vc, slot_pos, score_init=None, cluster=0):
+    L = capi.lib()
+    B, Hq, D = q.shape
+    Hkv, S = kc.shape[1], kc.shape[2]
+    out = torch.empty_like(q)
+    score = score_init.clone() if score_init is not None else torch.zeros(B, S, dtype=torch.float32, device=q.device)
+    err = torch.zeros(1, dtype=torch.int32, device=q.device)
+    st = torch.cuda.current_stream().cuda_stream
+    args = (st, B, Hq, Hkv, D, S, q.data_ptr(), kc.data_ptr(), vc.data_ptr(), slot_pos.data_ptr(), out.data_ptr(),
+            score.data_ptr(), err.data_ptr())
+    if cluster:
+        capi.check(L.kvbp_decode_attn_score_cs(*args, cluster), "attn")
+    else:
+        capi.check(L.kvbp_decode_attn_score(*args), "attn")
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0, capi.decode_dev_errors(int(err.item()))
+    return out.float(), score
+
+
+def make_case(B, Hq, Hkv, S, free_frac, seed):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    q = (torch.randn(B, Hq, 128, generator=g, device="cuda") / math.sqrt(128)).to(torch.bfloat16)
+    kc = torch.randn(B, Hkv, S, 128, generator=g, device="cuda").to(torch.bfloat16)
+    vc = torch.randn(B, Hkv, S, 128, generator=g, device="cuda").to(torch.bfloat16)
+    pos = torch.randperm(S * 4, generator=g, device="cuda")[:S].to(torch.int32).repeat(B, 1)
+    free = torch.rand(B, S, generator=g, device="cuda") < free_frac
+    pos[free] = -1
+    pos[:, 0] = 0  # at least one valid slot
+    return q, kc, vc, pos.contiguous()
+
+
+def assert_close(out, score, ref_out, ref_score, valid):
+    d = (out - ref_out).abs()
+    assert d.max().item() <= 1.6e-2, d.max().item()
+    assert (d == 0).float().mean().item() >= 0.97
+    rel = ((score - ref_score).abs() / ref_score.clamp_min(1e-30))[valid]
+    assert rel.max().item() <= 2e-2, rel.max().item()
+    assert (rel <= 1e-5).float().mean().item() >= 0.97
+    assert (score[~valid] == 0).all()
+
+
+CASES = [
+    # B, Hq, Hkv, S, free fraction
+    (2, 8, 2, 264, 0.05),  # tiny-qwen2 heads, capacity 256 + 8
+    (3, 4, 1, 100, 0.3),
+    (2, 28, 4, 1032, 0.01),  # Qwen2.5-7B group of 7
+    (1, 32, 8, 4104, 0.002),  # Qwen3-4B / microbench group of 4, capacity 4096
+    (2, 16, 2, 136, 0.0),  # group of 8
+    (1, 3, 3, 70, 0.1),  # group of 1
+    (2, 6, 2, 200, 0.2),  # group of 3
+    (1, 10, 2, 77, 0.1),  # group of 5
+    (1, 12, 2, 129, 0.1),  # group of 6
+    (4, 32, 8, 1, 0.0),  # a single slot
+]
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _lib():
+    build.build()
+    capi.lib()
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,S,free", CASES)
+def test_attention_matches_torch_reference(B, Hq, Hkv, S, free):
+    q, kc, vc, pos = make_case(B, Hq, Hkv, S, free, seed=S * 7 + Hq)
+    out, score = run_kernel(q, kc, vc, pos)
+    ref_out, ref_score = torch_reference(q, kc, vc, pos)
+    assert_close(out, score, ref_out, ref_score, pos >= 0)
+
+
+@pytest.mark.parametrize("cluster", [1, 2, 3, 5, 8])
+def test_attention_every_cluster_size(cluster):
+    q, kc, vc, pos = make_case(2, 28, 4, 1032, 0.05, seed=11)
+    out, score = run_kernel(q, kc, vc, pos, cluster=cluster)
+    ref_out, ref_score = torch_reference(q, kc, vc, pos)
+    assert_close(out, score, ref_out, ref_score, pos >= 0)
+
+
+def test_step_score_is_max_accumulated():
+    q, kc, vc, pos = make_case(2, 8, 2, 264, 0.1, seed=5)
+    init = torch.rand(2, 264, device="cuda") * 0.02
+    init[pos < 0] = 0
+    _, score = run_kernel(q, kc, vc, pos, score_init=init)
+    _, fresh = run_kernel(q, kc, vc, pos)
+    assert torch.equal(score, torch.maximum(init, fresh))
+
+
+def test_large_batch_microbench_shape_runs_clean():
+    # B=64, Hkv=8, G=4, capacity 1024: the operator microbench shape
+    q, kc, vc, pos = make_case(64, 32, 8, 1032, 0.0, seed=3)
+    out, score = run_kernel(q, kc, vc, pos)
+    ref_out, ref_score = torch_reference(q[:4], kc[:4], vc[:4], pos[:4])
+    assert_close(out[:4], score[:4], ref_out, ref_score, pos[:4] >= 0)
+    assert torch.isfinite(out).all()

@@ -1,0 +1,157 @@
+"""Eviction kernels (K2 score update, K3 append/evict, step-0 select + compact) vs. the
+reference's own decode/eviction traces, bit for bit, given equal scores.
+
+Each case of tests/golden/generator_kats.json is a run of the reference
+``KVCoupledQwen35Generator`` driven by ``oracle.stub_model.StubScoreModel``.  The
+oracle generator (checked against the same fixture on the CPU) replays it and records
+the per-step score vectors; those exact scores are written into ``step_score`` on the
+GPU, so every victim, slot table and count must match exactly.
+"""
+
+import ctypes as C
+import json
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from kvcacheboundaryprotection_b200 import build, capi
+from oracle.generator import generate, slot_count
+from oracle.policies import PolicySpec
+from oracle.stub_model import StubScoreModel
+
+from conftest import GOLDEN
+
+pytestmark = pytest.mark.gpu
+
+with open(os.path.join(GOLDEN, "generator_kats.json")) as _f:
+    CASES = json.load(_f)["cases"]
+
+
+class Driver:
+    """Minimal state + calls of the eviction kernels for one sequence batch."""
+
+    def __init__(self, B, S, W, evcap, max_new, cfg):
+        d = "cuda"
+        z = lambda *s, dt=torch.int32: torch.zeros(*s, dtype=dt, device=d)  # noqa: E731
+        self.B, self.S, self.W = B, S, W
+        self.slot_pos = torch.full((B, S), -1, dtype=torch.int32, device=d)
+        self.ins, self.last, self.cnt = z(B, S), z(B, S), z(B, S)
+        self.attn, self.maxa, self.pre = z(B, S, dt=torch.float32), z(B, S, dt=torch.float32), z(B, S, dt=torch.float32)
+        self.cumul = z(B, S, dt=torch.float64)
+        self.posmap = z(B, W)
+        self.step_score = z(B, S, dt=torch.float32)
+        self.seq_step, self.next_pos, self.cur_pos, self.write_slot = z(B), z(B), z(B), z(B)
+        self.tokens = z(B)
+        self.token_log = z(B, max(1, max_new))
+        self.retained_log = z(B, max_new + 1)
+        self.evlog, self.evcount = z(B, evcap), z(B)
+        self.err = z(1)
+        self.evcap, self.max_new = evcap, max_new
+        self.state = capi.State(B, S, W, *[t.data_ptr() for t in (self.slot_pos, self.ins, self.last, self.cnt, self.attn, self.maxa, self.cumul, self.pre, self.posmap)])
+        self.cfg = cfg
+        self.L = capi.lib()
+
+    @property
+    def st(self):
+        return torch.cuda.current_stream().cuda_stream
+
+    def prefill(self, P, scores):
+        victim = torch.zeros(self.B, P, dtype=torch.uint8, device="cuda")
+        n = C.c_int32()
+        sc = None if scores is None else torch.as_tensor(scores, dtype=torch.float32, device="cuda").reshape(self.B, P).contiguous()
+        capi.check(self.L.kvbp_prefill_select(self.st, self.B, P, C.byref(self.cfg), None if sc is None else sc.data_ptr(), victim.data_ptr(), self.evlog.data_ptr(), self.evcap, C.byref(n), self.err.data_ptr()), "select")
+        gsrc = torch.empty(self.B, self.S, dtype=torch.int32, device="cuda")
+        capi.check(self.L.kvbp_prefill_compact(self.st, C.byref(self.state), P, self.cfg.capacity, n.value, victim.data_ptr(), None if sc is None else sc.data_ptr(), gsrc.data_ptr(), self.evlog.data_ptr(), self.evcap, self.evcount.data_ptr(), self.seq_step.data_ptr(), self.next_pos.data_ptr(), self.retained_log.data_ptr(), self.max_new, self.step_score.data_ptr(), self.err.data_ptr()), "compact")
+        return gsrc
+
+    def append_evict(self):
+        capi.check(self.L.kvbp_append_evict(self.st, C.byref(self.state), C.byref(self.cfg), self.seq_step.data_ptr(), self.next_pos.data_ptr(), self.cur_pos.data_ptr(), self.write_slot.data_ptr(), self.tokens.data_ptr(), self.token_log.data_ptr(), self.max_new, self.evlog.data_ptr(), self.evcount.data_ptr(), self.evcap, self.retained_log.data_ptr(), self.err.data_ptr()), "append_evict")
+
+    def score_update(self):
+        capi.check(self.L.kvbp_score_update(self.st, C.byref(self.state), self.seq_step.data_ptr(), self.step_score.data_ptr(), self.err.data_ptr()), "score_update")
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _lib():
+    build.build()
+    capi.lib()
+
+
+def _spec(case):
+    prot = case["protect"]
+    return PolicySpec(case["policy"], case["capacity"], prot is not None, *(prot or (0.0, 0.0)))
+
+
+@pytest.mark.parametrize("case", CASES, ids=[c["name"] for c in CASES])
+def test_eviction_kernels_match_reference_trace(case):
+    P, cap, E, max_new = case["n_prompt"], case["capacity"], case["evict_every"], case["max_new_tokens"]
+    model = StubScoreModel(vocab=97, n_heads=4, n_kv_heads=2, n_layers=2, max_cache_len=P + max_new + 8, seed=case["seed"])
+    spec = _spec(case)
+    o = generate(model, spec, case["prompt"], max_new, evict_every=E, n_kv_heads=case["n_kv_heads"], regime=case["regime"])
+    assert o.positions_evicted == case["positions_evicted"]  # oracle == reference
+
+    n_pre, n_suf = capi.protection_sizes(cap, *(case["protect"] or (0.0, 0.0))) if case["protect"] else (0, 0)
+    cfg = capi.EvictCfg(cap, E, capi.policy_id(case["policy"]), int(case["protect"] is not None), n_pre, n_suf, int(case["regime"] == "decode"))
+    S = slot_count(cap, E, max_new, case["regime"])
+    D = Driver(1, S, (P + max_new + 2 + 31) // 32, P + max_new + 2, max_new, cfg)
+    pre = o.meta.prefill[:P] if case["policy"] != "lru" else None
+    D.prefill(P, pre)
+    assert D.slot_pos[0].cpu().numpy().tolist() == o.slot_tables[0].tolist()
+    for s in range(1, max_new + 1):
+        D.append_evict()
+        assert D.slot_pos[0].cpu().numpy().tolist() == o.slot_tables[s].tolist(), f"slot table after step {s}"
+        if s == max_new:
+            break
+        ks = o.step_scores[s - 1]
+        sp = D.slot_pos[0].cpu().numpy()
+        sc = np.zeros(S, np.float32)
+        sc[sp >= 0] = ks[sp[sp >= 0]]
+        D.step_score[0].copy_(torch.from_numpy(sc))
+        D.score_update()
+    torch.cuda.synchronize()
+    assert int(D.err.item()) == 0
+    n = int(D.evcount[0].item())
+    assert D.evlog[0, :n].cpu().numpy().tolist() == case["positions_evicted"]
+    assert [P] + D.retained_log[0].cpu().numpy().tolist() == case["retained_counts_by_step"]
+
+
+def test_step0_lru_string_order_at_1024():
+    # prompt 1024, capacity 256, protect 0.10: first victims follow str(pos) order
+    cfg = capi.EvictCfg(256, 8, 0, 1, 25, 25, 1)
+    D = Driver(2, 264, 40, 1200, 8, cfg)
+    D.prefill(1024, None)
+    torch.cuda.synchronize()
+    ev = D.evlog[:, :768].cpu().numpy()
+    assert ev[0, :8].tolist() == [100, 101, 102, 103, 104, 105, 106, 107]
+    assert (ev[0] == ev[1]).all()
+    m = PolicySpec("lru", 256, True)
+    from oracle.policies import Meta
+
+    assert ev[0].tolist() == m.select(list(range(1024)), Meta.zeros(1024), 768, 0)
+
+
+@pytest.mark.parametrize("policy", ["h2o_faithful", "h2o", "snapkv", "snapkv_faithful", "adakv", "quest", "streamingllm"])
+def test_step0_scored_policies_large_prompt(policy):
+    from oracle.policies import Meta
+
+    P, cap = 2048, 256
+    rng = np.random.default_rng(7)
+    scores = (rng.random(P) ** 4).astype(np.float32)
+    scores[rng.integers(0, P, 200)] = scores[5]  # ties on the score component
+    n_pre, n_suf = capi.protection_sizes(cap, 0.05, 0.05)
+    cfg = capi.EvictCfg(cap, 8, capi.policy_id(policy), 1, n_pre, n_suf, 1)
+    D = Driver(1, cap + 8, (P + 40) // 32 + 1, P + 16, 8, cfg)
+    D.prefill(P, scores)
+    torch.cuda.synchronize()
+    m = Meta.zeros(P)
+    m.attn[:] = m.max_attn[:] = m.prefill[:] = scores
+    m.cumul[:] = scores.astype(np.float64)
+    want = PolicySpec(policy, cap, True, 0.05, 0.05).select(list(range(P)), m, P - cap, 0)
+    from oracle.policies import hard_cap
+
+    rest = sorted(set(range(P)) - set(want))
+    want = want + hard_cap(rest, m, len(rest) - cap)
+    n = int(D.evcount[0].item())
+    assert D.evlog[0, :n].cpu().numpy().tolist() == want
