@@ -14,48 +14,60 @@
 //   score[slot] = max over the layer's query heads of p   -> atomicMax into step_score
 //
 // Work decomposition (B200): grid = (CS, Hkv, B) with a thread-block cluster of CS CTAs
-// per (sequence, kv head).  Each CTA owns a contiguous range of 64-slot tiles.  K tiles
-// then V tiles stream through a 4-stage shared-memory ring filled by 2-D TMA loads
-// (128-byte swizzle, no multicast).  Q.K^T runs on the tensor cores (mma.sync m16n8k16,
-// slots on M, the <= 8 query heads of the group on N).  The logits of the CTA's slots
-// stay in shared memory; the softmax max / sum are combined across the cluster through
-// distributed shared memory, so every probability is final before P.V and the K/V
-// cache is read exactly once.  P.V runs on the fp32 pipes (lane = 4 head dims), and the
-// partial outputs are summed across the cluster through DSMEM.
-#include <cooperative_groups.h>
-
+// per (sequence, kv head); each CTA owns a contiguous range of 64-slot tiles.  Warp 4
+// is a TMA producer that streams (K tile, V tile) pairs through a shared-memory ring
+// (2-D loads, 128-byte swizzle, no multicast; full/empty mbarriers).  Warps 0-3 each
+// own 16 slots of every tile and run one continuous flash-decoding pass with no
+// CTA-wide synchronisation per tile:
+//   Q.K^T   tensor cores (mma.sync m16n8k16: slots on M, the <= 8 query heads of the
+//           group on N); the rounded logits are kept in shared memory,
+//   softmax online per warp (running max / sum per head, rescaled partial output),
+//   P.V     tensor cores: V^T from the swizzled tile via ldmatrix.trans, the weights
+//           split into bf16 hi + lo parts (two mma, ~16-bit mantissa), fp32 accumulate.
+// At the end the four warps' (max, sum, O) are merged in shared memory and one st.async
+// round pushes every CTA's (max, sum) and its O slice r to cluster CTA r (transaction-
+// counted mbarrier).  Each CTA then forms the final max M and sum L, writes its slice
+// of bf16 output, and turns its stored logits into the exact probabilities
+// p = exp(s - M) / L for the per-slot score (max over heads -> atomicMax).  The K/V
+// cache is read exactly once, in a single stream.
 #include "common.cuh"
 #include "kvbp_internal.h"
-
-namespace cg = cooperative_groups;
 
 namespace kvbp {
 
 constexpr int kD = 128;
 constexpr int kTile = 64;
-constexpr int kStages = 4;
-constexpr int kWarps = 4;
-constexpr int kThreads = kWarps * 32;
-constexpr int kTileBytes = kTile * kD * 2;  // 16 KiB: two 64x64 bf16 boxes
-constexpr int kBoxBytes = kTileBytes / 2;
+#ifndef KVBP_ATTN_STAGES
+#define KVBP_ATTN_STAGES 2
+#endif
+constexpr int kStages = KVBP_ATTN_STAGES;
+constexpr int kConsumerWarps = 4;
+constexpr int kConsumers = kConsumerWarps * 32;
+constexpr int kThreads = kConsumers + 32;  // + one TMA producer warp
+constexpr int kHalfBytes = kTile * kD * 2;  // 16 KiB: K (or V) of one tile, two 64x64 boxes
+constexpr int kBoxBytes = kHalfBytes / 2;
+constexpr int kStageBytes = 2 * kHalfBytes;  // K tile + V tile
+constexpr int kMaxCluster = 8;
 
 struct AttnSmem {
   // byte offsets from the 1024-aligned base
-  int logits, valid, opart, octa, stats, bars, total;
+  int logits, escr, spos, orecv, srecv, wstat, bars, total;
 };
 
 __host__ __device__ inline int align_up(int x, int a) { return (x + a - 1) / a * a; }
 
 __host__ __device__ inline AttnSmem attn_smem_layout(int nloc_tiles) {
   AttnSmem L;
-  int nloc = nloc_tiles * kTile;
-  L.logits = kStages * kTileBytes;
-  L.valid = L.logits + nloc * 8 * 4;
-  L.opart = align_up(L.valid + nloc, 16);
-  L.octa = L.opart + kWarps * 8 * kD * 4;
-  L.stats = L.octa + 8 * kD * 4;
-  L.bars = align_up(L.stats + 4 * 8 * 4, 8);
-  L.total = L.bars + kStages * 8;
+  const int nloc = nloc_tiles * kTile;
+  L.logits = kStages * kStageBytes;  // [nloc][8] rounded logits
+  L.escr = L.logits + nloc * 8 * 4;  // [warp][16 rows][8] softmax weights of the current tile
+  L.spos = L.escr + kConsumerWarps * 16 * 8 * 4;
+  L.orecv = align_up(L.spos + nloc * 4, 16);  // [CS][per] received O slices
+  L.srecv = L.orecv + (8 * kD + kMaxCluster) * 4;  // [CS][16] received (max, sum)
+  L.wstat = L.srecv + kMaxCluster * 16 * 4;  // [warp][16] per-warp (max, sum) + CTA (max, sum) + flags
+  L.bars = align_up(L.wstat + (kConsumerWarps + 2) * 16 * 4, 8);
+  L.total = L.bars + (2 * kStages + 1) * 8;
+  // the [warp][8][128] partial outputs alias the ring at the end
   return L;
 }
 
@@ -81,52 +93,102 @@ __global__ void __launch_bounds__(kThreads) decode_attn_score_kernel(const __gri
   const AttnSmem L = attn_smem_layout(p.nloc_tiles);
   uint8_t* ring = base;
   float* logits = reinterpret_cast<float*>(base + L.logits);
-  uint8_t* valid = base + L.valid;
-  float* opart = reinterpret_cast<float*>(base + L.opart);
-  float* octa = reinterpret_cast<float*>(base + L.octa);
-  float* st_m = reinterpret_cast<float*>(base + L.stats);
-  float* st_l = st_m + 8;
-  float* fin_m = st_l + 8;
-  float* fin_l = fin_m + 8;
+  float* escr = reinterpret_cast<float*>(base + L.escr);
+  int* spos_s = reinterpret_cast<int*>(base + L.spos);
+  float* orecv = reinterpret_cast<float*>(base + L.orecv);
+  float* srecv = reinterpret_cast<float*>(base + L.srecv);
+  float* wstat = reinterpret_cast<float*>(base + L.wstat);  // [warp][m 8 | l 8]
+  float* cstat = wstat + kConsumerWarps * 16;                // CTA m[8], l[8]
+  int* flags = reinterpret_cast<int*>(cstat + 16);           // [0] bad, [1] issued
+  int* bad_flag = flags;
+  int* n_issued = flags + 1;
+  float* opart = reinterpret_cast<float*>(base);  // [warp][8][128], aliases the ring
   uint64_t* full = reinterpret_cast<uint64_t*>(base + L.bars);
+  uint64_t* empty = full + kStages;
+  uint64_t* xbar = empty + kStages;
 
-  cg::cluster_group cluster = cg::this_cluster();
   const int CS = p.cluster;
-  const int rank = static_cast<int>(cluster.block_rank());
+  uint32_t rank_u;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank_u));
+  const int rank = static_cast<int>(rank_u);
   const int kvh = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int t0 = (rank * p.tiles) / CS, t1 = ((rank + 1) * p.tiles) / CS;
-  const int nt = t1 - t0, ntot = 2 * nt, nloc = nt * kTile;
+  const int nt = t1 - t0, nloc = nt * kTile;
   const int S = p.S;
   const int row_base = (b * p.Hkv + kvh) * S;
-  const int* spos = p.slot_pos + static_cast<size_t>(b) * S;
-  float* sscore = p.step_score + static_cast<size_t>(b) * S;
+  const int per = (G * kD + CS - 1) / CS;  // output slice per CTA
+  const int n_mine = (rank * per < G * kD) ? ((rank * per + per < G * kD) ? per : G * kD - rank * per) : 0;
   const float NEG_INF = -__int_as_float(0x7f800000);
-
-  if (tid == 0) {
-    prefetch_tmap(&kmap);
-    prefetch_tmap(&vmap);
-    for (int s = 0; s < kStages; ++s) mbar_init(&full[s], 1);
-    fence_barrier_init();
-  }
-  __syncthreads();
 
   auto issue = [&](int u) {
     const int st = u % kStages;
-    uint8_t* dst = ring + st * kTileBytes;
-    const bool is_k = u < nt;
-    const int y = row_base + (t0 + (is_k ? u : u - nt)) * kTile;
-    mbar_expect_tx(&full[st], kTileBytes);
-    tma_load_2d(dst, is_k ? &kmap : &vmap, &full[st], 0, y);
-    tma_load_2d(dst + kBoxBytes, is_k ? &kmap : &vmap, &full[st], 64, y);
+    uint8_t* dst = ring + st * kStageBytes;
+    const int y = row_base + (t0 + u) * kTile;
+    mbar_expect_tx(&full[st], kStageBytes);
+    tma_load_2d(dst, &kmap, &full[st], 0, y);
+    tma_load_2d(dst + kBoxBytes, &kmap, &full[st], 64, y);
+    tma_load_2d(dst + kHalfBytes, &vmap, &full[st], 0, y);
+    tma_load_2d(dst + kHalfBytes + kBoxBytes, &vmap, &full[st], 64, y);
   };
-  if (tid == 0)
-    for (int u = 0; u < (ntot < kStages ? ntot : kStages); ++u) issue(u);
+  const int n_first = nt < kStages ? nt : kStages;
+  if (tid == kConsumers) {
+    prefetch_tmap(&kmap);
+    prefetch_tmap(&vmap);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumerWarps);
+    }
+    mbar_init(xbar, 1);
+    *bad_flag = 0;
+    fence_barrier_init();
+    // start streaming at once: the first stages depend on nothing but this CTA
+    for (int u = 0; u < n_first; ++u) issue(u);
+    *n_issued = n_first;
+  }
+  if (tid < kConsumers) {
+    const int* spos = p.slot_pos + static_cast<size_t>(b) * S;
+    for (int i = tid; i < nloc; i += kConsumers) {
+      const int slot = t0 * kTile + i;
+      spos_s[i] = slot < S ? spos[slot] : -1;
+    }
+  }
+  __syncthreads();
+  cluster_sync_all();  // every peer's barriers are initialised before any st.async
 
-  // B operand of the QK^T mma: lane holds q[head = lane/4][k = 2*(lane%4) (+8)] pairs.
+  // ================================ producer warp =================================
+  if (warp == kConsumerWarps) {
+    if (lane == 0) {
+      for (int u = n_first; u < nt; ++u) {
+        const int st = u % kStages;
+        if (*reinterpret_cast<volatile int*>(bad_flag)) break;
+        if (!mbar_wait_bounded(&empty[st], ((u / kStages) - 1) & 1)) {
+          set_err(p.err, kErrWaitTimeout);
+          atomicExch(bad_flag, 1);
+          break;
+        }
+        if (*reinterpret_cast<volatile int*>(bad_flag)) break;
+        issue(u);
+        *reinterpret_cast<volatile int*>(n_issued) = u + 1;
+      }
+      if (*reinterpret_cast<volatile int*>(bad_flag)) {
+        // error path: let the loads still in flight (the last one of each stage) land
+        // before this CTA can exit
+        const int ni = *reinterpret_cast<volatile int*>(n_issued);
+        for (int u = (ni > kStages ? ni - kStages : 0); u < ni; ++u)
+          mbar_wait_bounded(&full[u % kStages], (u / kStages) & 1, 1u << 16);
+      }
+    }
+    __syncwarp();
+    cluster_sync_all();  // matches the consumers' final cluster barrier
+    return;
+  }
+
+  // ================================ consumer warps ================================
+  if (tid == 0) mbar_expect_tx(xbar, CS * (16 + n_mine) * 4);  // local arrival; completes on the bytes
+  const int g = lane >> 2, t = lane & 3;
   uint32_t qb[8][2];
   {
-    const int g = lane >> 2, t = lane & 3;
     const uint32_t* qrow = reinterpret_cast<const uint32_t*>(
         p.q + (static_cast<size_t>(b) * p.Hq + kvh * G + (g < G ? g : 0)) * kD);
 #pragma unroll
@@ -135,20 +197,28 @@ __global__ void __launch_bounds__(kThreads) decode_attn_score_kernel(const __gri
       qb[kk][1] = g < G ? qrow[(kk * 16 + 8 + 2 * t) >> 1] : 0u;
     }
   }
+  const bool h0_ok = 2 * t < G, h1_ok = 2 * t + 1 < G;
+  float m0 = NEG_INF, m1 = NEG_INF;  // running max of heads 2t, 2t+1 over this warp's rows
+  float l0 = 0.f, l1 = 0.f;          // this lane's share of the running sums
+  float oacc[8][4];
+#pragma unroll
+  for (int m = 0; m < 8; ++m) oacc[m][0] = oacc[m][1] = oacc[m][2] = oacc[m][3] = 0.f;
+  float* ew = escr + warp * 16 * 8;
+  const int r0 = warp * 16;
 
-  bool bad = false;
-  // ---- phase 1: logits of every slot in this CTA's range -------------------------
   for (int u = 0; u < nt; ++u) {
     const int st = u % kStages;
-    const uint32_t par = (u / kStages) & 1;
-    if (!bad && !mbar_wait_bounded(&full[st], par)) {
-      bad = true;
+    bool ok_tile = !(*reinterpret_cast<volatile int*>(bad_flag));
+    if (ok_tile && !mbar_wait_bounded(&full[st], (u / kStages) & 1)) {
       set_err(p.err, kErrWaitTimeout);
+      atomicExch(bad_flag, 1);
+      ok_tile = false;
     }
-    if (!bad) {
-      const uint8_t* tb = ring + st * kTileBytes;
-      const int r0 = warp * 16;
-      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    if (ok_tile) {
+      const uint8_t* kt = ring + st * kStageBytes;
+      const uint8_t* vt = kt + kHalfBytes;
+      // ---- Q.K^T for rows r0..r0+15 (two independent mma chains) -------------------
+      float a0c[4] = {0.f, 0.f, 0.f, 0.f}, a1c[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int kk = 0; kk < 8; ++kk) {
         const int col = kk * 16;
@@ -156,146 +226,186 @@ __global__ void __launch_bounds__(kThreads) decode_attn_score_kernel(const __gri
         const int j = lane >> 3;
         const int row = r0 + (lane & 7) + ((j & 1) << 3);
         const int chunk = cb + (j >> 1);
-        const uint32_t addr = smem_u32(tb + box * kBoxBytes + row * 128 + ((chunk ^ (row & 7)) << 4));
-        uint32_t a0, a1, a2, a3;
-        ldmatrix_x4(addr, a0, a1, a2, a3);
-        mma_bf16_16816(acc, a0, a1, a2, a3, qb[kk][0], qb[kk][1]);
+        uint32_t x0, x1, x2, x3;
+        ldmatrix_x4(smem_u32(kt + box * kBoxBytes + row * 128 + ((chunk ^ (row & 7)) << 4)), x0, x1, x2, x3);
+        if (kk & 1)
+          mma_bf16_16816(a1c, x0, x1, x2, x3, qb[kk][0], qb[kk][1]);
+        else
+          mma_bf16_16816(a0c, x0, x1, x2, x3, qb[kk][0], qb[kk][1]);
       }
-      const int g = lane >> 2, t = lane & 3;
+      // ---- rounded logits (reference rounding points) -> shared memory ---------------
+      const int lta = u * kTile + r0 + g, ltb = lta + 8;
+      const bool va = spos_s[lta] >= 0, vb = spos_s[ltb] >= 0;
+      float sa0 = va ? bf16r(bf16r(a0c[0] + a1c[0]) * p.scale) : NEG_INF;
+      float sa1 = va ? bf16r(bf16r(a0c[1] + a1c[1]) * p.scale) : NEG_INF;
+      float sb0 = vb ? bf16r(bf16r(a0c[2] + a1c[2]) * p.scale) : NEG_INF;
+      float sb1 = vb ? bf16r(bf16r(a0c[3] + a1c[3]) * p.scale) : NEG_INF;
+      *reinterpret_cast<float2*>(&logits[lta * 8 + 2 * t]) = make_float2(sa0, sa1);
+      *reinterpret_cast<float2*>(&logits[ltb * 8 + 2 * t]) = make_float2(sb0, sb1);
+      // ---- online softmax over the warp's 16 rows -----------------------------------
+      float tm0 = fmaxf(sa0, sb0), tm1 = fmaxf(sa1, sb1);
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        const int row = r0 + g + half * 8;
-        const int slot = (t0 + u) * kTile + row;
-        const int lt = u * kTile + row;
-        const bool ok = slot < S && spos[slot] >= 0;
-        float2 sv;
-        sv.x = ok ? bf16r(bf16r(acc[half * 2 + 0]) * p.scale) : NEG_INF;
-        sv.y = ok ? bf16r(bf16r(acc[half * 2 + 1]) * p.scale) : NEG_INF;
-        *reinterpret_cast<float2*>(&logits[lt * 8 + 2 * t]) = sv;
-        if (t == 0) valid[lt] = ok ? 1 : 0;
+      for (int o = 4; o < 32; o <<= 1) {
+        tm0 = fmaxf(tm0, __shfl_xor_sync(0xffffffffu, tm0, o));
+        tm1 = fmaxf(tm1, __shfl_xor_sync(0xffffffffu, tm1, o));
+      }
+      const float n0 = fmaxf(m0, tm0), n1 = fmaxf(m1, tm1);
+      const float al0 = (m0 == NEG_INF) ? 1.f : expf(m0 - n0);
+      const float al1 = (m1 == NEG_INF) ? 1.f : expf(m1 - n1);
+      m0 = n0;
+      m1 = n1;
+      const float ea0 = (va && h0_ok) ? expf(sa0 - n0) : 0.f;
+      const float ea1 = (va && h1_ok) ? expf(sa1 - n1) : 0.f;
+      const float eb0 = (vb && h0_ok) ? expf(sb0 - n0) : 0.f;
+      const float eb1 = (vb && h1_ok) ? expf(sb1 - n1) : 0.f;
+      l0 = l0 * al0 + ea0 + eb0;
+      l1 = l1 * al1 + ea1 + eb1;
+      if (__any_sync(0xffffffffu, al0 != 1.f || al1 != 1.f)) {
+#pragma unroll
+        for (int m = 0; m < 8; ++m) {
+          oacc[m][0] *= al0;
+          oacc[m][1] *= al1;
+          oacc[m][2] *= al0;
+          oacc[m][3] *= al1;
+        }
+      }
+      *reinterpret_cast<float2*>(&ew[g * 8 + 2 * t]) = make_float2(ea0, ea1);
+      *reinterpret_cast<float2*>(&ew[(g + 8) * 8 + 2 * t]) = make_float2(eb0, eb1);
+      __syncwarp();
+      if (__any_sync(0xffffffffu, va || vb)) {
+        // ---- P.V: O^T (dims x heads) += V^T (dims x slots) * P^T (slots x heads) --------
+        const float p0 = ew[(2 * t) * 8 + g], p1 = ew[(2 * t + 1) * 8 + g];
+        const float p2 = ew[(2 * t + 8) * 8 + g], p3 = ew[(2 * t + 9) * 8 + g];
+        const float h0 = bf16r(p0), h1 = bf16r(p1), h2 = bf16r(p2), h3 = bf16r(p3);
+        const uint32_t bh0 = pack_bf16(h0, h1), bh1 = pack_bf16(h2, h3);
+        const uint32_t bl0 = pack_bf16(p0 - h0, p1 - h1), bl1 = pack_bf16(p2 - h2, p3 - h3);
+        const int slot = r0 + (lane & 7) + ((lane >> 4) << 3);
+#pragma unroll
+        for (int m = 0; m < 8; ++m) {
+          const int dchunk = m * 16 + (((lane >> 3) & 1) << 3);
+          const int box = dchunk >> 6, c = (dchunk & 63) >> 3;
+          uint32_t x0, x1, x2, x3;
+          ldmatrix_x4_trans(smem_u32(vt + box * kBoxBytes + slot * 128 + ((c ^ (slot & 7)) << 4)), x0, x1, x2, x3);
+          mma_bf16_16816(oacc[m], x0, x1, x2, x3, bh0, bh1);
+          mma_bf16_16816(oacc[m], x0, x1, x2, x3, bl0, bl1);
+        }
       }
     }
-    bad = __syncthreads_or(bad);
-    if (tid == 0 && !bad && u + kStages < ntot) issue(u + kStages);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[st]);
   }
 
-  // ---- softmax statistics, combined across the cluster ---------------------------
-  for (int h = warp; h < G; h += kWarps) {
-    float m = NEG_INF;
-    for (int i = lane; i < nloc; i += 32) m = fmaxf(m, logits[i * 8 + h]);
+  // ---- merge the four warps: per-head (max, sum), then the partial outputs ---------
 #pragma unroll
-    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    if (lane == 0) st_m[h] = bad ? NEG_INF : m;
+  for (int o = 4; o < 32; o <<= 1) {
+    l0 += __shfl_xor_sync(0xffffffffu, l0, o);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, o);
   }
-  cluster.sync();
-  if (tid < G) {
-    float M = NEG_INF;
-    for (int r = 0; r < CS; ++r) M = fmaxf(M, cluster.map_shared_rank(st_m, r)[tid]);
-    fin_m[tid] = M;
+  if (lane < 4) {
+    wstat[warp * 16 + 2 * lane] = m0;
+    wstat[warp * 16 + 2 * lane + 1] = m1;
+    wstat[warp * 16 + 8 + 2 * lane] = l0;
+    wstat[warp * 16 + 8 + 2 * lane + 1] = l1;
   }
-  __syncthreads();
-  for (int h = warp; h < G; h += kWarps) {
-    const float M = fin_m[h];
-    float sum = 0.f;
-    for (int i = lane; i < nloc; i += 32) {
-      const float s = logits[i * 8 + h];
-      const float e = (s == NEG_INF || M == NEG_INF) ? 0.f : expf(s - M);
-      logits[i * 8 + h] = e;
-      sum += e;
+  named_bar(1, kConsumers);  // also: every tile consumed, the ring is free for the partials
+  if (tid < 8) {
+    float mc = NEG_INF;
+    for (int w = 0; w < kConsumerWarps; ++w) mc = fmaxf(mc, wstat[w * 16 + tid]);
+    float lc = 0.f;
+    for (int w = 0; w < kConsumerWarps; ++w) {
+      const float mw = wstat[w * 16 + tid];
+      if (mw != NEG_INF) lc += wstat[w * 16 + 8 + tid] * expf(mw - mc);
     }
+    cstat[tid] = mc;
+    cstat[8 + tid] = lc;
+  }
+  {
+    // scale this warp's partial to the CTA max; heads >= G never leave the warp
+    const float mw0 = __shfl_sync(0xffffffffu, m0, t), mw1 = __shfl_sync(0xffffffffu, m1, t);
+    float mc0 = NEG_INF, mc1 = NEG_INF;
+    for (int w = 0; w < kConsumerWarps; ++w) {
+      mc0 = fmaxf(mc0, wstat[w * 16 + 2 * t]);
+      mc1 = fmaxf(mc1, wstat[w * 16 + 2 * t + 1]);
+    }
+    const float s0 = (mw0 == NEG_INF) ? 0.f : expf(mw0 - mc0);
+    const float s1 = (mw1 == NEG_INF) ? 0.f : expf(mw1 - mc1);
+    float* ow = opart + warp * 8 * kD;
 #pragma unroll
-    for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-    if (lane == 0) st_l[h] = bad ? 0.f : sum;
+    for (int m = 0; m < 8; ++m) {
+      if (h0_ok) {
+        ow[(2 * t) * kD + 16 * m + g] = oacc[m][0] * s0;
+        ow[(2 * t) * kD + 16 * m + g + 8] = oacc[m][2] * s0;
+      }
+      if (h1_ok) {
+        ow[(2 * t + 1) * kD + 16 * m + g] = oacc[m][1] * s1;
+        ow[(2 * t + 1) * kD + 16 * m + g + 8] = oacc[m][3] * s1;
+      }
+    }
   }
-  cluster.sync();
-  if (tid < G) {
-    float Lsum = 0.f;
-    for (int r = 0; r < CS; ++r) Lsum += cluster.map_shared_rank(st_l, r)[tid];
-    fin_l[tid] = Lsum;
-    if (Lsum <= 0.f && rank == 0) set_err(p.err, kErrNoValidSlot);
+  named_bar(1, kConsumers);
+  // ---- one st.async round: (max, sum) to every peer, O element e to CTA e / per ------
+  if (warp == 0 && lane < CS) {
+    const uint32_t rbar = mapa_u32(smem_u32(xbar), lane);
+    const uint32_t rdst = mapa_u32(smem_u32(srecv + rank * 16), lane);
+    for (int h = 0; h < 16; ++h) st_async_f32(rdst + 4 * h, cstat[h], rbar);
   }
-  __syncthreads();
-  for (int i = tid; i < nloc; i += kThreads) {
-    if (valid[i] && !bad) {
+  for (int e = tid; e < G * kD; e += kConsumers) {
+    float acc = 0.f;
+#pragma unroll
+    for (int w = 0; w < kConsumerWarps; ++w) acc += opart[w * 8 * kD + e];
+    const int r = e / per;
+    st_async_f32(mapa_u32(smem_u32(orecv + rank * per + (e - r * per)), r), acc, mapa_u32(smem_u32(xbar), r));
+  }
+  if (!mbar_wait_cluster_bounded(xbar, 0)) {
+    set_err(p.err, kErrWaitTimeout);
+    atomicExch(bad_flag, 1);
+  }
+  // ---- final max M and sum L per head (identical in every CTA of the cluster) ------
+  float Mh[G], iLh[G];
+#pragma unroll
+  for (int h = 0; h < G; ++h) {
+    float M = NEG_INF;
+    for (int c = 0; c < CS; ++c) M = fmaxf(M, srecv[c * 16 + h]);
+    float Ls = 0.f;
+    for (int c = 0; c < CS; ++c) {
+      const float mc = srecv[c * 16 + h];
+      if (mc != NEG_INF) Ls += srecv[c * 16 + 8 + h] * expf(mc - M);
+    }
+    Mh[h] = M;
+    iLh[h] = Ls;
+    if (tid == 0 && rank == 0 && !(Ls > 0.f)) set_err(p.err, kErrNoValidSlot);
+  }
+  // output slice
+  {
+    const int e0 = rank * per;
+    __nv_bfloat16* orow = p.out + (static_cast<size_t>(b) * p.Hq + kvh * G) * kD;
+    for (int j = tid; j < n_mine; j += kConsumers) {
+      const int h = (e0 + j) / kD;
+      float acc = 0.f;
+      for (int c = 0; c < CS; ++c) {
+        const float mc = srecv[c * 16 + h];
+        if (mc != NEG_INF) acc += orecv[c * per + j] * expf(mc - Mh[h]);
+      }
+      orow[e0 + j] = __float2bfloat16_rn(iLh[h] > 0.f ? acc / iLh[h] : 0.f);
+    }
+  }
+  // per-slot eviction score: max over the group's heads of p = exp(s - M) / L
+  if (!(*reinterpret_cast<volatile int*>(bad_flag))) {
+    float* sscore = p.step_score + static_cast<size_t>(b) * S;
+    for (int i = tid; i < nloc; i += kConsumers) {
+      if (spos_s[i] < 0) continue;
       float mx = 0.f;
 #pragma unroll
       for (int h = 0; h < G; ++h) {
-        const float l = fin_l[h];
-        const float pr = l > 0.f ? logits[i * 8 + h] / l : 0.f;
-        logits[i * 8 + h] = pr;
+        const float pr = iLh[h] > 0.f ? expf(logits[i * 8 + h] - Mh[h]) / iLh[h] : 0.f;
         mx = fmaxf(mx, pr);
       }
       if (mx != mx) set_err(p.err, kErrNanScore);
       atomicMax(reinterpret_cast<int*>(&sscore[t0 * kTile + i]), __float_as_int(mx));
-    } else {
-#pragma unroll
-      for (int h = 0; h < 8; ++h) logits[i * 8 + h] = 0.f;
     }
   }
-  __syncthreads();
-
-  // ---- phase 2: P . V ----------------------------------------------------------
-  float o[G][4];
-#pragma unroll
-  for (int h = 0; h < G; ++h) o[h][0] = o[h][1] = o[h][2] = o[h][3] = 0.f;
-  for (int u = nt; u < ntot; ++u) {
-    const int st = u % kStages;
-    const uint32_t par = (u / kStages) & 1;
-    if (!bad && !mbar_wait_bounded(&full[st], par)) {
-      bad = true;
-      set_err(p.err, kErrWaitTimeout);
-    }
-    if (!bad) {
-      const uint8_t* tb = ring + st * kTileBytes;
-      const int ul = u - nt;
-      const int box = lane >> 4, chunk = (lane & 15) >> 1;
-      for (int r = 0; r < 16; ++r) {
-        const int row = warp * 16 + r;
-        const int lt = ul * kTile + row;
-        if (!valid[lt]) continue;
-        const float4 p0 = *reinterpret_cast<const float4*>(&logits[lt * 8]);
-        const float4 p1 = *reinterpret_cast<const float4*>(&logits[lt * 8 + 4]);
-        const float pv[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
-        const uint2 w = *reinterpret_cast<const uint2*>(tb + box * kBoxBytes + row * 128 +
-                                                        ((chunk ^ (row & 7)) << 4) + ((lane & 1) << 3));
-        const float v0 = bf16lo(w.x), v1 = bf16hi(w.x), v2 = bf16lo(w.y), v3 = bf16hi(w.y);
-#pragma unroll
-        for (int h = 0; h < G; ++h) {
-          o[h][0] = fmaf(pv[h], v0, o[h][0]);
-          o[h][1] = fmaf(pv[h], v1, o[h][1]);
-          o[h][2] = fmaf(pv[h], v2, o[h][2]);
-          o[h][3] = fmaf(pv[h], v3, o[h][3]);
-        }
-      }
-    }
-    bad = __syncthreads_or(bad);
-    if (tid == 0 && !bad && u + kStages < ntot) issue(u + kStages);
-  }
-
-  // ---- reduce P.V partials: warps -> CTA -> cluster ------------------------------
-#pragma unroll
-  for (int h = 0; h < G; ++h)
-    *reinterpret_cast<float4*>(&opart[(warp * 8 + h) * kD + 4 * lane]) = make_float4(o[h][0], o[h][1], o[h][2], o[h][3]);
-  __syncthreads();
-  for (int e = tid; e < G * kD; e += kThreads) {
-    float acc = 0.f;
-#pragma unroll
-    for (int w = 0; w < kWarps; ++w) acc += opart[w * 8 * kD + e];
-    octa[e] = acc;
-  }
-  cluster.sync();
-  {
-    const int per = (G * kD + CS - 1) / CS;
-    const int e0 = rank * per;
-    const int e1 = (e0 + per < G * kD) ? e0 + per : G * kD;
-    __nv_bfloat16* orow = p.out + (static_cast<size_t>(b) * p.Hq + kvh * G) * kD;
-    for (int e = e0 + tid; e < e1; e += kThreads) {
-      float acc = 0.f;
-      for (int r = 0; r < CS; ++r) acc += cluster.map_shared_rank(octa, r)[e];
-      orow[e] = __float2bfloat16_rn(acc);
-    }
-  }
-  cluster.sync();  // peers may still be reading this CTA's shared memory
+  __syncwarp();
+  cluster_sync_all();  // no CTA leaves while a peer may still target its shared memory
 }
 
 // ------------------------------------------------------------------------------------
@@ -332,23 +442,21 @@ static int make_cache_map(CUtensorMap* map, const void* ptr, long long rows) {
   return kStatusOk;
 }
 
-// Choose CTAs per (sequence, kv head): minimise (total tiles + per-CTA overhead)
-// spread over ~2 resident CTAs per SM, plus the tail of one CTA.
+// CTAs per (sequence, kv head).  A CTA's fixed cost (launch, barrier setup, the final
+// exchange) is several microseconds, so clusters are kept as small as possible: the
+// smallest size that (a) keeps two CTAs per SM within shared memory and (b) launches
+// at least ~1.6 CTAs per SM in total.  Measured on B200 (decode microbench shapes).
 static int choose_cluster(int pairs, int tiles, int sms, int max_nloc_tiles) {
-  int best = 8;
-  double best_t = 1e30;
-  for (int cs = 1; cs <= 8; ++cs) {
-    const int per = (tiles + cs - 1) / cs;
-    if (per > max_nloc_tiles) continue;
-    const double slots = 2.0 * sms;
-    const double ctas = static_cast<double>(pairs) * cs;
-    const double t = (static_cast<double>(pairs) * tiles + ctas * 1.0) / slots + per + 1.0;
-    if (t < best_t - 1e-9) {
-      best_t = t;
-      best = cs;
-    }
-  }
-  return best;
+  int per_max = 1;
+  for (int per = 1; per <= max_nloc_tiles; ++per)
+    if (2 * (attn_smem_layout(per).total + 2048) <= 228 * 1024) per_max = per;
+  int cs = (tiles + per_max - 1) / per_max;
+  const int want = (16 * sms / 10 + pairs - 1) / pairs;
+  if (cs < want) cs = want;
+  if (cs > tiles) cs = tiles;
+  if (cs < 1) cs = 1;
+  if (cs > kMaxCluster) cs = kMaxCluster;
+  return cs;
 }
 
 template <int G>
@@ -429,6 +537,9 @@ int decode_attn_score(cudaStream_t stream, int B, int Hq, int Hkv, int D, int S,
   a.nloc_tiles = nloc_tiles;
   a.scale = __bfloat162float(__float2bfloat16_rn(1.0f / sqrtf(static_cast<float>(kD))));
   const int smem = attn_smem_layout(nloc_tiles).total + 1024;
+  if (smem > 227 * 1024)
+    return fail(kStatusUnsupported, "decode_attn_score: %d slots per CTA need %d B of shared memory", nloc_tiles * kTile,
+                smem);
 
   cudaError_t e;
   switch (G) {
