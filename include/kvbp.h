@@ -155,6 +155,22 @@ int kvbp_prefill_compact(kvbp_stream_t stream, const kvbp_state* st, int32_t P, 
                          int32_t* evlog, int32_t evcap, int32_t* evcount, int32_t* seq_step, int32_t* next_pos,
                          int32_t* retained_log, int32_t log_steps, float* step_score, int32_t* dev_err);
 
+/* Step-0 eviction for callers that cannot allocate device memory (no counterpart in
+ * the reference).  Same result as kvbp_prefill_select followed by kvbp_prefill_compact,
+ * but the per-position victim flags live in a fixed array inside this library instead of
+ * a caller buffer: a jax.ffi / XLA custom-call handler may only use the buffers XLA
+ * assigns it (XLA pre-allocates most of the GPU, so a cudaMalloc of its own can fail).
+ * Limit: batch * prompt <= 1,048,576 positions, else KVBP_ERR_ARG.  The array costs
+ * 1 MiB on every GPU that loads the library, until the process exits.  The first call
+ * on a device looks up the array's device address (with that device current); make that
+ * first call before any stream capture.  All calls share the array: calls that overlap
+ * on the GPU (e.g. on two streams) race; calls on one stream are ordered and safe.  Each
+ * call rewrites every flag it uses, so no clearing is needed. */
+int kvbp_prefill_evict_noalloc(kvbp_stream_t stream, const kvbp_state* st, int32_t P, const kvbp_evict_cfg* cfg,
+                               const float* scores, int32_t* gather_src, int32_t* evlog, int32_t evcap,
+                               int32_t* evcount, int32_t* seq_step, int32_t* next_pos, int32_t* retained_log,
+                               int32_t log_steps, float* step_score, int32_t* dev_err);
+
 /* K6 -- copies prompt K/V rows src [layers][B][Hkv][P][128] into the slot caches
  * dst [layers][B][Hkv][S][128] following gather_src. */
 int kvbp_gather_kv(kvbp_stream_t stream, const void* src_k, const void* src_v, void* dst_k, void* dst_v,

@@ -93,6 +93,10 @@ SIGNATURES = {
         C.c_int,
         [P, C.POINTER(State), I32, I32, I32, P, P, P, P, I32, P, P, P, P, I32, P, P],
     ),
+    "kvbp_prefill_evict_noalloc": (
+        C.c_int,
+        [P, C.POINTER(State), I32, C.POINTER(EvictCfg), P, P, P, I32, P, P, P, P, I32, P, P],
+    ),
     "kvbp_gather_kv": (C.c_int, [P, P, P, P, P, P, I32, I32, I32, I32, I32]),
     "kvbp_embed": (C.c_int, [P, I32, I32, I32, P, P, P, P]),
     "kvbp_add_rmsnorm": (C.c_int, [P, I32, I32, P, P, P, P, F32]),

@@ -878,3 +878,71 @@ int kvbp_gather_kv(kvbp_stream_t stream, const void* src_k, const void* src_v, v
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------------------------
+// Step-0 eviction that allocates nothing
+// ------------------------------------------------------------------------------------
+// Callers that cannot allocate device memory (a jax.ffi / XLA custom-call handler may only
+// use the buffers XLA assigns it, and XLA usually pre-allocates most of the GPU, so a
+// cudaMalloc from inside the handler bypasses its allocator and can fail) still need the
+// per-position victim flags that sit between kvbp_prefill_select and kvbp_prefill_compact.
+// This variant keeps them in a fixed array that every GPU loading the library holds until
+// the process exits.
+#include <mutex>
+
+namespace {
+
+constexpr long long kNoAllocMaxPositions = 1LL << 20;  // batch * prompt flags (1 MiB)
+constexpr int kNoAllocMaxDevices = 64;
+
+__device__ __align__(256) uint8_t g_prefill_victim_scratch[kNoAllocMaxPositions];
+
+std::mutex g_noalloc_mu;
+uint8_t* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+
+// Device address of the scratch array on the current device.  In host code the array's
+// name is only a host-side stand-in, so the address is looked up once per device (with
+// that device current) and cached.
+int noalloc_scratch(uint8_t** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return kvbp::fail(kvbp::kStatusCuda, "kvbp_prefill_evict_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= kNoAllocMaxDevices)
+    return kvbp::fail(kvbp::kStatusUnsupported, "kvbp_prefill_evict_noalloc: device %d beyond %d", dev, kNoAllocMaxDevices);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_prefill_victim_scratch);
+    if (e != cudaSuccess || !p)
+      return kvbp::fail(kvbp::kStatusCuda, "kvbp_prefill_evict_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+    g_noalloc_ptr[dev] = static_cast<uint8_t*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return kvbp::kStatusOk;
+}
+
+}  // namespace
+
+extern "C" int kvbp_prefill_evict_noalloc(kvbp_stream_t stream, const kvbp_state* st, int32_t P,
+                                          const kvbp_evict_cfg* cfg, const float* scores, int32_t* gather_src,
+                                          int32_t* evlog, int32_t evcap, int32_t* evcount, int32_t* seq_step,
+                                          int32_t* next_pos, int32_t* retained_log, int32_t log_steps,
+                                          float* step_score, int32_t* dev_err) {
+  if (!st || !cfg) return kvbp::fail(kvbp::kStatusArg, "kvbp_prefill_evict_noalloc: null state/config");
+  if (st->B <= 0 || P <= 0) return kvbp::fail(kvbp::kStatusArg, "kvbp_prefill_evict_noalloc: bad size");
+  const long long n = static_cast<long long>(st->B) * P;
+  if (n > kNoAllocMaxPositions)
+    return kvbp::fail(kvbp::kStatusArg,
+                      "kvbp_prefill_evict_noalloc: batch %d x prompt %d = %lld positions exceeds the fixed "
+                      "scratch of %lld; use kvbp_prefill_select + kvbp_prefill_compact with your own buffer",
+                      st->B, P, n, kNoAllocMaxPositions);
+  uint8_t* scratch = nullptr;
+  int s = noalloc_scratch(&scratch);
+  if (s) return s;
+  // kvbp_prefill_select rewrites every flag of the B*P range, so nothing needs clearing.
+  int32_t n_policy = 0;
+  s = kvbp_prefill_select(stream, st->B, P, cfg, scores, scratch, evlog, evcap, &n_policy, dev_err);
+  if (s) return s;
+  return kvbp_prefill_compact(stream, st, P, cfg->capacity, n_policy, scratch, scores, gather_src, evlog, evcap,
+                              evcount, seq_step, next_pos, retained_log, log_steps, step_score, dev_err);
+}
