@@ -185,6 +185,31 @@ int kvbp_add_rmsnorm(kvbp_stream_t stream, int32_t rows, int32_t hidden, void* h
                      void* out, float eps);
 /* act = bf16(bf16(g * bf16(sigmoid(g))) * u) for gu = [g | u] rows, jax_inference.py:702-704,1103-1107. */
 int kvbp_silu_mul(kvbp_stream_t stream, int32_t rows, int32_t ffn, const void* gu, void* act);
+/* ss_out[r] = sum over the row of h[r][:]^2 (fp32), rows <= 32: the RMSNorm statistics of
+ * the embedding output for the first decode GEMM's norm prologue. */
+int kvbp_row_sumsq(kvbp_stream_t stream, int32_t rows, int32_t hidden, const void* h, float* ss_out);
+
+/* Weight-streaming decode GEMM out[M][N] = X[M][K] . W[N][K]^T (bf16, fp32 accumulate),
+ * M <= 32, N and K multiples of 128 -- the q/k/v, o, gate/up, down and lm_head products
+ * of _forward_jittable (jax_inference.py:949-956,1081,1095-1107,1330-1333).
+ * Prologue: with norm_w != NULL, X is bf16((x * inv_rms[m]) * norm_w[k]) where x (ldx) is
+ *   the residual stream and inv_rms[m] = 1/sqrt(sum_t ss_parts[t][m] / K + eps) over the
+ *   n_parts partial sums ([n_parts][32] floats) -- RMSNorm (jax_inference.py:609-618).
+ * Epilogue 0 (plain): out = bf16(acc).
+ * Epilogue 1 (residual): out (the residual stream, ldo == N) = bf16(out + bf16(acc)) in
+ *   place, and ss_out[N/128][32] receives each 128-column tile's per-row sum of squares of
+ *   the new stream (the next norm's n_parts = N/128) -- jax_inference.py:1280,1325.
+ * Epilogue 2 (SwiGLU): W rows hold gate and up features interleaved in blocks of 64
+ *   (rows 128t..128t+63 = gate features 64t.., rows 128t+64.. = the matching up features);
+ *   out[M][N/2] = bf16(bf16(g * bf16(sigmoid(g))) * u) with g, u the bf16 GEMM outputs
+ *   (jax_inference.py:702-704,1103-1107).
+ * splits > 1 splits K over CTAs: partial [splits][M][N] fp32 and tickets [N/128] int32
+ * (all zero before the first call; the kernel leaves them zero) are workspace. */
+int kvbp_decode_gemm(kvbp_stream_t stream, int32_t epilogue, int32_t M, int32_t N, int32_t K, const void* w,
+                     const void* x, int32_t ldx, const float* ss_parts, int32_t n_parts, const void* norm_w, float eps,
+                     void* out, int32_t ldo, float* ss_out, float* partial, int32_t* tickets, int32_t splits,
+                     int32_t* dev_err);
+
 /* Greedy sampling: first index of the row maximum (numpy.argmax), kv_coupled_generator.py:344. */
 int kvbp_argmax(kvbp_stream_t stream, int32_t rows, int32_t vocab, int64_t ld, const void* logits, int32_t* out_ids);
 

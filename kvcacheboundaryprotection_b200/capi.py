@@ -102,6 +102,8 @@ SIGNATURES = {
     "kvbp_add_rmsnorm": (C.c_int, [P, I32, I32, P, P, P, P, F32]),
     "kvbp_silu_mul": (C.c_int, [P, I32, I32, P, P]),
     "kvbp_argmax": (C.c_int, [P, I32, I32, I64, P, P]),
+    "kvbp_row_sumsq": (C.c_int, [P, I32, I32, P, P]),
+    "kvbp_decode_gemm": (C.c_int, [P, I32, I32, I32, I32, P, P, I32, P, I32, P, F32, P, I32, P, P, P, I32, P]),
 }
 EXTRA_SIGNATURES = {
     "kvbp_decode_attn_score_cs": (C.c_int, [P, I32, I32, I32, I32, I32, P, P, P, P, P, P, P, I32]),

@@ -116,20 +116,22 @@ __global__ void __launch_bounds__(kThreads) decode_attn_score_kernel(const __gri
   const int t0 = (rank * p.tiles) / CS, t1 = ((rank + 1) * p.tiles) / CS;
   const int nt = t1 - t0, nloc = nt * kTile;
   const int S = p.S;
-  const int row_base = (b * p.Hkv + kvh) * S;
   const int per = (G * kD + CS - 1) / CS;  // output slice per CTA
   const int n_mine = (rank * per < G * kD) ? ((rank * per + per < G * kD) ? per : G * kD - rank * per) : 0;
   const float NEG_INF = -__int_as_float(0x7f800000);
 
+  // [pair][slot][128] view: rows past S are out of bounds and arrive as zeros without
+  // touching memory, so the last tile of a pair costs no extra HBM traffic
+  const int pair = b * p.Hkv + kvh;
   auto issue = [&](int u) {
     const int st = u % kStages;
     uint8_t* dst = ring + st * kStageBytes;
-    const int y = row_base + (t0 + u) * kTile;
+    const int y = (t0 + u) * kTile;
     mbar_expect_tx(&full[st], kStageBytes);
-    tma_load_2d(dst, &kmap, &full[st], 0, y);
-    tma_load_2d(dst + kBoxBytes, &kmap, &full[st], 64, y);
-    tma_load_2d(dst + kHalfBytes, &vmap, &full[st], 0, y);
-    tma_load_2d(dst + kHalfBytes + kBoxBytes, &vmap, &full[st], 64, y);
+    tma_load_3d(dst, &kmap, &full[st], 0, y, pair);
+    tma_load_3d(dst + kBoxBytes, &kmap, &full[st], 64, y, pair);
+    tma_load_3d(dst + kHalfBytes, &vmap, &full[st], 0, y, pair);
+    tma_load_3d(dst + kHalfBytes + kBoxBytes, &vmap, &full[st], 64, y, pair);
   };
   const int n_first = nt < kStages ? nt : kStages;
   if (tid == kConsumers) {
@@ -142,6 +144,10 @@ __global__ void __launch_bounds__(kThreads) decode_attn_score_kernel(const __gri
     mbar_init(xbar, 1);
     *bad_flag = 0;
     fence_barrier_init();
+  }
+  if (!KVBP_PDL_LATE) pdl_launch_dependents();
+  pdl_wait();  // q, slot positions and the new K/V row come from earlier kernels
+  if (tid == kConsumers) {
     // start streaming at once: the first stages depend on nothing but this CTA
     for (int u = 0; u < n_first; ++u) issue(u);
     *n_issued = n_first;
@@ -180,6 +186,7 @@ __global__ void __launch_bounds__(kThreads) decode_attn_score_kernel(const __gri
       }
     }
     __syncwarp();
+    if (KVBP_PDL_LATE) pdl_launch_dependents();
     cluster_sync_all();  // matches the consumers' final cluster barrier
     return;
   }
@@ -294,6 +301,7 @@ __global__ void __launch_bounds__(kThreads) decode_attn_score_kernel(const __gri
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[st]);
   }
+  if (KVBP_PDL_LATE) pdl_launch_dependents();
 
   // ---- merge the four warps: per-head (max, sum), then the partial outputs ---------
 #pragma unroll
@@ -427,15 +435,15 @@ static EncodeTiledFn get_encode_fn() {
   return fn;
 }
 
-// [rows, 128] bf16 view of a [B, Hkv, S, 128] cache; 64x64 boxes with 128-byte swizzle.
-static int make_cache_map(CUtensorMap* map, const void* ptr, long long rows) {
+// [pairs][S][128] bf16 view of a [B, Hkv, S, 128] cache; 64 x 64 x 1 boxes, 128-byte swizzle.
+static int make_cache_map(CUtensorMap* map, const void* ptr, long long pairs, int S) {
   EncodeTiledFn enc = get_encode_fn();
   if (!enc) return fail(kStatusCuda, "cuTensorMapEncodeTiled unavailable (driver too old or no GPU)");
-  cuuint64_t dims[2] = {static_cast<cuuint64_t>(kD), static_cast<cuuint64_t>(rows)};
-  cuuint64_t strides[1] = {static_cast<cuuint64_t>(kD * 2)};
-  cuuint32_t box[2] = {64, static_cast<cuuint32_t>(kTile)};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(kD), static_cast<cuuint64_t>(S), static_cast<cuuint64_t>(pairs)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(kD * 2), static_cast<cuuint64_t>(S) * kD * 2};
+  cuuint32_t box[3] = {64, static_cast<cuuint32_t>(kTile), 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(kStatusCuda, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
@@ -469,19 +477,7 @@ static cudaError_t launch_g(cudaStream_t stream, const CUtensorMap& km, const CU
     if (e != cudaSuccess) return e;
     configured_smem = smem;
   }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(a.cluster, a.Hkv, a.B);
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = a.cluster;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, km, vm, a);
+  return launch_pdl(kern, dim3(a.cluster, a.Hkv, a.B), dim3(kThreads), smem, stream, a.cluster, km, vm, a);
 }
 
 int decode_attn_score(cudaStream_t stream, int B, int Hq, int Hkv, int D, int S, const void* q, const void* kcache,
@@ -517,9 +513,9 @@ int decode_attn_score(cudaStream_t stream, int B, int Hq, int Hkv, int D, int S,
     return fail(kStatusUnsupported, "decode_attn_score: %d slots exceed the per-cluster limit", S);
 
   CUtensorMap km, vm;
-  int st = make_cache_map(&km, kcache, rows);
+  int st = make_cache_map(&km, kcache, static_cast<long long>(B) * Hkv, S);
   if (st) return st;
-  st = make_cache_map(&vm, vcache, rows);
+  st = make_cache_map(&vm, vcache, static_cast<long long>(B) * Hkv, S);
   if (st) return st;
 
   AttnArgs a;

@@ -32,6 +32,8 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 // ---- embedding gather --------------------------------------------------------------
 __global__ void embed_kernel(const __nv_bfloat16* __restrict__ table, const int* __restrict__ ids, int V, int H,
                              __nv_bfloat16* __restrict__ out, int* err) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int r = blockIdx.x;
   const int id = ids[r];
   if (id < 0 || id >= V) {
@@ -43,10 +45,27 @@ __global__ void embed_kernel(const __nv_bfloat16* __restrict__ table, const int*
   for (int i = threadIdx.x; i < H / 8; i += blockDim.x) dst[i] = src[i];
 }
 
+// ---- per-row sum of squares (feeds the RMSNorm prologue of the decode GEMM) -----------
+__global__ void row_sumsq_kernel(const __nv_bfloat16* __restrict__ h, int H, float* __restrict__ ss_out) {
+  pdl_launch_dependents();
+  pdl_wait();
+  __shared__ float red[32];
+  const size_t r = blockIdx.x;
+  float ss = 0.f;
+  for (int i = threadIdx.x * 2; i < H; i += blockDim.x * 2) {
+    const uint32_t hv = *reinterpret_cast<const uint32_t*>(h + r * H + i);
+    ss += bf16lo(hv) * bf16lo(hv) + bf16hi(hv) * bf16hi(hv);
+  }
+  ss = block_sum(ss, red);
+  if (threadIdx.x == 0) ss_out[r] = ss;
+}
+
 // ---- h = bf16(h + delta); out = bf16(rmsnorm(h) * w) ---------------------------------
 __global__ void add_rmsnorm_kernel(__nv_bfloat16* __restrict__ h, const __nv_bfloat16* __restrict__ delta,
                                    const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ out, int H,
                                    float eps) {
+  pdl_launch_dependents();
+  pdl_wait();
   __shared__ float red[32];
   const size_t r = blockIdx.x;
   __nv_bfloat16* hr = h + r * H;
@@ -83,6 +102,8 @@ __global__ void qkv_epilogue_kernel(const __nv_bfloat16* __restrict__ qkv, int l
                                     const int* __restrict__ write_slot, int rows_per_seq, int Hq, int Hkv, int S,
                                     __nv_bfloat16* __restrict__ q_out, __nv_bfloat16* __restrict__ kcache,
                                     __nv_bfloat16* __restrict__ vcache, int* err) {
+  pdl_launch_dependents();
+  pdl_wait();
   __shared__ float red[32];
   const int r = blockIdx.x, hh = blockIdx.y, i = threadIdx.x;
   const __nv_bfloat16* src = qkv + static_cast<size_t>(r) * ldq + hh * 128;
@@ -130,6 +151,8 @@ __global__ void qkv_epilogue_kernel(const __nv_bfloat16* __restrict__ qkv, int l
 // ---- SwiGLU: act = bf16(bf16(g * bf16(sigmoid(g))) * u) -------------------------------
 __global__ void silu_mul_kernel(const __nv_bfloat16* __restrict__ gu, int F, long long n,
                                 __nv_bfloat16* __restrict__ act) {
+  pdl_launch_dependents();
+  pdl_wait();
   for (long long e = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) * 2; e < n;
        e += static_cast<long long>(gridDim.x) * blockDim.x * 2) {
     const long long r = e / F, c = e % F;
@@ -161,6 +184,8 @@ __device__ __forceinline__ bool arg_better(float av, int ai, float bv, int bi) {
 }
 
 __global__ void argmax_kernel(const __nv_bfloat16* __restrict__ logits, long long ld, int V, int* __restrict__ out) {
+  pdl_launch_dependents();
+  pdl_wait();
   __shared__ float sv[32];
   __shared__ int si[32];
   const int r = blockIdx.x;
@@ -207,8 +232,8 @@ __global__ void argmax_kernel(const __nv_bfloat16* __restrict__ logits, long lon
 }
 
 // ------------------------------------------------------------------------------------
-static int check_launch(const char* what) {
-  cudaError_t e = cudaGetLastError();
+static int check_launch(const char* what, cudaError_t e0 = cudaSuccess) {
+  cudaError_t e = e0 != cudaSuccess ? e0 : cudaGetLastError();
   if (e != cudaSuccess) return fail(kStatusCuda, "%s launch: %s", what, cudaGetErrorString(e));
   return kStatusOk;
 }
@@ -216,18 +241,18 @@ static int check_launch(const char* what) {
 int embed(cudaStream_t st, int rows, int V, int H, const void* table, const int* ids, void* out, int* err) {
   if (!table || !ids || !out) return fail(kStatusArg, "embed: null pointer");
   if (rows <= 0 || H <= 0 || V <= 0 || H % 8) return fail(kStatusArg, "embed: bad size (H must be a multiple of 8)");
-  embed_kernel<<<rows, 128, 0, st>>>(static_cast<const __nv_bfloat16*>(table), ids, V, H,
+  const cudaError_t le = launch_pdl(embed_kernel, dim3(rows), dim3(128), 0, st, 0, static_cast<const __nv_bfloat16*>(table), ids, V, H,
                                      static_cast<__nv_bfloat16*>(out), err);
-  return check_launch("embed");
+  return check_launch("embed", le);
 }
 
 int add_rmsnorm(cudaStream_t st, int rows, int H, void* h, const void* delta, const void* w, void* out, float eps) {
   if (!h || !w || !out) return fail(kStatusArg, "add_rmsnorm: null pointer");
   if (rows <= 0 || H <= 0 || H % 2) return fail(kStatusArg, "add_rmsnorm: bad size");
-  add_rmsnorm_kernel<<<rows, 256, 0, st>>>(static_cast<__nv_bfloat16*>(h), static_cast<const __nv_bfloat16*>(delta),
+  const cudaError_t le = launch_pdl(add_rmsnorm_kernel, dim3(rows), dim3(256), 0, st, 0, static_cast<__nv_bfloat16*>(h), static_cast<const __nv_bfloat16*>(delta),
                                            static_cast<const __nv_bfloat16*>(w), static_cast<__nv_bfloat16*>(out), H,
                                            eps);
-  return check_launch("add_rmsnorm");
+  return check_launch("add_rmsnorm", le);
 }
 
 int qkv_epilogue(cudaStream_t st, int rows, int rows_per_seq, int Hq, int Hkv, int D, int S, const void* qkv, int ldq,
@@ -240,12 +265,19 @@ int qkv_epilogue(cudaStream_t st, int rows, int rows_per_seq, int Hq, int Hkv, i
     return fail(kStatusArg, "qkv_epilogue: bad size");
   if ((Hq + 2 * Hkv) > 65535) return fail(kStatusArg, "qkv_epilogue: too many heads");
   dim3 grid(rows, Hq + 2 * Hkv);
-  qkv_epilogue_kernel<<<grid, 64, 0, st>>>(
+  const cudaError_t le = launch_pdl(qkv_epilogue_kernel, grid, dim3(64), 0, st, 0, 
       static_cast<const __nv_bfloat16*>(qkv), ldq, static_cast<const __nv_bfloat16*>(bias),
       static_cast<const __nv_bfloat16*>(qnw), static_cast<const __nv_bfloat16*>(knw), eps, inv_freq, positions,
       write_slot, rows_per_seq, Hq, Hkv, S, static_cast<__nv_bfloat16*>(q_out), static_cast<__nv_bfloat16*>(kcache),
       static_cast<__nv_bfloat16*>(vcache), err);
-  return check_launch("qkv_epilogue");
+  return check_launch("qkv_epilogue", le);
+}
+
+int row_sumsq(cudaStream_t st, int rows, int H, const void* h, float* ss_out) {
+  if (!h || !ss_out) return fail(kStatusArg, "row_sumsq: null pointer");
+  if (rows <= 0 || rows > 32 || H <= 0 || H % 2) return fail(kStatusArg, "row_sumsq: bad size (rows 1..32)");
+  const cudaError_t le = launch_pdl(row_sumsq_kernel, dim3(rows), dim3(256), 0, st, 0, static_cast<const __nv_bfloat16*>(h), H, ss_out);
+  return check_launch("row_sumsq", le);
 }
 
 int silu_mul(cudaStream_t st, int rows, int F, const void* gu, void* act) {
@@ -254,9 +286,9 @@ int silu_mul(cudaStream_t st, int rows, int F, const void* gu, void* act) {
   const long long n = static_cast<long long>(rows) * F;
   long long blocks = (n / 2 + 255) / 256;
   if (blocks > 148 * 16) blocks = 148 * 16;
-  silu_mul_kernel<<<static_cast<int>(blocks), 256, 0, st>>>(static_cast<const __nv_bfloat16*>(gu), F, n,
+  const cudaError_t le = launch_pdl(silu_mul_kernel, dim3(static_cast<int>(blocks)), dim3(256), 0, st, 0, static_cast<const __nv_bfloat16*>(gu), F, n,
                                                              static_cast<__nv_bfloat16*>(act));
-  return check_launch("silu_mul");
+  return check_launch("silu_mul", le);
 }
 
 int argmax_rows(cudaStream_t st, int rows, int V, long long ld, const void* logits, int* out) {
@@ -264,8 +296,8 @@ int argmax_rows(cudaStream_t st, int rows, int V, long long ld, const void* logi
   if (rows <= 0 || V <= 0 || ld < V) return fail(kStatusArg, "argmax: bad size");
   if ((ld % 8) || (reinterpret_cast<uintptr_t>(logits) & 15))
     return fail(kStatusArg, "argmax: rows must be 16-byte aligned (ld % 8 == 0)");
-  argmax_kernel<<<rows, 1024, 0, st>>>(static_cast<const __nv_bfloat16*>(logits), ld, V, out);
-  return check_launch("argmax");
+  const cudaError_t le = launch_pdl(argmax_kernel, dim3(rows), dim3(1024), 0, st, 0, static_cast<const __nv_bfloat16*>(logits), ld, V, out);
+  return check_launch("argmax", le);
 }
 
 }  // namespace kvbp
@@ -285,6 +317,10 @@ int kvbp_embed(kvbp_stream_t stream, int32_t rows, int32_t vocab, int32_t hidden
 int kvbp_add_rmsnorm(kvbp_stream_t stream, int32_t rows, int32_t hidden, void* h, const void* delta, const void* w,
                      void* out, float eps) {
   return kvbp::add_rmsnorm(reinterpret_cast<cudaStream_t>(stream), rows, hidden, h, delta, w, out, eps);
+}
+
+int kvbp_row_sumsq(kvbp_stream_t stream, int32_t rows, int32_t hidden, const void* h, float* ss_out) {
+  return kvbp::row_sumsq(reinterpret_cast<cudaStream_t>(stream), rows, hidden, h, ss_out);
 }
 
 int kvbp_silu_mul(kvbp_stream_t stream, int32_t rows, int32_t ffn, const void* gu, void* act) {

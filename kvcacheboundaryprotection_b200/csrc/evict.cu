@@ -240,6 +240,8 @@ __device__ int select_bit_warp(const uint32_t* words, int W, int k) {
 // ------------------------------------------------------------------------------------
 __global__ void score_update_kernel(StateArgs st, const int* __restrict__ seq_step, float* __restrict__ step_score,
                                     int* err) {
+  pdl_launch_dependents();
+  pdl_wait();
   __shared__ float red[32];
   const int b = blockIdx.x;
   SeqState s = st.seq(b);
@@ -296,6 +298,8 @@ __device__ void log_victim(const AppendArgs& a, int b, int pos) {
 }
 
 __global__ void __launch_bounds__(kEvictThreads) append_evict_kernel(AppendArgs a) {
+  pdl_launch_dependents();
+  pdl_wait();
   extern __shared__ int s_vict[];  // [S] victim slots of this call, in eviction order
   __shared__ int red_i[32];
   __shared__ float red_f[32];
@@ -670,7 +674,8 @@ static bool state_ok(const StateArgs& s) {
 
 int score_update(cudaStream_t stream, const StateArgs& st, const int* seq_step, float* step_score, int* err) {
   if (!state_ok(st) || !seq_step || !step_score) return fail(kStatusArg, "score_update: bad argument");
-  score_update_kernel<<<st.B, 256, 0, stream>>>(st, seq_step, step_score, err);
+  cudaError_t le = launch_pdl(score_update_kernel, dim3(st.B), dim3(256), 0, stream, 0, st, seq_step, step_score, err);
+  if (le != cudaSuccess) return fail(kStatusCuda, "score_update launch: %s", cudaGetErrorString(le));
   return check_launch("score_update");
 }
 
@@ -689,7 +694,8 @@ int append_evict(cudaStream_t stream, const AppendArgs& a) {
     if (e != cudaSuccess) return fail(kStatusCuda, "append_evict: %s", cudaGetErrorString(e));
     configured = smem;
   }
-  append_evict_kernel<<<a.st.B, kEvictThreads, smem, stream>>>(a);
+  cudaError_t le = launch_pdl(append_evict_kernel, dim3(a.st.B), dim3(kEvictThreads), smem, stream, 0, a);
+  if (le != cudaSuccess) return fail(kStatusCuda, "append_evict launch: %s", cudaGetErrorString(le));
   return check_launch("append_evict");
 }
 

@@ -77,12 +77,32 @@ class EvictionSpec:
         return capi.protection_sizes(cap, self.prefix_frac, self.suffix_frac)
 
 
+def interleave_gate_up(gate: torch.Tensor, up: torch.Tensor, block: int = 64) -> torch.Tensor:
+    """[2F, H] with rows 128t..128t+63 = gate rows 64t.. and 128t+64.. = the matching up rows
+    (the layout the SwiGLU epilogue of kvbp_decode_gemm expects)."""
+    F, H = gate.shape
+    if F % block:
+        raise ValueError(f"ffn {F} must be a multiple of {block}")
+    return torch.stack([gate.view(F // block, block, H), up.view(F // block, block, H)], 1).reshape(2 * F, H).contiguous()
+
+
+def deinterleave_gate_up(gu: torch.Tensor, block: int = 64) -> torch.Tensor:
+    """[rows, 2F] GEMM output in interleaved feature order -> [rows, 2F] as [gate | up]."""
+    R, F2 = gu.shape
+    v = gu.view(R, F2 // (2 * block), 2, block)
+    return torch.cat([v[:, :, 0, :].reshape(R, F2 // 2), v[:, :, 1, :].reshape(R, F2 // 2)], 1)
+
+
 class FusedWeights:
     """Decoder weights on the device in the engine's layout (bf16): q/k/v stacked into
-    one [(Hq+2Hkv)*128, H] matrix (+ stacked bias), gate/up stacked into [2F, H]."""
+    one [(Hq+2Hkv)*128, H] matrix (+ stacked bias); gate/up interleaved in blocks of 64
+    rows for the own decode GEMM (``gemm="kvbp"``) or stacked [gate; up] for cuBLAS."""
 
-    def __init__(self, cfg: ModelConfig, w: Dict[str, torch.Tensor], device: torch.device):
+    def __init__(self, cfg: ModelConfig, w: Dict[str, torch.Tensor], device: torch.device, gemm: str = "kvbp"):
         c, d, bf = cfg, torch.device(device), torch.bfloat16
+        if gemm not in ("kvbp", "cublas"):
+            raise ValueError("gemm must be 'kvbp' or 'cublas'")
+        self.gemm = gemm
 
         def g(name):
             return w[name].to(device=d, dtype=bf).contiguous()
@@ -104,7 +124,9 @@ class FusedWeights:
                     "q_norm": g(f"l{i}.q_norm") if c.qk_norm else None,
                     "k_norm": g(f"l{i}.k_norm") if c.qk_norm else None,
                     "w_o": g(f"l{i}.wo"),
-                    "w_gu": torch.cat([g(f"l{i}.w_gate"), g(f"l{i}.w_up")], 0).contiguous(),
+                    "w_gu": interleave_gate_up(g(f"l{i}.w_gate"), g(f"l{i}.w_up"))
+                    if gemm == "kvbp"
+                    else torch.cat([g(f"l{i}.w_gate"), g(f"l{i}.w_up")], 0).contiguous(),
                     "w_down": g(f"l{i}.w_down"),
                 }
             )
@@ -129,6 +151,7 @@ class CappedKVEngine:
         max_new_tokens: int,
         device: Optional[torch.device] = None,
         kv_heads: Optional[List[int]] = None,
+        gemm: str = "kvbp",
     ):
         if cfg.head_dim != 128:
             raise ValueError("only head_dim 128 is supported")
@@ -157,6 +180,9 @@ class CappedKVEngine:
         self.S = C + (evict.evict_every if evict.regime == "decode" else max(1, self.max_new))
         self.W = (self.max_prompt + self.max_new + 2 + 31) // 32
         self.evcap = self.max_prompt + self.max_new + 2
+        self.gemm = weights.gemm if isinstance(weights, FusedWeights) else gemm
+        if self.gemm == "kvbp" and self.B > 32:
+            raise ValueError("the decode GEMM handles up to 32 sequences per GPU")
         self._load_weights(weights)
         self._alloc()
         self.graph: Optional[torch.cuda.CUDAGraph] = None
@@ -165,7 +191,7 @@ class CappedKVEngine:
 
     # ------------------------------------------------------------------ setup
     def _load_weights(self, w) -> None:
-        fw = w if isinstance(w, FusedWeights) else FusedWeights(self.cfg, w, self.dev)
+        fw = w if isinstance(w, FusedWeights) else FusedWeights(self.cfg, w, self.dev, gemm=self.gemm)
         self.fw = fw
         self.embed_w, self.lm_w, self.final_norm = fw.embed_w, fw.lm_w, fw.final_norm
         self.layers = fw.layers
@@ -209,6 +235,19 @@ class CappedKVEngine:
         self.act = z(B, F, dt=bf)
         self.dn = z(B, H, dt=bf)
         self.logits = z(B, V, dt=bf)
+        # own-GEMM workspace: RMSNorm partial sums, split-K partials and tickets
+        self.ss_a = z(max(1, H // 128), 32, dt=f32)
+        self.ss_b = z(max(1, H // 128), 32, dt=f32)
+        self.splits = {}
+        psize = 1
+        for name, (N, K) in {"qkv": (c.qkv_dim, H), "o": (H, c.n_heads * c.head_dim), "gu": (2 * F, H),
+                             "down": (H, F), "lm": (V, H)}.items():
+            sp = self._pick_splits(N, K)
+            self.splits[name] = sp
+            if sp > 1:
+                psize = max(psize, sp * B * N)
+        self.gemm_partial = z(psize, dt=f32)
+        self.gemm_tickets = z(max(c.qkv_dim, 2 * F, V, H) // 128 + 1)
         self._state = State(
             B, S, self.W,
             self.slot_pos.data_ptr(), self.insert_step.data_ptr(), self.last_access.data_ptr(),
@@ -219,6 +258,14 @@ class CappedKVEngine:
             self.ev.capacity, self.ev.evict_every, self.policy_id, int(self.ev.protect), self.n_prefix,
             self.n_suffix, int(self.ev.regime == "decode"),
         )
+
+    @staticmethod
+    def _pick_splits(N: int, K: int, sms: int = 148) -> int:
+        """Split K so the grid has about one CTA per SM (N / 128 column tiles per split);
+        measured best on B200 for the decode shapes (1 split once N / 128 >= #SMs)."""
+        tiles = max(1, N // 128)
+        want = int(round(sms / tiles))
+        return max(1, min(want, K // 128, 16))
 
     @property
     def stream(self) -> int:
@@ -306,6 +353,8 @@ class CappedKVEngine:
                 o = torch.mm(att, Lw["w_o"].t())
                 check(L.kvbp_add_rmsnorm(st, P, H, _ptr(h), _ptr(o), _ptr(Lw["post_norm"]), _ptr(x), c.eps), "rmsnorm")
                 gu = torch.mm(x, Lw["w_gu"].t())
+                if self.gemm == "kvbp":
+                    gu = deinterleave_gate_up(gu)
                 act = torch.empty(P, c.ffn, dtype=torch.bfloat16, device=d)
                 check(L.kvbp_silu_mul(st, P, c.ffn, _ptr(gu), _ptr(act)), "silu_mul")
                 delta = torch.mm(act, Lw["w_down"].t())
@@ -383,7 +432,56 @@ class CappedKVEngine:
             "append_evict",
         )
 
+    def _gemm(self, name, epi, N, K, w, x, ldx, out, ldo, norm_w=None, ss_in=None, n_parts=0, ss_out=None):
+        c = self.cfg
+        check(
+            lib().kvbp_decode_gemm(
+                self.stream, epi, self.B, N, K, _ptr(w), _ptr(x), ldx, _ptr(ss_in), n_parts, _ptr(norm_w), c.eps,
+                _ptr(out), ldo, _ptr(ss_out), _ptr(self.gemm_partial), _ptr(self.gemm_tickets), self.splits[name],
+                _ptr(self.dev_err),
+            ),
+            f"decode_gemm[{name}]",
+        )
+
     def _forward(self) -> None:
+        if self.gemm == "kvbp":
+            self._forward_kvbp()
+        else:
+            self._forward_cublas()
+
+    def _forward_kvbp(self) -> None:
+        """Forward with the own decode GEMMs: the RMSNorms ride in the GEMM prologues, the
+        residual adds and SwiGLU in the epilogues (6 launches per layer)."""
+        c, st, L, B = self.cfg, self.stream, lib(), self.B
+        H, D, F = c.hidden, c.head_dim, c.ffn
+        nt_h = H // 128
+        check(L.kvbp_embed(st, B, c.vocab, H, _ptr(self.embed_w), _ptr(self.tokens), _ptr(self.h), _ptr(self.dev_err)), "embed")
+        check(L.kvbp_row_sumsq(st, B, H, _ptr(self.h), _ptr(self.ss_a)), "row_sumsq")
+        ss_in, n_in = self.ss_a, 1
+        for li, Lw in enumerate(self.layers):
+            self._gemm("qkv", 0, c.qkv_dim, H, Lw["w_qkv"], self.h, H, self.qkv, c.qkv_dim, Lw["in_norm"], ss_in, n_in)
+            check(
+                L.kvbp_qkv_rope_scatter(
+                    st, B, 1, c.n_heads, c.n_kv_heads, D, self.S, _ptr(self.qkv), c.qkv_dim, _ptr(Lw["b_qkv"]),
+                    _ptr(Lw["q_norm"]), _ptr(Lw["k_norm"]), c.eps, _ptr(self.inv_freq), _ptr(self.cur_pos),
+                    _ptr(self.write_slot), _ptr(self.q), _ptr(self.kc[li]), _ptr(self.vc[li]), _ptr(self.dev_err),
+                ),
+                "qkv_rope_scatter",
+            )
+            check(
+                L.kvbp_decode_attn_score(
+                    st, B, c.n_heads, c.n_kv_heads, D, self.S, _ptr(self.q), _ptr(self.kc[li]), _ptr(self.vc[li]),
+                    _ptr(self.slot_pos), _ptr(self.attn_out), _ptr(self.step_score), _ptr(self.dev_err),
+                ),
+                "decode_attn_score",
+            )
+            self._gemm("o", 1, H, c.n_heads * D, Lw["w_o"], self.attn_out, c.n_heads * D, self.h, H, ss_out=self.ss_b)
+            self._gemm("gu", 2, 2 * F, H, Lw["w_gu"], self.h, H, self.act, F, Lw["post_norm"], self.ss_b, nt_h)
+            self._gemm("down", 1, H, F, Lw["w_down"], self.act, F, self.h, H, ss_out=self.ss_a)
+            ss_in, n_in = self.ss_a, nt_h
+        self._gemm("lm", 0, c.vocab, H, self.lm_w, self.h, H, self.logits, c.vocab, self.final_norm, ss_in, n_in)
+
+    def _forward_cublas(self) -> None:
         """Forward the token of every sequence at cur_pos, writing its K/V to write_slot."""
         c, st, L, B = self.cfg, self.stream, lib(), self.B
         H, D = c.hidden, c.head_dim
@@ -436,12 +534,13 @@ class CappedKVEngine:
         s = torch.cuda.Stream(self.dev)
         s.wait_stream(torch.cuda.current_stream(self.dev))
         # cuBLAS creates its handle and workspace lazily; do that outside the capture
-        with torch.cuda.stream(s):
-            L0 = self.layers[0]
-            for a, w, o in ((self.x, L0["w_qkv"], self.qkv), (self.attn_out, L0["w_o"], self.o),
-                            (self.x, L0["w_gu"], self.gu), (self.act, L0["w_down"], self.dn),
-                            (self.x, self.lm_w, self.logits)):
-                torch.mm(a, w.t(), out=o)
+        if self.gemm == "cublas":
+            with torch.cuda.stream(s):
+                L0 = self.layers[0]
+                for a, w, o in ((self.x, L0["w_qkv"], self.qkv), (self.attn_out, L0["w_o"], self.o),
+                                (self.x, L0["w_gu"], self.gu), (self.act, L0["w_down"], self.dn),
+                                (self.x, self.lm_w, self.logits)):
+                    torch.mm(a, w.t(), out=o)
         s.synchronize()
         g = torch.cuda.CUDAGraph()
         with torch.cuda.stream(s):

@@ -1,0 +1,131 @@
+"""kvbp_decode_gemm vs. a plain PyTorch fp32 reference of the same op.
+
+Reference op: out = bf16(X @ W^T) with X, W bf16 and fp32 accumulation.  With the norm
+prologue X = bf16((h * inv_rms) * w_norm), inv_rms = 1/sqrt(mean(h^2) + eps) (fp32).
+Residual epilogue: h <- bf16(h + bf16(acc)), plus per-128-column sums of squares of the
+new h.  SwiGLU epilogue: act = bf16(bf16(g * bf16(sigmoid(g))) * u), g/u = bf16 outputs.
+
+Tolerance: the kernel accumulates K in a different order (mma tiles, split-K partials),
+so an output may land on the neighbouring bf16 value: >= 99 % of outputs bit-identical,
+the rest within 2 bf16 ulps (relative 2^-7).  Split-K results are deterministic.
+"""
+
+import math
+
+import pytest
+import torch
+
+from kvcacheboundaryprotection_b200 import build, capi
+from kvcacheboundaryprotection_b200.engine import interleave_gate_up
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _lib():
+    build.build()
+    capi.lib()
+
+
+def _close(got, ref):
+    got, ref = got.float(), ref.float()
+    exact = (got == ref).float().mean().item()
+    rel = ((got - ref).abs() / ref.abs().clamp_min(1e-3)).max().item()
+    assert exact >= 0.99, exact
+    assert rel <= 2.0**-6, rel
+
+
+def _run(epi, M, N, K, splits, norm=False, seed=0):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    W = (torch.randn(N, K, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+    x = torch.randn(M, K, generator=g, device="cuda").to(torch.bfloat16)
+    out_cols = N // 2 if epi == 2 else N
+    out = torch.zeros(M, out_cols, dtype=torch.bfloat16, device="cuda")
+    if epi == 1:
+        out = torch.randn(M, N, generator=g, device="cuda").to(torch.bfloat16)
+    h_before = out.clone()
+    nw = (1 + 0.1 * torch.randn(K, generator=g, device="cuda")).to(torch.bfloat16) if norm else None
+    ss = (x.float() ** 2).sum(1)
+    ss_parts = torch.zeros(1, 32, device="cuda")
+    ss_parts[0, :M] = ss
+    ss_out = torch.zeros(N // 128, 32, device="cuda")
+    partial = torch.zeros(splits * M * N + 1, device="cuda")
+    tickets = torch.zeros(N // 128 + 1, dtype=torch.int32, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    L = capi.lib()
+    st = torch.cuda.current_stream().cuda_stream
+    capi.check(
+        L.kvbp_decode_gemm(st, epi, M, N, K, W.data_ptr(), x.data_ptr(), K, ss_parts.data_ptr() if norm else None,
+                           1, nw.data_ptr() if norm else None, 1e-6, out.data_ptr(), out.shape[1],
+                           ss_out.data_ptr() if epi == 1 else None, partial.data_ptr(), tickets.data_ptr(), splits,
+                           err.data_ptr()),
+        "gemm",
+    )
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    assert int(tickets.abs().sum().item()) == 0  # tickets left ready for the next launch
+    xin = x
+    if norm:
+        inv = 1.0 / torch.sqrt(ss / K + 1e-6)
+        xin = ((x.float() * inv[:, None]) * nw.float()).to(torch.bfloat16)
+    acc = xin.float() @ W.float().t()
+    return W, x, xin, acc, out, h_before, ss_out
+
+
+@pytest.mark.parametrize("M", [1, 7, 16, 17, 32])
+@pytest.mark.parametrize("splits", [1, 3])
+def test_plain(M, splits):
+    _, _, _, acc, out, _, _ = _run(0, M, 512, 1024, splits)
+    _close(out, acc.to(torch.bfloat16))
+
+
+@pytest.mark.parametrize("splits", [1, 8])
+def test_plain_with_norm_prologue(splits):
+    _, _, _, acc, out, _, _ = _run(0, 16, 4608, 3584, splits, norm=True, seed=3)
+    _close(out, acc.to(torch.bfloat16))
+
+
+@pytest.mark.parametrize("M,splits", [(16, 8), (5, 1), (32, 4)])
+def test_residual_epilogue(M, splits):
+    _, _, _, acc, out, h0, ss_out = _run(1, M, 3584, 1024, splits, seed=5)
+    ref = (h0.float() + acc.to(torch.bfloat16).float()).to(torch.bfloat16)
+    # near cancellation a one-ulp difference of bf16(acc) is large relative to h + acc:
+    # bound the error by the operands' magnitude instead
+    scale = h0.float().abs() + acc.abs()
+    assert ((out.float() - ref.float()).abs() <= 2.0**-7 * scale + 1e-6).all()
+    assert (out == ref).float().mean().item() >= 0.99
+    ss_ref = (out.float() ** 2).view(M, 28, 128).sum(-1).t()  # [tiles][M]
+    assert torch.allclose(ss_out[:, :M], ss_ref, rtol=1e-5, atol=1e-5)
+    assert (ss_out[:, M:] == 0).all()
+
+
+@pytest.mark.parametrize("M", [3, 16])
+def test_swiglu_epilogue_with_norm(M):
+    g = torch.Generator(device="cuda").manual_seed(9)
+    F, H = 256, 512
+    Wg = (torch.randn(F, H, generator=g, device="cuda") * 0.05).to(torch.bfloat16)
+    Wu = (torch.randn(F, H, generator=g, device="cuda") * 0.05).to(torch.bfloat16)
+    Wil = interleave_gate_up(Wg, Wu)
+    h = torch.randn(M, H, generator=g, device="cuda").to(torch.bfloat16)
+    nw = torch.ones(H, dtype=torch.bfloat16, device="cuda")
+    ss = torch.zeros(1, 32, device="cuda")
+    ss[0, :M] = (h.float() ** 2).sum(1)
+    act = torch.zeros(M, F, dtype=torch.bfloat16, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    L = capi.lib()
+    capi.check(L.kvbp_decode_gemm(torch.cuda.current_stream().cuda_stream, 2, M, 2 * F, H, Wil.data_ptr(), h.data_ptr(), H,
+                                  ss.data_ptr(), 1, nw.data_ptr(), 1e-6, act.data_ptr(), F, None, None, None, 1,
+                                  err.data_ptr()), "gemm")
+    torch.cuda.synchronize()
+    inv = 1.0 / torch.sqrt((h.float() ** 2).mean(1) + 1e-6)
+    x = ((h.float() * inv[:, None]) * nw.float()).to(torch.bfloat16).float()
+    gv = (x @ Wg.float().t()).to(torch.bfloat16).float()
+    uv = (x @ Wu.float().t()).to(torch.bfloat16).float()
+    sig = torch.sigmoid(gv).to(torch.bfloat16).float()
+    ref = ((gv * sig).to(torch.bfloat16).float() * uv).to(torch.bfloat16)
+    _close(act, ref)
+
+
+def test_split_k_is_deterministic():
+    outs = [_run(0, 16, 3584, 18944, 8, seed=11)[4] for _ in range(2)]
+    assert torch.equal(outs[0], outs[1])
