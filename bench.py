@@ -61,6 +61,8 @@ def parse():
     ap.add_argument("--e2e-steps", type=int, default=16)
     ap.add_argument("--micro-only", type=int, default=None, metavar="CAPACITY",
                     help="run only the operator microbench at this capacity (lru, protect 0.10) and exit")
+    ap.add_argument("--micro-gemm", action="store_true",
+                    help="run only the decode GEMM microbench (one layer's projections + lm_head) and exit")
     return ap.parse_args()
 
 
@@ -326,7 +328,7 @@ def run_microbench(cap_list=(256, 1024, 4096), policies=("lru", "attention-mass"
     """Operator microbench: one fused decode attention + eviction step for 64 sequences,
     8 kv heads x group 4, head_dim 128 (slot append + cadence eviction, K/V scatter,
     attention + per-slot score, score update).  Each timed step is preceded by an L2
-    flush (a 512 MB write) outside the CUDA-event pair."""
+    flush (a 512 MB read, which leaves no dirty lines behind) outside the CUDA-event pair."""
     import ctypes as C_
 
     import torch
@@ -378,7 +380,7 @@ def run_microbench(cap_list=(256, 1024, 4096), policies=("lru", "attention-mass"
                 tot = 0.0
                 attn_only = 0.0
                 for it in range(iters):
-                    flush.fill_(float(it))
+                    flush.sum()
                     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                     e0.record()
                     gr.replay()
@@ -388,7 +390,7 @@ def run_microbench(cap_list=(256, 1024, 4096), policies=("lru", "attention-mass"
                 # attention kernel alone (same L2 discipline)
                 s_ = torch.cuda.current_stream().cuda_stream
                 for it in range(iters):
-                    flush.fill_(float(it))
+                    flush.sum()
                     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                     e0.record()
                     check(L.kvbp_decode_attn_score(s_, B, Hq, Hkv, D, S, q.data_ptr(), kc.data_ptr(), vc.data_ptr(), st["slot_pos"].data_ptr(), attn_out.data_ptr(), st["step_score"].data_ptr(), err.data_ptr()), "attn")
@@ -419,6 +421,83 @@ def run_microbench(cap_list=(256, 1024, 4096), policies=("lru", "attention-mass"
                 del gr
         del kc, vc
     return {"peak_gbs": hbm, "peak_kind": peak_kind, "batch": B, "kv_heads": Hkv, "group": G, "rows": out}
+
+
+def run_gemm_microbench(preset="qwen2.5-7b", M=16, iters=10, sweep=False):
+    """Operator microbench of kvbp_decode_gemm on one decoder layer's projections (and the
+    lm_head) of ``preset``: M activation rows against bf16 weights streamed from HBM, each
+    with the epilogue and norm prologue the decode step uses and the engine's split-K
+    choice (``sweep``: also other split counts).  A 512 MB read flushes L2 before every
+    timed launch; the same shapes through torch.mm (cuBLAS, plain output, row-major
+    weights) are timed beside it for context."""
+    import torch
+
+    from kvcacheboundaryprotection_b200.capi import check, lib
+    from kvcacheboundaryprotection_b200.config import get_config
+    from kvcacheboundaryprotection_b200.engine import CappedKVEngine, pack_weight
+
+    L = lib()
+    cfg = get_config(preset)
+    dev = torch.device("cuda")
+    hbm, _, peak_kind = peaks()
+    H, F, V = cfg.hidden, cfg.ffn, cfg.vocab
+    qkv_n = (cfg.n_heads + 2 * cfg.n_kv_heads) * cfg.head_dim
+    shapes = (  # name, N, K, epilogue (0 plain, 1 residual, 2 SwiGLU), norm prologue
+        ("qkv", qkv_n, H, 0, True),
+        ("o", H, cfg.n_heads * cfg.head_dim, 1, False),
+        ("gate_up", 2 * F, H, 2, True),
+        ("down", H, F, 1, False),
+        ("lm_head", V, H, 0, True),
+    )
+    flush = torch.empty(512 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    g = torch.Generator(device=dev).manual_seed(0)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    rows = []
+    for name, N, K, epi, norm in shapes:
+        W = (torch.randn(N, K, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        Wp = pack_weight(W)
+        x = torch.randn(M, K, generator=g, device=dev).to(torch.bfloat16)
+        out = torch.zeros(M, N // 2 if epi == 2 else N, dtype=torch.bfloat16, device=dev)
+        nw = torch.ones(K, dtype=torch.bfloat16, device=dev)
+        ss_parts = torch.ones(1, 32, device=dev)
+        ss_out = torch.zeros(N // 128, 32, device=dev)
+        pick = CappedKVEngine._pick_splits(N, K)
+        cands = [pick]
+        if sweep:
+            cands += [sp for sp in (1, 2, 3, 4, 5, 6, 7, 8, 10, 12, 16) if sp != pick and sp <= K // 128]
+
+        def timed(fn):
+            fn()
+            ts = []
+            for it in range(iters):
+                flush.sum()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                fn()
+                e1.record()
+                torch.cuda.synchronize()
+                ts.append(e0.elapsed_time(e1) * 1000)
+            return statistics.median(ts)
+
+        byts = N * K * 2 + M * K * 2 + out.numel() * 2 * (2 if epi == 1 else 1)
+        cub = timed(lambda: torch.mm(x, W.t()))
+        for sp in cands:
+            def ours(sp=sp):
+                s = torch.cuda.current_stream().cuda_stream
+                check(L.kvbp_decode_gemm(s, epi, M, N, K, Wp.data_ptr(), x.data_ptr(), K,
+                                         ss_parts.data_ptr() if norm else None, 1, nw.data_ptr() if norm else None,
+                                         1e-6, out.data_ptr(), out.shape[1], ss_out.data_ptr() if epi == 1 else None,
+                                         sp, err.data_ptr()), "decode_gemm")
+
+            us = timed(ours)
+            rows.append({"gemm": name, "N": N, "K": K, "splits": sp, "us": round(us, 2),
+                         "gbs": round(byts / us / 1e3, 1), "frac": round(byts / us / 1e3 / hbm, 4),
+                         "cublas_us": round(cub, 2)})
+        del W, Wp
+    torch.cuda.synchronize()
+    if int(err.item()):
+        raise RuntimeError("device error in GEMM microbench")
+    return {"peak_gbs": hbm, "peak_kind": peak_kind, "rows_M": M, "preset": preset, "rows": rows}
 
 
 def micro_bytes(B, Hq, Hkv, valid, E):
@@ -604,6 +683,12 @@ def main():
         kbuild.build()
         print(json.dumps(run_microbench(cap_list=(a.micro_only,), policies=("lru",), fracs=(0.10,), iters=5)), flush=True)
         return
+    if a.micro_gemm:
+        from kvcacheboundaryprotection_b200 import build as kbuild
+
+        kbuild.build()
+        print(json.dumps(run_gemm_microbench(WORKLOADS[a.workload][0], sweep=True)), flush=True)
+        return
     if world > 1:
         torch.cuda.set_device(local_rank)
         from datetime import timedelta
@@ -617,6 +702,7 @@ def main():
             del fw
             torch.cuda.empty_cache()
             out["kernel_microbench"] = run_microbench()
+            out["gemm_microbench"] = run_gemm_microbench(WORKLOADS[a.workload][0])
         if not a.no_cpu:
             times, sample = cpu_reference_step_times(a.workload, 4, 1)
             v = 1.0 / (sum(times) / len(times))

@@ -192,6 +192,7 @@ int kvbp_row_sumsq(kvbp_stream_t stream, int32_t rows, int32_t hidden, const voi
 /* Weight-streaming decode GEMM out[M][N] = X[M][K] . W[N][K]^T (bf16, fp32 accumulate),
  * M <= 32, N and K multiples of 128 -- the q/k/v, o, gate/up, down and lm_head products
  * of _forward_jittable (jax_inference.py:949-956,1081,1095-1107,1330-1333).
+ * w_packed is W in the packed layout written by kvbp_pack_weight.
  * Prologue: with norm_w != NULL, X is bf16((x * inv_rms[m]) * norm_w[k]) where x (ldx) is
  *   the residual stream and inv_rms[m] = 1/sqrt(sum_t ss_parts[t][m] / K + eps) over the
  *   n_parts partial sums ([n_parts][32] floats) -- RMSNorm (jax_inference.py:609-618).
@@ -203,12 +204,21 @@ int kvbp_row_sumsq(kvbp_stream_t stream, int32_t rows, int32_t hidden, const voi
  *   (rows 128t..128t+63 = gate features 64t.., rows 128t+64.. = the matching up features);
  *   out[M][N/2] = bf16(bf16(g * bf16(sigmoid(g))) * u) with g, u the bf16 GEMM outputs
  *   (jax_inference.py:702-704,1103-1107).
- * splits > 1 splits K over CTAs: partial [splits][M][N] fp32 and tickets [N/128] int32
- * (all zero before the first call; the kernel leaves them zero) are workspace. */
-int kvbp_decode_gemm(kvbp_stream_t stream, int32_t epilogue, int32_t M, int32_t N, int32_t K, const void* w,
+ * splits (1..min(16, K/128)) CTAs share each 128-column tile's K range as one thread-block
+ * cluster and reduce their partial sums in shared memory, in a fixed order: the result
+ * does not depend on timing.  No workspace. */
+int kvbp_decode_gemm(kvbp_stream_t stream, int32_t epilogue, int32_t M, int32_t N, int32_t K, const void* w_packed,
                      const void* x, int32_t ldx, const float* ss_parts, int32_t n_parts, const void* norm_w, float eps,
-                     void* out, int32_t ldo, float* ss_out, float* partial, int32_t* tickets, int32_t splits,
-                     int32_t* dev_err);
+                     void* out, int32_t ldo, float* ss_out, int32_t splits, int32_t* dev_err);
+
+/* Converts a row-major bf16 weight W[N][K] (N, K multiples of 128) to the decode GEMM's
+ * packed layout and back: each 128-row x 128-column block becomes one contiguous 32 KiB
+ * run of two 128 x 64 halves whose 16-byte chunks are XOR-swizzled by row (chunk
+ * c of row r stored at c ^ (r % 8)), the image of a 128-byte-swizzled shared-memory
+ * tile.  src and dst must not overlap.  (No counterpart in the reference, whose weights
+ * stay row-major.) */
+int kvbp_pack_weight(kvbp_stream_t stream, int32_t N, int32_t K, const void* src, void* dst);
+int kvbp_unpack_weight(kvbp_stream_t stream, int32_t N, int32_t K, const void* src, void* dst);
 
 /* Greedy sampling: first index of the row maximum (numpy.argmax), kv_coupled_generator.py:344. */
 int kvbp_argmax(kvbp_stream_t stream, int32_t rows, int32_t vocab, int64_t ld, const void* logits, int32_t* out_ids);

@@ -221,6 +221,7 @@ __global__ void __launch_bounds__(kThreads) decode_attn_score_kernel(const __gri
       atomicExch(bad_flag, 1);
       ok_tile = false;
     }
+    ok_tile = __all_sync(0xffffffffu, ok_tile);  // warp-uniform: the tile's mma/ldmatrix are warp-wide
     if (ok_tile) {
       const uint8_t* kt = ring + st * kStageBytes;
       const uint8_t* vt = kt + kHalfBytes;
@@ -477,7 +478,7 @@ static cudaError_t launch_g(cudaStream_t stream, const CUtensorMap& km, const CU
     if (e != cudaSuccess) return e;
     configured_smem = smem;
   }
-  return launch_pdl(kern, dim3(a.cluster, a.Hkv, a.B), dim3(kThreads), smem, stream, a.cluster, km, vm, a);
+  return launch_pdl(kern, dim3(a.cluster, a.Hkv, a.B), dim3(kThreads), smem, stream, dim3(a.cluster, 1, 1), km, vm, a);
 }
 
 int decode_attn_score(cudaStream_t stream, int B, int Hq, int Hkv, int D, int S, const void* q, const void* kcache,

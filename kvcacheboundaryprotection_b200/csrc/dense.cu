@@ -241,7 +241,7 @@ static int check_launch(const char* what, cudaError_t e0 = cudaSuccess) {
 int embed(cudaStream_t st, int rows, int V, int H, const void* table, const int* ids, void* out, int* err) {
   if (!table || !ids || !out) return fail(kStatusArg, "embed: null pointer");
   if (rows <= 0 || H <= 0 || V <= 0 || H % 8) return fail(kStatusArg, "embed: bad size (H must be a multiple of 8)");
-  const cudaError_t le = launch_pdl(embed_kernel, dim3(rows), dim3(128), 0, st, 0, static_cast<const __nv_bfloat16*>(table), ids, V, H,
+  const cudaError_t le = launch_pdl(embed_kernel, dim3(rows), dim3(128), 0, st, dim3(0), static_cast<const __nv_bfloat16*>(table), ids, V, H,
                                      static_cast<__nv_bfloat16*>(out), err);
   return check_launch("embed", le);
 }
@@ -249,7 +249,7 @@ int embed(cudaStream_t st, int rows, int V, int H, const void* table, const int*
 int add_rmsnorm(cudaStream_t st, int rows, int H, void* h, const void* delta, const void* w, void* out, float eps) {
   if (!h || !w || !out) return fail(kStatusArg, "add_rmsnorm: null pointer");
   if (rows <= 0 || H <= 0 || H % 2) return fail(kStatusArg, "add_rmsnorm: bad size");
-  const cudaError_t le = launch_pdl(add_rmsnorm_kernel, dim3(rows), dim3(256), 0, st, 0, static_cast<__nv_bfloat16*>(h), static_cast<const __nv_bfloat16*>(delta),
+  const cudaError_t le = launch_pdl(add_rmsnorm_kernel, dim3(rows), dim3(256), 0, st, dim3(0), static_cast<__nv_bfloat16*>(h), static_cast<const __nv_bfloat16*>(delta),
                                            static_cast<const __nv_bfloat16*>(w), static_cast<__nv_bfloat16*>(out), H,
                                            eps);
   return check_launch("add_rmsnorm", le);
@@ -265,7 +265,7 @@ int qkv_epilogue(cudaStream_t st, int rows, int rows_per_seq, int Hq, int Hkv, i
     return fail(kStatusArg, "qkv_epilogue: bad size");
   if ((Hq + 2 * Hkv) > 65535) return fail(kStatusArg, "qkv_epilogue: too many heads");
   dim3 grid(rows, Hq + 2 * Hkv);
-  const cudaError_t le = launch_pdl(qkv_epilogue_kernel, grid, dim3(64), 0, st, 0, 
+  const cudaError_t le = launch_pdl(qkv_epilogue_kernel, grid, dim3(64), 0, st, dim3(0), 
       static_cast<const __nv_bfloat16*>(qkv), ldq, static_cast<const __nv_bfloat16*>(bias),
       static_cast<const __nv_bfloat16*>(qnw), static_cast<const __nv_bfloat16*>(knw), eps, inv_freq, positions,
       write_slot, rows_per_seq, Hq, Hkv, S, static_cast<__nv_bfloat16*>(q_out), static_cast<__nv_bfloat16*>(kcache),
@@ -276,7 +276,7 @@ int qkv_epilogue(cudaStream_t st, int rows, int rows_per_seq, int Hq, int Hkv, i
 int row_sumsq(cudaStream_t st, int rows, int H, const void* h, float* ss_out) {
   if (!h || !ss_out) return fail(kStatusArg, "row_sumsq: null pointer");
   if (rows <= 0 || rows > 32 || H <= 0 || H % 2) return fail(kStatusArg, "row_sumsq: bad size (rows 1..32)");
-  const cudaError_t le = launch_pdl(row_sumsq_kernel, dim3(rows), dim3(256), 0, st, 0, static_cast<const __nv_bfloat16*>(h), H, ss_out);
+  const cudaError_t le = launch_pdl(row_sumsq_kernel, dim3(rows), dim3(256), 0, st, dim3(0), static_cast<const __nv_bfloat16*>(h), H, ss_out);
   return check_launch("row_sumsq", le);
 }
 
@@ -286,7 +286,7 @@ int silu_mul(cudaStream_t st, int rows, int F, const void* gu, void* act) {
   const long long n = static_cast<long long>(rows) * F;
   long long blocks = (n / 2 + 255) / 256;
   if (blocks > 148 * 16) blocks = 148 * 16;
-  const cudaError_t le = launch_pdl(silu_mul_kernel, dim3(static_cast<int>(blocks)), dim3(256), 0, st, 0, static_cast<const __nv_bfloat16*>(gu), F, n,
+  const cudaError_t le = launch_pdl(silu_mul_kernel, dim3(static_cast<int>(blocks)), dim3(256), 0, st, dim3(0), static_cast<const __nv_bfloat16*>(gu), F, n,
                                                              static_cast<__nv_bfloat16*>(act));
   return check_launch("silu_mul", le);
 }
@@ -296,7 +296,7 @@ int argmax_rows(cudaStream_t st, int rows, int V, long long ld, const void* logi
   if (rows <= 0 || V <= 0 || ld < V) return fail(kStatusArg, "argmax: bad size");
   if ((ld % 8) || (reinterpret_cast<uintptr_t>(logits) & 15))
     return fail(kStatusArg, "argmax: rows must be 16-byte aligned (ld % 8 == 0)");
-  const cudaError_t le = launch_pdl(argmax_kernel, dim3(rows), dim3(1024), 0, st, 0, static_cast<const __nv_bfloat16*>(logits), ld, V, out);
+  const cudaError_t le = launch_pdl(argmax_kernel, dim3(rows), dim3(1024), 0, st, dim3(0), static_cast<const __nv_bfloat16*>(logits), ld, V, out);
   return check_launch("argmax", le);
 }
 

@@ -674,7 +674,7 @@ static bool state_ok(const StateArgs& s) {
 
 int score_update(cudaStream_t stream, const StateArgs& st, const int* seq_step, float* step_score, int* err) {
   if (!state_ok(st) || !seq_step || !step_score) return fail(kStatusArg, "score_update: bad argument");
-  cudaError_t le = launch_pdl(score_update_kernel, dim3(st.B), dim3(256), 0, stream, 0, st, seq_step, step_score, err);
+  cudaError_t le = launch_pdl(score_update_kernel, dim3(st.B), dim3(256), 0, stream, dim3(0), st, seq_step, step_score, err);
   if (le != cudaSuccess) return fail(kStatusCuda, "score_update launch: %s", cudaGetErrorString(le));
   return check_launch("score_update");
 }
@@ -694,7 +694,7 @@ int append_evict(cudaStream_t stream, const AppendArgs& a) {
     if (e != cudaSuccess) return fail(kStatusCuda, "append_evict: %s", cudaGetErrorString(e));
     configured = smem;
   }
-  cudaError_t le = launch_pdl(append_evict_kernel, dim3(a.st.B), dim3(kEvictThreads), smem, stream, 0, a);
+  cudaError_t le = launch_pdl(append_evict_kernel, dim3(a.st.B), dim3(kEvictThreads), smem, stream, dim3(0), a);
   if (le != cudaSuccess) return fail(kStatusCuda, "append_evict launch: %s", cudaGetErrorString(le));
   return check_launch("append_evict");
 }

@@ -4,22 +4,28 @@
 // (src/counterfact_kv_eviction/jax_inference.py:949-956,1081,1095-1107,1330-1333), whose
 // outputs the reference rounds to bf16.
 //
-// The weights dominate the traffic (M is tiny), so the kernel is an HBM stream: a
-// producer warp feeds 128 x 128 weight tiles through a shared-memory ring with 2-D TMA
-// loads (128-byte swizzle), and four consumer warps run mma.sync m16n8k16 with the
-// activations as the M operand (16 rows per m-tile) and 32 output features per warp.
+// The weights dominate the traffic (M is tiny), so the kernel is an HBM stream.  Weights
+// are stored pre-tiled ("packed"): every 128-feature x 128-k block is one contiguous
+// 32 KiB run laid out exactly as a 128-byte-swizzled shared-memory tile (two 128 x 64
+// halves), so a CTA streams one contiguous range of HBM with 1-D bulk copies -- full
+// DRAM pages, no tensor map, no per-row 128-byte fragments.  A producer warp feeds a
+// 3-stage ring; four consumer warps run mma.sync m16n8k16 with the activations as the
+// M operand (16 rows per m-tile, loaded by 2-D TMA) and 32 output features per warp.
+//
+// Split-K: the `splits` CTAs of one column tile form a thread-block cluster.  Each CTA
+// leaves its fp32 partial tile in its own shared memory; after a cluster barrier CTA r
+// reduces rows [r*M/splits, (r+1)*M/splits) by reading every peer's tile over DSMEM in
+// rank order (deterministic) and runs the epilogue on them.
+//
 // Fusions that remove the per-token glue kernels of the step:
-//   * NORM prologue: the producer warp builds each activation chunk as
-//     bf16((h * inv_rms[m]) * w_norm[k]) from the residual stream h, with inv_rms formed
-//     from per-tile sums of squares written by the previous GEMM's RESID epilogue
-//     (RMSNorm, jax_inference.py:609-618, without a separate kernel).
+//   * NORM prologue: activation fragments are formed as bf16((h * inv_rms[m]) * w_norm[k])
+//     from the residual stream h, with inv_rms from per-tile sums of squares written by
+//     the previous GEMM's RESID epilogue (RMSNorm, jax_inference.py:609-618).
 //   * RESID epilogue: h = bf16(h + bf16(acc)) in place (the residual adds
 //     jax_inference.py:1280,1325) plus this tile's sum of squares of the new h per row.
 //   * SWIGLU epilogue: weight rows are stored gate/up interleaved in blocks of 64, so a
 //     tile holds 64 gate and the matching 64 up features and writes
 //     act = bf16(bf16(g * bf16(sigmoid(g))) * u) (jax_inference.py:702-704,1103-1107).
-// Split-K (when N / 128 is small) writes fp32 partials; the last CTA of each column tile
-// (atomic ticket) sums them in split order, so results are deterministic.
 #include "common.cuh"
 #include "kvbp_internal.h"
 
@@ -33,12 +39,16 @@ constexpr int kStages = 3;
 constexpr int kConsumerWarps = 4;  // 32 features each
 constexpr int kConsumers = kConsumerWarps * 32;
 constexpr int kThreads = kConsumers + 32;
-constexpr int kWBytes = BN * BK * 2;  // 32 KiB: two 128 x 64 boxes
+constexpr int kWBytes = BN * BK * 2;  // 32 KiB: two 128 x 64 halves
 constexpr int kWBox = kWBytes / 2;
+constexpr int kBlockElems = BN * BK;  // one packed block
+constexpr int kRedStride = BN + 8;    // fp32 partial tile row stride (fewer bank conflicts)
+constexpr int kMaxSplits = 16;
 
 enum Epi : int { kPlain = 0, kResid = 1, kSwiGLU = 2 };
 
 struct Args {
+  const __nv_bfloat16* w;  // packed [N/128][K/128][2][128][64] (swizzled 16-byte chunks)
   const __nv_bfloat16* x;  // [M][ldx] activations (plain) or residual stream h (norm)
   int ldx;
   const float* ss_parts;   // NORM: [n_parts][32] per-row partial sums of squares of h
@@ -47,46 +57,45 @@ struct Args {
   float eps;
   __nv_bfloat16* out;  // PLAIN/SWIGLU: [M][ldo]; RESID: h [M][ldo], updated in place
   int ldo;
-  float* ss_out;   // RESID: [N / BN][32] partial sums of squares of the new h
-  float* partial;  // split-K: [splits][M][N] fp32
-  int* tickets;    // split-K: [N / BN], zero between launches
+  float* ss_out;  // RESID: [N / BN][32] partial sums of squares of the new h
   int M, N, K, splits;
   int* err;
 };
 
 template <int MT, int EPI, bool NORM>
-__global__ void __launch_bounds__(kThreads) decode_gemm_kernel(const __grid_constant__ CUtensorMap wmap,
-                                                               const __grid_constant__ CUtensorMap xmap, const Args a) {
+__global__ void __launch_bounds__(kThreads) decode_gemm_kernel(const __grid_constant__ CUtensorMap xmap,
+                                                               const Args a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   constexpr int kABox = MT * 16 * 128;  // one 64-wide k box of the activation chunk
   constexpr int kStageBytes = kWBytes + 2 * kABox;
+  static_assert(MT * 16 * kRedStride * 4 <= kStages * kStageBytes, "partial tile must fit in the ring");
   uint8_t* ring = base;  // [stage][W 32 KiB | A box 0 | A box 1]
   __nv_bfloat16* wn_s = reinterpret_cast<__nv_bfloat16*>(base + kStages * kStageBytes);  // [stage][128] norm weights
   const int kc = a.K / BK;
-  const int c0 = (blockIdx.y * kc) / a.splits, c1 = ((blockIdx.y + 1) * kc) / a.splits;
+  const int cs = a.splits;
+  const int c0 = (blockIdx.y * kc) / cs, c1 = ((blockIdx.y + 1) * kc) / cs;
   const int nch = c1 - c0;
   float* inv_rms = reinterpret_cast<float*>(wn_s + kStages * BK);  // [32]
-  float* red = inv_rms + 32;                         // [4 warps][32] epilogue sums
-  int* flag = reinterpret_cast<int*>(red + 4 * 32);  // [0] bad, [1] last-CTA
+  float* red = inv_rms + 32;                         // [32 rows][2 halves] epilogue sums
+  int* flag = reinterpret_cast<int*>(red + 2 * 32);  // [0] bad, [1] its snapshot after the main loop
   uint64_t* full = reinterpret_cast<uint64_t*>(flag + 4);
   uint64_t* empty = full + kStages;
+  float* rtile = reinterpret_cast<float*>(ring);  // [16*MT][kRedStride] partial tile, after the main loop
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int tile = blockIdx.x, split = blockIdx.y;
+  const int tile = blockIdx.x;
   const int n0 = tile * BN;
   const int M = a.M;
+  const __nv_bfloat16* wblk = a.w + (static_cast<size_t>(tile) * kc + c0) * kBlockElems;
 
-  // one stage = two arrivals on full[st]: the constant part (weight tile, norm weights)
+  // one stage = two arrivals on full[st]: the constant part (weight block, norm weights)
   // and the activation chunk, which the previous kernel produced
   auto issue_weights = [&](int u) {
     const int st = u % kStages;
-    const int kb = (c0 + u) * BK;
-    uint8_t* sb = ring + st * kStageBytes;
     mbar_expect_tx(&full[st], kWBytes + (NORM ? BK * 2 : 0));
-    tma_load_2d(sb, &wmap, &full[st], kb, n0);
-    tma_load_2d(sb + kWBox, &wmap, &full[st], kb + 64, n0);
-    if (NORM) bulk_load(wn_s + st * BK, a.norm_w + kb, BK * 2, &full[st]);
+    bulk_load(ring + st * kStageBytes, wblk + static_cast<size_t>(u) * kBlockElems, kWBytes, &full[st]);
+    if (NORM) bulk_load(wn_s + st * BK, a.norm_w + (c0 + u) * BK, BK * 2, &full[st]);
   };
   auto issue_acts = [&](int u) {
     const int st = u % kStages;
@@ -96,12 +105,7 @@ __global__ void __launch_bounds__(kThreads) decode_gemm_kernel(const __grid_cons
     tma_load_2d(sb + kWBytes, &xmap, &full[st], kb, 0);
     tma_load_2d(sb + kWBytes + kABox, &xmap, &full[st], kb + 64, 0);
   };
-  auto issue_stage = [&](int u) {
-    issue_weights(u);
-    issue_acts(u);
-  };
   if (tid == kConsumers) {
-    prefetch_tmap(&wmap);
     prefetch_tmap(&xmap);
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 2);
@@ -113,16 +117,14 @@ __global__ void __launch_bounds__(kThreads) decode_gemm_kernel(const __grid_cons
     for (int u = 0; u < nch && u < kStages; ++u) issue_weights(u);
   }
   if (!KVBP_PDL_LATE) pdl_launch_dependents();
-  pdl_wait();  // activations, norm statistics and workspace belong to earlier kernels
+  pdl_wait();  // activations, norm statistics and h belong to earlier kernels
   if (tid == kConsumers)
     for (int u = 0; u < nch && u < kStages; ++u) issue_acts(u);
-  if (NORM && tid < kConsumers) {
-    if (tid < 32) {
-      float ss = 0.f;
-      if (tid < M)
-        for (int t = 0; t < a.n_parts; ++t) ss += a.ss_parts[t * 32 + tid];
-      inv_rms[tid] = 1.0f / sqrtf(ss / static_cast<float>(a.K) + a.eps);
-    }
+  if (NORM && tid < 32) {
+    float ss = 0.f;
+    if (tid < M)
+      for (int t = 0; t < a.n_parts; ++t) ss += a.ss_parts[t * 32 + tid];
+    inv_rms[tid] = 1.0f / sqrtf(ss / static_cast<float>(a.K) + a.eps);
   }
   __syncthreads();
 
@@ -138,7 +140,8 @@ __global__ void __launch_bounds__(kThreads) decode_gemm_kernel(const __grid_cons
           atomicExch(flag, 1);
           break;
         }
-        issue_stage(u);
+        issue_weights(u);
+        issue_acts(u);
         issued = u + 1;
       }
       if (*reinterpret_cast<volatile int*>(flag)) {
@@ -147,7 +150,12 @@ __global__ void __launch_bounds__(kThreads) decode_gemm_kernel(const __grid_cons
           mbar_wait_bounded(&full[u % kStages], (u / kStages) & 1, 1u << 16);
       }
     }
+    __syncwarp();
     if (KVBP_PDL_LATE) pdl_launch_dependents();
+    if (cs > 1) {  // the consumers' two cluster barriers
+      cluster_sync_all();
+      cluster_sync_all();
+    }
     return;
   }
 
@@ -166,12 +174,13 @@ __global__ void __launch_bounds__(kThreads) decode_gemm_kernel(const __grid_cons
   }
   for (int u = 0; u < nch; ++u) {
     const int st = u % kStages;
-    if (*reinterpret_cast<volatile int*>(flag)) break;
-    if (!mbar_wait_bounded(&full[st], (u / kStages) & 1)) {
+    bool go = !*reinterpret_cast<volatile int*>(flag);
+    if (go && !mbar_wait_bounded(&full[st], (u / kStages) & 1)) {
       set_err(a.err, kErrWaitTimeout);
       atomicExch(flag, 1);
-      break;
+      go = false;
     }
+    if (!__all_sync(0xffffffffu, go)) break;  // the warp leaves together (ldmatrix/mma are warp-wide)
     const uint8_t* wb = ring + st * kStageBytes;
     const uint8_t* ab = wb + kWBytes;
 #pragma unroll
@@ -217,129 +226,115 @@ __global__ void __launch_bounds__(kThreads) decode_gemm_kernel(const __grid_cons
     if (lane == 0) mbar_arrive(&empty[st]);
   }
   if (KVBP_PDL_LATE) pdl_launch_dependents();  // the next kernel may start its weight stream
-  // acc[mt][j]: rows 16mt+g (c0,c1) and 16mt+g+8 (c2,c3); features n0 + warp*32 + 8j + 2t (+1)
 
-  // ---- split-K: partials, then the last CTA of this column tile reduces ------------
-  if (a.splits > 1) {
-    float* pbase = a.partial + static_cast<size_t>(split) * M * a.N;
-#pragma unroll
-    for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int n = n0 + warp * 32 + 8 * j + 2 * t;
-        const int r0 = mt * 16 + g, r1 = r0 + 8;
-        if (r0 < M) *reinterpret_cast<float2*>(&pbase[static_cast<size_t>(r0) * a.N + n]) = make_float2(acc[mt][j][0], acc[mt][j][1]);
-        if (r1 < M) *reinterpret_cast<float2*>(&pbase[static_cast<size_t>(r1) * a.N + n]) = make_float2(acc[mt][j][2], acc[mt][j][3]);
-      }
-    __threadfence();
-    named_bar(1, kConsumers);
-    if (tid == 0) {
-      const int prev = atomicAdd(&a.tickets[tile], 1);
-      flag[1] = (prev == a.splits - 1);
-    }
-    named_bar(1, kConsumers);
-    if (!flag[1]) return;
-    __threadfence();
-    // last CTA: sum every split in order
-#pragma unroll
-    for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int n = n0 + warp * 32 + 8 * j + 2 * t;
-        const int r0 = mt * 16 + g, r1 = r0 + 8;
-        float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-        for (int sp = 0; sp < a.splits; ++sp) {
-          const float* pb = a.partial + static_cast<size_t>(sp) * M * a.N;
-          if (r0 < M) {
-            const float2 v = __ldcg(reinterpret_cast<const float2*>(&pb[static_cast<size_t>(r0) * a.N + n]));
-            s0 += v.x;
-            s1 += v.y;
-          }
-          if (r1 < M) {
-            const float2 v = __ldcg(reinterpret_cast<const float2*>(&pb[static_cast<size_t>(r1) * a.N + n]));
-            s2 += v.x;
-            s3 += v.y;
-          }
-        }
-        acc[mt][j][0] = s0;
-        acc[mt][j][1] = s1;
-        acc[mt][j][2] = s2;
-        acc[mt][j][3] = s3;
-      }
-    if (tid == 0) a.tickets[tile] = 0;  // ready for the next launch
-  }
-
-  // ---- epilogues -------------------------------------------------------------------
-  if (EPI == kPlain) {
-#pragma unroll
-    for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int n = n0 + warp * 32 + 8 * j + 2 * t;
-        const int r0 = mt * 16 + g, r1 = r0 + 8;
-        if (r0 < M) *reinterpret_cast<uint32_t*>(&a.out[static_cast<size_t>(r0) * a.ldo + n]) = pack_bf16(acc[mt][j][0], acc[mt][j][1]);
-        if (r1 < M) *reinterpret_cast<uint32_t*>(&a.out[static_cast<size_t>(r1) * a.ldo + n]) = pack_bf16(acc[mt][j][2], acc[mt][j][3]);
-      }
-  } else if (EPI == kResid) {
-    // h = bf16(h + bf16(acc)); per-row sum of squares of the new h over this tile
-    float ssr[MT][2];
-#pragma unroll
-    for (int mt = 0; mt < MT; ++mt) ssr[mt][0] = ssr[mt][1] = 0.f;
-#pragma unroll
-    for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int n = n0 + warp * 32 + 8 * j + 2 * t;
-#pragma unroll
-        for (int hr = 0; hr < 2; ++hr) {
-          const int r = mt * 16 + g + 8 * hr;
-          if (r < M) {
-            uint32_t* hp = reinterpret_cast<uint32_t*>(&a.out[static_cast<size_t>(r) * a.ldo + n]);
-            const uint32_t hv = *hp;
-            const float x0 = bf16r(bf16lo(hv) + bf16r(acc[mt][j][2 * hr]));
-            const float x1 = bf16r(bf16hi(hv) + bf16r(acc[mt][j][2 * hr + 1]));
-            *hp = pack_bf16(x0, x1);
-            ssr[mt][hr] += x0 * x0 + x1 * x1;
-          }
-        }
-      }
-    // reduce over the 4 lanes sharing a row (t), then over the 4 warps in order
-#pragma unroll
-    for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-      for (int hr = 0; hr < 2; ++hr) {
-        float v = ssr[mt][hr];
-        v += __shfl_xor_sync(0xffffffffu, v, 1);
-        v += __shfl_xor_sync(0xffffffffu, v, 2);
-        if (t == 0) red[warp * 32 + mt * 16 + g + 8 * hr] = v;
-      }
-    named_bar(1, kConsumers);
-    if (tid < 32) {
-      float s = 0.f;
-      for (int w = 0; w < kConsumerWarps; ++w) s += red[w * 32 + tid];
-      a.ss_out[tile * 32 + tid] = (tid < M) ? s : 0.f;
-    }
-  } else {  // SwiGLU: features 0..63 of the tile are gate, 64..127 the matching up
-    __nv_bfloat16* stile = reinterpret_cast<__nv_bfloat16*>(ring);  // ring is free now
-    named_bar(1, kConsumers);
+  // ---- partial tile -> this CTA's shared memory (the ring is idle once every warp is done)
+  // acc[mt][j]: rows 16mt+g (c0,c1) and 16mt+g+8 (c2,c3); columns warp*32 + 8j + 2t (+1)
+  named_bar(1, kConsumers);
+  if (tid == 0) flag[1] = *reinterpret_cast<volatile int*>(flag);  // one snapshot for every consumer
+  named_bar(1, kConsumers);
+  const bool ok = !flag[1];
+  if (ok) {
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const int c = warp * 32 + 8 * j + 2 * t;
-        const int r0 = mt * 16 + g, r1 = r0 + 8;
-        *reinterpret_cast<uint32_t*>(&stile[r0 * BN + c]) = pack_bf16(acc[mt][j][0], acc[mt][j][1]);
-        *reinterpret_cast<uint32_t*>(&stile[r1 * BN + c]) = pack_bf16(acc[mt][j][2], acc[mt][j][3]);
+        const int r0 = mt * 16 + g;
+        *reinterpret_cast<float2*>(&rtile[r0 * kRedStride + c]) = make_float2(acc[mt][j][0], acc[mt][j][1]);
+        *reinterpret_cast<float2*>(&rtile[(r0 + 8) * kRedStride + c]) = make_float2(acc[mt][j][2], acc[mt][j][3]);
       }
-    named_bar(1, kConsumers);
-    const int f0 = tile * (BN / 2);
-    for (int e = tid; e < M * (BN / 2); e += kConsumers) {
-      const int r = e / (BN / 2), j = e % (BN / 2);
-      const float gv = __bfloat162float(stile[r * BN + j]);
-      const float uv = __bfloat162float(stile[r * BN + 64 + j]);
-      const float sig = bf16r(1.0f / (1.0f + expf(-gv)));
-      a.out[static_cast<size_t>(r) * a.ldo + f0 + j] = __float2bfloat16_rn(bf16r(gv * sig) * uv);
+  }
+  if (cs > 1) cluster_sync_all();  // every partial tile of the cluster is complete
+  else named_bar(1, kConsumers);
+
+  // ---- reduce this CTA's row slice over the cluster (rank order) and run the epilogue
+  const int rank = blockIdx.y;  // cluster shape (1, splits, 1): rank == split index
+  const int r_lo = (rank * M) / cs, r_hi = ((rank + 1) * M) / cs;
+  const uint32_t rt_local = smem_u32(rtile);
+  auto sum_pair = [&](int r, int c) -> float2 {  // columns c, c+1 of row r, summed over splits
+    if (cs == 1) return *reinterpret_cast<const float2*>(&rtile[r * kRedStride + c]);
+    const uint32_t off = static_cast<uint32_t>((r * kRedStride + c) * 4);
+    float2 s = ld_dsmem_f2(mapa_u32(rt_local + off, 0));
+    for (int q = 1; q < cs; ++q) {
+      const float2 v = ld_dsmem_f2(mapa_u32(rt_local + off, q));
+      s.x += v.x;
+      s.y += v.y;
     }
+    return s;
+  };
+  auto sum_one = [&](int r, int c) -> float {
+    if (cs == 1) return rtile[r * kRedStride + c];
+    const uint32_t off = static_cast<uint32_t>((r * kRedStride + c) * 4);
+    float s = ld_dsmem_f32(mapa_u32(rt_local + off, 0));
+    for (int q = 1; q < cs; ++q) s += ld_dsmem_f32(mapa_u32(rt_local + off, q));
+    return s;
+  };
+  const int nrows = r_hi - r_lo;
+  if (ok) {
+    if (EPI == kPlain) {
+      for (int e = tid; e < nrows * (BN / 2); e += kConsumers) {
+        const int r = r_lo + e / (BN / 2), c = 2 * (e % (BN / 2));
+        const float2 v = sum_pair(r, c);
+        *reinterpret_cast<uint32_t*>(&a.out[static_cast<size_t>(r) * a.ldo + n0 + c]) = pack_bf16(v.x, v.y);
+      }
+    } else if (EPI == kResid) {
+      // h = bf16(h + bf16(acc)); 64 threads (two warps) per row, so each warp holds half a row
+      for (int e0 = 0; e0 < nrows * (BN / 2); e0 += kConsumers) {
+        const int e = e0 + tid;
+        float ss = 0.f;
+        if (e < nrows * (BN / 2)) {
+          const int r = r_lo + e / (BN / 2), c = 2 * (e % (BN / 2));
+          const float2 v = sum_pair(r, c);
+          uint32_t* hp = reinterpret_cast<uint32_t*>(&a.out[static_cast<size_t>(r) * a.ldo + n0 + c]);
+          const uint32_t hv = *hp;
+          const float x0 = bf16r(bf16lo(hv) + bf16r(v.x));
+          const float x1 = bf16r(bf16hi(hv) + bf16r(v.y));
+          *hp = pack_bf16(x0, x1);
+          ss = x0 * x0 + x1 * x1;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        // e / 64 is the slice row of this warp's half row, (e / 32) & 1 the half
+        if (lane == 0 && e < nrows * (BN / 2)) red[2 * (e / (BN / 2)) + ((e >> 5) & 1)] = ss;
+      }
+      named_bar(1, kConsumers);
+      if (tid < 32) {
+        const int r = tid;
+        if (r >= r_lo && r < r_hi) a.ss_out[tile * 32 + r] = red[2 * (r - r_lo)] + red[2 * (r - r_lo) + 1];
+        if (rank == 0 && r >= M) a.ss_out[tile * 32 + r] = 0.f;
+      }
+    } else {  // SwiGLU: features 0..63 of the tile are gate, 64..127 the matching up
+      const int f0 = tile * (BN / 2);
+      for (int e = tid; e < nrows * (BN / 2); e += kConsumers) {
+        const int r = r_lo + e / (BN / 2), j = e % (BN / 2);
+        const float gv = bf16r(sum_one(r, j));
+        const float uv = bf16r(sum_one(r, 64 + j));
+        const float sig = bf16r(1.0f / (1.0f + expf(-gv)));
+        a.out[static_cast<size_t>(r) * a.ldo + f0 + j] = __float2bfloat16_rn(bf16r(gv * sig) * uv);
+      }
+    }
+  }
+  if (cs > 1) cluster_sync_all();  // no CTA leaves while a peer may still read its tile
+}
+
+// Packed weight layout: element (n, k) of a row-major [N][K] matrix lives in block
+// (n / 128, k / 128), half (k % 128) / 64, row n % 128, 16-byte chunk
+// ((k % 64) / 8) ^ (n % 8), element k % 8.  One thread moves one 16-byte chunk.
+__device__ __forceinline__ size_t packed_chunk(int n, int kch, int kc_total) {
+  const int tile = n >> 7, r = n & 127;
+  const int kb = kch >> 4, half = (kch >> 3) & 1, c = kch & 7;
+  return ((static_cast<size_t>(tile) * kc_total + kb) * 2 + half) * (128 * 8) + r * 8 + (c ^ (r & 7));
+}
+
+__global__ void pack_weight_kernel(const uint4* __restrict__ src, uint4* __restrict__ dst, int N, int K, int unpack) {
+  const int kch_row = K / 8;  // 16-byte chunks per row
+  const size_t total = static_cast<size_t>(N) * kch_row;
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const int n = static_cast<int>(i / kch_row), kch = static_cast<int>(i % kch_row);
+    const size_t p = packed_chunk(n, kch, K / 128);
+    if (unpack) dst[i] = src[p];
+    else dst[p] = src[i];
   }
 }
 
@@ -364,23 +359,30 @@ static EncodeTiledFnG encode_fn_g() {
   return fn;
 }
 
+static int gemm_smem_bytes(int MT) {
+  using namespace gemm;
+  return kStages * (kWBytes + MT * 16 * BK * 2) + kStages * BK * 2 + (32 + 2 * 32) * 4 + 16 + 2 * kStages * 8 + 1024;
+}
+
 template <int MT, int EPI, bool NORM>
-static cudaError_t launch_gemm(cudaStream_t stream, const CUtensorMap& map, const CUtensorMap& xmap,
-                               const gemm::Args& a, int smem) {
+static cudaError_t launch_gemm(cudaStream_t stream, const CUtensorMap& xmap, const gemm::Args& a) {
   auto kern = gemm::decode_gemm_kernel<MT, EPI, NORM>;
-  static int configured = 0;
-  if (smem > configured) {
+  const int smem = gemm_smem_bytes(MT);
+  static bool configured = false;
+  if (!configured) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     if (e != cudaSuccess) return e;
-    configured = smem;
+    configured = true;
   }
   dim3 grid(a.N / gemm::BN, a.splits);
-  return launch_pdl(kern, grid, dim3(gemm::kThreads), smem, stream, 0, map, xmap, a);
+  return launch_pdl(kern, grid, dim3(gemm::kThreads), smem, stream, a.splits > 1 ? dim3(1, a.splits, 1) : dim3(0),
+                    xmap, a);
 }
 
 int decode_gemm(cudaStream_t stream, int epi, int M, int N, int K, const void* w, const void* x, int ldx,
                 const float* ss_parts, int n_parts, const void* norm_w, float eps, void* out, int ldo, float* ss_out,
-                float* partial, int* tickets, int splits, int* err) {
+                int splits, int* err) {
   using namespace gemm;
   if (!w || !x || !out) return fail(kStatusArg, "decode_gemm: null pointer");
   if (M <= 0 || M > 32) return fail(kStatusUnsupported, "decode_gemm: M = %d outside 1..32", M);
@@ -391,34 +393,27 @@ int decode_gemm(cudaStream_t stream, int epi, int M, int N, int K, const void* w
   if (norm && (!ss_parts || n_parts <= 0)) return fail(kStatusArg, "decode_gemm: norm needs ss_parts");
   if (epi == kResid && !ss_out) return fail(kStatusArg, "decode_gemm: residual epilogue needs ss_out");
   if (epi == kResid && N != ldo) return fail(kStatusArg, "decode_gemm: residual epilogue needs ldo == N");
-  if (splits < 1 || splits > K / BK) return fail(kStatusArg, "decode_gemm: bad split count %d", splits);
-  if (splits > 1 && (!partial || !tickets)) return fail(kStatusArg, "decode_gemm: split-K needs partial and tickets");
-  if (N / BN > 65535 || splits > 65535) return fail(kStatusArg, "decode_gemm: grid too large");
+  if (splits < 1 || splits > kMaxSplits || splits > K / BK)
+    return fail(kStatusArg, "decode_gemm: split count %d outside 1..min(16, K/128)", splits);
+  if (N / BN > 65535) return fail(kStatusArg, "decode_gemm: grid too large");
   if ((reinterpret_cast<uintptr_t>(w) & 15) || (reinterpret_cast<uintptr_t>(x) & 15) || (ldx % 8) ||
       (reinterpret_cast<uintptr_t>(norm_w) & 15) || (reinterpret_cast<uintptr_t>(out) & 3) || (ldo % 2))
     return fail(kStatusArg, "decode_gemm: W, x, norm_w rows must be 16-byte aligned and out rows 4-byte aligned");
   EncodeTiledFnG enc = encode_fn_g();
   if (!enc) return fail(kStatusCuda, "cuTensorMapEncodeTiled unavailable");
-  CUtensorMap map;
-  cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(N)};
-  cuuint64_t strides[1] = {static_cast<cuuint64_t>(K) * 2};
-  cuuint32_t box[2] = {64, static_cast<cuuint32_t>(BN)};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(w), dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return fail(kStatusCuda, "decode_gemm: cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
   const int MT = M > 16 ? 2 : 1;
   // activations [M][K] (row stride ldx): boxes of 64 k x 16*MT rows, rows >= M read as zero
   CUtensorMap xmap;
   cuuint64_t xdims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(M)};
   cuuint64_t xstrides[1] = {static_cast<cuuint64_t>(ldx) * 2};
   cuuint32_t xbox[2] = {64, static_cast<cuuint32_t>(16 * MT)};
-  r = enc(&xmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(x), xdims, xstrides, xbox, estr,
-          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(&xmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(x), xdims, xstrides, xbox, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(kStatusCuda, "decode_gemm: activation map failed (%d)", static_cast<int>(r));
   Args a;
+  a.w = static_cast<const __nv_bfloat16*>(w);
   a.x = static_cast<const __nv_bfloat16*>(x);
   a.ldx = ldx;
   a.ss_parts = ss_parts;
@@ -428,18 +423,14 @@ int decode_gemm(cudaStream_t stream, int epi, int M, int N, int K, const void* w
   a.out = static_cast<__nv_bfloat16*>(out);
   a.ldo = ldo;
   a.ss_out = ss_out;
-  a.partial = partial;
-  a.tickets = tickets;
   a.M = M;
   a.N = N;
   a.K = K;
   a.splits = splits;
   a.err = err;
-  const int smem = kStages * (kWBytes + MT * 16 * BK * 2) + kStages * BK * 2 + (32 + 4 * 32) * 4 + 16 +
-                   2 * kStages * 8 + 1024;
   cudaError_t e = cudaSuccess;
 #define KVBP_GEMM_CASE(mt, ep, nm) \
-  if (MT == mt && epi == ep && norm == nm) e = launch_gemm<mt, ep, nm>(stream, map, xmap, a, smem); else
+  if (MT == mt && epi == ep && norm == nm) e = launch_gemm<mt, ep, nm>(stream, xmap, a); else
   KVBP_GEMM_CASE(1, kPlain, false)
   KVBP_GEMM_CASE(1, kPlain, true)
   KVBP_GEMM_CASE(1, kResid, false)
@@ -456,14 +447,41 @@ int decode_gemm(cudaStream_t stream, int epi, int M, int N, int K, const void* w
   return kStatusOk;
 }
 
+int pack_weight(cudaStream_t stream, int N, int K, const void* src, void* dst, int unpack) {
+  if (!src || !dst) return fail(kStatusArg, "pack_weight: null pointer");
+  if (N <= 0 || K <= 0 || N % 128 || K % 128)
+    return fail(kStatusUnsupported, "pack_weight: N (%d) and K (%d) must be positive multiples of 128", N, K);
+  if ((reinterpret_cast<uintptr_t>(src) & 15) || (reinterpret_cast<uintptr_t>(dst) & 15))
+    return fail(kStatusArg, "pack_weight: src and dst must be 16-byte aligned");
+  const size_t bytes = static_cast<size_t>(N) * K * 2;
+  const uintptr_t s0 = reinterpret_cast<uintptr_t>(src), d0 = reinterpret_cast<uintptr_t>(dst);
+  if (s0 < d0 + bytes && d0 < s0 + bytes) return fail(kStatusArg, "pack_weight: src and dst overlap");
+  const size_t chunks = static_cast<size_t>(N) * (K / 8);
+  size_t blocks = (chunks + 255) / 256;
+  if (blocks > 148 * 32) blocks = 148 * 32;
+  gemm::pack_weight_kernel<<<static_cast<int>(blocks), 256, 0, stream>>>(static_cast<const uint4*>(src),
+                                                                          static_cast<uint4*>(dst), N, K, unpack);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(kStatusCuda, "pack_weight launch: %s", cudaGetErrorString(e));
+  return kStatusOk;
+}
+
 }  // namespace kvbp
 
 #include "../../include/kvbp.h"
 
 extern "C" int kvbp_decode_gemm(kvbp_stream_t stream, int32_t epilogue, int32_t M, int32_t N, int32_t K,
-                                const void* w, const void* x, int32_t ldx, const float* ss_parts, int32_t n_parts,
-                                const void* norm_w, float eps, void* out, int32_t ldo, float* ss_out, float* partial,
-                                int32_t* tickets, int32_t splits, int32_t* dev_err) {
-  return kvbp::decode_gemm(reinterpret_cast<cudaStream_t>(stream), epilogue, M, N, K, w, x, ldx, ss_parts, n_parts,
-                           norm_w, eps, out, ldo, ss_out, partial, tickets, splits, dev_err);
+                                const void* w_packed, const void* x, int32_t ldx, const float* ss_parts,
+                                int32_t n_parts, const void* norm_w, float eps, void* out, int32_t ldo, float* ss_out,
+                                int32_t splits, int32_t* dev_err) {
+  return kvbp::decode_gemm(reinterpret_cast<cudaStream_t>(stream), epilogue, M, N, K, w_packed, x, ldx, ss_parts,
+                           n_parts, norm_w, eps, out, ldo, ss_out, splits, dev_err);
+}
+
+extern "C" int kvbp_pack_weight(kvbp_stream_t stream, int32_t N, int32_t K, const void* src, void* dst) {
+  return kvbp::pack_weight(reinterpret_cast<cudaStream_t>(stream), N, K, src, dst, 0);
+}
+
+extern "C" int kvbp_unpack_weight(kvbp_stream_t stream, int32_t N, int32_t K, const void* src, void* dst) {
+  return kvbp::pack_weight(reinterpret_cast<cudaStream_t>(stream), N, K, src, dst, 1);
 }

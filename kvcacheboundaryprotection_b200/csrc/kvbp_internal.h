@@ -19,10 +19,11 @@ enum Status : int {
 int fail(int status, const char* fmt, ...);
 
 // Launches ``kernel`` with programmatic stream serialization (the kernel calls
-// pdl_wait() before reading what the previous kernel wrote) and an optional cluster.
+// pdl_wait() before reading what the previous kernel wrote) and, when cluster.x > 0,
+// thread-block clusters of that shape.
 template <typename... KArgs, typename... Args>
 cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
-                       int cluster_x, Args&&... args) {
+                       dim3 cluster, Args&&... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
@@ -35,11 +36,11 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
   attr[n].val.programmaticStreamSerializationAllowed = 1;
   ++n;
 #endif
-  if (cluster_x > 0) {
+  if (cluster.x > 0) {
     attr[n].id = cudaLaunchAttributeClusterDimension;
-    attr[n].val.clusterDim.x = cluster_x;
-    attr[n].val.clusterDim.y = 1;
-    attr[n].val.clusterDim.z = 1;
+    attr[n].val.clusterDim.x = cluster.x;
+    attr[n].val.clusterDim.y = cluster.y;
+    attr[n].val.clusterDim.z = cluster.z;
     ++n;
   }
   cfg.attrs = attr;

@@ -93,10 +93,34 @@ def deinterleave_gate_up(gu: torch.Tensor, block: int = 64) -> torch.Tensor:
     return torch.cat([v[:, :, 0, :].reshape(R, F2 // 2), v[:, :, 1, :].reshape(R, F2 // 2)], 1)
 
 
+def pack_weight(w: torch.Tensor) -> torch.Tensor:
+    """Row-major bf16 [N, K] -> the decode GEMM's packed layout (same shape and size;
+    kvbp_pack_weight describes the element order)."""
+    N, K = w.shape
+    out = torch.empty_like(w)
+    check(lib().kvbp_pack_weight(torch.cuda.current_stream(w.device).cuda_stream, N, K, _ptr(w), _ptr(out)),
+          "pack_weight")
+    return out
+
+
+def unpack_weight(w: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Inverse of pack_weight (into ``out`` when given)."""
+    N, K = w.shape
+    if out is None:
+        out = torch.empty_like(w)
+    check(lib().kvbp_unpack_weight(torch.cuda.current_stream(w.device).cuda_stream, N, K, _ptr(w), _ptr(out)),
+          "unpack_weight")
+    return out
+
+
 class FusedWeights:
     """Decoder weights on the device in the engine's layout (bf16): q/k/v stacked into
     one [(Hq+2Hkv)*128, H] matrix (+ stacked bias); gate/up interleaved in blocks of 64
-    rows for the own decode GEMM (``gemm="kvbp"``) or stacked [gate; up] for cuBLAS."""
+    rows for the own decode GEMM (``gemm="kvbp"``) or stacked [gate; up] for cuBLAS.
+    With ``gemm="kvbp"`` the projection matrices and lm_head are stored packed
+    (pack_weight); ``rowmajor`` gives a row-major view for the prefill's cuBLAS GEMMs."""
+
+    PACKED = ("w_qkv", "w_o", "w_gu", "w_down")
 
     def __init__(self, cfg: ModelConfig, w: Dict[str, torch.Tensor], device: torch.device, gemm: str = "kvbp"):
         c, d, bf = cfg, torch.device(device), torch.bfloat16
@@ -131,6 +155,24 @@ class FusedWeights:
                 }
             )
         self.inv_freq = torch.from_numpy(inv_freq_table(c.head_dim, c.rope_theta)).to(d)
+        self._scratch = None
+        if gemm == "kvbp":
+            with torch.cuda.device(d):
+                for L in self.layers:
+                    for k in self.PACKED:
+                        L[k] = pack_weight(L[k])
+                self.lm_w = pack_weight(self.lm_w)
+
+    def rowmajor(self, w: torch.Tensor) -> torch.Tensor:
+        """Row-major copy of a packed projection matrix (a reused scratch buffer, valid
+        until the next call); the tensor itself when the weights are not packed."""
+        if self.gemm != "kvbp":
+            return w
+        n = w.numel()
+        if self._scratch is None or self._scratch.numel() < n:
+            biggest = max(L[k].numel() for L in self.layers for k in self.PACKED)
+            self._scratch = torch.empty(max(n, biggest), dtype=torch.bfloat16, device=w.device)
+        return unpack_weight(w, self._scratch[:n].view(w.shape))
 
     def nbytes(self) -> int:
         n = self.embed_w.numel() + (0 if self.lm_w is self.embed_w else self.lm_w.numel()) + self.final_norm.numel()
@@ -235,19 +277,14 @@ class CappedKVEngine:
         self.act = z(B, F, dt=bf)
         self.dn = z(B, H, dt=bf)
         self.logits = z(B, V, dt=bf)
-        # own-GEMM workspace: RMSNorm partial sums, split-K partials and tickets
+        # own-GEMM RMSNorm partial sums and split-K cluster sizes
         self.ss_a = z(max(1, H // 128), 32, dt=f32)
         self.ss_b = z(max(1, H // 128), 32, dt=f32)
-        self.splits = {}
-        psize = 1
-        for name, (N, K) in {"qkv": (c.qkv_dim, H), "o": (H, c.n_heads * c.head_dim), "gu": (2 * F, H),
-                             "down": (H, F), "lm": (V, H)}.items():
-            sp = self._pick_splits(N, K)
-            self.splits[name] = sp
-            if sp > 1:
-                psize = max(psize, sp * B * N)
-        self.gemm_partial = z(psize, dt=f32)
-        self.gemm_tickets = z(max(c.qkv_dim, 2 * F, V, H) // 128 + 1)
+        self.splits = {
+            name: self._pick_splits(N, K)
+            for name, (N, K) in {"qkv": (c.qkv_dim, H), "o": (H, c.n_heads * c.head_dim), "gu": (2 * F, H),
+                                 "down": (H, F), "lm": (V, H)}.items()
+        }
         self._state = State(
             B, S, self.W,
             self.slot_pos.data_ptr(), self.insert_step.data_ptr(), self.last_access.data_ptr(),
@@ -335,7 +372,7 @@ class CappedKVEngine:
             colmax = torch.zeros(P, dtype=torch.float32, device=d) if need_scores else None
             for li, Lw in enumerate(self.layers):
                 check(L.kvbp_add_rmsnorm(st, P, H, _ptr(h), _ptr(delta), _ptr(Lw["in_norm"]), _ptr(x), c.eps), "rmsnorm")
-                qkv = torch.mm(x, Lw["w_qkv"].t())
+                qkv = torch.mm(x, self.fw.rowmajor(Lw["w_qkv"]).t())
                 q = torch.empty(P, c.n_heads, D, dtype=torch.bfloat16, device=d)
                 kb, vb = pre_k[li, b], pre_v[li, b]
                 check(
@@ -350,20 +387,27 @@ class CappedKVEngine:
                 att = self._prefill_attention(q, kb, vb, need_scores, lcol)
                 if need_scores:
                     torch.maximum(colmax, lcol, out=colmax)
-                o = torch.mm(att, Lw["w_o"].t())
+                o = torch.mm(att, self.fw.rowmajor(Lw["w_o"]).t())
                 check(L.kvbp_add_rmsnorm(st, P, H, _ptr(h), _ptr(o), _ptr(Lw["post_norm"]), _ptr(x), c.eps), "rmsnorm")
-                gu = torch.mm(x, Lw["w_gu"].t())
+                gu = torch.mm(x, self.fw.rowmajor(Lw["w_gu"]).t())
                 if self.gemm == "kvbp":
                     gu = deinterleave_gate_up(gu)
                 act = torch.empty(P, c.ffn, dtype=torch.bfloat16, device=d)
                 check(L.kvbp_silu_mul(st, P, c.ffn, _ptr(gu), _ptr(act)), "silu_mul")
-                delta = torch.mm(act, Lw["w_down"].t())
+                delta = torch.mm(act, self.fw.rowmajor(Lw["w_down"]).t())
                 del gu, act, qkv, q
             hl = h[P - 1 : P].contiguous()
             dl = delta[P - 1 : P].contiguous()
             xl = torch.empty_like(hl)
             check(L.kvbp_add_rmsnorm(st, 1, H, _ptr(hl), _ptr(dl), _ptr(self.final_norm), _ptr(xl), c.eps), "rmsnorm")
-            torch.mm(xl, self.lm_w.t(), out=self.logits[b : b + 1])
+            if self.gemm == "kvbp":  # lm_head is packed: one row through the decode GEMM
+                check(
+                    L.kvbp_decode_gemm(st, 0, 1, c.vocab, H, _ptr(self.lm_w), _ptr(xl), H, None, 0, None, c.eps,
+                                       _ptr(self.logits[b : b + 1]), c.vocab, None, self.splits["lm"], _ptr(self.dev_err)),
+                    "decode_gemm[lm]",
+                )
+            else:
+                torch.mm(xl, self.lm_w.t(), out=self.logits[b : b + 1])
             if need_scores:
                 scores[b] = colmax
         self._select_and_compact(P, scores, pre_k, pre_v)
@@ -437,8 +481,7 @@ class CappedKVEngine:
         check(
             lib().kvbp_decode_gemm(
                 self.stream, epi, self.B, N, K, _ptr(w), _ptr(x), ldx, _ptr(ss_in), n_parts, _ptr(norm_w), c.eps,
-                _ptr(out), ldo, _ptr(ss_out), _ptr(self.gemm_partial), _ptr(self.gemm_tickets), self.splits[name],
-                _ptr(self.dev_err),
+                _ptr(out), ldo, _ptr(ss_out), self.splits[name], _ptr(self.dev_err),
             ),
             f"decode_gemm[{name}]",
         )
