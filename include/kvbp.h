@@ -211,6 +211,18 @@ int kvbp_decode_gemm(kvbp_stream_t stream, int32_t epilogue, int32_t M, int32_t 
                      const void* x, int32_t ldx, const float* ss_parts, int32_t n_parts, const void* norm_w, float eps,
                      void* out, int32_t ldo, float* ss_out, int32_t splits, int32_t* dev_err);
 
+/* kvbp_decode_gemm for the stacked q/k/v projection (N = (n_heads + 2 n_kv_heads) * 128,
+ * norm prologue as above) fused with kvbp_qkv_rope_scatter's per-head work: each
+ * 128-feature tile is one head, finished in the epilogue with bias, q/k RMSNorm, RoPE
+ * and the store of q to q_out[M][n_heads][128] or of k/v to kcache/vcache
+ * [M][n_kv_heads][S][128] at slot write_slot[m] (skipped when < 0; >= S sets
+ * KVBP_ERR_INDEX).  jax_inference.py:949-956,975-978,1000-1012. */
+int kvbp_decode_qkv_gemm(kvbp_stream_t stream, int32_t M, int32_t n_heads, int32_t n_kv_heads, int32_t K,
+                         const void* w_packed, const void* x, int32_t ldx, const float* ss_parts, int32_t n_parts,
+                         const void* norm_w, float eps, const void* bias, const void* q_norm, const void* k_norm,
+                         const float* inv_freq, const int32_t* positions, const int32_t* write_slot, int32_t S,
+                         void* q_out, void* kcache, void* vcache, int32_t splits, int32_t* dev_err);
+
 /* Converts a row-major bf16 weight W[N][K] (N, K multiples of 128) to the decode GEMM's
  * packed layout and back: each 128-row x 128-column block becomes one contiguous 32 KiB
  * run of two 128 x 64 halves whose 16-byte chunks are XOR-swizzled by row (chunk

@@ -104,6 +104,8 @@ SIGNATURES = {
     "kvbp_argmax": (C.c_int, [P, I32, I32, I64, P, P]),
     "kvbp_row_sumsq": (C.c_int, [P, I32, I32, P, P]),
     "kvbp_decode_gemm": (C.c_int, [P, I32, I32, I32, I32, P, P, I32, P, I32, P, F32, P, I32, P, I32, P]),
+    "kvbp_decode_qkv_gemm": (C.c_int, [P, I32, I32, I32, I32, P, P, I32, P, I32, P, F32, P, P, P, P, P, P, I32, P, P,
+                                       P, I32, P]),
     "kvbp_pack_weight": (C.c_int, [P, I32, I32, P, P]),
     "kvbp_unpack_weight": (C.c_int, [P, I32, I32, P, P]),
 }

@@ -26,6 +26,11 @@
 //   * SWIGLU epilogue: weight rows are stored gate/up interleaved in blocks of 64, so a
 //     tile holds 64 gate and the matching 64 up features and writes
 //     act = bf16(bf16(g * bf16(sigmoid(g))) * u) (jax_inference.py:702-704,1103-1107).
+//   * QKV epilogue: a 128-feature tile of the stacked q/k/v projection is exactly one
+//     head, so the tile finishes it in place: bias, q/k RMSNorm (Qwen3), RoPE, and the
+//     store of q to its buffer or of k/v into the slot the sequence writes this step
+//     (jax_inference.py:953-956,975-978,1000-1012) -- the same arithmetic as
+//     kvbp_qkv_rope_scatter.
 #include "common.cuh"
 #include "kvbp_internal.h"
 
@@ -45,7 +50,7 @@ constexpr int kBlockElems = BN * BK;  // one packed block
 constexpr int kRedStride = BN + 8;    // fp32 partial tile row stride (fewer bank conflicts)
 constexpr int kMaxSplits = 16;
 
-enum Epi : int { kPlain = 0, kResid = 1, kSwiGLU = 2 };
+enum Epi : int { kPlain = 0, kResid = 1, kSwiGLU = 2, kQKV = 3 };
 
 struct Args {
   const __nv_bfloat16* w;  // packed [N/128][K/128][2][128][64] (swizzled 16-byte chunks)
@@ -60,6 +65,17 @@ struct Args {
   float* ss_out;  // RESID: [N / BN][32] partial sums of squares of the new h
   int M, N, K, splits;
   int* err;
+  // QKV epilogue (head h = tile: q heads, then k heads, then v heads)
+  const __nv_bfloat16* bias;  // [N] or null
+  const __nv_bfloat16* qnw;   // [128] q RMSNorm weight or null
+  const __nv_bfloat16* knw;   // [128] k RMSNorm weight or null
+  const float* inv_freq;      // [64]
+  const int* positions;       // [M]
+  const int* write_slot;      // [M]
+  int Hq, Hkv, S;
+  __nv_bfloat16* q_out;   // [M][Hq][128]
+  __nv_bfloat16* kcache;  // [M][Hkv][S][128]
+  __nv_bfloat16* vcache;
 };
 
 template <int MT, int EPI, bool NORM>
@@ -303,7 +319,7 @@ __global__ void __launch_bounds__(kThreads) decode_gemm_kernel(const __grid_cons
         if (r >= r_lo && r < r_hi) a.ss_out[tile * 32 + r] = red[2 * (r - r_lo)] + red[2 * (r - r_lo) + 1];
         if (rank == 0 && r >= M) a.ss_out[tile * 32 + r] = 0.f;
       }
-    } else {  // SwiGLU: features 0..63 of the tile are gate, 64..127 the matching up
+    } else if (EPI == kSwiGLU) {  // features 0..63 of the tile are gate, 64..127 the matching up
       const int f0 = tile * (BN / 2);
       for (int e = tid; e < nrows * (BN / 2); e += kConsumers) {
         const int r = r_lo + e / (BN / 2), j = e % (BN / 2);
@@ -311,6 +327,60 @@ __global__ void __launch_bounds__(kThreads) decode_gemm_kernel(const __grid_cons
         const float uv = bf16r(sum_one(r, 64 + j));
         const float sig = bf16r(1.0f / (1.0f + expf(-gv)));
         a.out[static_cast<size_t>(r) * a.ldo + f0 + j] = __float2bfloat16_rn(bf16r(gv * sig) * uv);
+      }
+    } else {  // QKV: one head per tile; 64 threads per row, thread i holds features i, i + 64
+      const int hh = tile, i = tid & 63;
+      const bool is_q = hh < a.Hq, is_k = !is_q && hh < a.Hq + a.Hkv;
+      const __nv_bfloat16* nw = is_q ? a.qnw : (is_k ? a.knw : nullptr);
+      for (int e0 = 0; e0 < nrows * 64; e0 += kConsumers) {  // two rows per pass
+        const int e = e0 + tid;
+        const bool live = e < nrows * 64;
+        const int r = r_lo + e / 64;
+        float x0 = 0.f, x1 = 0.f;
+        if (live) {
+          x0 = bf16r(sum_one(r, i));  // the GEMM's bf16 output
+          x1 = bf16r(sum_one(r, i + 64));
+          if (a.bias) {
+            x0 = bf16r(x0 + __bfloat162float(a.bias[hh * 128 + i]));
+            x1 = bf16r(x1 + __bfloat162float(a.bias[hh * 128 + i + 64]));
+          }
+        }
+        if (nw) {  // CTA-uniform: RMSNorm over the head's 128 features
+          float ss = x0 * x0 + x1 * x1;
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+          if (lane == 0) red[warp] = ss;
+          named_bar(1, kConsumers);
+          const float tot = red[(warp >> 1) * 2] + red[(warp >> 1) * 2 + 1];
+          named_bar(1, kConsumers);  // red is reused by the next pass
+          const float inv = 1.0f / sqrtf(tot / 128.0f + a.eps);
+          x0 = bf16r((x0 * inv) * __bfloat162float(nw[i]));
+          x1 = bf16r((x1 * inv) * __bfloat162float(nw[i + 64]));
+        }
+        if (!live) continue;
+        if (is_q || is_k) {
+          const float ang = static_cast<float>(a.positions[r]) * a.inv_freq[i];
+          const float c = bf16r(cosf(ang)), sn = bf16r(sinf(ang));
+          const float y0 = bf16r(bf16r(x0 * c) - bf16r(x1 * sn));
+          const float y1 = bf16r(bf16r(x1 * c) + bf16r(x0 * sn));
+          x0 = y0;
+          x1 = y1;
+        }
+        __nv_bfloat16* dst;
+        if (is_q) {
+          dst = a.q_out + (static_cast<size_t>(r) * a.Hq + hh) * 128;
+        } else {
+          const int slot = a.write_slot[r];
+          if (slot < 0) continue;  // position evicted before its forward: nothing to store
+          if (slot >= a.S) {
+            set_err(a.err, kErrIndex);
+            continue;
+          }
+          const int kvh = is_k ? hh - a.Hq : hh - a.Hq - a.Hkv;
+          dst = (is_k ? a.kcache : a.vcache) + ((static_cast<size_t>(r) * a.Hkv + kvh) * a.S + slot) * 128;
+        }
+        dst[i] = __float2bfloat16_rn(x0);
+        dst[i + 64] = __float2bfloat16_rn(x1);
       }
     }
   }
@@ -380,39 +450,19 @@ static cudaError_t launch_gemm(cudaStream_t stream, const CUtensorMap& xmap, con
                     xmap, a);
 }
 
+static int decode_gemm_launch(cudaStream_t stream, int epi, gemm::Args& a);
+
 int decode_gemm(cudaStream_t stream, int epi, int M, int N, int K, const void* w, const void* x, int ldx,
                 const float* ss_parts, int n_parts, const void* norm_w, float eps, void* out, int ldo, float* ss_out,
                 int splits, int* err) {
   using namespace gemm;
-  if (!w || !x || !out) return fail(kStatusArg, "decode_gemm: null pointer");
-  if (M <= 0 || M > 32) return fail(kStatusUnsupported, "decode_gemm: M = %d outside 1..32", M);
-  if (N <= 0 || K <= 0 || N % BN || K % BK)
-    return fail(kStatusUnsupported, "decode_gemm: N (%d) and K (%d) must be positive multiples of 128", N, K);
   if (epi < kPlain || epi > kSwiGLU) return fail(kStatusArg, "decode_gemm: unknown epilogue %d", epi);
-  const bool norm = norm_w != nullptr;
-  if (norm && (!ss_parts || n_parts <= 0)) return fail(kStatusArg, "decode_gemm: norm needs ss_parts");
+  if (!out) return fail(kStatusArg, "decode_gemm: null pointer");
   if (epi == kResid && !ss_out) return fail(kStatusArg, "decode_gemm: residual epilogue needs ss_out");
   if (epi == kResid && N != ldo) return fail(kStatusArg, "decode_gemm: residual epilogue needs ldo == N");
-  if (splits < 1 || splits > kMaxSplits || splits > K / BK)
-    return fail(kStatusArg, "decode_gemm: split count %d outside 1..min(16, K/128)", splits);
-  if (N / BN > 65535) return fail(kStatusArg, "decode_gemm: grid too large");
-  if ((reinterpret_cast<uintptr_t>(w) & 15) || (reinterpret_cast<uintptr_t>(x) & 15) || (ldx % 8) ||
-      (reinterpret_cast<uintptr_t>(norm_w) & 15) || (reinterpret_cast<uintptr_t>(out) & 3) || (ldo % 2))
-    return fail(kStatusArg, "decode_gemm: W, x, norm_w rows must be 16-byte aligned and out rows 4-byte aligned");
-  EncodeTiledFnG enc = encode_fn_g();
-  if (!enc) return fail(kStatusCuda, "cuTensorMapEncodeTiled unavailable");
-  const int MT = M > 16 ? 2 : 1;
-  // activations [M][K] (row stride ldx): boxes of 64 k x 16*MT rows, rows >= M read as zero
-  CUtensorMap xmap;
-  cuuint64_t xdims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(M)};
-  cuuint64_t xstrides[1] = {static_cast<cuuint64_t>(ldx) * 2};
-  cuuint32_t xbox[2] = {64, static_cast<cuuint32_t>(16 * MT)};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(&xmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(x), xdims, xstrides, xbox, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return fail(kStatusCuda, "decode_gemm: activation map failed (%d)", static_cast<int>(r));
-  Args a;
+  if ((reinterpret_cast<uintptr_t>(out) & 3) || (ldo % 2))
+    return fail(kStatusArg, "decode_gemm: out rows must be 4-byte aligned");
+  Args a = {};
   a.w = static_cast<const __nv_bfloat16*>(w);
   a.x = static_cast<const __nv_bfloat16*>(x);
   a.ldx = ldx;
@@ -428,6 +478,77 @@ int decode_gemm(cudaStream_t stream, int epi, int M, int N, int K, const void* w
   a.K = K;
   a.splits = splits;
   a.err = err;
+  return decode_gemm_launch(stream, epi, a);
+}
+
+int decode_qkv_gemm(cudaStream_t stream, int M, int Hq, int Hkv, int K, const void* w, const void* x, int ldx,
+                    const float* ss_parts, int n_parts, const void* norm_w, float eps, const void* bias,
+                    const void* q_norm, const void* k_norm, const float* inv_freq, const int* positions,
+                    const int* write_slot, int S, void* q_out, void* kcache, void* vcache, int splits, int* err) {
+  using namespace gemm;
+  if (!inv_freq || !positions || !write_slot || !q_out || !kcache || !vcache)
+    return fail(kStatusArg, "decode_qkv_gemm: null pointer");
+  if (Hq <= 0 || Hkv <= 0 || Hq % Hkv || S <= 0) return fail(kStatusArg, "decode_qkv_gemm: bad head counts or S");
+  Args a = {};
+  a.w = static_cast<const __nv_bfloat16*>(w);
+  a.x = static_cast<const __nv_bfloat16*>(x);
+  a.ldx = ldx;
+  a.ss_parts = ss_parts;
+  a.n_parts = n_parts;
+  a.norm_w = static_cast<const __nv_bfloat16*>(norm_w);
+  a.eps = eps;
+  a.M = M;
+  a.N = (Hq + 2 * Hkv) * 128;
+  a.K = K;
+  a.splits = splits;
+  a.err = err;
+  a.bias = static_cast<const __nv_bfloat16*>(bias);
+  a.qnw = static_cast<const __nv_bfloat16*>(q_norm);
+  a.knw = static_cast<const __nv_bfloat16*>(k_norm);
+  a.inv_freq = inv_freq;
+  a.positions = positions;
+  a.write_slot = write_slot;
+  a.Hq = Hq;
+  a.Hkv = Hkv;
+  a.S = S;
+  a.q_out = static_cast<__nv_bfloat16*>(q_out);
+  a.kcache = static_cast<__nv_bfloat16*>(kcache);
+  a.vcache = static_cast<__nv_bfloat16*>(vcache);
+  return decode_gemm_launch(stream, kQKV, a);
+}
+
+static int decode_gemm_launch(cudaStream_t stream, int epi, gemm::Args& a) {
+  using namespace gemm;
+  const int M = a.M, N = a.N, K = a.K, splits = a.splits, ldx = a.ldx, n_parts = a.n_parts;
+  const void* w = a.w;
+  const void* x = a.x;
+  const void* norm_w = a.norm_w;
+  const float* ss_parts = a.ss_parts;
+  if (!w || !x) return fail(kStatusArg, "decode_gemm: null pointer");
+  if (M <= 0 || M > 32) return fail(kStatusUnsupported, "decode_gemm: M = %d outside 1..32", M);
+  if (N <= 0 || K <= 0 || N % BN || K % BK)
+    return fail(kStatusUnsupported, "decode_gemm: N (%d) and K (%d) must be positive multiples of 128", N, K);
+  const bool norm = norm_w != nullptr;
+  if (norm && (!ss_parts || n_parts <= 0)) return fail(kStatusArg, "decode_gemm: norm needs ss_parts");
+  if (splits < 1 || splits > kMaxSplits || splits > K / BK)
+    return fail(kStatusArg, "decode_gemm: split count %d outside 1..min(16, K/128)", splits);
+  if (N / BN > 65535) return fail(kStatusArg, "decode_gemm: grid too large");
+  if ((reinterpret_cast<uintptr_t>(w) & 15) || (reinterpret_cast<uintptr_t>(x) & 15) || (ldx % 8) ||
+      (reinterpret_cast<uintptr_t>(norm_w) & 15))
+    return fail(kStatusArg, "decode_gemm: W, x and norm_w rows must be 16-byte aligned");
+  EncodeTiledFnG enc = encode_fn_g();
+  if (!enc) return fail(kStatusCuda, "cuTensorMapEncodeTiled unavailable");
+  const int MT = M > 16 ? 2 : 1;
+  // activations [M][K] (row stride ldx): boxes of 64 k x 16*MT rows, rows >= M read as zero
+  CUtensorMap xmap;
+  cuuint64_t xdims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(M)};
+  cuuint64_t xstrides[1] = {static_cast<cuuint64_t>(ldx) * 2};
+  cuuint32_t xbox[2] = {64, static_cast<cuuint32_t>(16 * MT)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(&xmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(x), xdims, xstrides, xbox, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(kStatusCuda, "decode_gemm: activation map failed (%d)", static_cast<int>(r));
   cudaError_t e = cudaSuccess;
 #define KVBP_GEMM_CASE(mt, ep, nm) \
   if (MT == mt && epi == ep && norm == nm) e = launch_gemm<mt, ep, nm>(stream, xmap, a); else
@@ -441,6 +562,10 @@ int decode_gemm(cudaStream_t stream, int epi, int M, int N, int K, const void* w
   KVBP_GEMM_CASE(2, kResid, false)
   KVBP_GEMM_CASE(2, kSwiGLU, true)
   KVBP_GEMM_CASE(2, kSwiGLU, false)
+  KVBP_GEMM_CASE(1, kQKV, true)
+  KVBP_GEMM_CASE(1, kQKV, false)
+  KVBP_GEMM_CASE(2, kQKV, true)
+  KVBP_GEMM_CASE(2, kQKV, false)
   return fail(kStatusUnsupported, "decode_gemm: epilogue %d with norm=%d not built", epi, static_cast<int>(norm));
 #undef KVBP_GEMM_CASE
   if (e != cudaSuccess) return fail(kStatusCuda, "decode_gemm launch: %s", cudaGetErrorString(e));
@@ -476,6 +601,17 @@ extern "C" int kvbp_decode_gemm(kvbp_stream_t stream, int32_t epilogue, int32_t 
                                 int32_t splits, int32_t* dev_err) {
   return kvbp::decode_gemm(reinterpret_cast<cudaStream_t>(stream), epilogue, M, N, K, w_packed, x, ldx, ss_parts,
                            n_parts, norm_w, eps, out, ldo, ss_out, splits, dev_err);
+}
+
+extern "C" int kvbp_decode_qkv_gemm(kvbp_stream_t stream, int32_t M, int32_t n_heads, int32_t n_kv_heads, int32_t K,
+                                    const void* w_packed, const void* x, int32_t ldx, const float* ss_parts,
+                                    int32_t n_parts, const void* norm_w, float eps, const void* bias,
+                                    const void* q_norm, const void* k_norm, const float* inv_freq,
+                                    const int32_t* positions, const int32_t* write_slot, int32_t S, void* q_out,
+                                    void* kcache, void* vcache, int32_t splits, int32_t* dev_err) {
+  return kvbp::decode_qkv_gemm(reinterpret_cast<cudaStream_t>(stream), M, n_heads, n_kv_heads, K, w_packed, x, ldx,
+                               ss_parts, n_parts, norm_w, eps, bias, q_norm, k_norm, inv_freq, positions, write_slot,
+                               S, q_out, kcache, vcache, splits, dev_err);
 }
 
 extern "C" int kvbp_pack_weight(kvbp_stream_t stream, int32_t N, int32_t K, const void* src, void* dst) {

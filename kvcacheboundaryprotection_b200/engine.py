@@ -298,11 +298,12 @@ class CappedKVEngine:
 
     @staticmethod
     def _pick_splits(N: int, K: int, sms: int = 148) -> int:
-        """Split K so the grid has about one CTA per SM (N / 128 column tiles per split);
-        measured best on B200 for the decode shapes (1 split once N / 128 >= #SMs)."""
+        """Split K so that the grid holds about 256 CTAs (N / 128 column tiles per split,
+        at most 7 CTAs per cluster): measured best on B200 for the 7B decode shapes
+        (q/k/v 7, o and down 7, gate/up and lm_head 1)."""
         tiles = max(1, N // 128)
-        want = int(round(sms / tiles))
-        return max(1, min(want, K // 128, 16))
+        want = (256 * sms // 148) // tiles
+        return max(1, min(want, K // 128, 7))
 
     @property
     def stream(self) -> int:
@@ -493,8 +494,9 @@ class CappedKVEngine:
             self._forward_cublas()
 
     def _forward_kvbp(self) -> None:
-        """Forward with the own decode GEMMs: the RMSNorms ride in the GEMM prologues, the
-        residual adds and SwiGLU in the epilogues (6 launches per layer)."""
+        """Forward with the own decode GEMMs: the RMSNorms ride in the GEMM prologues; the
+        q/k/v bias, norm, RoPE and cache store, the residual adds and SwiGLU in the
+        epilogues (5 launches per layer)."""
         c, st, L, B = self.cfg, self.stream, lib(), self.B
         H, D, F = c.hidden, c.head_dim, c.ffn
         nt_h = H // 128
@@ -502,14 +504,14 @@ class CappedKVEngine:
         check(L.kvbp_row_sumsq(st, B, H, _ptr(self.h), _ptr(self.ss_a)), "row_sumsq")
         ss_in, n_in = self.ss_a, 1
         for li, Lw in enumerate(self.layers):
-            self._gemm("qkv", 0, c.qkv_dim, H, Lw["w_qkv"], self.h, H, self.qkv, c.qkv_dim, Lw["in_norm"], ss_in, n_in)
             check(
-                L.kvbp_qkv_rope_scatter(
-                    st, B, 1, c.n_heads, c.n_kv_heads, D, self.S, _ptr(self.qkv), c.qkv_dim, _ptr(Lw["b_qkv"]),
-                    _ptr(Lw["q_norm"]), _ptr(Lw["k_norm"]), c.eps, _ptr(self.inv_freq), _ptr(self.cur_pos),
-                    _ptr(self.write_slot), _ptr(self.q), _ptr(self.kc[li]), _ptr(self.vc[li]), _ptr(self.dev_err),
+                L.kvbp_decode_qkv_gemm(
+                    st, B, c.n_heads, c.n_kv_heads, H, _ptr(Lw["w_qkv"]), _ptr(self.h), H, _ptr(ss_in), n_in,
+                    _ptr(Lw["in_norm"]), c.eps, _ptr(Lw["b_qkv"]), _ptr(Lw["q_norm"]), _ptr(Lw["k_norm"]),
+                    _ptr(self.inv_freq), _ptr(self.cur_pos), _ptr(self.write_slot), self.S, _ptr(self.q),
+                    _ptr(self.kc[li]), _ptr(self.vc[li]), self.splits["qkv"], _ptr(self.dev_err),
                 ),
-                "qkv_rope_scatter",
+                "decode_qkv_gemm",
             )
             check(
                 L.kvbp_decode_attn_score(

@@ -154,3 +154,65 @@ def test_bad_split_count_is_rejected():
         rc = L.kvbp_decode_gemm(torch.cuda.current_stream().cuda_stream, 0, 1, 128, 256, t.data_ptr(), t.data_ptr(),
                                 256, None, 0, None, 1e-6, o.data_ptr(), 128, None, sp, None)
         assert rc != 0
+
+
+@pytest.mark.parametrize("Hq,Hkv,K,M,splits,bias,qk_norm", [(28, 4, 3584, 16, 7, True, False),
+                                                             (16, 8, 1024, 5, 3, False, True),
+                                                             (8, 2, 512, 32, 1, True, True)])
+def test_fused_qkv_matches_gemm_plus_rope_scatter(Hq, Hkv, K, M, splits, bias, qk_norm):
+    """kvbp_decode_qkv_gemm == kvbp_decode_gemm (plain, norm prologue) followed by
+    kvbp_qkv_rope_scatter on the same inputs."""
+    from kvcacheboundaryprotection_b200.engine import inv_freq_table
+
+    g = torch.Generator(device="cuda").manual_seed(Hq + K)
+    D, S = 128, 40
+    N = (Hq + 2 * Hkv) * D
+    W = (torch.randn(N, K, generator=g, device="cuda") * 0.03).to(torch.bfloat16)
+    Wp = pack_weight(W)
+    h = torch.randn(M, K, generator=g, device="cuda").to(torch.bfloat16)
+    nw = (1 + 0.1 * torch.randn(K, generator=g, device="cuda")).to(torch.bfloat16)
+    ss = torch.zeros(1, 32, device="cuda")
+    ss[0, :M] = (h.float() ** 2).sum(1)
+    b = (0.1 * torch.randn(N, generator=g, device="cuda")).to(torch.bfloat16) if bias else None
+    qn = (1 + 0.1 * torch.randn(D, generator=g, device="cuda")).to(torch.bfloat16) if qk_norm else None
+    kn = (1 + 0.1 * torch.randn(D, generator=g, device="cuda")).to(torch.bfloat16) if qk_norm else None
+    inv = torch.from_numpy(inv_freq_table(D, 1e6)).cuda()
+    pos = torch.randint(0, 5000, (M,), generator=g, device="cuda", dtype=torch.int32)
+    ws = torch.randperm(S, generator=g, device="cuda")[:M].to(torch.int32) if M <= S else None
+    if ws is None:
+        ws = (torch.arange(M, device="cuda", dtype=torch.int32) % S)
+    ws[0] = -1  # an evicted position: nothing stored
+    kc0 = torch.randn(M, Hkv, S, D, generator=g, device="cuda").to(torch.bfloat16)
+    vc0 = torch.randn(M, Hkv, S, D, generator=g, device="cuda").to(torch.bfloat16)
+    L = capi.lib()
+    st = torch.cuda.current_stream().cuda_stream
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    P = lambda t: None if t is None else t.data_ptr()  # noqa: E731
+    # reference path: plain GEMM, then the standalone epilogue kernel
+    qkv = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    q1 = torch.zeros(M, Hq, D, dtype=torch.bfloat16, device="cuda")
+    kc1, vc1 = kc0.clone(), vc0.clone()
+    capi.check(L.kvbp_decode_gemm(st, 0, M, N, K, Wp.data_ptr(), h.data_ptr(), K, ss.data_ptr(), 1, nw.data_ptr(),
+                                  1e-6, qkv.data_ptr(), N, None, splits, err.data_ptr()), "gemm")
+    capi.check(L.kvbp_qkv_rope_scatter(st, M, 1, Hq, Hkv, D, S, qkv.data_ptr(), N, P(b), P(qn), P(kn), 1e-6,
+                                       inv.data_ptr(), pos.data_ptr(), ws.data_ptr(), q1.data_ptr(), kc1.data_ptr(),
+                                       vc1.data_ptr(), err.data_ptr()), "rope")
+    q2 = torch.zeros_like(q1)
+    kc2, vc2 = kc0.clone(), vc0.clone()
+    capi.check(L.kvbp_decode_qkv_gemm(st, M, Hq, Hkv, K, Wp.data_ptr(), h.data_ptr(), K, ss.data_ptr(), 1,
+                                      nw.data_ptr(), 1e-6, P(b), P(qn), P(kn), inv.data_ptr(), pos.data_ptr(),
+                                      ws.data_ptr(), S, q2.data_ptr(), kc2.data_ptr(), vc2.data_ptr(), splits,
+                                      err.data_ptr()), "qkv_gemm")
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    if not qk_norm:
+        assert torch.equal(q1, q2) and torch.equal(kc1, kc2) and torch.equal(vc1, vc2)
+    else:  # the head norm sums in another order: rare one-ulp differences
+        for a_, b_ in ((q1, q2), (kc1, kc2), (vc1, vc2)):
+            assert (a_ == b_).float().mean().item() >= 0.99
+            assert ((a_.float() - b_.float()).abs() <= 2.0**-7 * a_.float().abs() + 1e-6).all()
+    # untouched slots keep their contents; the evicted row stored nothing
+    mask = torch.ones(M, S, dtype=torch.bool, device="cuda")
+    rows = torch.arange(M, device="cuda")
+    mask[rows[ws >= 0], ws[ws >= 0].long()] = False
+    assert torch.equal(kc2.permute(0, 2, 1, 3)[mask], kc0.permute(0, 2, 1, 3)[mask])
