@@ -365,7 +365,7 @@ def run_microbench(cap_list=(256, 1024, 4096), policies=("lru", "attention-mass"
                     s = torch.cuda.current_stream().cuda_stream
                     check(L.kvbp_append_evict(s, C_.byref(st["state"]), C_.byref(cfg), st["seq_step"].data_ptr(), st["next_pos"].data_ptr(), st["cur_pos"].data_ptr(), st["write_slot"].data_ptr(), None, None, 0, st["evlog"].data_ptr(), st["evcount"].data_ptr(), st["evcap"], None, err.data_ptr()), "append")
                     check(L.kvbp_qkv_rope_scatter(s, B, 1, Hq, Hkv, D, S, qkv.data_ptr(), (Hq + 2 * Hkv) * D, None, None, None, 1e-6, inv.data_ptr(), st["cur_pos"].data_ptr(), st["write_slot"].data_ptr(), q.data_ptr(), kc.data_ptr(), vc.data_ptr(), err.data_ptr()), "qkv")
-                    check(L.kvbp_decode_attn_score(s, B, Hq, Hkv, D, S, q.data_ptr(), kc.data_ptr(), vc.data_ptr(), st["slot_pos"].data_ptr(), attn_out.data_ptr(), st["step_score"].data_ptr(), err.data_ptr()), "attn")
+                    check(L.kvbp_decode_attn_score(s, B, Hq, Hkv, D, S, q.data_ptr(), kc.data_ptr(), vc.data_ptr(), st["slot_pos"].data_ptr(), st["write_slot"].data_ptr(), attn_out.data_ptr(), st["step_score"].data_ptr(), err.data_ptr()), "attn")
                     check(L.kvbp_score_update(s, C_.byref(st["state"]), st["seq_step"].data_ptr(), st["step_score"].data_ptr(), err.data_ptr()), "score")
 
                 for _ in range(3):
@@ -393,7 +393,7 @@ def run_microbench(cap_list=(256, 1024, 4096), policies=("lru", "attention-mass"
                     flush.sum()
                     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                     e0.record()
-                    check(L.kvbp_decode_attn_score(s_, B, Hq, Hkv, D, S, q.data_ptr(), kc.data_ptr(), vc.data_ptr(), st["slot_pos"].data_ptr(), attn_out.data_ptr(), st["step_score"].data_ptr(), err.data_ptr()), "attn")
+                    check(L.kvbp_decode_attn_score(s_, B, Hq, Hkv, D, S, q.data_ptr(), kc.data_ptr(), vc.data_ptr(), st["slot_pos"].data_ptr(), st["write_slot"].data_ptr(), attn_out.data_ptr(), st["step_score"].data_ptr(), err.data_ptr()), "attn")
                     e1.record()
                     torch.cuda.synchronize()
                     attn_only += e0.elapsed_time(e1)

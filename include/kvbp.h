@@ -99,10 +99,15 @@ void kvbp_protection_sizes(int32_t capacity, double prefix_frac, double suffix_f
  * reduction (max over heads :1345, over layers :1670-1673).
  * q [B][Hq][128] bf16; kcache/vcache [B][Hkv][S][128] bf16 (16-byte aligned);
  * slot_pos [B][S]; out [B][Hq][128] bf16; step_score [B][S] float (non-negative,
- * updated with max(existing, max over this layer's heads of p)).  Hq/Hkv <= 8. */
+ * updated with max(existing, max over this layer's heads of p)).  Hq/Hkv <= 8.
+ * write_slot [B] may be NULL.  When given, it names the one cache slot per sequence
+ * (< 0: none) that the kvbp kernels immediately before this call on the stream write
+ * this step (kvbp_decode_qkv_gemm / kvbp_qkv_rope_scatter with one row per sequence);
+ * the kernel then starts reading the other rows before those kernels finish.  Every
+ * row such a kernel writes must be listed. */
 int kvbp_decode_attn_score(kvbp_stream_t stream, int32_t B, int32_t Hq, int32_t Hkv, int32_t head_dim, int32_t S,
-                           const void* q, const void* kcache, const void* vcache, const int32_t* slot_pos, void* out,
-                           float* step_score, int32_t* dev_err);
+                           const void* q, const void* kcache, const void* vcache, const int32_t* slot_pos,
+                           const int32_t* write_slot, void* out, float* step_score, int32_t* dev_err);
 
 /* K4 -- QKV epilogue + scatter of the new K/V into its slot.  Replaces the bias add
  * (jax_inference.py:953-956), q/k RMSNorm (:975-978), RoPE (:621-637,1000-1001) and the

@@ -78,7 +78,7 @@ SIGNATURES = {
     "kvbp_last_error": (C.c_char_p, []),
     "kvbp_policy_id": (C.c_int, [C.c_char_p]),
     "kvbp_protection_sizes": (None, [I32, F64, F64, C.POINTER(C.c_int32), C.POINTER(C.c_int32)]),
-    "kvbp_decode_attn_score": (C.c_int, [P, I32, I32, I32, I32, I32, P, P, P, P, P, P, P]),
+    "kvbp_decode_attn_score": (C.c_int, [P, I32, I32, I32, I32, I32, P, P, P, P, P, P, P, P]),
     "kvbp_qkv_rope_scatter": (
         C.c_int,
         [P, I32, I32, I32, I32, I32, I32, P, I32, P, P, P, F32, P, P, P, P, P, P, P],
@@ -110,7 +110,7 @@ SIGNATURES = {
     "kvbp_unpack_weight": (C.c_int, [P, I32, I32, P, P]),
 }
 EXTRA_SIGNATURES = {
-    "kvbp_decode_attn_score_cs": (C.c_int, [P, I32, I32, I32, I32, I32, P, P, P, P, P, P, P, I32]),
+    "kvbp_decode_attn_score_cs": (C.c_int, [P, I32, I32, I32, I32, I32, P, P, P, P, P, P, P, P, I32]),
 }
 
 _LIB: Optional[C.CDLL] = None

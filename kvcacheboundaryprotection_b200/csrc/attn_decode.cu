@@ -30,6 +30,14 @@
 // of bf16 output, and turns its stored logits into the exact probabilities
 // p = exp(s - M) / L for the per-slot score (max over heads -> atomicMax).  The K/V
 // cache is read exactly once, in a single stream.
+//
+// Early streaming: the kernel is launched with programmatic dependent launch, so its
+// CTAs can be resident while the q/k/v kernel before it finishes.  When the caller
+// passes write_slot (the one slot per sequence that the preceding kernels store this
+// step's K/V into), the producer issues the first stages before waiting on that kernel
+// -- every other cache row is unchanged since the previous step -- and the warp that
+// owns the written row re-reads it from global memory into the staged tile after the
+// wait.
 #include "common.cuh"
 #include "kvbp_internal.h"
 
@@ -51,7 +59,7 @@ constexpr int kMaxCluster = 8;
 
 struct AttnSmem {
   // byte offsets from the 1024-aligned base
-  int logits, escr, spos, orecv, srecv, wstat, bars, total;
+  int logits, escr, spos, orecv, srecv, wstat, fin, bars, total;
 };
 
 __host__ __device__ inline int align_up(int x, int a) { return (x + a - 1) / a * a; }
@@ -65,7 +73,8 @@ __host__ __device__ inline AttnSmem attn_smem_layout(int nloc_tiles) {
   L.orecv = align_up(L.spos + nloc * 4, 16);  // [CS][per] received O slices
   L.srecv = L.orecv + (8 * kD + kMaxCluster) * 4;  // [CS][16] received (max, sum)
   L.wstat = L.srecv + kMaxCluster * 16 * 4;  // [warp][16] per-warp (max, sum) + CTA (max, sum) + flags
-  L.bars = align_up(L.wstat + (kConsumerWarps + 2) * 16 * 4, 8);
+  L.fin = align_up(L.wstat + (kConsumerWarps + 2) * 16 * 4, 16);  // final M[8], L[8], scale[cluster][8]
+  L.bars = align_up(L.fin + (16 + kMaxCluster * 8) * 4, 8);
   L.total = L.bars + (2 * kStages + 1) * 8;
   // the [warp][8][128] partial outputs alias the ring at the end
   return L;
@@ -73,7 +82,10 @@ __host__ __device__ inline AttnSmem attn_smem_layout(int nloc_tiles) {
 
 struct AttnArgs {
   const __nv_bfloat16* q;  // [B, Hq, D]
+  const __nv_bfloat16* kc;  // [B, Hkv, S, D] (row re-reads after the wait)
+  const __nv_bfloat16* vc;
   const int* slot_pos;     // [B, S]; < 0 = free slot
+  const int* write_slot;   // [B] or null: see "Early streaming"
   __nv_bfloat16* out;      // [B, Hq, D]
   float* step_score;       // [B, S], non-negative; atomicMax target
   int* err;
@@ -134,6 +146,7 @@ __global__ void __launch_bounds__(kThreads) decode_attn_score_kernel(const __gri
     tma_load_3d(dst + kHalfBytes + kBoxBytes, &vmap, &full[st], 64, y, pair);
   };
   const int n_first = nt < kStages ? nt : kStages;
+  const bool early = p.write_slot != nullptr;
   if (tid == kConsumers) {
     prefetch_tmap(&kmap);
     prefetch_tmap(&vmap);
@@ -144,11 +157,14 @@ __global__ void __launch_bounds__(kThreads) decode_attn_score_kernel(const __gri
     mbar_init(xbar, 1);
     *bad_flag = 0;
     fence_barrier_init();
+    if (early) {  // all rows but write_slot's are final: stream before the wait
+      for (int u = 0; u < n_first; ++u) issue(u);
+      *n_issued = n_first;
+    }
   }
   if (!KVBP_PDL_LATE) pdl_launch_dependents();
   pdl_wait();  // q, slot positions and the new K/V row come from earlier kernels
-  if (tid == kConsumers) {
-    // start streaming at once: the first stages depend on nothing but this CTA
+  if (tid == kConsumers && !early) {
     for (int u = 0; u < n_first; ++u) issue(u);
     *n_issued = n_first;
   }
@@ -212,6 +228,7 @@ __global__ void __launch_bounds__(kThreads) decode_attn_score_kernel(const __gri
   for (int m = 0; m < 8; ++m) oacc[m][0] = oacc[m][1] = oacc[m][2] = oacc[m][3] = 0.f;
   float* ew = escr + warp * 16 * 8;
   const int r0 = warp * 16;
+  const int wslot = early ? p.write_slot[b] : -1;  // row of this step's K/V (read after the wait)
 
   for (int u = 0; u < nt; ++u) {
     const int st = u % kStages;
@@ -222,6 +239,21 @@ __global__ void __launch_bounds__(kThreads) decode_attn_score_kernel(const __gri
       ok_tile = false;
     }
     ok_tile = __all_sync(0xffffffffu, ok_tile);  // warp-uniform: the tile's mma/ldmatrix are warp-wide
+    if (ok_tile && u < n_first && wslot >= 0 && wslot < S) {
+      // a tile staged before the wait may hold a stale copy of this step's row: the warp
+      // that owns the row (rows r0..r0+15 of the tile) reloads it, K by lanes 0-15 and V by
+      // lanes 16-31, one 16-byte chunk each, at the 128-byte-swizzled position
+      const int lr = wslot - (t0 + u) * kTile;
+      if (lr >= r0 && lr < r0 + 16) {
+        const int half = lane >> 4, ch = lane & 15, box = ch >> 3, c = ch & 7;
+        const __nv_bfloat16* src = (half ? p.vc : p.kc) + (static_cast<size_t>(pair) * S + wslot) * kD + ch * 8;
+        const uint4 v = __ldcg(reinterpret_cast<const uint4*>(src));
+        uint8_t* dst = ring + st * kStageBytes + half * kHalfBytes + box * kBoxBytes + lr * 128 + ((c ^ (lr & 7)) << 4);
+        *reinterpret_cast<uint4*>(dst) = v;
+        fence_proxy_async_smem();  // the stage is refilled by TMA later
+        __syncwarp();
+      }
+    }
     if (ok_tile) {
       const uint8_t* kt = ring + st * kStageBytes;
       const uint8_t* vt = kt + kHalfBytes;
@@ -358,32 +390,54 @@ __global__ void __launch_bounds__(kThreads) decode_attn_score_kernel(const __gri
     const uint32_t rdst = mapa_u32(smem_u32(srecv + rank * 16), lane);
     for (int h = 0; h < 16; ++h) st_async_f32(rdst + 4 * h, cstat[h], rbar);
   }
-  for (int e = tid; e < G * kD; e += kConsumers) {
-    float acc = 0.f;
+  if (per % 4 == 0) {  // 16-byte pieces never straddle two CTAs' slices
+    for (int e = 4 * tid; e < G * kD; e += 4 * kConsumers) {
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-    for (int w = 0; w < kConsumerWarps; ++w) acc += opart[w * 8 * kD + e];
-    const int r = e / per;
-    st_async_f32(mapa_u32(smem_u32(orecv + rank * per + (e - r * per)), r), acc, mapa_u32(smem_u32(xbar), r));
+      for (int w = 0; w < kConsumerWarps; ++w) {
+        const float4 v = *reinterpret_cast<const float4*>(&opart[w * 8 * kD + e]);
+        acc.x += v.x;
+        acc.y += v.y;
+        acc.z += v.z;
+        acc.w += v.w;
+      }
+      const int r = e / per;
+      st_async_v4(mapa_u32(smem_u32(orecv + rank * per + (e - r * per)), r), acc, mapa_u32(smem_u32(xbar), r));
+    }
+  } else {
+    for (int e = tid; e < G * kD; e += kConsumers) {
+      float acc = 0.f;
+#pragma unroll
+      for (int w = 0; w < kConsumerWarps; ++w) acc += opart[w * 8 * kD + e];
+      const int r = e / per;
+      st_async_f32(mapa_u32(smem_u32(orecv + rank * per + (e - r * per)), r), acc, mapa_u32(smem_u32(xbar), r));
+    }
   }
   if (!mbar_wait_cluster_bounded(xbar, 0)) {
     set_err(p.err, kErrWaitTimeout);
     atomicExch(bad_flag, 1);
   }
   // ---- final max M and sum L per head (identical in every CTA of the cluster) ------
-  float Mh[G], iLh[G];
-#pragma unroll
-  for (int h = 0; h < G; ++h) {
+  // thread h of the first warp forms head h's M, L and each CTA's rescale exp(m_c - M)
+  float* finM = reinterpret_cast<float*>(base + L.fin);
+  float* finL = finM + 8;
+  float* fscale = finL + 8;  // [c][8]
+  if (tid < G) {
+    const int h = tid;
     float M = NEG_INF;
     for (int c = 0; c < CS; ++c) M = fmaxf(M, srecv[c * 16 + h]);
     float Ls = 0.f;
     for (int c = 0; c < CS; ++c) {
       const float mc = srecv[c * 16 + h];
-      if (mc != NEG_INF) Ls += srecv[c * 16 + 8 + h] * expf(mc - M);
+      const float f = (mc != NEG_INF) ? expf(mc - M) : 0.f;
+      fscale[c * 8 + h] = f;
+      if (mc != NEG_INF) Ls += srecv[c * 16 + 8 + h] * f;
     }
-    Mh[h] = M;
-    iLh[h] = Ls;
-    if (tid == 0 && rank == 0 && !(Ls > 0.f)) set_err(p.err, kErrNoValidSlot);
+    finM[h] = M;
+    finL[h] = Ls;
+    if (rank == 0 && !(Ls > 0.f)) set_err(p.err, kErrNoValidSlot);
   }
+  named_bar(1, kConsumers);
   // output slice
   {
     const int e0 = rank * per;
@@ -392,14 +446,20 @@ __global__ void __launch_bounds__(kThreads) decode_attn_score_kernel(const __gri
       const int h = (e0 + j) / kD;
       float acc = 0.f;
       for (int c = 0; c < CS; ++c) {
-        const float mc = srecv[c * 16 + h];
-        if (mc != NEG_INF) acc += orecv[c * per + j] * expf(mc - Mh[h]);
+        if (srecv[c * 16 + h] != NEG_INF) acc += orecv[c * per + j] * fscale[c * 8 + h];
       }
-      orow[e0 + j] = __float2bfloat16_rn(iLh[h] > 0.f ? acc / iLh[h] : 0.f);
+      const float Lh = finL[h];
+      orow[e0 + j] = __float2bfloat16_rn(Lh > 0.f ? acc / Lh : 0.f);
     }
   }
   // per-slot eviction score: max over the group's heads of p = exp(s - M) / L
   if (!(*reinterpret_cast<volatile int*>(bad_flag))) {
+    float Mh[G], iLh[G];
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+      Mh[h] = finM[h];
+      iLh[h] = finL[h];
+    }
     float* sscore = p.step_score + static_cast<size_t>(b) * S;
     for (int i = tid; i < nloc; i += kConsumers) {
       if (spos_s[i] < 0) continue;
@@ -482,8 +542,8 @@ static cudaError_t launch_g(cudaStream_t stream, const CUtensorMap& km, const CU
 }
 
 int decode_attn_score(cudaStream_t stream, int B, int Hq, int Hkv, int D, int S, const void* q, const void* kcache,
-                      const void* vcache, const int* slot_pos, void* out, float* step_score, int* err,
-                      int cluster_override) {
+                      const void* vcache, const int* slot_pos, const int* write_slot, void* out, float* step_score,
+                      int* err, int cluster_override) {
   if (!q || !kcache || !vcache || !slot_pos || !out || !step_score)
     return fail(kStatusArg, "decode_attn_score: null pointer");
   if (D != kD) return fail(kStatusUnsupported, "decode_attn_score: head_dim %d unsupported (only 128)", D);
@@ -521,7 +581,10 @@ int decode_attn_score(cudaStream_t stream, int B, int Hq, int Hkv, int D, int S,
 
   AttnArgs a;
   a.q = static_cast<const __nv_bfloat16*>(q);
+  a.kc = static_cast<const __nv_bfloat16*>(kcache);
+  a.vc = static_cast<const __nv_bfloat16*>(vcache);
   a.slot_pos = slot_pos;
+  a.write_slot = write_slot;
   a.out = static_cast<__nv_bfloat16*>(out);
   a.step_score = step_score;
   a.err = err;
@@ -559,17 +622,18 @@ int decode_attn_score(cudaStream_t stream, int B, int Hq, int Hkv, int D, int S,
 
 extern "C" int kvbp_decode_attn_score(kvbp_stream_t stream, int32_t B, int32_t Hq, int32_t Hkv, int32_t head_dim,
                                       int32_t S, const void* q, const void* kcache, const void* vcache,
-                                      const int32_t* slot_pos, void* out, float* step_score, int32_t* dev_err) {
+                                      const int32_t* slot_pos, const int32_t* write_slot, void* out,
+                                      float* step_score, int32_t* dev_err) {
   return kvbp::decode_attn_score(reinterpret_cast<cudaStream_t>(stream), B, Hq, Hkv, head_dim, S, q, kcache, vcache,
-                                 slot_pos, out, step_score, dev_err, 0);
+                                 slot_pos, write_slot, out, step_score, dev_err, 0);
 }
 
 // Same as kvbp_decode_attn_score with an explicit cluster size (CTAs per sequence and
 // kv head, 1..8); 0 selects automatically.  Used by tests and tuning sweeps.
 extern "C" int kvbp_decode_attn_score_cs(kvbp_stream_t stream, int32_t B, int32_t Hq, int32_t Hkv, int32_t head_dim,
                                          int32_t S, const void* q, const void* kcache, const void* vcache,
-                                         const int32_t* slot_pos, void* out, float* step_score, int32_t* dev_err,
-                                         int32_t cluster) {
+                                         const int32_t* slot_pos, const int32_t* write_slot, void* out,
+                                         float* step_score, int32_t* dev_err, int32_t cluster) {
   return kvbp::decode_attn_score(reinterpret_cast<cudaStream_t>(stream), B, Hq, Hkv, head_dim, S, q, kcache, vcache,
-                                 slot_pos, out, step_score, dev_err, cluster);
+                                 slot_pos, write_slot, out, step_score, dev_err, cluster);
 }

@@ -165,6 +165,19 @@ __device__ __forceinline__ void st_async_f32(uint32_t remote_addr, float v, uint
                : "memory");
 }
 
+// Orders this thread's generic-proxy shared-memory writes before later async-proxy
+// (TMA) accesses of the same memory.
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// Four floats into the shared memory of cluster CTA (remote_addr from mapa), counted
+// on that CTA's mbarrier (remote_bar) as 16 transaction bytes.
+__device__ __forceinline__ void st_async_v4(uint32_t remote_addr, float4 v, uint32_t remote_bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
+                   remote_addr),
+               "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"(remote_bar)
+               : "memory");
+}
+
 // One float / two floats from shared memory of the cluster CTA that a mapa address
 // points into.
 __device__ __forceinline__ float ld_dsmem_f32(uint32_t cluster_addr) {

@@ -49,8 +49,8 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
 }
 
 int decode_attn_score(cudaStream_t stream, int B, int Hq, int Hkv, int D, int S, const void* q, const void* kcache,
-                      const void* vcache, const int* slot_pos, void* out, float* step_score, int* err,
-                      int cluster_override);
+                      const void* vcache, const int* slot_pos, const int* write_slot, void* out, float* step_score,
+                      int* err, int cluster_override);
 
 // Policy identifiers understood by the eviction kernels.
 enum PolicyId : int {

@@ -516,7 +516,8 @@ class CappedKVEngine:
             check(
                 L.kvbp_decode_attn_score(
                     st, B, c.n_heads, c.n_kv_heads, D, self.S, _ptr(self.q), _ptr(self.kc[li]), _ptr(self.vc[li]),
-                    _ptr(self.slot_pos), _ptr(self.attn_out), _ptr(self.step_score), _ptr(self.dev_err),
+                    _ptr(self.slot_pos), _ptr(self.write_slot), _ptr(self.attn_out), _ptr(self.step_score),
+                    _ptr(self.dev_err),
                 ),
                 "decode_attn_score",
             )
@@ -546,7 +547,8 @@ class CappedKVEngine:
             check(
                 L.kvbp_decode_attn_score(
                     st, B, c.n_heads, c.n_kv_heads, D, self.S, _ptr(self.q), _ptr(self.kc[li]), _ptr(self.vc[li]),
-                    _ptr(self.slot_pos), _ptr(self.attn_out), _ptr(self.step_score), _ptr(self.dev_err),
+                    _ptr(self.slot_pos), _ptr(self.write_slot), _ptr(self.attn_out), _ptr(self.step_score),
+                    _ptr(self.dev_err),
                 ),
                 "decode_attn_score",
             )

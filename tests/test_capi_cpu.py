@@ -53,11 +53,11 @@ def test_protection_sizes_match_python(L, cap, pf, sf, expect):
 
 def test_host_validation_rejects_bad_arguments(L):
     # null pointers are rejected on the host before any CUDA call
-    st = L.kvbp_decode_attn_score(None, 1, 4, 1, 128, 64, None, None, None, None, None, None, None)
+    st = L.kvbp_decode_attn_score(None, 1, 4, 1, 128, 64, None, None, None, None, None, None, None, None)
     assert st == 1 and b"null" in L.kvbp_last_error()
-    st = L.kvbp_decode_attn_score(None, 1, 4, 1, 64, 64, 1, 1, 1, 1, 1, 1, None)
+    st = L.kvbp_decode_attn_score(None, 1, 4, 1, 64, 64, 1, 1, 1, 1, None, 1, 1, None)
     assert st == 2  # head_dim 64 unsupported
-    st = L.kvbp_decode_attn_score(None, 1, 18, 2, 128, 64, 16, 16, 16, 16, 16, 16, None)
+    st = L.kvbp_decode_attn_score(None, 1, 18, 2, 128, 64, 16, 16, 16, 16, None, 16, 16, None)
     assert st == 2  # group of 9 heads unsupported
     assert L.kvbp_argmax(None, 1, 100, 50, 16, 16) == 1  # ld < vocab
     cfg = capi.EvictCfg(0, 8, 0, 1, 25, 25, 1)

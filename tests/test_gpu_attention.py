@@ -52,8 +52,8 @@ def run_kernel(q, kc, vc, slot_pos, score_init=None, cluster=0):
     score = score_init.clone() if score_init is not None else torch.zeros(B, S, dtype=torch.float32, device=q.device)
     err = torch.zeros(1, dtype=torch.int32, device=q.device)
     st = torch.cuda.current_stream().cuda_stream
-    args = (st, B, Hq, Hkv, D, S, q.data_ptr(), kc.data_ptr(), vc.data_ptr(), slot_pos.data_ptr(), out.data_ptr(),
-            score.data_ptr(), err.data_ptr())
+    args = (st, B, Hq, Hkv, D, S, q.data_ptr(), kc.data_ptr(), vc.data_ptr(), slot_pos.data_ptr(), None,
+            out.data_ptr(), score.data_ptr(), err.data_ptr())
     if cluster:
         capi.check(L.kvbp_decode_attn_score_cs(*args, cluster), "attn")
     else:
@@ -138,3 +138,48 @@ def test_large_batch_microbench_shape_runs_clean():
     ref_out, ref_score = torch_reference(q[:4], kc[:4], vc[:4], pos[:4])
     assert_close(out[:4], score[:4], ref_out, ref_score, pos[:4] >= 0)
     assert torch.isfinite(out).all()
+
+
+@pytest.mark.parametrize("cluster", [0, 1, 3])
+def test_early_streaming_with_write_slot_matches_plain(cluster):
+    """With write_slot the kernel stages its first tiles before the preceding K/V store
+    finishes and reloads the written row; the result must equal a call without it."""
+    from kvcacheboundaryprotection_b200.engine import inv_freq_table
+
+    g = torch.Generator(device="cuda").manual_seed(17)
+    B, Hq, Hkv, D, S = 4, 28, 4, 128, 1032
+    tiles = (S + 63) // 64
+    cs = cluster or 4
+    kc = torch.randn(B, Hkv, S, D, generator=g, device="cuda").to(torch.bfloat16)
+    vc = torch.randn(B, Hkv, S, D, generator=g, device="cuda").to(torch.bfloat16)
+    slot_pos = torch.arange(S, device="cuda", dtype=torch.int32).repeat(B, 1)
+    slot_pos[:, 1000:] = -1
+    t0_rank1 = (1 * tiles) // cs if cs > 1 else 1
+    ws = torch.tensor([3, t0_rank1 * 64 + 5, 999, -1], dtype=torch.int32, device="cuda")
+    qkv = torch.randn(B, (Hq + 2 * Hkv) * D, generator=g, device="cuda").to(torch.bfloat16)
+    pos = torch.tensor([7, 900, 4000, 12], dtype=torch.int32, device="cuda")
+    inv = torch.from_numpy(inv_freq_table(D, 1e6)).cuda()
+    q = torch.empty(B, Hq, D, dtype=torch.bfloat16, device="cuda")
+    L = capi.lib()
+    st = torch.cuda.current_stream().cuda_stream
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    outs = []
+    for use_ws in (True, False):
+        kc_i, vc_i = kc.clone(), vc.clone()
+        out = torch.zeros(B, Hq, D, dtype=torch.bfloat16, device="cuda")
+        score = torch.zeros(B, S, dtype=torch.float32, device="cuda")
+        torch.cuda.synchronize()
+        capi.check(L.kvbp_qkv_rope_scatter(st, B, 1, Hq, Hkv, D, S, qkv.data_ptr(), (Hq + 2 * Hkv) * D, None, None,
+                                           None, 1e-6, inv.data_ptr(), pos.data_ptr(), ws.data_ptr(), q.data_ptr(),
+                                           kc_i.data_ptr(), vc_i.data_ptr(), err.data_ptr()), "rope")
+        capi.check(L.kvbp_decode_attn_score_cs(st, B, Hq, Hkv, D, S, q.data_ptr(), kc_i.data_ptr(), vc_i.data_ptr(),
+                                               slot_pos.data_ptr(), ws.data_ptr() if use_ws else None,
+                                               out.data_ptr(), score.data_ptr(), err.data_ptr(), cluster), "attn")
+        torch.cuda.synchronize()
+        assert int(err.item()) == 0
+        outs.append((out, score, kc_i))
+    assert torch.equal(outs[0][0], outs[1][0])
+    assert torch.equal(outs[0][1], outs[1][1])
+    # and the written rows really are part of the attention (the reference agrees)
+    ref_out, ref_score = torch_reference(q, outs[1][2], vc_i, slot_pos)
+    assert (outs[0][0].float() - ref_out).abs().max().item() <= 1.6e-2
