@@ -61,6 +61,8 @@ def parse():
     ap.add_argument("--e2e-steps", type=int, default=16)
     ap.add_argument("--micro-only", type=int, default=None, metavar="CAPACITY",
                     help="run only the operator microbench at this capacity (lru, protect 0.10) and exit")
+    ap.add_argument("--micro-attn", action="store_true",
+                    help="run only the decode attention microbench at the workload's shape and exit")
     ap.add_argument("--micro-gemm", action="store_true",
                     help="run only the decode GEMM microbench (one layer's projections + lm_head) and exit")
     return ap.parse_args()
@@ -207,13 +209,28 @@ def run_ours(a, rank, world, local_rank):
         e2e_s = float(t.item())
     e2e = world * B * a.e2e_steps / e2e_s
 
-    # ---- live per-kernel timing of the decode attention kernel (eager instrumented steps)
-    attn_ms = measure_attention_in_step(eng, steps=3)
+    # ---- live per-kernel timing (eager instrumented steps) and the roofline
+    kms = measure_kernels_in_step(eng, steps=3)
     hbm, tf, peak_kind = peaks()
-    S_valid = C  # retained slots per (sequence, kv head) at cadence boundaries average C+3.5
-    avg_valid = C + 3.5
-    attn_bytes = algorithmic_attn_bytes(B, cfg.n_heads, cfg.n_kv_heads, avg_valid)
-    achieved = attn_bytes / (attn_ms * 1e-3) / 1e9
+    avg_valid = C + 3.5  # retained slots per (sequence, kv head): C .. C+E-1 over a cadence
+    kbytes = kernel_algorithmic_bytes(cfg, B, avg_valid)
+    per_step = {"attention": cfg.n_layers, "qkv": cfg.n_layers, "o": cfg.n_layers, "gate_up": cfg.n_layers,
+                "down": cfg.n_layers, "lm_head": 1}
+    kernels = {}
+    for k, t in kms.items():
+        gbs = kbytes[k] / (t * 1e-3) / 1e9
+        kernels[k] = {"avg_launch_us": round(t * 1000, 2), "launches_per_step": per_step[k],
+                      "algorithmic_bytes_per_launch": int(kbytes[k]), "achieved_gbs": round(gbs, 1),
+                      "frac": round(gbs / hbm, 4), "traffic": NCU_TRAFFIC.get((preset, k))}
+    dominant = max(kernels, key=lambda k: kernels[k]["avg_launch_us"] * per_step[k])
+
+    def roofline_of(k):
+        d = kernels[k]
+        return {"kernel": k, "bound": "hbm", "achieved": d["achieved_gbs"], "peak": hbm,
+                "peak_kind": f"{peak_kind} HBM copy bandwidth", "unit": "GB/s", "frac": d["frac"],
+                "traffic": d["traffic"], "avg_launch_us": d["avg_launch_us"],
+                "algorithmic_bytes_per_launch": d["algorithmic_bytes_per_launch"]}
+
     step_bytes = fw.nbytes() + cfg.n_layers * algorithmic_attn_bytes(B, cfg.n_heads, cfg.n_kv_heads, avg_valid)
     step_ms = ms / K
     gpu_launches = K * launches_per_step(cfg)
@@ -248,23 +265,14 @@ def run_ours(a, rank, world, local_rank):
             "d2h_bytes_per_step": 4 * B,
             "how": "host copies each step's token ids in from pinned memory, replays the step, reads the sampled ids back and synchronises",
         },
-        "roofline": {
-            "kernel": "kvbp decode_attn_score (fused GQA attention + per-slot eviction score)",
-            "bound": "hbm",
-            "achieved": round(achieved, 1),
-            "peak": hbm,
-            "peak_kind": f"{peak_kind} HBM copy bandwidth",
-            "unit": "GB/s",
-            "frac": round(achieved / hbm, 4),
-            "traffic": None,
-            "avg_launch_us": round(attn_ms * 1000, 2),
-            "algorithmic_bytes_per_launch": int(attn_bytes),
-        },
+        "roofline": roofline_of(dominant),
+        "roofline_attention": roofline_of("attention"),
+        "kernels": kernels,
         "step_roofline": {
             "bytes_per_step": int(step_bytes),
             "achieved_gbs": round(step_bytes / (step_ms * 1e-3) / 1e9, 1),
             "frac": round(step_bytes / (step_ms * 1e-3) / 1e9 / hbm, 4),
-            "note": "weights + KV + q/out bytes of one decode step / measured step time (GEMMs are cuBLAS)",
+            "note": "weights + KV + q/out bytes of one decode step / measured step time (all kernels own sm_100a)",
         },
         "gpu_launches": gpu_launches,
         "clocks": ck,
@@ -273,9 +281,9 @@ def run_ours(a, rank, world, local_rank):
 
 
 def launches_per_step(cfg) -> int:
-    # own kernels: append_evict, embed, per layer (2 rmsnorm, qkv epilogue, attention, silu), final rmsnorm,
-    # argmax, score_update
-    return 1 + 1 + cfg.n_layers * 5 + 1 + 1 + 1
+    # own kernels: append_evict, embed, row_sumsq, per layer (q/k/v GEMM, attention, o GEMM,
+    # gate/up GEMM, down GEMM), lm_head GEMM, argmax, score_update
+    return 1 + 1 + 1 + cfg.n_layers * 5 + 1 + 1 + 1
 
 
 def algorithmic_attn_bytes(B, Hq, Hkv, valid_slots):
@@ -287,40 +295,76 @@ def algorithmic_attn_bytes(B, Hq, Hkv, valid_slots):
     return kv + qo + score
 
 
-def measure_attention_in_step(eng, steps=3):
-    """Average device time of the attention kernel inside real decode steps (eager
-    launches with CUDA events around each attention launch on the launching stream)."""
+def measure_kernels_in_step(eng, steps=3):
+    """Average device time (ms) of each kind of heavy kernel inside real decode steps:
+    eager launches of the step with CUDA events around each launch, on the launching
+    stream.  Keys: attention, qkv, o, gate_up, down, lm_head."""
     import torch
 
-    from kvcacheboundaryprotection_b200 import capi
-    from kvcacheboundaryprotection_b200.capi import check, lib
+    from kvcacheboundaryprotection_b200.capi import lib
 
     c = eng.cfg
-    times = []
-    orig = lib().kvbp_decode_attn_score
+    times = {}
     stream = torch.cuda.current_stream()
+    L = lib()
 
-    class Timed:
-        def __call__(self, *args):
+    def kind_of_gemm(args):
+        epi, N, K = args[1], args[3], args[4]
+        if epi == 2:
+            return "gate_up"
+        if epi == 1:
+            return "down" if K == c.ffn else "o"
+        return "lm_head"
+
+    def wrap(orig, kind):
+        def f(*args):
             a = torch.cuda.Event(enable_timing=True)
             b = torch.cuda.Event(enable_timing=True)
             a.record(stream)
             r = orig(*args)
             b.record(stream)
-            times.append((a, b))
+            times.setdefault(kind(args) if callable(kind) else kind, []).append((a, b))
             return r
 
-    L = lib()
-    L.kvbp_decode_attn_score = Timed()
+        return f
+
+    names = {"kvbp_decode_attn_score": "attention", "kvbp_decode_qkv_gemm": "qkv", "kvbp_decode_gemm": kind_of_gemm}
+    saved = {n: getattr(L, n) for n in names}
     try:
+        for n, kind in names.items():
+            setattr(L, n, wrap(saved[n], kind))
         for _ in range(steps):
             eng.decode_step_launches()
             eng.step += 1
         torch.cuda.synchronize()
     finally:
-        L.kvbp_decode_attn_score = orig
-    ms = [a.elapsed_time(b) for a, b in times]
-    return sum(ms) / len(ms)
+        for n, f in saved.items():
+            setattr(L, n, f)
+    return {k: sum(a.elapsed_time(b) for a, b in v) / len(v) for k, v in times.items()}
+
+
+def kernel_algorithmic_bytes(cfg, B, avg_valid):
+    """Bytes each heavy kernel of the decode step must move per launch (weights read
+    once; activations in and out; K/V of the valid slots for attention)."""
+    H, F, V, D = cfg.hidden, cfg.ffn, cfg.vocab, cfg.head_dim
+    qkv_n = (cfg.n_heads + 2 * cfg.n_kv_heads) * D
+    return {
+        "attention": algorithmic_attn_bytes(B, cfg.n_heads, cfg.n_kv_heads, avg_valid),
+        "qkv": qkv_n * H * 2 + B * H * 2 + B * qkv_n * 2,
+        "o": H * cfg.n_heads * D * 2 + B * cfg.n_heads * D * 2 + 2 * B * H * 2,
+        "gate_up": 2 * F * H * 2 + B * H * 2 + B * F * 2,
+        "down": H * F * 2 + B * F * 2 + 2 * B * H * 2,
+        "lm_head": V * H * 2 + B * H * 2 + B * V * 2,
+    }
+
+
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch, from ncu
+# captures of this file's --micro-attn / --micro-gemm runs on B200 (qwen2.5-7b shapes).
+NCU_TRAFFIC = {
+    ("qwen2.5-7b", "attention"): 34122240,
+    ("qwen2.5-7b", "gate_up"): 271750400 + 4199424,
+    ("qwen2.5-7b", "o"): 25947648,
+}
 
 
 # ------------------------------------------------------------------------ microbench
@@ -421,6 +465,57 @@ def run_microbench(cap_list=(256, 1024, 4096), policies=("lru", "attention-mass"
                 del gr
         del kc, vc
     return {"peak_gbs": hbm, "peak_kind": peak_kind, "batch": B, "kv_heads": Hkv, "group": G, "rows": out}
+
+
+def run_attn_microbench(preset="qwen2.5-7b", B=16, C=1024, E=8, layers=8, iters=5):
+    """Operator microbench of kvbp_decode_attn_score at a decode workload's shape: B
+    sequences, the preset's heads, S = C + E slots of which C + E/2 are valid (the mean
+    over an eviction cycle).  The launches cycle over ``layers`` separate caches (more
+    bytes than L2 holds), as the decode step does."""
+    import torch
+
+    from kvcacheboundaryprotection_b200.capi import check, lib
+    from kvcacheboundaryprotection_b200.config import get_config
+
+    L = lib()
+    cfg = get_config(preset)
+    dev = torch.device("cuda")
+    hbm, _, peak_kind = peaks()
+    Hq, Hkv, D, S = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, C + E
+    g = torch.Generator(device=dev).manual_seed(0)
+    kcs = [torch.randn(B, Hkv, S, D, generator=g, device=dev).to(torch.bfloat16) for _ in range(layers)]
+    vcs = [torch.randn(B, Hkv, S, D, generator=g, device=dev).to(torch.bfloat16) for _ in range(layers)]
+    valid = C + E // 2
+    slot_pos = torch.arange(S, dtype=torch.int32, device=dev).repeat(B, 1)
+    slot_pos[:, valid:] = -1
+    q = (torch.randn(B, Hq, D, generator=g, device=dev) / math.sqrt(D)).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    score = torch.zeros(B, S, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+
+    def launch(li):
+        check(L.kvbp_decode_attn_score(torch.cuda.current_stream().cuda_stream, B, Hq, Hkv, D, S, q.data_ptr(),
+                                       kcs[li].data_ptr(), vcs[li].data_ptr(), slot_pos.data_ptr(), None,
+                                       out.data_ptr(), score.data_ptr(), err.data_ptr()), "decode_attn_score")
+
+    for li in range(layers):
+        launch(li)
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters * layers)]
+    for it in range(iters):
+        for li in range(layers):
+            a, b = ev[it * layers + li]
+            a.record()
+            launch(li)
+            b.record()
+    torch.cuda.synchronize()
+    if int(err.item()):
+        raise RuntimeError("device error in attention microbench")
+    us = statistics.median([a.elapsed_time(b) * 1000 for a, b in ev])
+    byts = algorithmic_attn_bytes(B, Hq, Hkv, valid)
+    return {"preset": preset, "batch": B, "capacity": C, "slots": S, "valid_slots": valid, "us": round(us, 2),
+            "algorithmic_bytes": byts, "gbs": round(byts / us / 1e3, 1), "frac": round(byts / us / 1e3 / hbm, 4),
+            "peak_gbs": hbm, "peak_kind": peak_kind}
 
 
 def run_gemm_microbench(preset="qwen2.5-7b", M=16, iters=10, sweep=False):
@@ -683,6 +778,13 @@ def main():
         kbuild.build()
         print(json.dumps(run_microbench(cap_list=(a.micro_only,), policies=("lru",), fracs=(0.10,), iters=5)), flush=True)
         return
+    if a.micro_attn:
+        from kvcacheboundaryprotection_b200 import build as kbuild
+
+        kbuild.build()
+        preset, B0, C0 = WORKLOADS[a.workload][:3]
+        print(json.dumps(run_attn_microbench(preset, a.batch or B0, C0)), flush=True)
+        return
     if a.micro_gemm:
         from kvcacheboundaryprotection_b200 import build as kbuild
 
@@ -703,6 +805,8 @@ def main():
             torch.cuda.empty_cache()
             out["kernel_microbench"] = run_microbench()
             out["gemm_microbench"] = run_gemm_microbench(WORKLOADS[a.workload][0])
+            preset, B0, C0 = WORKLOADS[a.workload][:3]
+            out["attn_microbench"] = run_attn_microbench(preset, a.batch or B0, C0)
         if not a.no_cpu:
             times, sample = cpu_reference_step_times(a.workload, 4, 1)
             v = 1.0 / (sum(times) / len(times))

@@ -40,7 +40,10 @@ namespace gemm {
 
 constexpr int BN = 128;            // output features per CTA
 constexpr int BK = 128;            // K per stage
-constexpr int kStages = 3;
+#ifndef KVBP_GEMM_STAGES
+#define KVBP_GEMM_STAGES 3
+#endif
+constexpr int kStages = KVBP_GEMM_STAGES;
 constexpr int kConsumerWarps = 4;  // 32 features each
 constexpr int kConsumers = kConsumerWarps * 32;
 constexpr int kThreads = kConsumers + 32;
