@@ -205,6 +205,8 @@ int kvbp_row_sumsq(kvbp_stream_t stream, int32_t rows, int32_t hidden, const voi
  * Epilogue 1 (residual): out (the residual stream, ldo == N) = bf16(out + bf16(acc)) in
  *   place, and ss_out[N/128][32] receives each 128-column tile's per-row sum of squares of
  *   the new stream (the next norm's n_parts = N/128) -- jax_inference.py:1280,1325.
+ * Epilogue 3 (fp32): out is float [M][ldo] and receives the unrounded sums (a tensor-
+ *   parallel shard's partial of a row-parallel projection, before the allreduce).
  * Epilogue 2 (SwiGLU): W rows hold gate and up features interleaved in blocks of 64
  *   (rows 128t..128t+63 = gate features 64t.., rows 128t+64.. = the matching up features);
  *   out[M][N/2] = bf16(bf16(g * bf16(sigmoid(g))) * u) with g, u the bf16 GEMM outputs
@@ -239,6 +241,21 @@ int kvbp_unpack_weight(kvbp_stream_t stream, int32_t N, int32_t K, const void* s
 
 /* Greedy sampling: first index of the row maximum (numpy.argmax), kv_coupled_generator.py:344. */
 int kvbp_argmax(kvbp_stream_t stream, int32_t rows, int32_t vocab, int64_t ld, const void* logits, int32_t* out_ids);
+
+/* Greedy sampling over a vocabulary shard (tensor parallelism): keys_out[r] encodes the
+ * shard's (maximum value, index_offset + first index of it) so that the largest key over
+ * all shards (an allreduce-MAX on int64) is the global numpy.argmax; kvbp_key_to_token
+ * turns the reduced keys back into token ids. */
+int kvbp_argmax_key(kvbp_stream_t stream, int32_t rows, int32_t vocab, int64_t ld, const void* logits,
+                    int32_t index_offset, int64_t* keys_out);
+int kvbp_key_to_token(kvbp_stream_t stream, int32_t rows, const int64_t* keys, int32_t* tokens);
+
+/* Residual add of a reduced fp32 projection (tensor parallelism: after the allreduce of
+ * the o / down shards' partial sums): h = bf16(h + bf16(delta)) for rows <= 32, and
+ * ss_out[hidden/128][32] = each 128-column tile's per-row sum of squares of the new h
+ * (the next decode GEMM's norm statistics) -- jax_inference.py:1280,1325. */
+int kvbp_residual_add(kvbp_stream_t stream, int32_t rows, int32_t hidden, void* h, const float* delta,
+                      float* ss_out);
 
 #ifdef __cplusplus
 }

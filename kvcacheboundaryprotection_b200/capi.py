@@ -107,6 +107,9 @@ SIGNATURES = {
     "kvbp_decode_qkv_gemm": (C.c_int, [P, I32, I32, I32, I32, P, P, I32, P, I32, P, F32, P, P, P, P, P, P, I32, P, P,
                                        P, I32, P]),
     "kvbp_pack_weight": (C.c_int, [P, I32, I32, P, P]),
+    "kvbp_argmax_key": (C.c_int, [P, I32, I32, I64, P, I32, P]),
+    "kvbp_key_to_token": (C.c_int, [P, I32, P, P]),
+    "kvbp_residual_add": (C.c_int, [P, I32, I32, P, P, P]),
     "kvbp_unpack_weight": (C.c_int, [P, I32, I32, P, P]),
 }
 EXTRA_SIGNATURES = {

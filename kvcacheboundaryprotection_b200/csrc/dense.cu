@@ -183,7 +183,8 @@ __device__ __forceinline__ bool arg_better(float av, int ai, float bv, int bi) {
   return av > bv || (av == bv && ai < bi);
 }
 
-__global__ void argmax_kernel(const __nv_bfloat16* __restrict__ logits, long long ld, int V, int* __restrict__ out) {
+__global__ void argmax_kernel(const __nv_bfloat16* __restrict__ logits, long long ld, int V, int* __restrict__ out,
+                              long long* __restrict__ keys, int index_offset) {
   pdl_launch_dependents();
   pdl_wait();
   __shared__ float sv[32];
@@ -227,8 +228,50 @@ __global__ void argmax_kernel(const __nv_bfloat16* __restrict__ logits, long lon
       const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
       if (arg_better(ov, oi, bv, bi)) bv = ov, bi = oi;
     }
-    if (lane == 0) out[r] = bi;
+    if (lane == 0) {
+      if (out) out[r] = bi;
+      if (keys) {
+        // (value, lowest index) as one integer: the largest key over vocabulary shards is
+        // the global first maximum
+        uint32_t u = __float_as_uint(bv);
+        u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+        const uint32_t idx = static_cast<uint32_t>(bi + index_offset);
+        keys[r] = static_cast<long long>((static_cast<unsigned long long>(u) << 32) | (0xFFFFFFFFu - idx));
+      }
+    }
   }
+}
+
+__global__ void key_to_token_kernel(const long long* __restrict__ keys, int rows, int* __restrict__ tokens) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r < rows)
+    tokens[r] = static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(static_cast<unsigned long long>(keys[r]) & 0xFFFFFFFFull));
+}
+
+// ---- residual add of a reduced fp32 delta: h = bf16(h + bf16(delta)), plus the
+// per-128-column-tile sums of squares of the new h (the next norm prologue's input) ----
+__global__ void residual_add_kernel(__nv_bfloat16* __restrict__ h, const float* __restrict__ delta, int rows, int H,
+                                    float* __restrict__ ss_out) {
+  pdl_launch_dependents();
+  pdl_wait();
+  __shared__ float red[4][32];
+  const int tile = blockIdx.x, c = threadIdx.x, lane = c & 31, warp = c >> 5;
+  const int col = tile * 128 + c;
+  for (int r = 0; r < 32; ++r) {
+    float ss = 0.f;
+    if (r < rows) {
+      const size_t i = static_cast<size_t>(r) * H + col;
+      const float x = bf16r(__bfloat162float(h[i]) + bf16r(delta[i]));
+      h[i] = __float2bfloat16_rn(x);
+      ss = x * x;
+    }
+    ss = warp_sum(ss);
+    if (lane == 0) red[warp][r] = ss;
+  }
+  __syncthreads();
+  if (c < 32) ss_out[tile * 32 + c] = (c < rows) ? (red[0][c] + red[1][c]) + (red[2][c] + red[3][c]) : 0.f;
 }
 
 // ------------------------------------------------------------------------------------
@@ -296,8 +339,38 @@ int argmax_rows(cudaStream_t st, int rows, int V, long long ld, const void* logi
   if (rows <= 0 || V <= 0 || ld < V) return fail(kStatusArg, "argmax: bad size");
   if ((ld % 8) || (reinterpret_cast<uintptr_t>(logits) & 15))
     return fail(kStatusArg, "argmax: rows must be 16-byte aligned (ld % 8 == 0)");
-  const cudaError_t le = launch_pdl(argmax_kernel, dim3(rows), dim3(1024), 0, st, dim3(0), static_cast<const __nv_bfloat16*>(logits), ld, V, out);
+  const cudaError_t le = launch_pdl(argmax_kernel, dim3(rows), dim3(1024), 0, st, dim3(0),
+                                    static_cast<const __nv_bfloat16*>(logits), ld, V, out,
+                                    static_cast<long long*>(nullptr), 0);
   return check_launch("argmax", le);
+}
+
+int argmax_key(cudaStream_t st, int rows, int V, long long ld, const void* logits, int index_offset,
+               long long* keys) {
+  if (!logits || !keys) return fail(kStatusArg, "argmax_key: null pointer");
+  if (rows <= 0 || V <= 0 || ld < V || index_offset < 0) return fail(kStatusArg, "argmax_key: bad size");
+  if ((ld % 8) || (reinterpret_cast<uintptr_t>(logits) & 15))
+    return fail(kStatusArg, "argmax_key: rows must be 16-byte aligned (ld % 8 == 0)");
+  const cudaError_t le = launch_pdl(argmax_kernel, dim3(rows), dim3(1024), 0, st, dim3(0),
+                                    static_cast<const __nv_bfloat16*>(logits), ld, V, static_cast<int*>(nullptr),
+                                    keys, index_offset);
+  return check_launch("argmax_key", le);
+}
+
+int key_to_token(cudaStream_t st, int rows, const long long* keys, int* tokens) {
+  if (!keys || !tokens) return fail(kStatusArg, "key_to_token: null pointer");
+  if (rows <= 0) return fail(kStatusArg, "key_to_token: bad size");
+  const cudaError_t le = launch_pdl(key_to_token_kernel, dim3((rows + 127) / 128), dim3(128), 0, st, dim3(0), keys,
+                                    rows, tokens);
+  return check_launch("key_to_token", le);
+}
+
+int residual_add(cudaStream_t st, int rows, int H, void* h, const float* delta, float* ss_out) {
+  if (!h || !delta || !ss_out) return fail(kStatusArg, "residual_add: null pointer");
+  if (rows <= 0 || rows > 32 || H <= 0 || H % 128) return fail(kStatusArg, "residual_add: rows 1..32, hidden % 128");
+  const cudaError_t le = launch_pdl(residual_add_kernel, dim3(H / 128), dim3(128), 0, st, dim3(0),
+                                    static_cast<__nv_bfloat16*>(h), delta, rows, H, ss_out);
+  return check_launch("residual_add", le);
 }
 
 }  // namespace kvbp
@@ -329,6 +402,22 @@ int kvbp_silu_mul(kvbp_stream_t stream, int32_t rows, int32_t ffn, const void* g
 
 int kvbp_argmax(kvbp_stream_t stream, int32_t rows, int32_t vocab, int64_t ld, const void* logits, int32_t* out_ids) {
   return kvbp::argmax_rows(reinterpret_cast<cudaStream_t>(stream), rows, vocab, ld, logits, out_ids);
+}
+
+int kvbp_argmax_key(kvbp_stream_t stream, int32_t rows, int32_t vocab, int64_t ld, const void* logits,
+                    int32_t index_offset, int64_t* keys_out) {
+  return kvbp::argmax_key(reinterpret_cast<cudaStream_t>(stream), rows, vocab, ld, logits, index_offset,
+                          reinterpret_cast<long long*>(keys_out));
+}
+
+int kvbp_key_to_token(kvbp_stream_t stream, int32_t rows, const int64_t* keys, int32_t* tokens) {
+  return kvbp::key_to_token(reinterpret_cast<cudaStream_t>(stream), rows, reinterpret_cast<const long long*>(keys),
+                            tokens);
+}
+
+int kvbp_residual_add(kvbp_stream_t stream, int32_t rows, int32_t hidden, void* h, const float* delta,
+                      float* ss_out) {
+  return kvbp::residual_add(reinterpret_cast<cudaStream_t>(stream), rows, hidden, h, delta, ss_out);
 }
 
 int kvbp_qkv_rope_scatter(kvbp_stream_t stream, int32_t rows, int32_t rows_per_seq, int32_t Hq, int32_t Hkv,

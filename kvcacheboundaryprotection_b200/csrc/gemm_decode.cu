@@ -53,7 +53,7 @@ constexpr int kBlockElems = BN * BK;  // one packed block
 constexpr int kRedStride = BN + 8;    // fp32 partial tile row stride (fewer bank conflicts)
 constexpr int kMaxSplits = 16;
 
-enum Epi : int { kPlain = 0, kResid = 1, kSwiGLU = 2, kQKV = 3 };
+enum Epi : int { kPlain = 0, kResid = 1, kSwiGLU = 2, kF32 = 3, kQKV = 4 };
 
 struct Args {
   const __nv_bfloat16* w;  // packed [N/128][K/128][2][128][64] (swizzled 16-byte chunks)
@@ -63,7 +63,7 @@ struct Args {
   int n_parts;
   const __nv_bfloat16* norm_w;  // NORM: [K]
   float eps;
-  __nv_bfloat16* out;  // PLAIN/SWIGLU: [M][ldo]; RESID: h [M][ldo], updated in place
+  __nv_bfloat16* out;  // PLAIN/SWIGLU: [M][ldo]; RESID: h [M][ldo], updated in place; F32: float [M][ldo]
   int ldo;
   float* ss_out;  // RESID: [N / BN][32] partial sums of squares of the new h
   int M, N, K, splits;
@@ -296,6 +296,12 @@ __global__ void __launch_bounds__(kThreads) decode_gemm_kernel(const __grid_cons
         const float2 v = sum_pair(r, c);
         *reinterpret_cast<uint32_t*>(&a.out[static_cast<size_t>(r) * a.ldo + n0 + c]) = pack_bf16(v.x, v.y);
       }
+    } else if (EPI == kF32) {  // unrounded partial sums (a tensor-parallel shard's share)
+      float* of = reinterpret_cast<float*>(a.out);
+      for (int e = tid; e < nrows * (BN / 2); e += kConsumers) {
+        const int r = r_lo + e / (BN / 2), c = 2 * (e % (BN / 2));
+        *reinterpret_cast<float2*>(&of[static_cast<size_t>(r) * a.ldo + n0 + c]) = sum_pair(r, c);
+      }
     } else if (EPI == kResid) {
       // h = bf16(h + bf16(acc)); 64 threads (two warps) per row, so each warp holds half a row
       for (int e0 = 0; e0 < nrows * (BN / 2); e0 += kConsumers) {
@@ -459,8 +465,10 @@ int decode_gemm(cudaStream_t stream, int epi, int M, int N, int K, const void* w
                 const float* ss_parts, int n_parts, const void* norm_w, float eps, void* out, int ldo, float* ss_out,
                 int splits, int* err) {
   using namespace gemm;
-  if (epi < kPlain || epi > kSwiGLU) return fail(kStatusArg, "decode_gemm: unknown epilogue %d", epi);
+  if (epi < kPlain || epi > kF32) return fail(kStatusArg, "decode_gemm: unknown epilogue %d", epi);
   if (!out) return fail(kStatusArg, "decode_gemm: null pointer");
+  if (epi == kF32 && ((reinterpret_cast<uintptr_t>(out) & 7) || (ldo % 2)))
+    return fail(kStatusArg, "decode_gemm: fp32 output rows must be 8-byte aligned");
   if (epi == kResid && !ss_out) return fail(kStatusArg, "decode_gemm: residual epilogue needs ss_out");
   if (epi == kResid && N != ldo) return fail(kStatusArg, "decode_gemm: residual epilogue needs ldo == N");
   if ((reinterpret_cast<uintptr_t>(out) & 3) || (ldo % 2))
@@ -565,6 +573,10 @@ static int decode_gemm_launch(cudaStream_t stream, int epi, gemm::Args& a) {
   KVBP_GEMM_CASE(2, kResid, false)
   KVBP_GEMM_CASE(2, kSwiGLU, true)
   KVBP_GEMM_CASE(2, kSwiGLU, false)
+  KVBP_GEMM_CASE(1, kF32, false)
+  KVBP_GEMM_CASE(1, kF32, true)
+  KVBP_GEMM_CASE(2, kF32, false)
+  KVBP_GEMM_CASE(2, kF32, true)
   KVBP_GEMM_CASE(1, kQKV, true)
   KVBP_GEMM_CASE(1, kQKV, false)
   KVBP_GEMM_CASE(2, kQKV, true)

@@ -1,0 +1,75 @@
+"""Tensor-parallel plan and weight sharding (CPU): every head, FFN column and vocabulary
+row is owned exactly as the plan says, and the shards' partial products sum back to the
+unsharded projections."""
+
+import pytest
+import torch
+
+from kvcacheboundaryprotection_b200.config import get_config
+from kvcacheboundaryprotection_b200.tp import local_config, shard_weights, tp_plan
+from kvcacheboundaryprotection_b200.weights import init_weights
+
+
+@pytest.mark.parametrize("preset,world", [("qwen2.5-7b", 1), ("qwen2.5-7b", 2), ("qwen2.5-7b", 4),
+                                          ("qwen2.5-7b", 8), ("qwen2.5-3b", 8), ("qwen3-4b", 8),
+                                          ("tiny-qwen2", 2), ("tiny-qwen2", 4)])
+def test_plan_covers_everything_once(preset, world):
+    cfg = get_config(preset)
+    plans = [tp_plan(cfg, world, r) for r in range(world)]
+    qs = sorted(q for p in plans for q in p.q_heads)
+    assert qs == list(range(cfg.n_heads))  # every query head on exactly one rank
+    for p in plans:
+        G = cfg.group
+        assert all(q // G in p.kv_heads for q in p.q_heads)  # a query head sits with its KV head
+        assert 1 <= len(p.q_heads) // len(p.kv_heads) <= 8
+        assert p.kv_replicas == max(1, world // cfg.n_kv_heads)
+    kvs = sorted(k for p in plans for k in p.kv_heads)
+    assert kvs == sorted(list(range(cfg.n_kv_heads)) * max(1, world // cfg.n_kv_heads))
+    for lo_key, hi_key, total in (("ffn_lo", "ffn_hi", cfg.ffn), ("vocab_lo", "vocab_hi", cfg.vocab)):
+        spans = [(getattr(p, lo_key), getattr(p, hi_key)) for p in plans]
+        assert spans[0][0] == 0 and spans[-1][1] == total
+        assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
+        assert all((hi - lo) % 128 == 0 and hi > lo for lo, hi in spans)
+        sizes = [hi - lo for lo, hi in spans]
+        assert max(sizes) - min(sizes) <= 128
+
+
+def test_bad_world_sizes_are_rejected():
+    with pytest.raises(ValueError):
+        tp_plan(get_config("qwen2.5-7b"), 3, 0)  # 4 KV heads do not split over 3 ranks
+    with pytest.raises(ValueError):
+        tp_plan(get_config("tiny-qwen2"), 16, 0)  # 8 replicas of a KV head, 4 query heads each
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_sharded_projections_sum_to_the_full_ones(world):
+    cfg = get_config("tiny-qwen2").with_(n_layers=1, vocab=1024)
+    w = {k: v.float() for k, v in init_weights(cfg, seed=3).items()}
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(3, cfg.hidden, generator=g)
+    att = torch.randn(3, cfg.n_heads * cfg.head_dim, generator=g)
+    act = torch.randn(3, cfg.ffn, generator=g)
+    o_full = att @ w["l0.wo"].t()
+    d_full = act @ w["l0.w_down"].t()
+    o_sum = torch.zeros_like(o_full)
+    d_sum = torch.zeros_like(d_full)
+    logits = []
+    for r in range(world):
+        p = tp_plan(cfg, world, r)
+        lc = local_config(cfg, p)
+        s = shard_weights(cfg, w, p)
+        assert s["l0.wq"].shape == (lc.n_heads * 128, cfg.hidden)
+        assert s["l0.wk"].shape == (lc.n_kv_heads * 128, cfg.hidden)
+        assert s["l0.w_gate"].shape == (lc.ffn, cfg.hidden) and s["l0.w_down"].shape == (cfg.hidden, lc.ffn)
+        att_r = torch.cat([att[:, q * 128 : (q + 1) * 128] for q in p.q_heads], 1)
+        o_sum += att_r @ s["l0.wo"].t()
+        d_sum += act[:, p.ffn_lo : p.ffn_hi] @ s["l0.w_down"].t()
+        # column-parallel q rows are the full projection's rows of the rank's heads
+        q_full = x @ w["l0.wq"].t()
+        q_r = x @ s["l0.wq"].t()
+        for i, q in enumerate(p.q_heads):
+            assert torch.allclose(q_r[:, i * 128 : (i + 1) * 128], q_full[:, q * 128 : (q + 1) * 128])
+        logits.append(x @ s["lm_head"].t())
+    assert torch.allclose(o_sum, o_full, atol=1e-4)
+    assert torch.allclose(d_sum, d_full, atol=1e-4)
+    assert torch.allclose(torch.cat(logits, 1), x @ w["lm_head"].t(), atol=1e-4)
