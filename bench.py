@@ -39,11 +39,13 @@ REPO = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, REPO)
 
 WORKLOADS = {
-    # name: preset, batch/GPU, capacity, prompt, policy
-    "qwen2.5-7b": ("qwen2.5-7b", 16, 1024, 32768, "attention-mass"),
-    "qwen2.5-3b": ("qwen2.5-3b", 32, 256, 2048, "lru"),
-    "qwen3-4b": ("qwen3-4b", 1, 4096, 65536, "lru"),
-    "tiny-qwen2": ("tiny-qwen2", 1, 256, 1024, "lru"),
+    # name: preset, batch, capacity, prompt, policy, multi-GPU parallelism
+    # (tp: the batch is split over nothing -- every rank decodes all sequences with its
+    #  KV-head group; dp: every rank decodes its own `batch` sequences)
+    "qwen2.5-7b": ("qwen2.5-7b", 16, 1024, 32768, "attention-mass", "tp"),
+    "qwen2.5-3b": ("qwen2.5-3b", 32, 256, 2048, "lru", "dp"),
+    "qwen3-4b": ("qwen3-4b", 1, 4096, 65536, "lru", "tp"),
+    "tiny-qwen2": ("tiny-qwen2", 1, 256, 1024, "lru", "dp"),
 }
 METRIC = "decode tok/s (Qwen2.5-7B arch, cap 1024) at 1/2/4/8 B200; kernel HBM GB/s"
 
@@ -55,7 +57,10 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="qwen2.5-7b", choices=sorted(WORKLOADS))
-    ap.add_argument("--batch", type=int, default=None, help="sequences per GPU")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="sequences (per GPU under data parallelism, in total under tensor parallelism)")
+    ap.add_argument("--parallel", default="auto", choices=["auto", "tp", "dp"],
+                    help="multi-GPU scheme (auto: the workload's own, see WORKLOADS)")
     ap.add_argument("--no-micro", action="store_true", help="skip the operator microbench sweep")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     ap.add_argument("--e2e-steps", type=int, default=16)
@@ -145,18 +150,30 @@ def run_ours(a, rank, world, local_rank):
     kbuild.build()
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
-    preset, B0, C, P, policy = WORKLOADS[a.workload]
+    preset, B0, C, P, policy, par = WORKLOADS[a.workload]
+    par = par if a.parallel == "auto" else a.parallel
+    tp = world > 1 and par == "tp"
     B = a.batch or B0
     cfg = get_config(preset)
     K, W = a.steps, a.warmup
-    weights = init_weights(cfg, seed=0, device=dev)
-    fw = FusedWeights(cfg, weights, dev)
-    del weights
-    torch.cuda.empty_cache()
     spec = EvictionSpec(policy, C, 8, True, 0.10, 0.10)
     n_new = W + K + a.e2e_steps + 16
-    eng = CappedKVEngine(cfg, fw, batch=B, evict=spec, max_prompt_len=P, max_new_tokens=n_new, device=dev)
-    eng.synthetic_prefill(P, seed=1234 + rank)
+    weights = init_weights(cfg, seed=0, device=dev)
+    if tp:
+        from kvcacheboundaryprotection_b200.tp import TPEngine, local_config, shard_weights, tp_plan
+
+        plan = tp_plan(cfg, world, rank)
+        fw = FusedWeights(local_config(cfg, plan), shard_weights(cfg, weights, plan), dev)
+        del weights
+        torch.cuda.empty_cache()
+        eng = TPEngine(cfg, fw, plan=plan, batch=B, evict=spec, max_prompt_len=P, max_new_tokens=n_new, device=dev)
+        eng.synthetic_prefill(P, seed=1234)  # the same state on every rank
+    else:
+        fw = FusedWeights(cfg, weights, dev)
+        del weights
+        torch.cuda.empty_cache()
+        eng = CappedKVEngine(cfg, fw, batch=B, evict=spec, max_prompt_len=P, max_new_tokens=n_new, device=dev)
+        eng.synthetic_prefill(P, seed=1234 + rank)
     torch.cuda.synchronize()
     eng.capture()
     for _ in range(W):
@@ -183,7 +200,8 @@ def run_ours(a, rank, world, local_rank):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
         dist.barrier()
-    value = world * B * K / (ms / 1000.0)
+    seqs = B if tp else world * B  # sequences decoded per step by the whole job
+    value = seqs * K / (ms / 1000.0)
     eng.check_device_errors()
 
     # ---- end to end through host buffers: host feeds each step's tokens and reads them back
@@ -207,13 +225,13 @@ def run_ours(a, rank, world, local_rank):
         t = torch.tensor([e2e_s], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t.item())
-    e2e = world * B * a.e2e_steps / e2e_s
+    e2e = seqs * a.e2e_steps / e2e_s
 
     # ---- live per-kernel timing (eager instrumented steps) and the roofline
     kms = measure_kernels_in_step(eng, steps=3)
     hbm, tf, peak_kind = peaks()
     avg_valid = C + 3.5  # retained slots per (sequence, kv head): C .. C+E-1 over a cadence
-    kbytes = kernel_algorithmic_bytes(cfg, B, avg_valid)
+    kbytes = kernel_algorithmic_bytes(eng.cfg, B, avg_valid)  # this rank's shapes
     per_step = {"attention": cfg.n_layers, "qkv": cfg.n_layers, "o": cfg.n_layers, "gate_up": cfg.n_layers,
                 "down": cfg.n_layers, "lm_head": 1}
     kernels = {}
@@ -221,7 +239,7 @@ def run_ours(a, rank, world, local_rank):
         gbs = kbytes[k] / (t * 1e-3) / 1e9
         kernels[k] = {"avg_launch_us": round(t * 1000, 2), "launches_per_step": per_step[k],
                       "algorithmic_bytes_per_launch": int(kbytes[k]), "achieved_gbs": round(gbs, 1),
-                      "frac": round(gbs / hbm, 4), "traffic": NCU_TRAFFIC.get((preset, k))}
+                      "frac": round(gbs / hbm, 4), "traffic": None if tp else NCU_TRAFFIC.get((preset, k))}
     dominant = max(kernels, key=lambda k: kernels[k]["avg_launch_us"] * per_step[k])
 
     def roofline_of(k):
@@ -231,7 +249,8 @@ def run_ours(a, rank, world, local_rank):
                 "traffic": d["traffic"], "avg_launch_us": d["avg_launch_us"],
                 "algorithmic_bytes_per_launch": d["algorithmic_bytes_per_launch"]}
 
-    step_bytes = fw.nbytes() + cfg.n_layers * algorithmic_attn_bytes(B, cfg.n_heads, cfg.n_kv_heads, avg_valid)
+    lc = eng.cfg
+    step_bytes = fw.nbytes() + cfg.n_layers * algorithmic_attn_bytes(B, lc.n_heads, lc.n_kv_heads, avg_valid)
     step_ms = ms / K
     gpu_launches = K * launches_per_step(cfg)
     out = {
@@ -243,19 +262,20 @@ def run_ours(a, rank, world, local_rank):
         "warmup": W,
         "ms_per_step": round(step_ms, 4),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if tp else "weak",
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic (seeded random bf16 weights N(0,0.02); decode from a synthetic post-prefill state)",
         "config": {
             "workload": f"{preset} decode, capacity {C}, {policy} eviction every 8 steps, protect-frac 0.10, "
-            f"{B} sequences/GPU, prompt {P}, greedy",
+            + (f"{B} sequences tensor-parallel over {world} GPUs" if tp else f"{B} sequences/GPU")
+            + f", prompt {P}, greedy",
             "batch_per_gpu": B,
-            "global_batch": B * world,
+            "global_batch": seqs,
             "capacity": C,
             "prompt_len": P,
             "policy": policy,
-            "parallelism": f"dp{world}",
+            "parallelism": f"tp{world}" if tp else f"dp{world}",
             "l2": "inputs larger than L2 (all weights streamed every step)",
         },
         "e2e": {
@@ -312,7 +332,7 @@ def measure_kernels_in_step(eng, steps=3):
         epi, N, K = args[1], args[3], args[4]
         if epi == 2:
             return "gate_up"
-        if epi == 1:
+        if epi in (1, 3):  # residual in place, or fp32 partial sums under tensor parallelism
             return "down" if K == c.ffn else "o"
         return "lm_head"
 
@@ -664,7 +684,7 @@ def cpu_reference_step_times(workload, steps, warmup, budget_s=None):
     from oracle.policies import Meta, PolicySpec
     from kvcacheboundaryprotection_b200.config import get_config
 
-    preset, _, C, P, policy = WORKLOADS[workload]
+    preset, _, C, P, policy, _ = WORKLOADS[workload]
     cfg = get_config(preset)
     rng = np.random.default_rng(0)
     n_layers_sample = 1
@@ -737,7 +757,8 @@ def run_reference(a, rank):
         return None
     times, sample = cpu_reference_step_times(a.workload, a.steps, a.warmup)
     tok_s = 1.0 / (sum(times) / len(times))
-    preset, B0, C, P, policy = WORKLOADS[a.workload]
+    preset, B0, C, P, policy, par = WORKLOADS[a.workload]
+    tp = a.gpus > 1 and (par if a.parallel == "auto" else a.parallel) == "tp"
     return {
         "impl": "reference",
         "metric": METRIC,
@@ -748,7 +769,7 @@ def run_reference(a, rank):
         "warmup": a.warmup,
         "ms_per_step": round(1000 * sum(times) / len(times), 3),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if tp else "weak",
         "vs_baseline": None,
         "dtype": "f32 (bf16-rounded values)",
         "data": "synthetic",
@@ -795,7 +816,7 @@ def main():
         torch.cuda.set_device(local_rank)
         from datetime import timedelta
 
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local_rank))
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local_rank))
     out, eng, fw = run_ours(a, rank, world, local_rank)
     del eng
     torch.cuda.empty_cache()
