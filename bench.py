@@ -425,12 +425,18 @@ def run_microbench(cap_list=(256, 1024, 4096), policies=("lru", "attention-mass"
                 inv = torch.from_numpy(inv_freq_table(D, 1e6)).to(dev)
                 err = torch.zeros(1, dtype=torch.int32, device=dev)
 
-                def step():
+                def step(ev=None):
                     s = torch.cuda.current_stream().cuda_stream
+                    mark = (lambda i: ev[i].record()) if ev else (lambda i: None)
+                    mark(0)
                     check(L.kvbp_append_evict(s, C_.byref(st["state"]), C_.byref(cfg), st["seq_step"].data_ptr(), st["next_pos"].data_ptr(), st["cur_pos"].data_ptr(), st["write_slot"].data_ptr(), None, None, 0, st["evlog"].data_ptr(), st["evcount"].data_ptr(), st["evcap"], None, err.data_ptr()), "append")
+                    mark(1)
                     check(L.kvbp_qkv_rope_scatter(s, B, 1, Hq, Hkv, D, S, qkv.data_ptr(), (Hq + 2 * Hkv) * D, None, None, None, 1e-6, inv.data_ptr(), st["cur_pos"].data_ptr(), st["write_slot"].data_ptr(), q.data_ptr(), kc.data_ptr(), vc.data_ptr(), err.data_ptr()), "qkv")
+                    mark(2)
                     check(L.kvbp_decode_attn_score(s, B, Hq, Hkv, D, S, q.data_ptr(), kc.data_ptr(), vc.data_ptr(), st["slot_pos"].data_ptr(), st["write_slot"].data_ptr(), attn_out.data_ptr(), st["step_score"].data_ptr(), err.data_ptr()), "attn")
+                    mark(3)
                     check(L.kvbp_score_update(s, C_.byref(st["state"]), st["seq_step"].data_ptr(), st["step_score"].data_ptr(), err.data_ptr()), "score")
+                    mark(4)
 
                 for _ in range(3):
                     step()
@@ -461,6 +467,15 @@ def run_microbench(cap_list=(256, 1024, 4096), policies=("lru", "attention-mass"
                     e1.record()
                     torch.cuda.synchronize()
                     attn_only += e0.elapsed_time(e1)
+                # the step's kernels one by one (eager, events between launches), over one
+                # eviction cycle of E steps
+                per = [0.0] * 4
+                for it in range(E):
+                    ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+                    step(ev)
+                    torch.cuda.synchronize()
+                    for k in range(4):
+                        per[k] += ev[k].elapsed_time(ev[k + 1]) * 1000 / E
                 torch.cuda.synchronize()
                 if int(err.item()):
                     raise RuntimeError("device error in microbench: " + str(capi.decode_dev_errors(int(err.item()))))
@@ -480,6 +495,8 @@ def run_microbench(cap_list=(256, 1024, 4096), policies=("lru", "attention-mass"
                         "attn_us": round(aus, 2),
                         "attn_gbs": round(ab / (aus * 1e-6) / 1e9, 1),
                         "attn_frac": round(ab / (aus * 1e-6) / 1e9 / hbm, 4),
+                        "eager_us": {"append_evict": round(per[0], 2), "qkv_rope_scatter": round(per[1], 2),
+                                     "attention": round(per[2], 2), "score_update": round(per[3], 2)},
                     }
                 )
                 del gr

@@ -14,17 +14,19 @@
 //   score[slot] = max over the layer's query heads of p   -> atomicMax into step_score
 //
 // Work decomposition (B200): grid = (CS, Hkv, B) with a thread-block cluster of CS CTAs
-// per (sequence, kv head); each CTA owns a contiguous range of 64-slot tiles.  Warp 4
-// is a TMA producer that streams (K tile, V tile) pairs through a shared-memory ring
-// (2-D loads, 128-byte swizzle, no multicast; full/empty mbarriers).  Warps 0-3 each
-// own 16 slots of every tile and run one continuous flash-decoding pass with no
-// CTA-wide synchronisation per tile:
+// per (sequence, kv head); each CTA owns a contiguous range of 64-slot tiles.  The last
+// warp is a TMA producer that streams (K tile, V tile) pairs through a shared-memory ring
+// (tensor-map loads, 128-byte swizzle, no multicast; full/empty mbarriers).  The consumer
+// warps form two groups of four that take alternate tiles (two tiles in flight through
+// the compute, so one group's dependent mma/softmax chain overlaps the other's); within a
+// group each warp owns 16 slots of the tile.  Every warp runs one continuous
+// flash-decoding pass with no CTA-wide synchronisation per tile:
 //   Q.K^T   tensor cores (mma.sync m16n8k16: slots on M, the <= 8 query heads of the
 //           group on N); the rounded logits are kept in shared memory,
 //   softmax online per warp (running max / sum per head, rescaled partial output),
 //   P.V     tensor cores: V^T from the swizzled tile via ldmatrix.trans, the weights
 //           split into bf16 hi + lo parts (two mma, ~16-bit mantissa), fp32 accumulate.
-// At the end the four warps' (max, sum, O) are merged in shared memory and one st.async
+// At the end the warps' (max, sum, O) are merged in shared memory and one st.async
 // round pushes every CTA's (max, sum) and its O slice r to cluster CTA r (transaction-
 // counted mbarrier).  Each CTA then forms the final max M and sum L, writes its slice
 // of bf16 output, and turns its stored logits into the exact probabilities
@@ -49,9 +51,10 @@ constexpr int kTile = 64;
 #define KVBP_ATTN_STAGES 2
 #endif
 constexpr int kStages = KVBP_ATTN_STAGES;
-constexpr int kConsumerWarps = 4;
-constexpr int kConsumers = kConsumerWarps * 32;
-constexpr int kThreads = kConsumers + 32;  // + one TMA producer warp
+// Consumer warps come in groups of four; group g takes tiles g, g + GR, ... (GR = 1 or
+// 2, a template parameter).  Threads per CTA: 4 * GR warps + one TMA producer warp.
+__host__ __device__ constexpr int attn_threads(int groups) { return 4 * groups * 32 + 32; }
+constexpr int kMinBlocks = 2;  // two CTAs per SM: registers are capped to fit
 constexpr int kHalfBytes = kTile * kD * 2;  // 16 KiB: K (or V) of one tile, two 64x64 boxes
 constexpr int kBoxBytes = kHalfBytes / 2;
 constexpr int kStageBytes = 2 * kHalfBytes;  // K tile + V tile
@@ -64,16 +67,16 @@ struct AttnSmem {
 
 __host__ __device__ inline int align_up(int x, int a) { return (x + a - 1) / a * a; }
 
-__host__ __device__ inline AttnSmem attn_smem_layout(int nloc_tiles) {
+__host__ __device__ inline AttnSmem attn_smem_layout(int nloc_tiles, int consumer_warps) {
   AttnSmem L;
   const int nloc = nloc_tiles * kTile;
   L.logits = kStages * kStageBytes;  // [nloc][8] rounded logits
   L.escr = L.logits + nloc * 8 * 4;  // [warp][16 rows][8] softmax weights of the current tile
-  L.spos = L.escr + kConsumerWarps * 16 * 8 * 4;
+  L.spos = L.escr + consumer_warps * 16 * 8 * 4;
   L.orecv = align_up(L.spos + nloc * 4, 16);  // [CS][per] received O slices
   L.srecv = L.orecv + (8 * kD + kMaxCluster) * 4;  // [CS][16] received (max, sum)
   L.wstat = L.srecv + kMaxCluster * 16 * 4;  // [warp][16] per-warp (max, sum) + CTA (max, sum) + flags
-  L.fin = align_up(L.wstat + (kConsumerWarps + 2) * 16 * 4, 16);  // final M[8], L[8], scale[cluster][8]
+  L.fin = align_up(L.wstat + (consumer_warps + 2) * 16 * 4, 16);  // final M[8], L[8], scale[cluster][8]
   L.bars = align_up(L.fin + (16 + kMaxCluster * 8) * 4, 8);
   L.total = L.bars + (2 * kStages + 1) * 8;
   // the [warp][8][128] partial outputs alias the ring at the end
@@ -96,13 +99,15 @@ struct AttnArgs {
   float scale;     // bfloat16(1/sqrt(D)) as float
 };
 
-template <int G>
-__global__ void __launch_bounds__(kThreads) decode_attn_score_kernel(const __grid_constant__ CUtensorMap kmap,
+template <int G, int GR>
+__global__ void __launch_bounds__(attn_threads(GR), kMinBlocks) decode_attn_score_kernel(const __grid_constant__ CUtensorMap kmap,
                                                                      const __grid_constant__ CUtensorMap vmap,
                                                                      const AttnArgs p) {
+  constexpr int kConsumerWarps = 4 * GR;
+  constexpr int kConsumers = kConsumerWarps * 32;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const AttnSmem L = attn_smem_layout(p.nloc_tiles);
+  const AttnSmem L = attn_smem_layout(p.nloc_tiles, kConsumerWarps);
   uint8_t* ring = base;
   float* logits = reinterpret_cast<float*>(base + L.logits);
   float* escr = reinterpret_cast<float*>(base + L.escr);
@@ -152,7 +157,7 @@ __global__ void __launch_bounds__(kThreads) decode_attn_score_kernel(const __gri
     prefetch_tmap(&vmap);
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kConsumerWarps);
+      mbar_init(&empty[s], 4);  // the four warps of the group that consumes the tile
     }
     mbar_init(xbar, 1);
     *bad_flag = 0;
@@ -227,10 +232,11 @@ __global__ void __launch_bounds__(kThreads) decode_attn_score_kernel(const __gri
 #pragma unroll
   for (int m = 0; m < 8; ++m) oacc[m][0] = oacc[m][1] = oacc[m][2] = oacc[m][3] = 0.f;
   float* ew = escr + warp * 16 * 8;
-  const int r0 = warp * 16;
+  const int r0 = (warp & 3) * 16;  // the warp's 16 slots of each tile its group takes
+  const int grp = warp >> 2;
   const int wslot = early ? p.write_slot[b] : -1;  // row of this step's K/V (read after the wait)
 
-  for (int u = 0; u < nt; ++u) {
+  for (int u = grp; u < nt; u += GR) {
     const int st = u % kStages;
     bool ok_tile = !(*reinterpret_cast<volatile int*>(bad_flag));
     if (ok_tile && !mbar_wait_bounded(&full[st], (u / kStages) & 1)) {
@@ -336,7 +342,7 @@ __global__ void __launch_bounds__(kThreads) decode_attn_score_kernel(const __gri
   }
   if (KVBP_PDL_LATE) pdl_launch_dependents();
 
-  // ---- merge the four warps: per-head (max, sum), then the partial outputs ---------
+  // ---- merge the warps: per-head (max, sum), then the partial outputs ---------------
 #pragma unroll
   for (int o = 4; o < 32; o <<= 1) {
     l0 += __shfl_xor_sync(0xffffffffu, l0, o);
@@ -518,7 +524,7 @@ static int make_cache_map(CUtensorMap* map, const void* ptr, long long pairs, in
 static int choose_cluster(int pairs, int tiles, int sms, int max_nloc_tiles) {
   int per_max = 1;
   for (int per = 1; per <= max_nloc_tiles; ++per)
-    if (2 * (attn_smem_layout(per).total + 2048) <= 228 * 1024) per_max = per;
+    if (2 * (attn_smem_layout(per, 8).total + 2048) <= 228 * 1024) per_max = per;
   int cs = (tiles + per_max - 1) / per_max;
   const int want = (16 * sms / 10 + pairs - 1) / pairs;
   if (cs < want) cs = want;
@@ -528,17 +534,18 @@ static int choose_cluster(int pairs, int tiles, int sms, int max_nloc_tiles) {
   return cs;
 }
 
-template <int G>
+template <int G, int GR>
 static cudaError_t launch_g(cudaStream_t stream, const CUtensorMap& km, const CUtensorMap& vm, const AttnArgs& a,
                             int smem) {
-  auto kern = decode_attn_score_kernel<G>;
+  auto kern = decode_attn_score_kernel<G, GR>;
   static int configured_smem = 0;
   if (smem > configured_smem) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     configured_smem = smem;
   }
-  return launch_pdl(kern, dim3(a.cluster, a.Hkv, a.B), dim3(kThreads), smem, stream, dim3(a.cluster, 1, 1), km, vm, a);
+  return launch_pdl(kern, dim3(a.cluster, a.Hkv, a.B), dim3(attn_threads(GR)), smem, stream, dim3(a.cluster, 1, 1), km,
+                    vm, a);
 }
 
 int decode_attn_score(cudaStream_t stream, int B, int Hq, int Hkv, int D, int S, const void* q, const void* kcache,
@@ -596,22 +603,31 @@ int decode_attn_score(cudaStream_t stream, int B, int Hq, int Hkv, int D, int S,
   a.cluster = cs;
   a.nloc_tiles = nloc_tiles;
   a.scale = __bfloat162float(__float2bfloat16_rn(1.0f / sqrtf(static_cast<float>(kD))));
-  const int smem = attn_smem_layout(nloc_tiles).total + 1024;
+  // two consumer groups pay off once a CTA streams enough tiles to keep both busy
+  const int groups = nloc_tiles >= 8 ? 2 : 1;
+  const int smem = attn_smem_layout(nloc_tiles, 4 * groups).total + 1024;
   if (smem > 227 * 1024)
     return fail(kStatusUnsupported, "decode_attn_score: %d slots per CTA need %d B of shared memory", nloc_tiles * kTile,
                 smem);
 
   cudaError_t e;
+#define KVBP_ATTN_CASE(g)                                                                        \
+  case g:                                                                                        \
+    e = groups == 2 ? launch_g<g, 2>(stream, km, vm, a, smem) : launch_g<g, 1>(stream, km, vm, a, smem); \
+    break;
   switch (G) {
-    case 1: e = launch_g<1>(stream, km, vm, a, smem); break;
-    case 2: e = launch_g<2>(stream, km, vm, a, smem); break;
-    case 3: e = launch_g<3>(stream, km, vm, a, smem); break;
-    case 4: e = launch_g<4>(stream, km, vm, a, smem); break;
-    case 5: e = launch_g<5>(stream, km, vm, a, smem); break;
-    case 6: e = launch_g<6>(stream, km, vm, a, smem); break;
-    case 7: e = launch_g<7>(stream, km, vm, a, smem); break;
-    default: e = launch_g<8>(stream, km, vm, a, smem); break;
+    KVBP_ATTN_CASE(1)
+    KVBP_ATTN_CASE(2)
+    KVBP_ATTN_CASE(3)
+    KVBP_ATTN_CASE(4)
+    KVBP_ATTN_CASE(5)
+    KVBP_ATTN_CASE(6)
+    KVBP_ATTN_CASE(7)
+    default:
+      e = groups == 2 ? launch_g<8, 2>(stream, km, vm, a, smem) : launch_g<8, 1>(stream, km, vm, a, smem);
+      break;
   }
+#undef KVBP_ATTN_CASE
   if (e != cudaSuccess) return fail(kStatusCuda, "decode_attn_score launch: %s", cudaGetErrorString(e));
   return kStatusOk;
 }

@@ -236,36 +236,57 @@ __device__ int select_bit_warp(const uint32_t* words, int W, int k) {
 }
 
 // ------------------------------------------------------------------------------------
-// score update: kv_coupled_generator.py:504-516, over the valid slots of one sequence
+// score update: kv_coupled_generator.py:504-516, over the valid slots of one sequence.
+// The slots of a sequence are split over a cluster of CTAs: each forms the maximum of
+// its share, the CTAs exchange them through DSMEM (the access threshold needs the
+// sequence-wide maximum), then each updates its share.
 // ------------------------------------------------------------------------------------
-__global__ void score_update_kernel(StateArgs st, const int* __restrict__ seq_step, float* __restrict__ step_score,
-                                    int* err) {
+constexpr int kScoreThreads = 256;
+
+__global__ void __launch_bounds__(kScoreThreads) score_update_kernel(StateArgs st, const int* __restrict__ seq_step,
+                                                                     float* __restrict__ step_score, int* err) {
   pdl_launch_dependents();
   pdl_wait();
   __shared__ float red[32];
-  const int b = blockIdx.x;
-  SeqState s = st.seq(b);
-  float* sc = step_score + static_cast<size_t>(b) * st.S;
-  const int step = seq_step[b];
+  __shared__ float cta_max;
+  const int b = blockIdx.y, CS = gridDim.x;
+  uint32_t rank;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank));
+  const int lo = (static_cast<int>(rank) * st.S) / CS, hi = ((static_cast<int>(rank) + 1) * st.S) / CS;
+  const SeqState s = st.seq(b);
+  const int* __restrict__ spos = s.slot_pos;
+  float* __restrict__ sc = step_score + static_cast<size_t>(b) * st.S;
   float mx = 0.f;
-  for (int i = threadIdx.x; i < st.S; i += blockDim.x)
-    if (s.slot_pos[i] >= 0) mx = fmaxf(mx, sc[i]);
+  for (int i = lo + threadIdx.x; i < hi; i += kScoreThreads)
+    if (spos[i] >= 0) mx = fmaxf(mx, sc[i]);
   mx = block_max_float(mx, red);
-  const float thr = static_cast<float>(0.05 * static_cast<double>(mx));
-  for (int i = threadIdx.x; i < st.S; i += blockDim.x) {
-    if (s.slot_pos[i] >= 0) {
-      const float ks = sc[i];
+  if (threadIdx.x == 0) cta_max = mx;
+  cluster_sync_all();
+  float gmx = 0.f;
+  const uint32_t local = smem_u32(&cta_max);
+  for (int q = 0; q < CS; ++q) gmx = fmaxf(gmx, ld_dsmem_f32(mapa_u32(local, q)));
+  const float thr = static_cast<float>(0.05 * static_cast<double>(gmx));
+  const int step = seq_step[b];
+  float* __restrict__ attn = s.attn;
+  float* __restrict__ maxa = s.max_attn;
+  double* __restrict__ cumul = s.cumul;
+  int* __restrict__ last = s.last_access;
+  int* __restrict__ cnt = s.access_count;
+  for (int i = lo + threadIdx.x; i < hi; i += kScoreThreads) {
+    const float ks = sc[i];
+    if (spos[i] >= 0) {
       if (ks != ks) set_err(err, kErrNanScore);
-      s.attn[i] = ks;
-      s.max_attn[i] = fmaxf(s.max_attn[i], ks);
-      s.cumul[i] = __dadd_rn(s.cumul[i], static_cast<double>(ks));
+      attn[i] = ks;
+      maxa[i] = fmaxf(maxa[i], ks);
+      cumul[i] = __dadd_rn(cumul[i], static_cast<double>(ks));
       if (ks > thr) {
-        s.last_access[i] = step;
-        s.access_count[i] += 1;
+        last[i] = step;
+        cnt[i] += 1;
       }
     }
     sc[i] = 0.f;
   }
+  cluster_sync_all();  // peers have read cta_max before this CTA leaves
 }
 
 // ------------------------------------------------------------------------------------
@@ -674,7 +695,13 @@ static bool state_ok(const StateArgs& s) {
 
 int score_update(cudaStream_t stream, const StateArgs& st, const int* seq_step, float* step_score, int* err) {
   if (!state_ok(st) || !seq_step || !step_score) return fail(kStatusArg, "score_update: bad argument");
-  cudaError_t le = launch_pdl(score_update_kernel, dim3(st.B), dim3(256), 0, stream, dim3(0), st, seq_step, step_score, err);
+  // a cluster of up to 8 CTAs per sequence, each with at most ~512 slots
+  int cs = (st.S + 511) / 512;
+  if (cs > 8) cs = 8;
+  if (cs < 1) cs = 1;
+  if (st.B > 65535) return fail(kStatusArg, "score_update: batch %d too large", st.B);
+  cudaError_t le = launch_pdl(score_update_kernel, dim3(cs, st.B), dim3(kScoreThreads), 0, stream, dim3(cs, 1, 1), st,
+                              seq_step, step_score, err);
   if (le != cudaSuccess) return fail(kStatusCuda, "score_update launch: %s", cudaGetErrorString(le));
   return check_launch("score_update");
 }
