@@ -40,13 +40,16 @@ sys.path.insert(0, REPO)
 
 WORKLOADS = {
     # name: preset, batch, capacity, prompt, policy, multi-GPU parallelism
-    # (tp: the batch is split over nothing -- every rank decodes all sequences with its
-    #  KV-head group; dp: every rank decodes its own `batch` sequences)
-    "qwen2.5-7b": ("qwen2.5-7b", 16, 1024, 32768, "attention-mass", "tp"),
+    # (dp: independent sequences shard with no data-path collective -- every rank decodes
+    #  its own `batch` sequences, weak scaling; tp: one decode of `batch` sequences over
+    #  all ranks' KV-head groups, strong scaling).  The 7B workload's line is data
+    #  parallel; its tensor-parallel decode is measured beside it ("tensor_parallel").
+    "qwen2.5-7b": ("qwen2.5-7b", 16, 1024, 32768, "attention-mass", "dp"),
     "qwen2.5-3b": ("qwen2.5-3b", 32, 256, 2048, "lru", "dp"),
     "qwen3-4b": ("qwen3-4b", 1, 4096, 65536, "lru", "tp"),
     "tiny-qwen2": ("tiny-qwen2", 1, 256, 1024, "lru", "dp"),
 }
+ALSO_TP = {"qwen2.5-7b"}
 METRIC = "decode tok/s (Qwen2.5-7B arch, cap 1024) at 1/2/4/8 B200; kernel HBM GB/s"
 
 
@@ -62,6 +65,8 @@ def parse():
     ap.add_argument("--parallel", default="auto", choices=["auto", "tp", "dp"],
                     help="multi-GPU scheme (auto: the workload's own, see WORKLOADS)")
     ap.add_argument("--no-micro", action="store_true", help="skip the operator microbench sweep")
+    ap.add_argument("--nccl-allreduce", action="store_true",
+                    help="tensor parallelism: reduce the o/down partials with NCCL instead of the fused NVLink GEMM")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     ap.add_argument("--e2e-steps", type=int, default=16)
     ap.add_argument("--micro-only", type=int, default=None, metavar="CAPACITY",
@@ -138,6 +143,61 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------------ ours
+def run_tp_side(a, rank, world, local_rank):
+    """Tensor-parallel decode of the workload's sequences over all ranks (one decode of
+    `batch` sequences per step, KV-head groups sharded), K graph replays timed with
+    device events (max over ranks)."""
+    import torch
+    import torch.distributed as dist
+
+    from kvcacheboundaryprotection_b200.config import get_config
+    from kvcacheboundaryprotection_b200.engine import EvictionSpec, FusedWeights
+    from kvcacheboundaryprotection_b200.tp import TPEngine, local_config, shard_weights, tp_plan
+    from kvcacheboundaryprotection_b200.weights import init_weights
+
+    dev = torch.device("cuda", local_rank)
+    preset, B0, C, P, policy, _ = WORKLOADS[a.workload]
+    B = a.batch or B0
+    cfg = get_config(preset)
+    K, W = a.steps, a.warmup
+    plan = tp_plan(cfg, world, rank)
+    weights = init_weights(cfg, seed=0, device=dev)
+    fw = FusedWeights(local_config(cfg, plan), shard_weights(cfg, weights, plan), dev)
+    del weights
+    torch.cuda.empty_cache()
+    eng = TPEngine(cfg, fw, plan=plan, fused_allreduce=not a.nccl_allreduce, batch=B,
+                   evict=EvictionSpec(policy, C, 8, True, 0.10, 0.10), max_prompt_len=P, max_new_tokens=W + K + 16,
+                   device=dev)
+    eng.synthetic_prefill(P, seed=1234)
+    eng.capture()
+    for _ in range(W):
+        eng.run_step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(K):
+        eng.run_step()
+    e1.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1)], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    eng.check_device_errors()
+    eng.graph = None
+    del eng
+    torch.cuda.empty_cache()
+    return {
+        "parallelism": f"tp{world}",
+        "value": round(B * K / (ms / 1000.0), 2),
+        "unit": "tok/s",
+        "ms_per_step": round(ms / K, 4),
+        "scaling": "strong",
+        "global_batch": B,
+        "allreduce": "nccl" if a.nccl_allreduce else "fused NVLink GEMM epilogue (o, down) + NCCL (score, argmax)",
+    }
+
+
 def run_ours(a, rank, world, local_rank):
     import torch
     import torch.distributed as dist
@@ -166,7 +226,8 @@ def run_ours(a, rank, world, local_rank):
         fw = FusedWeights(local_config(cfg, plan), shard_weights(cfg, weights, plan), dev)
         del weights
         torch.cuda.empty_cache()
-        eng = TPEngine(cfg, fw, plan=plan, batch=B, evict=spec, max_prompt_len=P, max_new_tokens=n_new, device=dev)
+        eng = TPEngine(cfg, fw, plan=plan, fused_allreduce=not a.nccl_allreduce, batch=B, evict=spec,
+                       max_prompt_len=P, max_new_tokens=n_new, device=dev)
         eng.synthetic_prefill(P, seed=1234)  # the same state on every rank
     else:
         fw = FusedWeights(cfg, weights, dev)
@@ -276,6 +337,8 @@ def run_ours(a, rank, world, local_rank):
             "prompt_len": P,
             "policy": policy,
             "parallelism": f"tp{world}" if tp else f"dp{world}",
+            "allreduce": ("nccl" if a.nccl_allreduce else "fused NVLink GEMM epilogue (o, down) + NCCL (score, argmax)")
+            if tp else None,
             "l2": "inputs larger than L2 (all weights streamed every step)",
         },
         "e2e": {
@@ -348,7 +411,8 @@ def measure_kernels_in_step(eng, steps=3):
 
         return f
 
-    names = {"kvbp_decode_attn_score": "attention", "kvbp_decode_qkv_gemm": "qkv", "kvbp_decode_gemm": kind_of_gemm}
+    names = {"kvbp_decode_attn_score": "attention", "kvbp_decode_qkv_gemm": "qkv", "kvbp_decode_gemm": kind_of_gemm,
+             "kvbp_decode_gemm_allreduce": lambda args: "down" if args[3] == c.ffn else "o"}
     saved = {n: getattr(L, n) for n in names}
     try:
         for n, kind in names.items():
@@ -835,8 +899,13 @@ def main():
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local_rank))
     out, eng, fw = run_ours(a, rank, world, local_rank)
+    eng.graph = None  # a graph holding NCCL calls goes before the process group
     del eng
     torch.cuda.empty_cache()
+    if world > 1 and a.parallel == "auto" and a.workload in ALSO_TP:
+        del fw
+        torch.cuda.empty_cache()
+        out["tensor_parallel"] = run_tp_side(a, rank, world, local_rank)
     if rank == 0 and world == 1:
         if not a.no_micro:
             del fw

@@ -45,6 +45,7 @@ typedef struct CUstream_st* kvbp_stream_t; /* == cudaStream_t */
 #define KVBP_DEV_WAIT_TIMEOUT 8
 #define KVBP_DEV_NO_VALID_SLOT 16
 #define KVBP_DEV_LOG_OVERFLOW 32
+#define KVBP_DEV_PEER_TIMEOUT 64
 
 /* Policy ids: the reference CLI names (scripts/run_v3_jax.py:145-148, built at
  * :500-518); "attention-mass" is an alias of "h2o_faithful". */
@@ -229,6 +230,24 @@ int kvbp_decode_qkv_gemm(kvbp_stream_t stream, int32_t M, int32_t n_heads, int32
                          const void* norm_w, float eps, const void* bias, const void* q_norm, const void* k_norm,
                          const float* inv_freq, const int32_t* positions, const int32_t* write_slot, int32_t S,
                          void* q_out, void* kcache, void* vcache, int32_t splits, int32_t* dev_err);
+
+/* Tensor-parallel row-parallel projection with the allreduce fused in: this rank's
+ * partial Y = X . W^T (fp32, W packed) is pushed tile by tile into the symmetric buffer
+ * of every rank of the group (peer_bases[q] = rank q's buffer, mapped into this process;
+ * a device array), and each tile is finished as h = bf16(h + bf16(sum over ranks, in
+ * rank order)) with ss_out as in epilogue 1 -- identical on every rank.  Buffer layout
+ * (buffer_bytes each): u32 flags [2][world][N/128][splits], then at the next 256-byte
+ * boundary fp32 [2][world][M][N]; the flags are zeroed (and the ranks synchronised)
+ * before a run.  call_index (0..254) numbers the allreduces of one step (parity =
+ * call_index & 1 double-buffers the receive area) and *epoch must differ between steps
+ * (flags hold epoch * 256 + call_index + 1).  Every rank must make the same calls in the
+ * same order; waits are bounded (KVBP_DEV_PEER_TIMEOUT).  One rank per GPU: the ranks'
+ * kernels wait on each other and must run concurrently; the call is rejected when the
+ * whole grid cannot be resident at once. */
+int kvbp_decode_gemm_allreduce(kvbp_stream_t stream, int32_t M, int32_t N, int32_t K, const void* w_packed,
+                               const void* x, int32_t ldx, void* h, float* ss_out, int32_t splits,
+                               const uint64_t* peer_bases, int32_t world, int32_t rank, int32_t call_index,
+                               const int32_t* epoch, int64_t buffer_bytes, int32_t* dev_err);
 
 /* Converts a row-major bf16 weight W[N][K] (N, K multiples of 128) to the decode GEMM's
  * packed layout and back: each 128-row x 128-column block becomes one contiguous 32 KiB

@@ -17,6 +17,7 @@ enum DeviceError : int {
   kErrWaitTimeout = 8,    // a bounded mbarrier wait gave up
   kErrNoValidSlot = 16,   // attention found no valid slot for a (sequence, kv head)
   kErrLogOverflow = 32,   // the eviction log is full
+  kErrPeerTimeout = 64,   // a bounded wait for another GPU's flag gave up
 };
 
 __device__ __forceinline__ void set_err(int* err, int bit) {

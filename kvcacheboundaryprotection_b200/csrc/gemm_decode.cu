@@ -26,6 +26,12 @@
 //   * SWIGLU epilogue: weight rows are stored gate/up interleaved in blocks of 64, so a
 //     tile holds 64 gate and the matching 64 up features and writes
 //     act = bf16(bf16(g * bf16(sigmoid(g))) * u) (jax_inference.py:702-704,1103-1107).
+//   * RESID + ALLREDUCE epilogue (tensor parallelism, one rank per GPU): each CTA pushes
+//     its rows of the rank's fp32 partial tile into every rank's symmetric receive buffer
+//     over NVLink (peer stores), raises a per-(tile, row slice) flag on every rank
+//     (release, system scope), waits for the flags of all ranks (acquire, bounded), and
+//     then sums the ranks' rows in rank order before the residual add -- the o/down
+//     allreduce-SUM fused into the GEMM, identical on every rank.
 //   * QKV epilogue: a 128-feature tile of the stacked q/k/v projection is exactly one
 //     head, so the tile finishes it in place: bias, q/k RMSNorm (Qwen3), RoPE, and the
 //     store of q to its buffer or of k/v into the slot the sequence writes this step
@@ -53,7 +59,7 @@ constexpr int kBlockElems = BN * BK;  // one packed block
 constexpr int kRedStride = BN + 8;    // fp32 partial tile row stride (fewer bank conflicts)
 constexpr int kMaxSplits = 16;
 
-enum Epi : int { kPlain = 0, kResid = 1, kSwiGLU = 2, kF32 = 3, kQKV = 4 };
+enum Epi : int { kPlain = 0, kResid = 1, kSwiGLU = 2, kF32 = 3, kQKV = 4, kResidAR = 5 };
 
 struct Args {
   const __nv_bfloat16* w;  // packed [N/128][K/128][2][128][64] (swizzled 16-byte chunks)
@@ -79,7 +85,28 @@ struct Args {
   __nv_bfloat16* q_out;   // [M][Hq][128]
   __nv_bfloat16* kcache;  // [M][Hkv][S][128]
   __nv_bfloat16* vcache;
+  // RESID + ALLREDUCE epilogue: every rank's symmetric buffer holds
+  //   flags u32 [2][world][N/128][splits], then (256-byte aligned) recv f32 [2][world][M][N]
+  const unsigned long long* peers;  // [world] base address of each rank's buffer (device array)
+  int world, rank, call;            // call: index of this allreduce within the step (parity = call & 1)
+  const int* epoch;                 // device counter that differs between steps
 };
+
+__host__ __device__ inline size_t ar_flag_words(int world, int tiles, int splits) {
+  return static_cast<size_t>(2) * world * tiles * splits;
+}
+__host__ __device__ inline size_t ar_recv_offset(int world, int tiles, int splits) {
+  return (ar_flag_words(world, tiles, splits) * 4 + 255) / 256 * 256;
+}
+
+__device__ __forceinline__ void st_release_sys_u32(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
 
 template <int MT, int EPI, bool NORM>
 __global__ void __launch_bounds__(kThreads) decode_gemm_kernel(const __grid_constant__ CUtensorMap xmap,
@@ -328,6 +355,67 @@ __global__ void __launch_bounds__(kThreads) decode_gemm_kernel(const __grid_cons
         if (r >= r_lo && r < r_hi) a.ss_out[tile * 32 + r] = red[2 * (r - r_lo)] + red[2 * (r - r_lo) + 1];
         if (rank == 0 && r >= M) a.ss_out[tile * 32 + r] = 0.f;
       }
+    } else if (EPI == kResidAR) {
+      const int W = a.world, tiles = gridDim.x;
+      const int par = a.call & 1;
+      const uint32_t v = static_cast<uint32_t>(*a.epoch) * 256u + static_cast<uint32_t>(a.call) + 1u;
+      const size_t roff = ar_recv_offset(W, tiles, cs);
+      // 1. this rank's rows of the tile into every rank's receive buffer (slot `rank`)
+      for (int e = tid; e < nrows * (BN / 2); e += kConsumers) {
+        const int r = r_lo + e / (BN / 2), c = 2 * (e % (BN / 2));
+        const float2 val = sum_pair(r, c);
+        const size_t off = ((static_cast<size_t>(par) * W + a.rank) * M + r) * a.N + n0 + c;
+        for (int q = 0; q < W; ++q)
+          *reinterpret_cast<float2*>(reinterpret_cast<float*>(a.peers[q] + roff) + off) = val;
+      }
+      __threadfence_system();
+      named_bar(1, kConsumers);
+      const size_t fslot = (static_cast<size_t>(tile) * cs + blockIdx.y);
+      if (tid < W)
+        st_release_sys_u32(reinterpret_cast<uint32_t*>(a.peers[tid]) + (static_cast<size_t>(par) * W + a.rank) * tiles * cs + fslot, v);
+      // 2. every rank's rows of this slice have landed here
+      if (tid < W) {
+        const uint32_t* f = reinterpret_cast<const uint32_t*>(a.peers[a.rank]) + (static_cast<size_t>(par) * W + tid) * tiles * cs + fslot;
+        uint32_t spins = 0;
+        while (ld_acquire_sys_u32(f) != v) {
+          if (++spins > (1u << 24)) {
+            set_err(a.err, kErrPeerTimeout);
+            break;
+          }
+          if (spins > 64) __nanosleep(128);
+        }
+      }
+      named_bar(1, kConsumers);
+      // 3. sum the ranks' partials in rank order, residual add, sums of squares
+      const float* recv = reinterpret_cast<const float*>(a.peers[a.rank] + roff);
+      for (int e0 = 0; e0 < nrows * (BN / 2); e0 += kConsumers) {
+        const int e = e0 + tid;
+        float ss = 0.f;
+        if (e < nrows * (BN / 2)) {
+          const int r = r_lo + e / (BN / 2), c = 2 * (e % (BN / 2));
+          float2 sum = __ldcg(reinterpret_cast<const float2*>(recv + ((static_cast<size_t>(par) * W + 0) * M + r) * a.N + n0 + c));
+          for (int q = 1; q < W; ++q) {
+            const float2 t2 = __ldcg(reinterpret_cast<const float2*>(recv + ((static_cast<size_t>(par) * W + q) * M + r) * a.N + n0 + c));
+            sum.x += t2.x;
+            sum.y += t2.y;
+          }
+          uint32_t* hp = reinterpret_cast<uint32_t*>(&a.out[static_cast<size_t>(r) * a.ldo + n0 + c]);
+          const uint32_t hv = *hp;
+          const float x0 = bf16r(bf16lo(hv) + bf16r(sum.x));
+          const float x1 = bf16r(bf16hi(hv) + bf16r(sum.y));
+          *hp = pack_bf16(x0, x1);
+          ss = x0 * x0 + x1 * x1;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        if (lane == 0 && e < nrows * (BN / 2)) red[2 * (e / (BN / 2)) + ((e >> 5) & 1)] = ss;
+      }
+      named_bar(1, kConsumers);
+      if (tid < 32) {
+        const int r = tid;
+        if (r >= r_lo && r < r_hi) a.ss_out[tile * 32 + r] = red[2 * (r - r_lo)] + red[2 * (r - r_lo) + 1];
+        if (rank == 0 && r >= M) a.ss_out[tile * 32 + r] = 0.f;
+      }
     } else if (EPI == kSwiGLU) {  // features 0..63 of the tile are gate, 64..127 the matching up
       const int f0 = tile * (BN / 2);
       for (int e = tid; e < nrows * (BN / 2); e += kConsumers) {
@@ -528,6 +616,64 @@ int decode_qkv_gemm(cudaStream_t stream, int M, int Hq, int Hkv, int K, const vo
   return decode_gemm_launch(stream, kQKV, a);
 }
 
+int decode_gemm_allreduce(cudaStream_t stream, int M, int N, int K, const void* w, const void* x, int ldx, void* h,
+                          float* ss_out, int splits, const unsigned long long* peers, int world, int rank, int call,
+                          const int* epoch, long long buffer_bytes, int* err) {
+  using namespace gemm;
+  if (!h || !ss_out || !peers || !epoch) return fail(kStatusArg, "decode_gemm_allreduce: null pointer");
+  if (world < 1 || world > 64 || rank < 0 || rank >= world || call < 0 || call > 254)
+    return fail(kStatusArg, "decode_gemm_allreduce: bad world %d / rank %d / call %d", world, rank, call);
+  if (N <= 0 || N % BN || splits < 1 || splits > kMaxSplits) return fail(kStatusArg, "decode_gemm_allreduce: bad size");
+  {
+    // the ranks' CTAs wait on each other: every CTA of the grid must be resident at once
+    const int MT = M > 16 ? 2 : 1;
+    const int smem = gemm_smem_bytes(MT);
+    auto kern = MT == 2 ? decode_gemm_kernel<2, kResidAR, false> : decode_gemm_kernel<1, kResidAR, false>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e != cudaSuccess) return fail(kStatusCuda, "decode_gemm_allreduce: %s", cudaGetErrorString(e));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(N / BN, splits);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 1;
+    attr.val.clusterDim.y = splits;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    e = cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg);
+    if (e != cudaSuccess) return fail(kStatusCuda, "decode_gemm_allreduce: occupancy query: %s", cudaGetErrorString(e));
+    if (clusters < N / BN)
+      return fail(kStatusUnsupported, "decode_gemm_allreduce: %d column tiles but only %d clusters of %d resident",
+                  N / BN, clusters, splits);
+  }
+  const size_t need = ar_recv_offset(world, N / BN, splits) + static_cast<size_t>(2) * world * M * N * 4;
+  if (buffer_bytes < 0 || static_cast<size_t>(buffer_bytes) < need)
+    return fail(kStatusArg, "decode_gemm_allreduce: symmetric buffer of %lld bytes < %zu needed", buffer_bytes, need);
+  if (reinterpret_cast<uintptr_t>(h) & 3) return fail(kStatusArg, "decode_gemm_allreduce: h rows must be 4-byte aligned");
+  Args a = {};
+  a.w = static_cast<const __nv_bfloat16*>(w);
+  a.x = static_cast<const __nv_bfloat16*>(x);
+  a.ldx = ldx;
+  a.out = static_cast<__nv_bfloat16*>(h);
+  a.ldo = N;
+  a.ss_out = ss_out;
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.splits = splits;
+  a.err = err;
+  a.peers = peers;
+  a.world = world;
+  a.rank = rank;
+  a.call = call;
+  a.epoch = epoch;
+  return decode_gemm_launch(stream, kResidAR, a);
+}
+
 static int decode_gemm_launch(cudaStream_t stream, int epi, gemm::Args& a) {
   using namespace gemm;
   const int M = a.M, N = a.N, K = a.K, splits = a.splits, ldx = a.ldx, n_parts = a.n_parts;
@@ -577,6 +723,8 @@ static int decode_gemm_launch(cudaStream_t stream, int epi, gemm::Args& a) {
   KVBP_GEMM_CASE(1, kF32, true)
   KVBP_GEMM_CASE(2, kF32, false)
   KVBP_GEMM_CASE(2, kF32, true)
+  KVBP_GEMM_CASE(1, kResidAR, false)
+  KVBP_GEMM_CASE(2, kResidAR, false)
   KVBP_GEMM_CASE(1, kQKV, true)
   KVBP_GEMM_CASE(1, kQKV, false)
   KVBP_GEMM_CASE(2, kQKV, true)
@@ -627,6 +775,16 @@ extern "C" int kvbp_decode_qkv_gemm(kvbp_stream_t stream, int32_t M, int32_t n_h
   return kvbp::decode_qkv_gemm(reinterpret_cast<cudaStream_t>(stream), M, n_heads, n_kv_heads, K, w_packed, x, ldx,
                                ss_parts, n_parts, norm_w, eps, bias, q_norm, k_norm, inv_freq, positions, write_slot,
                                S, q_out, kcache, vcache, splits, dev_err);
+}
+
+extern "C" int kvbp_decode_gemm_allreduce(kvbp_stream_t stream, int32_t M, int32_t N, int32_t K,
+                                          const void* w_packed, const void* x, int32_t ldx, void* h, float* ss_out,
+                                          int32_t splits, const uint64_t* peer_bases, int32_t world, int32_t rank,
+                                          int32_t call_index, const int32_t* epoch, int64_t buffer_bytes,
+                                          int32_t* dev_err) {
+  return kvbp::decode_gemm_allreduce(reinterpret_cast<cudaStream_t>(stream), M, N, K, w_packed, x, ldx, h, ss_out,
+                                     splits, reinterpret_cast<const unsigned long long*>(peer_bases), world, rank,
+                                     call_index, epoch, buffer_bytes, dev_err);
 }
 
 extern "C" int kvbp_pack_weight(kvbp_stream_t stream, int32_t N, int32_t K, const void* src, void* dst) {

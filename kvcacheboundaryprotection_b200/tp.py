@@ -145,12 +145,47 @@ class NcclCollective:
         dist.all_reduce(t, op=dist.ReduceOp.SUM if op == "sum" else dist.ReduceOp.MAX, group=self.group)
 
 
+class SymmetricBuffer:
+    """A device buffer mapped into every rank of the process group (torch symmetric
+    memory): ``peers`` is a device array of the ranks' base addresses, for the decode
+    GEMM's fused allreduce."""
+
+    def __init__(self, nbytes: int, device: torch.device, group=None):
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm_mem
+
+        group = group or dist.group.WORLD
+        self.nbytes = (int(nbytes) + 255) // 256 * 256
+        self.buf = symm_mem.empty(self.nbytes, dtype=torch.uint8, device=device)
+        self.handle = symm_mem.rendezvous(self.buf, group.group_name)
+        self.peers = torch.tensor(list(self.handle.buffer_ptrs), dtype=torch.int64, device=device)
+        self.group = group
+        self.reset()
+
+    def reset(self) -> None:
+        """Zero the flags and receive areas on every rank, then synchronise the ranks."""
+        import torch.distributed as dist
+
+        self.buf.zero_()
+        torch.cuda.synchronize(self.buf.device)
+        dist.barrier(group=self.group)
+
+
+def allreduce_buffer_bytes(world: int, M: int, N: int, splits: int) -> int:
+    """Size of the symmetric buffer kvbp_decode_gemm_allreduce needs (include/kvbp.h)."""
+    flags = 2 * world * (N // 128) * splits * 4
+    return (flags + 255) // 256 * 256 + 2 * world * M * N * 4
+
+
 class TPEngine(CappedKVEngine):
     """One rank of a tensor-parallel decode.  ``weights`` is the FULL weight dict (it is
     sharded here) or this rank's prebuilt ``FusedWeights``.  ``collective`` performs the
-    reductions when the step runs as one rank of a process group."""
+    reductions when the step runs as one rank of a process group.  With
+    ``fused_allreduce`` (one rank per GPU in a real process group) the o/down partial sums
+    are reduced inside the GEMMs over NVLink instead of by ``collective``."""
 
-    def __init__(self, cfg: ModelConfig, weights, *, plan: TPPlan, collective: Callable = None, **kw):
+    def __init__(self, cfg: ModelConfig, weights, *, plan: TPPlan, collective: Callable = None,
+                 fused_allreduce: bool = False, **kw):
         if kw.get("gemm", "kvbp") != "kvbp":
             raise ValueError("tensor parallelism runs on the own decode GEMMs")
         self.full_cfg = cfg
@@ -164,6 +199,26 @@ class TPEngine(CappedKVEngine):
         super().__init__(lcfg, weights, **kw)
         self.part = torch.zeros(self.B, cfg.hidden, dtype=torch.float32, device=self.dev)
         self.keys = torch.zeros(self.B, dtype=torch.int64, device=self.dev)
+        # the fused allreduce pairs the same (tile, row slice) on every rank: use one split
+        # count for o and down across ranks (their K differs when the shards are uneven)
+        for name, k_of in (("o", lambda p: len(p.q_heads) * cfg.head_dim), ("down", lambda p: p.ffn_hi - p.ffn_lo)):
+            self.splits[name] = min(self._pick_splits(cfg.hidden, k_of(tp_plan(cfg, plan.world, r)))
+                                    for r in range(plan.world))
+        self.symm = None
+        if fused_allreduce and plan.world > 1:
+            sp = max(self.splits["o"], self.splits["down"])
+            self.symm = SymmetricBuffer(allreduce_buffer_bytes(plan.world, self.B, cfg.hidden, sp), self.dev)
+
+    def _allreduce_gemm(self, name, K, w, x, ldx, call, ss_out) -> None:
+        c = self.cfg
+        check(
+            lib().kvbp_decode_gemm_allreduce(
+                self.stream, self.B, c.hidden, K, _ptr(w), _ptr(x), ldx, _ptr(self.h), _ptr(ss_out), self.splits[name],
+                _ptr(self.symm.peers), self.plan.world, self.plan.rank, call, _ptr(self.seq_step), self.symm.nbytes,
+                _ptr(self.dev_err),
+            ),
+            f"decode_gemm_allreduce[{name}]",
+        )
 
     # ------------------------------------------------------------------ decode
     def _forward_phases(self, sample: bool = True) -> Iterator[Phase]:
@@ -192,13 +247,19 @@ class TPEngine(CappedKVEngine):
                 ),
                 "decode_attn_score",
             )
-            self._gemm("o", 3, H, c.n_heads * D, Lw["w_o"], self.attn_out, c.n_heads * D, self.part, H)
-            yield ("sum", self.part)
-            check(L.kvbp_residual_add(st, B, H, _ptr(self.h), _ptr(self.part), _ptr(self.ss_b)), "residual_add")
+            if self.symm is not None:  # allreduce fused into the GEMM over NVLink
+                self._allreduce_gemm("o", c.n_heads * D, Lw["w_o"], self.attn_out, c.n_heads * D, 2 * li, self.ss_b)
+            else:
+                self._gemm("o", 3, H, c.n_heads * D, Lw["w_o"], self.attn_out, c.n_heads * D, self.part, H)
+                yield ("sum", self.part)
+                check(L.kvbp_residual_add(st, B, H, _ptr(self.h), _ptr(self.part), _ptr(self.ss_b)), "residual_add")
             self._gemm("gu", 2, 2 * F, H, Lw["w_gu"], self.h, H, self.act, F, Lw["post_norm"], self.ss_b, nt_h)
-            self._gemm("down", 3, H, F, Lw["w_down"], self.act, F, self.part, H)
-            yield ("sum", self.part)
-            check(L.kvbp_residual_add(st, B, H, _ptr(self.h), _ptr(self.part), _ptr(self.ss_a)), "residual_add")
+            if self.symm is not None:
+                self._allreduce_gemm("down", F, Lw["w_down"], self.act, F, 2 * li + 1, self.ss_a)
+            else:
+                self._gemm("down", 3, H, F, Lw["w_down"], self.act, F, self.part, H)
+                yield ("sum", self.part)
+                check(L.kvbp_residual_add(st, B, H, _ptr(self.h), _ptr(self.part), _ptr(self.ss_a)), "residual_add")
             ss_in, n_in = self.ss_a, nt_h
         if sample:
             self._gemm("lm", 0, c.vocab, H, self.lm_w, self.h, H, self.logits, c.vocab, self.final_norm, ss_in, n_in)
@@ -247,6 +308,8 @@ class TPEngine(CappedKVEngine):
                 t[li].copy_(full[:, kv])
                 del full
         self.tokens.copy_(torch.randint(0, fc.vocab, (self.B,), generator=g, device=self.dev, dtype=torch.int32))
+        if self.symm is not None:
+            self.symm.reset()
 
     def prefill_phases(self, input_ids: torch.Tensor) -> Iterator[Phase]:
         """Step 0 (prompt forward, scores, forced eviction, compaction, first token) with
@@ -325,6 +388,8 @@ class TPEngine(CappedKVEngine):
     def prefill(self, input_ids: torch.Tensor) -> None:
         for op, t in self.prefill_phases(input_ids):
             self.coll(op, t)
+        if self.symm is not None:
+            self.symm.reset()
 
 
 def run_lockstep(phase_iters: Sequence[Iterator[Phase]]) -> None:
