@@ -110,6 +110,17 @@ int kvbp_decode_attn_score(kvbp_stream_t stream, int32_t B, int32_t Hq, int32_t 
                            const void* q, const void* kcache, const void* vcache, const int32_t* slot_pos,
                            const int32_t* write_slot, void* out, float* step_score, int32_t* dev_err);
 
+/* K5 -- causal prefill attention of one sequence and layer on the tcgen05 tensor cores,
+ * with the per-key score.  q [P][Hq][128] bf16 (after RoPE), kcache/vcache
+ * [Hkv][P][128] bf16 (16-byte aligned), out [P][Hq][128] bf16 = the attention output
+ * (jax_inference.py:1018-1050 with the causal mask :1169-1179).  colmax [P] float (may
+ * be NULL, non-negative on entry) is max-accumulated with each key's largest probability
+ * over the heads and query rows (jax_inference.py:1754-1760; pass the same buffer for
+ * every layer to get the max over layers). */
+int kvbp_prefill_attn_score(kvbp_stream_t stream, int32_t P, int32_t Hq, int32_t Hkv, int32_t head_dim,
+                            const void* q, const void* kcache, const void* vcache, void* out, float* colmax,
+                            int32_t* dev_err);
+
 /* K4 -- QKV epilogue + scatter of the new K/V into its slot.  Replaces the bias add
  * (jax_inference.py:953-956), q/k RMSNorm (:975-978), RoPE (:621-637,1000-1001) and the
  * cache write dynamic_update_slice (:1011-1012).  qkv [rows][ldq] bf16 holds the Hq

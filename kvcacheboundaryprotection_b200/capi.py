@@ -107,6 +107,7 @@ SIGNATURES = {
     "kvbp_decode_gemm": (C.c_int, [P, I32, I32, I32, I32, P, P, I32, P, I32, P, F32, P, I32, P, I32, P]),
     "kvbp_decode_qkv_gemm": (C.c_int, [P, I32, I32, I32, I32, P, P, I32, P, I32, P, F32, P, P, P, P, P, P, I32, P, P,
                                        P, I32, P]),
+    "kvbp_prefill_attn_score": (C.c_int, [P, I32, I32, I32, I32, P, P, P, P, P, P]),
     "kvbp_decode_gemm_allreduce": (C.c_int, [P, I32, I32, I32, P, P, I32, P, P, I32, P, I32, I32, I32, P, I64, P]),
     "kvbp_pack_weight": (C.c_int, [P, I32, I32, P, P]),
     "kvbp_argmax_key": (C.c_int, [P, I32, I32, I64, P, I32, P]),

@@ -1,0 +1,408 @@
+// Causal prefill attention with the per-key score on the 5th-generation tensor cores
+// (tcgen05 + TMEM), one sequence, one layer.
+//
+// Reference: the prefill branch of JAXModelAdapter (jax_inference.py:1684-1790) runs
+// _attention_layer (:1018-1050) over the prompt with the causal mask (:1169-1179); the
+// generator reduces the probabilities to one score per key position, max over layers,
+// heads and query rows (jax_inference.py:1754-1760, kv_coupled_generator.py:636-658).
+// Rounding points as in the decode kernel: s = bf16(bf16(q.k) * bf16(1/sqrt(128))),
+// fp32 softmax, out = bf16(sum_j p_j * fp32(v_j)), score[j] = max p[., j].
+//
+// One CTA per (128-query tile, query head); 4 warps, thread t owns query row t.
+//   pass 1: S = Q.K^T tile by tile (tcgen05.mma, M = 128 queries, N = 128 keys,
+//           K = 128 dims, bf16 in, fp32 accumulator in TMEM); each thread reads its row
+//           from TMEM and keeps the running max M and sum L of exp(s - M).
+//   pass 2: S again; p = exp(s - M) / L exactly (the final statistics are known), the
+//           per-key maximum over the tile's rows goes to the score with atomicMax, and
+//           O += P.V on the tensor cores with P split into bf16 hi + lo parts (two MMAs,
+//           ~16-bit mantissa; V is exact in bf16) and O accumulated in TMEM.
+// Q, K and V tiles arrive by 3-D TMA (128-byte swizzle) in the K-major layout the MMA
+// descriptors describe; P is written by the threads in the same swizzled layout.  V is
+// the MN-major B operand of P.V.  K tiles are double-buffered (the next tile's load
+// overlaps the current tile's softmax work).
+#include "common.cuh"
+#include "kvbp_internal.h"
+
+namespace kvbp {
+namespace pf {
+
+constexpr int kRows = 128;        // queries per CTA (= TMEM lanes)
+constexpr int kKeys = 128;        // keys per tile
+constexpr int kD = 128;
+constexpr int kThreads = 128;
+constexpr int kHalf = kRows * 128;  // one 64-column half of a [128][128] bf16 tile: 16 KiB
+constexpr int kTile = 2 * kHalf;    // 32 KiB
+constexpr int kTmemCols = 256;      // S: columns 0..127, O: columns 128..255
+
+// smem layout (from a 1024-aligned base)
+constexpr int kOffQ = 0;
+constexpr int kOffK0 = kOffQ + kTile;
+constexpr int kOffK1 = kOffK0 + kTile;
+constexpr int kOffV = kOffK1 + kTile;
+constexpr int kOffPh = kOffV + kTile;
+constexpr int kOffPl = kOffPh + kTile;
+constexpr int kOffBars = kOffPl + kTile;   // bar_q, bar_k[2], bar_v, bar_mma
+constexpr int kOffMisc = kOffBars + 64;    // tmem address, flags
+constexpr int kSmem = kOffMisc + 64 + 1024;
+
+// Shared-memory matrix descriptor: 128-byte swizzle, version 1 (tcgen05).
+__device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  return static_cast<uint64_t>((saddr >> 4) & 0x3FFF) | (static_cast<uint64_t>((lbo >> 4) & 0x3FFF) << 16) |
+         (static_cast<uint64_t>((sbo >> 4) & 0x3FFF) << 32) | (static_cast<uint64_t>(1) << 46) |
+         (static_cast<uint64_t>(2) << 61);
+}
+
+// kind::f16 instruction descriptor: D f32, A/B bf16, A K-major, B K- or MN-major, M x N
+__host__ __device__ constexpr uint32_t idesc(int M, int N, int b_mn_major) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(b_mn_major) << 16) |
+         (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t id, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+      "l"(da), "l"(db), "r"(id), "r"(acc));
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+struct Args {
+  int P, Hq, Hkv, G;
+  float scale;         // bf16(1/sqrt(128)) as float
+  __nv_bfloat16* out;  // [P][Hq][128]
+  float* colmax;       // [P] or null: max-accumulated per-key score
+  int* err;
+};
+
+__global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(const __grid_constant__ CUtensorMap qmap,
+                                                                  const __grid_constant__ CUtensorMap kmap,
+                                                                  const __grid_constant__ CUtensorMap vmap,
+                                                                  const Args a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bar_q = reinterpret_cast<uint64_t*>(base + kOffBars);
+  uint64_t* bar_k = bar_q + 1;  // [2]
+  uint64_t* bar_v = bar_q + 3;
+  uint64_t* bar_mma = bar_q + 4;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(base + kOffMisc);
+  int* bad = reinterpret_cast<int*>(base + kOffMisc + 4);
+  const int tid = threadIdx.x, warp = tid >> 5;
+  // largest query tiles first: they carry the most keys under the causal mask
+  const int ntq = (a.P + kRows - 1) / kRows;
+  const int qt = ntq - 1 - static_cast<int>(blockIdx.x);
+  const int h = blockIdx.y, g = h / a.G;
+  const int q0 = qt * kRows;
+  const int row = q0 + tid;  // this thread's query position
+  const int nkt = qt + 1;    // key tiles 0 .. the diagonal one
+  const float NEG_INF = -__int_as_float(0x7f800000);
+
+  if (tid == 0) {
+    prefetch_tmap(&qmap);
+    prefetch_tmap(&kmap);
+    prefetch_tmap(&vmap);
+    for (int i = 0; i < 5; ++i) mbar_init(bar_q + i, 1);
+    *bad = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tslot)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+  const uint32_t tS = tmem, tO = tmem + 128;
+  const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+
+  uint8_t* sQ = base + kOffQ;
+  uint8_t* sK0 = base + kOffK0;
+  uint8_t* sK1 = base + kOffK1;
+  uint8_t* sV = base + kOffV;
+  uint8_t* sPh = base + kOffPh;
+  uint8_t* sPl = base + kOffPl;
+  const uint32_t idS = idesc(128, 128, 0), idO = idesc(128, 128, 1);
+
+  auto kbuf = [&](int buf) { return buf ? sK1 : sK0; };
+  auto load_k = [&](int kt, int buf) {
+    mbar_expect_tx(&bar_k[buf], kTile);
+    tma_load_3d(kbuf(buf), &kmap, &bar_k[buf], 0, kt * kKeys, g);
+    tma_load_3d(kbuf(buf) + kHalf, &kmap, &bar_k[buf], 64, kt * kKeys, g);
+  };
+  auto load_v = [&](int kt) {
+    mbar_expect_tx(bar_v, kTile);
+    tma_load_3d(sV, &vmap, bar_v, 0, kt * kKeys, g);
+    tma_load_3d(sV + kHalf, &vmap, bar_v, 64, kt * kKeys, g);
+  };
+  auto issue_s = [&](int buf) {  // S = Q . K^T, K = 128 dims in steps of 16
+    for (int ks = 0; ks < 8; ++ks) {
+      const uint32_t off = (ks >> 2) * kHalf + (ks & 3) * 32;
+      mma_bf16(tS, sdesc(smem_u32(sQ) + off, 16, 1024), sdesc(smem_u32(kbuf(buf)) + off, 16, 1024), idS, ks > 0);
+    }
+  };
+  uint32_t kph[2] = {0, 0}, vph = 0, mph = 0;
+  auto wait_or_fail = [&](uint64_t* bar, uint32_t ph) {
+    if (!mbar_wait_bounded(bar, ph)) {
+      set_err(a.err, kErrWaitTimeout);
+      atomicExch(bad, 1);
+    }
+  };
+  auto healthy = [&]() { return !*reinterpret_cast<volatile int*>(bad); };
+
+  if (tid == 0) {
+    mbar_expect_tx(bar_q, kTile);
+    tma_load_3d(sQ, &qmap, bar_q, 0, h, q0);
+    tma_load_3d(sQ + kHalf, &qmap, bar_q, 64, h, q0);
+    load_k(0, 0);
+    wait_or_fail(bar_q, 0);
+  }
+
+  // ---------------- pass 1: row statistics ----------------
+  float m = NEG_INF, l = 0.f;
+  for (int kt = 0; kt < nkt; ++kt) {
+    const int buf = kt & 1;
+    if (tid == 0 && healthy()) {
+      wait_or_fail(&bar_k[buf], kph[buf]);
+      tc_fence_after();
+      issue_s(buf);
+      mma_commit(bar_mma);
+      if (kt + 1 < nkt) load_k(kt + 1, buf ^ 1);  // the other buffer's MMA finished last iteration
+    }
+    kph[buf] ^= 1;
+    wait_or_fail(bar_mma, mph);
+    mph ^= 1;
+    tc_fence_after();
+    // warp-uniform: tcgen05.ld is a whole-warp instruction
+    if (__all_sync(0xffffffffu, healthy())) {
+      for (int c0 = 0; c0 < kKeys; c0 += 32) {
+        float s[32];
+        tmem_ld32(tS + lane_base + c0, s);
+        float mt = NEG_INF;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const int key = kt * kKeys + c0 + j;
+          s[j] = (key <= row && key < a.P) ? bf16r(bf16r(s[j]) * a.scale) : NEG_INF;
+          mt = fmaxf(mt, s[j]);
+        }
+        if (mt != NEG_INF) {
+          const float mn = fmaxf(m, mt);
+          float add = 0.f;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) add += (s[j] != NEG_INF) ? expf(s[j] - mn) : 0.f;
+          l = (m == NEG_INF ? 0.f : l * expf(m - mn)) + add;
+          m = mn;
+        }
+      }
+    }
+    tc_fence_before();
+    __syncthreads();  // S is read by every thread before the next tile overwrites it
+  }
+
+  // ---------------- pass 2: exact probabilities, score, O = P.V ----------------
+  if (tid == 0 && healthy()) load_k(0, 0);  // the K buffers' phases continue from pass 1
+  for (int kt = 0; kt < nkt; ++kt) {
+    const int buf = kt & 1;
+    if (tid == 0 && healthy()) {
+      wait_or_fail(&bar_k[buf], kph[buf]);
+      tc_fence_after();
+      issue_s(buf);
+      mma_commit(bar_mma);
+      load_v(kt);  // the previous tile's P.V (waited on below) no longer reads sV
+      if (kt + 1 < nkt) load_k(kt + 1, buf ^ 1);
+    }
+    kph[buf] ^= 1;
+    wait_or_fail(bar_mma, mph);
+    mph ^= 1;
+    tc_fence_after();
+    if (__all_sync(0xffffffffu, healthy())) {
+      for (int c0 = 0; c0 < kKeys; c0 += 32) {
+        float s[32];
+        tmem_ld32(tS + lane_base + c0, s);
+        uint32_t ph[16], pl[16];
+#pragma unroll
+        for (int j = 0; j < 32; j += 2) {
+          float pp[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int key = kt * kKeys + c0 + j + u;
+            float p = 0.f;
+            if (key <= row && key < a.P && row < a.P) {
+              const float sv = bf16r(bf16r(s[j + u]) * a.scale);
+              p = expf(sv - m) / l;
+            }
+            pp[u] = p;
+            // per-key maximum over this tile's rows: the warp's 32 rows, then atomicMax
+            if (a.colmax) {
+              float mx = p;
+#pragma unroll
+              for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+              if ((tid & 31) == 0 && key < a.P && mx > 0.f)
+                atomicMax(reinterpret_cast<int*>(a.colmax + key), __float_as_int(mx));
+            }
+          }
+          const float h0 = bf16r(pp[0]), h1 = bf16r(pp[1]);
+          ph[j / 2] = pack_bf16(h0, h1);
+          pl[j / 2] = pack_bf16(pp[0] - h0, pp[1] - h1);
+        }
+        // the row's 32 keys into the K-major swizzled A operand: 4 chunks of 8 keys
+        const int half = c0 >> 6;
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+          const int chunk = ((c0 & 63) >> 3) + cc;
+          const uint32_t off = half * kHalf + tid * 128 + ((chunk ^ (tid & 7)) << 4);
+          *reinterpret_cast<uint4*>(sPh + off) = make_uint4(ph[4 * cc], ph[4 * cc + 1], ph[4 * cc + 2], ph[4 * cc + 3]);
+          *reinterpret_cast<uint4*>(sPl + off) = make_uint4(pl[4 * cc], pl[4 * cc + 1], pl[4 * cc + 2], pl[4 * cc + 3]);
+        }
+      }
+    }
+    fence_proxy_async_smem();  // P is read by the tensor cores next
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0 && healthy()) {
+      wait_or_fail(bar_v, vph);
+      tc_fence_after();
+      for (int ks = 0; ks < 8; ++ks) {  // K = 128 keys in steps of 16
+        const uint32_t aoff = (ks >> 2) * kHalf + (ks & 3) * 32;
+        const uint64_t dv = sdesc(smem_u32(sV) + ks * 16 * 128, kHalf, 1024);  // MN-major V
+        mma_bf16(tO, sdesc(smem_u32(sPh) + aoff, 16, 1024), dv, idO, (kt > 0 || ks > 0));
+        mma_bf16(tO, sdesc(smem_u32(sPl) + aoff, 16, 1024), dv, idO, 1);
+      }
+      mma_commit(bar_mma);
+    }
+    vph ^= 1;
+    wait_or_fail(bar_mma, mph);  // P.V done: P, V and S may be overwritten
+    mph ^= 1;
+    tc_fence_after();
+  }
+
+  // ---------------- O -> bf16 output ----------------
+  if (__all_sync(0xffffffffu, healthy())) {
+    __nv_bfloat16* orow = a.out + (static_cast<size_t>(row) * a.Hq + h) * kD;
+    for (int c0 = 0; c0 < kD; c0 += 32) {
+      float o[32];
+      tmem_ld32(tO + lane_base + c0, o);  // every lane: the load is warp-wide
+      if (row < a.P) {
+        uint32_t w[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) w[j] = pack_bf16(o[2 * j], o[2 * j + 1]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          reinterpret_cast<uint4*>(orow + c0)[j] = make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+}
+
+}  // namespace pf
+
+// ------------------------------------------------------------------------------------
+// host side
+// ------------------------------------------------------------------------------------
+using EncodeTiledFnP = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFnP encode_fn_p() {
+  static EncodeTiledFnP fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFnP>(ptr);
+  }
+  return fn;
+}
+
+static int map3(CUtensorMap* m, const void* ptr, cuuint64_t d0, cuuint64_t d1, cuuint64_t d2, cuuint64_t s1,
+                cuuint64_t s2, cuuint32_t b1, cuuint32_t b2) {
+  EncodeTiledFnP enc = encode_fn_p();
+  if (!enc) return fail(kStatusCuda, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[3] = {d0, d1, d2};
+  cuuint64_t strides[2] = {s1, s2};
+  cuuint32_t box[3] = {64, b1, b2};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(kStatusCuda, "prefill_attn: tensor map failed (%d)", static_cast<int>(r));
+  return kStatusOk;
+}
+
+int prefill_attn(cudaStream_t stream, int P, int Hq, int Hkv, int D, const void* q, const void* kc, const void* vc,
+                 void* out, float* colmax, int* err) {
+  using namespace pf;
+  if (!q || !kc || !vc || !out) return fail(kStatusArg, "prefill_attn: null pointer");
+  if (D != kD) return fail(kStatusUnsupported, "prefill_attn: head_dim %d unsupported (only 128)", D);
+  if (P <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv) return fail(kStatusArg, "prefill_attn: bad sizes");
+  if ((P + kRows - 1) / kRows > 65535 || Hq > 65535) return fail(kStatusArg, "prefill_attn: grid too large");
+  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(kc) | reinterpret_cast<uintptr_t>(vc)) & 15)
+    return fail(kStatusArg, "prefill_attn: q, k, v must be 16-byte aligned");
+  if (reinterpret_cast<uintptr_t>(out) & 15) return fail(kStatusArg, "prefill_attn: out must be 16-byte aligned");
+  CUtensorMap qm, km, vm;
+  // q [P][Hq][128]: dims (d, head, position), one head x 128 positions per box
+  int st = map3(&qm, q, kD, Hq, P, static_cast<cuuint64_t>(kD) * 2, static_cast<cuuint64_t>(Hq) * kD * 2, 1, kRows);
+  if (st) return st;
+  // k, v [Hkv][P][128]: dims (d, position, kv head), 128 positions per box
+  st = map3(&km, kc, kD, P, Hkv, static_cast<cuuint64_t>(kD) * 2, static_cast<cuuint64_t>(P) * kD * 2, kKeys, 1);
+  if (st) return st;
+  st = map3(&vm, vc, kD, P, Hkv, static_cast<cuuint64_t>(kD) * 2, static_cast<cuuint64_t>(P) * kD * 2, kKeys, 1);
+  if (st) return st;
+  Args a;
+  a.P = P;
+  a.Hq = Hq;
+  a.Hkv = Hkv;
+  a.G = Hq / Hkv;
+  a.scale = __bfloat162float(__float2bfloat16_rn(1.0f / sqrtf(static_cast<float>(kD))));
+  a.out = static_cast<__nv_bfloat16*>(out);
+  a.colmax = colmax;
+  a.err = err;
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(prefill_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    if (e != cudaSuccess) return fail(kStatusCuda, "prefill_attn: %s", cudaGetErrorString(e));
+    configured = true;
+  }
+  dim3 grid((P + kRows - 1) / kRows, Hq);
+  prefill_attn_kernel<<<grid, kThreads, kSmem, stream>>>(qm, km, vm, a);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(kStatusCuda, "prefill_attn launch: %s", cudaGetErrorString(e));
+  return kStatusOk;
+}
+
+}  // namespace kvbp
+
+#include "../../include/kvbp.h"
+
+extern "C" int kvbp_prefill_attn_score(kvbp_stream_t stream, int32_t P, int32_t Hq, int32_t Hkv, int32_t head_dim,
+                                       const void* q, const void* kcache, const void* vcache, void* out,
+                                       float* colmax, int32_t* dev_err) {
+  return kvbp::prefill_attn(reinterpret_cast<cudaStream_t>(stream), P, Hq, Hkv, head_dim, q, kcache, vcache, out,
+                            colmax, dev_err);
+}

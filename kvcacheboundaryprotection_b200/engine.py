@@ -314,36 +314,25 @@ class CappedKVEngine:
 
     # ------------------------------------------------------------------ prefill
     def _prefill_attention(self, q, kbuf, vbuf, need_scores, colmax):
-        """Causal prefill attention with the reference's rounding points, on the GPU.
+        """Causal prefill attention with the reference's rounding points on the tcgen05
+        tensor cores (kvbp_prefill_attn_score).
 
         q [P, Hq, D] bf16; kbuf/vbuf [Hkv, P, D] bf16.  Returns [P, Hq*D] bf16 and folds
         the per-key max over heads and query rows of the probabilities into ``colmax``
         (jax_inference.py:1018-1050 with the causal mask :1169-1179, per-key max
-        :1754-1760).  Implemented with cuBLAS/torch ops (bf16 QK^T output, fp32 softmax
-        and fp32 P.V).
+        :1754-1760).
         """
         c = self.cfg
         P = q.shape[0]
-        G, D = c.group, c.head_dim
-        out = torch.empty(P, c.n_heads, D, dtype=torch.bfloat16, device=self.dev)
-        scale = torch.tensor(scale_bf16(D), dtype=torch.bfloat16, device=self.dev)
-        R = max(1, min(P, (1 << 27) // max(1, P * G * 4)))
-        cols = torch.arange(P, device=self.dev)
-        for g in range(c.n_kv_heads):
-            K = kbuf[g]
-            V = vbuf[g].float()
-            for r0 in range(0, P, R):
-                r1 = min(P, r0 + R)
-                qg = q[r0:r1, g * G : (g + 1) * G, :].reshape((r1 - r0) * G, D)
-                s = torch.matmul(qg, K[:r1].t())
-                s = (s * scale).float()
-                rows = torch.arange(r0, r1, device=self.dev).repeat_interleave(G)
-                s = s + torch.where(cols[None, :r1] > rows[:, None], -1e9, 0.0)
-                p = torch.softmax(s, dim=-1)
-                out[r0:r1, g * G : (g + 1) * G, :] = (p @ V[:r1]).reshape(r1 - r0, G, D).to(torch.bfloat16)
-                if need_scores:
-                    torch.maximum(colmax[:r1], p.amax(0), out=colmax[:r1])
-        return out.reshape(P, c.n_heads * D)
+        out = torch.empty(P, c.n_heads, c.head_dim, dtype=torch.bfloat16, device=self.dev)
+        check(
+            lib().kvbp_prefill_attn_score(
+                self.stream, P, c.n_heads, c.n_kv_heads, c.head_dim, _ptr(q), _ptr(kbuf), _ptr(vbuf), _ptr(out),
+                _ptr(colmax) if need_scores else None, _ptr(self.dev_err),
+            ),
+            "prefill_attn_score",
+        )
+        return out.reshape(P, c.n_heads * c.head_dim)
 
     def prefill(self, input_ids: torch.Tensor) -> None:
         """Step 0 for the whole batch: forward the prompts, score positions (non-LRU),
