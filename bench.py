@@ -73,6 +73,8 @@ def parse():
                     help="run only the operator microbench at this capacity (lru, protect 0.10) and exit")
     ap.add_argument("--micro-attn", action="store_true",
                     help="run only the decode attention microbench at the workload's shape and exit")
+    ap.add_argument("--micro-prefill", type=int, default=None, metavar="PROMPT_LEN",
+                    help="run only the tcgen05 prefill attention microbench at this prompt length and exit")
     ap.add_argument("--micro-gemm", action="store_true",
                     help="run only the decode GEMM microbench (one layer's projections + lm_head) and exit")
     return ap.parse_args()
@@ -619,6 +621,56 @@ def run_attn_microbench(preset="qwen2.5-7b", B=16, C=1024, E=8, layers=8, iters=
             "peak_gbs": hbm, "peak_kind": peak_kind}
 
 
+def run_prefill_microbench(preset="qwen2.5-7b", P=8192, iters=3):
+    """Operator microbench of kvbp_prefill_attn_score (tcgen05 causal prefill attention
+    with the per-key score) for one layer of one sequence at the preset's heads.
+    Algorithmic FLOPs = 4 * (P^2 / 2) * 128 * Hq (Q.K^T and P.V over the causal half);
+    the kernel executes twice that on the tensor cores (Q.K^T in both passes, P.V as bf16
+    hi + lo parts)."""
+    import torch
+
+    from kvcacheboundaryprotection_b200.capi import check, lib
+    from kvcacheboundaryprotection_b200.config import get_config
+
+    L = lib()
+    cfg = get_config(preset)
+    dev = torch.device("cuda")
+    _, tf, peak_kind = peaks()
+    Hq, Hkv, D = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
+    g = torch.Generator(device=dev).manual_seed(0)
+    q = torch.randn(P, Hq, D, generator=g, device=dev).to(torch.bfloat16)
+    k = torch.randn(Hkv, P, D, generator=g, device=dev).to(torch.bfloat16)
+    v = torch.randn(Hkv, P, D, generator=g, device=dev).to(torch.bfloat16)
+    out = torch.empty(P, Hq, D, dtype=torch.bfloat16, device=dev)
+    colmax = torch.zeros(P, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+
+    def run():
+        check(L.kvbp_prefill_attn_score(torch.cuda.current_stream().cuda_stream, P, Hq, Hkv, D, q.data_ptr(),
+                                        k.data_ptr(), v.data_ptr(), out.data_ptr(), colmax.data_ptr(),
+                                        err.data_ptr()), "prefill_attn_score")
+
+    run()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(iters):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        run()
+        e1.record()
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1))
+    if int(err.item()):
+        raise RuntimeError("device error in prefill microbench")
+    ms = statistics.median(ts)
+    alg = 4.0 * (P * P / 2.0) * D * Hq
+    return {"preset": preset, "prompt": P, "heads": [Hq, Hkv], "ms": round(ms, 3),
+            "algorithmic_tflops": round(alg / (ms * 1e-3) / 1e12, 1),
+            "tensor_tflops_executed": round(2 * alg / (ms * 1e-3) / 1e12, 1),
+            "peak_tflops": tf, "peak_kind": f"{peak_kind} dense bf16 (cuBLAS)",
+            "frac_executed": round(2 * alg / (ms * 1e-3) / 1e12 / tf, 4)}
+
+
 def run_gemm_microbench(preset="qwen2.5-7b", M=16, iters=10, sweep=False):
     """Operator microbench of kvbp_decode_gemm on one decoder layer's projections (and the
     lm_head) of ``preset``: M activation rows against bf16 weights streamed from HBM, each
@@ -887,6 +939,12 @@ def main():
         preset, B0, C0 = WORKLOADS[a.workload][:3]
         print(json.dumps(run_attn_microbench(preset, a.batch or B0, C0)), flush=True)
         return
+    if a.micro_prefill is not None:
+        from kvcacheboundaryprotection_b200 import build as kbuild
+
+        kbuild.build()
+        print(json.dumps(run_prefill_microbench(WORKLOADS[a.workload][0], a.micro_prefill)), flush=True)
+        return
     if a.micro_gemm:
         from kvcacheboundaryprotection_b200 import build as kbuild
 
@@ -914,6 +972,7 @@ def main():
             out["gemm_microbench"] = run_gemm_microbench(WORKLOADS[a.workload][0])
             preset, B0, C0 = WORKLOADS[a.workload][:3]
             out["attn_microbench"] = run_attn_microbench(preset, a.batch or B0, C0)
+            out["prefill_microbench"] = run_prefill_microbench(preset, 8192)
         if not a.no_cpu:
             times, sample = cpu_reference_step_times(a.workload, 4, 1)
             v = 1.0 / (sum(times) / len(times))

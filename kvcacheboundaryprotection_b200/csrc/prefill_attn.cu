@@ -8,14 +8,20 @@
 // Rounding points as in the decode kernel: s = bf16(bf16(q.k) * bf16(1/sqrt(128))),
 // fp32 softmax, out = bf16(sum_j p_j * fp32(v_j)), score[j] = max p[., j].
 //
-// One CTA per (128-query tile, query head); 4 warps, thread t owns query row t.
-//   pass 1: S = Q.K^T tile by tile (tcgen05.mma, M = 128 queries, N = 128 keys,
-//           K = 128 dims, bf16 in, fp32 accumulator in TMEM); each thread reads its row
-//           from TMEM and keeps the running max M and sum L of exp(s - M).
-//   pass 2: S again; p = exp(s - M) / L exactly (the final statistics are known), the
-//           per-key maximum over the tile's rows goes to the score with atomicMax, and
-//           O += P.V on the tensor cores with P split into bf16 hi + lo parts (two MMAs,
-//           ~16-bit mantissa; V is exact in bf16) and O accumulated in TMEM.
+// One CTA per (128-query tile, query head), warp-specialised:
+//   * one control warp issues the TMA loads (Q once, K tiles double-buffered, V) and the
+//     tcgen05.mma instructions, and commits them to mbarriers;
+//   * 16 softmax warps: warp w reads TMEM lanes 32*(w % 4) .. +31 (its 32 query rows) and
+//     columns 32*(w / 4) .. +31 of every score tile, so four warps share each row.
+//   pass 1: S = Q.K^T tile by tile (M = 128 queries, N = 128 keys, K = 128 dims, bf16 in,
+//           fp32 accumulator in TMEM, two S buffers so the next tile's MMA overlaps this
+//           tile's softmax work); each thread keeps the running max and sum of exp(s - M)
+//           of its row share; the four shares are merged at the end of the pass.
+//   pass 2: S again; p = exp(s - M) / L exactly (the final statistics are known); the
+//           per-key maximum over the tile's rows (a butterfly max across the warp's 32
+//           rows, then one atomicMax per key and warp) goes to the score; P is written
+//           in bf16 hi + lo parts (two MMAs, ~16-bit mantissa; V is exact in bf16) and
+//           O += P.V accumulates in TMEM.
 // Q, K and V tiles arrive by 3-D TMA (128-byte swizzle) in the K-major layout the MMA
 // descriptors describe; P is written by the threads in the same swizzled layout.  V is
 // the MN-major B operand of P.V.  K tiles are double-buffered (the next tile's load
@@ -29,10 +35,12 @@ namespace pf {
 constexpr int kRows = 128;        // queries per CTA (= TMEM lanes)
 constexpr int kKeys = 128;        // keys per tile
 constexpr int kD = 128;
-constexpr int kThreads = 128;
+constexpr int kCWarps = 16;       // softmax warps
+constexpr int kConsumers = kCWarps * 32;
+constexpr int kThreads = kConsumers + 32;  // + the control warp
 constexpr int kHalf = kRows * 128;  // one 64-column half of a [128][128] bf16 tile: 16 KiB
 constexpr int kTile = 2 * kHalf;    // 32 KiB
-constexpr int kTmemCols = 256;      // S: columns 0..127, O: columns 128..255
+constexpr int kTmemCols = 512;      // S0: 0..127, S1: 128..255, O: 256..383
 
 // smem layout (from a 1024-aligned base)
 constexpr int kOffQ = 0;
@@ -41,8 +49,9 @@ constexpr int kOffK1 = kOffK0 + kTile;
 constexpr int kOffV = kOffK1 + kTile;
 constexpr int kOffPh = kOffV + kTile;
 constexpr int kOffPl = kOffPh + kTile;
-constexpr int kOffBars = kOffPl + kTile;   // bar_q, bar_k[2], bar_v, bar_mma
-constexpr int kOffMisc = kOffBars + 64;    // tmem address, flags
+constexpr int kOffStat = kOffPl + kTile;              // float2 [4 column groups][128 rows]
+constexpr int kOffBars = kOffStat + 4 * kRows * 8;    // 12 mbarriers
+constexpr int kOffMisc = kOffBars + 128;              // tmem address, flags
 constexpr int kSmem = kOffMisc + 64 + 1024;
 
 // Shared-memory matrix descriptor: 128-byte swizzle, version 1 (tcgen05).
@@ -102,31 +111,39 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(const __grid_
                                                                   const Args a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bar_q = reinterpret_cast<uint64_t*>(base + kOffBars);
-  uint64_t* bar_k = bar_q + 1;  // [2]
-  uint64_t* bar_v = bar_q + 3;
-  uint64_t* bar_mma = bar_q + 4;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(base + kOffBars);
+  uint64_t* qfull = bars + 0;
+  uint64_t* kfull = bars + 1;   // [2] K tile landed
+  uint64_t* kfree = bars + 3;   // [2] the Q.K^T that read the K buffer is done
+  uint64_t* vfull = bars + 5;
+  uint64_t* sfull = bars + 6;   // [2] S buffer written
+  uint64_t* sfree = bars + 8;   // [2] every softmax warp has read the S buffer
+  uint64_t* pfull = bars + 10;  // every softmax warp has written its share of P
+  uint64_t* pvdone = bars + 11; // O += P.V done (P and V may be overwritten)
+  float2* stat = reinterpret_cast<float2*>(base + kOffStat);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(base + kOffMisc);
   int* bad = reinterpret_cast<int*>(base + kOffMisc + 4);
-  const int tid = threadIdx.x, warp = tid >> 5;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   // largest query tiles first: they carry the most keys under the causal mask
   const int ntq = (a.P + kRows - 1) / kRows;
   const int qt = ntq - 1 - static_cast<int>(blockIdx.x);
   const int h = blockIdx.y, g = h / a.G;
   const int q0 = qt * kRows;
-  const int row = q0 + tid;  // this thread's query position
-  const int nkt = qt + 1;    // key tiles 0 .. the diagonal one
+  const int nkt = qt + 1;  // key tiles 0 .. the diagonal one
+  const int T = 2 * nkt;   // S tiles over both passes
   const float NEG_INF = -__int_as_float(0x7f800000);
 
   if (tid == 0) {
-    prefetch_tmap(&qmap);
-    prefetch_tmap(&kmap);
-    prefetch_tmap(&vmap);
-    for (int i = 0; i < 5; ++i) mbar_init(bar_q + i, 1);
+    for (int i = 0; i < 12; ++i) mbar_init(bars + i, (i == 8 || i == 9 || i == 10) ? kCWarps : 1);
     *bad = 0;
     fence_barrier_init();
   }
-  if (warp == 0) {
+  if (warp == kCWarps) {
+    if (lane == 0) {
+      prefetch_tmap(&qmap);
+      prefetch_tmap(&kmap);
+      prefetch_tmap(&vmap);
+    }
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tslot)),
                  "r"(kTmemCols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
@@ -135,188 +152,203 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(const __grid_
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tslot;
-  const uint32_t tS = tmem, tO = tmem + 128;
-  const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
-
+  const uint32_t tO = tmem + 256;
   uint8_t* sQ = base + kOffQ;
-  uint8_t* sK0 = base + kOffK0;
-  uint8_t* sK1 = base + kOffK1;
   uint8_t* sV = base + kOffV;
   uint8_t* sPh = base + kOffPh;
   uint8_t* sPl = base + kOffPl;
-  const uint32_t idS = idesc(128, 128, 0), idO = idesc(128, 128, 1);
-
-  auto kbuf = [&](int buf) { return buf ? sK1 : sK0; };
-  auto load_k = [&](int kt, int buf) {
-    mbar_expect_tx(&bar_k[buf], kTile);
-    tma_load_3d(kbuf(buf), &kmap, &bar_k[buf], 0, kt * kKeys, g);
-    tma_load_3d(kbuf(buf) + kHalf, &kmap, &bar_k[buf], 64, kt * kKeys, g);
-  };
-  auto load_v = [&](int kt) {
-    mbar_expect_tx(bar_v, kTile);
-    tma_load_3d(sV, &vmap, bar_v, 0, kt * kKeys, g);
-    tma_load_3d(sV + kHalf, &vmap, bar_v, 64, kt * kKeys, g);
-  };
-  auto issue_s = [&](int buf) {  // S = Q . K^T, K = 128 dims in steps of 16
-    for (int ks = 0; ks < 8; ++ks) {
-      const uint32_t off = (ks >> 2) * kHalf + (ks & 3) * 32;
-      mma_bf16(tS, sdesc(smem_u32(sQ) + off, 16, 1024), sdesc(smem_u32(kbuf(buf)) + off, 16, 1024), idS, ks > 0);
-    }
-  };
-  uint32_t kph[2] = {0, 0}, vph = 0, mph = 0;
+  auto kbuf = [&](int b) { return base + (b ? kOffK1 : kOffK0); };
+  auto healthy = [&]() { return !*reinterpret_cast<volatile int*>(bad); };
   auto wait_or_fail = [&](uint64_t* bar, uint32_t ph) {
     if (!mbar_wait_bounded(bar, ph)) {
       set_err(a.err, kErrWaitTimeout);
       atomicExch(bad, 1);
     }
   };
-  auto healthy = [&]() { return !*reinterpret_cast<volatile int*>(bad); };
 
-  if (tid == 0) {
-    mbar_expect_tx(bar_q, kTile);
-    tma_load_3d(sQ, &qmap, bar_q, 0, h, q0);
-    tma_load_3d(sQ + kHalf, &qmap, bar_q, 64, h, q0);
-    load_k(0, 0);
-    wait_or_fail(bar_q, 0);
-  }
-
-  // ---------------- pass 1: row statistics ----------------
-  float m = NEG_INF, l = 0.f;
-  for (int kt = 0; kt < nkt; ++kt) {
-    const int buf = kt & 1;
-    if (tid == 0 && healthy()) {
-      wait_or_fail(&bar_k[buf], kph[buf]);
-      tc_fence_after();
-      issue_s(buf);
-      mma_commit(bar_mma);
-      if (kt + 1 < nkt) load_k(kt + 1, buf ^ 1);  // the other buffer's MMA finished last iteration
+  // =============================== control warp =====================================
+  if (warp == kCWarps) {
+    if (lane == 0) {
+      const uint32_t idS = idesc(128, 128, 0), idO = idesc(128, 128, 1);
+      auto key_tile = [&](int j) { return j < nkt ? j : j - nkt; };
+      auto issue_k = [&](int j) {  // K tile of S-tile j into buffer j & 1
+        const int b = j & 1;
+        if (j >= 2) wait_or_fail(&kfree[b], ((j >> 1) - 1) & 1);
+        mbar_expect_tx(&kfull[b], kTile);
+        tma_load_3d(kbuf(b), &kmap, &kfull[b], 0, key_tile(j) * kKeys, g);
+        tma_load_3d(kbuf(b) + kHalf, &kmap, &kfull[b], 64, key_tile(j) * kKeys, g);
+      };
+      auto issue_s = [&](int j) {  // S-tile j = Q . K^T into S buffer j & 1
+        const int b = j & 1;
+        wait_or_fail(&kfull[b], (j >> 1) & 1);
+        if (j >= 2) wait_or_fail(&sfree[b], ((j >> 1) - 1) & 1);
+        tc_fence_after();
+        for (int ks = 0; ks < 8; ++ks) {
+          const uint32_t off = (ks >> 2) * kHalf + (ks & 3) * 32;
+          mma_bf16(tmem + b * 128, sdesc(smem_u32(sQ) + off, 16, 1024), sdesc(smem_u32(kbuf(b)) + off, 16, 1024),
+                   idS, ks > 0);
+        }
+        mma_commit(&sfull[b]);
+        mma_commit(&kfree[b]);
+      };
+      mbar_expect_tx(qfull, kTile);
+      tma_load_3d(sQ, &qmap, qfull, 0, h, q0);
+      tma_load_3d(sQ + kHalf, &qmap, qfull, 64, h, q0);
+      issue_k(0);
+      if (T > 1) issue_k(1);
+      wait_or_fail(qfull, 0);
+      if (healthy()) issue_s(0);
+      for (int j = 0; j < T && healthy(); ++j) {
+        if (j + 1 < T) issue_s(j + 1);
+        if (j + 2 < T) issue_k(j + 2);
+        if (j >= nkt) {  // pass 2: O += P.V for key tile kt
+          const int kt = j - nkt;
+          if (kt > 0) wait_or_fail(pvdone, (kt - 1) & 1);  // the V buffer is free
+          mbar_expect_tx(vfull, kTile);
+          tma_load_3d(sV, &vmap, vfull, 0, kt * kKeys, g);
+          tma_load_3d(sV + kHalf, &vmap, vfull, 64, kt * kKeys, g);
+          wait_or_fail(pfull, kt & 1);
+          wait_or_fail(vfull, kt & 1);
+          tc_fence_after();
+          for (int ks = 0; ks < 8; ++ks) {  // K = 128 keys in steps of 16
+            const uint32_t aoff = (ks >> 2) * kHalf + (ks & 3) * 32;
+            const uint64_t dv = sdesc(smem_u32(sV) + ks * 16 * 128, kHalf, 1024);  // MN-major V
+            mma_bf16(tO, sdesc(smem_u32(sPh) + aoff, 16, 1024), dv, idO, (kt > 0 || ks > 0));
+            mma_bf16(tO, sdesc(smem_u32(sPl) + aoff, 16, 1024), dv, idO, 1);
+          }
+          mma_commit(pvdone);
+        }
+      }
     }
-    kph[buf] ^= 1;
-    wait_or_fail(bar_mma, mph);
-    mph ^= 1;
-    tc_fence_after();
-    // warp-uniform: tcgen05.ld is a whole-warp instruction
-    if (__all_sync(0xffffffffu, healthy())) {
-      for (int c0 = 0; c0 < kKeys; c0 += 32) {
-        float s[32];
-        tmem_ld32(tS + lane_base + c0, s);
+    __syncwarp();
+  } else {
+    // =============================== softmax warps ====================================
+    const int lg = warp & 3, cg = warp >> 2;
+    const int rloc = lg * 32 + lane;  // TMEM lane = query row within the tile
+    const int row = q0 + rloc;
+    const uint32_t lane_base = static_cast<uint32_t>(lg * 32) << 16;
+    float m = NEG_INF, l = 0.f;
+    // ---- pass 1: row statistics over this warp's columns
+    for (int j = 0; j < nkt; ++j) {
+      const int b = j & 1;
+      wait_or_fail(&sfull[b], (j >> 1) & 1);
+      tc_fence_after();
+      float s[32];
+      const bool ok = __all_sync(0xffffffffu, healthy());
+      if (ok) tmem_ld32(tmem + b * 128 + lane_base + cg * 32, s);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sfree[b]);
+      if (ok) {
         float mt = NEG_INF;
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const int key = kt * kKeys + c0 + j;
-          s[j] = (key <= row && key < a.P) ? bf16r(bf16r(s[j]) * a.scale) : NEG_INF;
-          mt = fmaxf(mt, s[j]);
+        for (int i = 0; i < 32; ++i) {
+          const int key = j * kKeys + cg * 32 + i;
+          s[i] = (key <= row && key < a.P) ? bf16r(bf16r(s[i]) * a.scale) : NEG_INF;
+          mt = fmaxf(mt, s[i]);
         }
         if (mt != NEG_INF) {
           const float mn = fmaxf(m, mt);
           float add = 0.f;
 #pragma unroll
-          for (int j = 0; j < 32; ++j) add += (s[j] != NEG_INF) ? expf(s[j] - mn) : 0.f;
+          for (int i = 0; i < 32; ++i) add += (s[i] != NEG_INF) ? expf(s[i] - mn) : 0.f;
           l = (m == NEG_INF ? 0.f : l * expf(m - mn)) + add;
           m = mn;
         }
       }
     }
-    tc_fence_before();
-    __syncthreads();  // S is read by every thread before the next tile overwrites it
-  }
-
-  // ---------------- pass 2: exact probabilities, score, O = P.V ----------------
-  if (tid == 0 && healthy()) load_k(0, 0);  // the K buffers' phases continue from pass 1
-  for (int kt = 0; kt < nkt; ++kt) {
-    const int buf = kt & 1;
-    if (tid == 0 && healthy()) {
-      wait_or_fail(&bar_k[buf], kph[buf]);
-      tc_fence_after();
-      issue_s(buf);
-      mma_commit(bar_mma);
-      load_v(kt);  // the previous tile's P.V (waited on below) no longer reads sV
-      if (kt + 1 < nkt) load_k(kt + 1, buf ^ 1);
+    // ---- merge the four column groups' statistics of each row
+    stat[cg * kRows + rloc] = make_float2(m, l);
+    named_bar(1, kConsumers);
+    {
+      float M = NEG_INF;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) M = fmaxf(M, stat[c * kRows + rloc].x);
+      float Ls = 0.f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const float2 st = stat[c * kRows + rloc];
+        if (st.x != NEG_INF) Ls += st.y * expf(st.x - M);
+      }
+      m = M;
+      l = Ls;
     }
-    kph[buf] ^= 1;
-    wait_or_fail(bar_mma, mph);
-    mph ^= 1;
+    // ---- pass 2: exact probabilities, per-key score, P for the tensor cores
+    for (int kt = 0; kt < nkt; ++kt) {
+      const int j = nkt + kt, b = j & 1;
+      wait_or_fail(&sfull[b], (j >> 1) & 1);
+      tc_fence_after();
+      float s[32];
+      const bool ok = __all_sync(0xffffffffu, healthy());
+      if (ok) tmem_ld32(tmem + b * 128 + lane_base + cg * 32, s);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sfree[b]);
+      float p[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int key = kt * kKeys + cg * 32 + i;
+        p[i] = (ok && key <= row && key < a.P && row < a.P) ? expf(bf16r(bf16r(s[i]) * a.scale) - m) / l : 0.f;
+      }
+      if (a.colmax) {
+        // butterfly max across the warp's 32 rows: afterwards lane i holds the maximum of
+        // key (tile column cg * 32 + i)
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = p[i];
+#pragma unroll
+        for (int sft = 16; sft >= 1; sft >>= 1) {
+          const bool upper = (lane & sft) != 0;
+#pragma unroll
+          for (int i = 0; i < sft; ++i) {
+            const float send = upper ? v[i] : v[i + sft];
+            const float keep = upper ? v[i + sft] : v[i];
+            v[i] = fmaxf(keep, __shfl_xor_sync(0xffffffffu, send, sft));
+          }
+        }
+        const int key = kt * kKeys + cg * 32 + lane;
+        if (ok && key < a.P && v[0] > 0.f) atomicMax(reinterpret_cast<int*>(a.colmax + key), __float_as_int(v[0]));
+      }
+      if (kt > 0) wait_or_fail(pvdone, (kt - 1) & 1);  // the previous P.V has read P
+      uint32_t ph[16], pl[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float h0 = bf16r(p[2 * i]), h1 = bf16r(p[2 * i + 1]);
+        ph[i] = pack_bf16(h0, h1);
+        pl[i] = pack_bf16(p[2 * i] - h0, p[2 * i + 1] - h1);
+      }
+      // the row's 32 keys into the K-major swizzled A operand: 4 chunks of 8 keys
+      const int half = cg >> 1;
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) {
+        const int chunk = (cg & 1) * 4 + cc;
+        const uint32_t off = half * kHalf + rloc * 128 + ((chunk ^ (rloc & 7)) << 4);
+        *reinterpret_cast<uint4*>(sPh + off) = make_uint4(ph[4 * cc], ph[4 * cc + 1], ph[4 * cc + 2], ph[4 * cc + 3]);
+        *reinterpret_cast<uint4*>(sPl + off) = make_uint4(pl[4 * cc], pl[4 * cc + 1], pl[4 * cc + 2], pl[4 * cc + 3]);
+      }
+      fence_proxy_async_smem();  // P is read by the tensor cores next
+      __syncwarp();
+      if (lane == 0) mbar_arrive(pfull);
+    }
+    // ---- O -> bf16 output (this warp's 32 of the 128 dims)
+    wait_or_fail(pvdone, (nkt - 1) & 1);
     tc_fence_after();
     if (__all_sync(0xffffffffu, healthy())) {
-      for (int c0 = 0; c0 < kKeys; c0 += 32) {
-        float s[32];
-        tmem_ld32(tS + lane_base + c0, s);
-        uint32_t ph[16], pl[16];
-#pragma unroll
-        for (int j = 0; j < 32; j += 2) {
-          float pp[2];
-#pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const int key = kt * kKeys + c0 + j + u;
-            float p = 0.f;
-            if (key <= row && key < a.P && row < a.P) {
-              const float sv = bf16r(bf16r(s[j + u]) * a.scale);
-              p = expf(sv - m) / l;
-            }
-            pp[u] = p;
-            // per-key maximum over this tile's rows: the warp's 32 rows, then atomicMax
-            if (a.colmax) {
-              float mx = p;
-#pragma unroll
-              for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-              if ((tid & 31) == 0 && key < a.P && mx > 0.f)
-                atomicMax(reinterpret_cast<int*>(a.colmax + key), __float_as_int(mx));
-            }
-          }
-          const float h0 = bf16r(pp[0]), h1 = bf16r(pp[1]);
-          ph[j / 2] = pack_bf16(h0, h1);
-          pl[j / 2] = pack_bf16(pp[0] - h0, pp[1] - h1);
-        }
-        // the row's 32 keys into the K-major swizzled A operand: 4 chunks of 8 keys
-        const int half = c0 >> 6;
-#pragma unroll
-        for (int cc = 0; cc < 4; ++cc) {
-          const int chunk = ((c0 & 63) >> 3) + cc;
-          const uint32_t off = half * kHalf + tid * 128 + ((chunk ^ (tid & 7)) << 4);
-          *reinterpret_cast<uint4*>(sPh + off) = make_uint4(ph[4 * cc], ph[4 * cc + 1], ph[4 * cc + 2], ph[4 * cc + 3]);
-          *reinterpret_cast<uint4*>(sPl + off) = make_uint4(pl[4 * cc], pl[4 * cc + 1], pl[4 * cc + 2], pl[4 * cc + 3]);
-        }
-      }
-    }
-    fence_proxy_async_smem();  // P is read by the tensor cores next
-    tc_fence_before();
-    __syncthreads();
-    if (tid == 0 && healthy()) {
-      wait_or_fail(bar_v, vph);
-      tc_fence_after();
-      for (int ks = 0; ks < 8; ++ks) {  // K = 128 keys in steps of 16
-        const uint32_t aoff = (ks >> 2) * kHalf + (ks & 3) * 32;
-        const uint64_t dv = sdesc(smem_u32(sV) + ks * 16 * 128, kHalf, 1024);  // MN-major V
-        mma_bf16(tO, sdesc(smem_u32(sPh) + aoff, 16, 1024), dv, idO, (kt > 0 || ks > 0));
-        mma_bf16(tO, sdesc(smem_u32(sPl) + aoff, 16, 1024), dv, idO, 1);
-      }
-      mma_commit(bar_mma);
-    }
-    vph ^= 1;
-    wait_or_fail(bar_mma, mph);  // P.V done: P, V and S may be overwritten
-    mph ^= 1;
-    tc_fence_after();
-  }
-
-  // ---------------- O -> bf16 output ----------------
-  if (__all_sync(0xffffffffu, healthy())) {
-    __nv_bfloat16* orow = a.out + (static_cast<size_t>(row) * a.Hq + h) * kD;
-    for (int c0 = 0; c0 < kD; c0 += 32) {
       float o[32];
-      tmem_ld32(tO + lane_base + c0, o);  // every lane: the load is warp-wide
+      tmem_ld32(tO + lane_base + cg * 32, o);
       if (row < a.P) {
         uint32_t w[16];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) w[j] = pack_bf16(o[2 * j], o[2 * j + 1]);
+        for (int i = 0; i < 16; ++i) w[i] = pack_bf16(o[2 * i], o[2 * i + 1]);
+        uint4* dst = reinterpret_cast<uint4*>(a.out + (static_cast<size_t>(row) * a.Hq + h) * kD + cg * 32);
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
-          reinterpret_cast<uint4*>(orow + c0)[j] = make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+        for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
       }
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+  if (warp == kCWarps) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
 }
 
 }  // namespace pf
