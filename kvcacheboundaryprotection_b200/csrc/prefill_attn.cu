@@ -17,7 +17,8 @@
 //           fp32 accumulator in TMEM, two S buffers so the next tile's MMA overlaps this
 //           tile's softmax work); each thread keeps the running max and sum of exp(s - M)
 //           of its row share; the four shares are merged at the end of the pass.
-//   pass 2: S again; p = exp(s - M) / L exactly (the final statistics are known); the
+//   pass 2: S again; p = exp(s - M) / L (the final statistics are known; the exponential
+//           is the fast hardware one, relative error ~1e-6, and 1/L is formed once); the
 //           per-key maximum over the tile's rows (a butterfly max across the warp's 32
 //           rows, then one atomicMax per key and warp) goes to the score; P is written
 //           in bf16 hi + lo parts (two MMAs, ~16-bit mantissa; V is exact in bf16) and
@@ -251,8 +252,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(const __grid_
           const float mn = fmaxf(m, mt);
           float add = 0.f;
 #pragma unroll
-          for (int i = 0; i < 32; ++i) add += (s[i] != NEG_INF) ? expf(s[i] - mn) : 0.f;
-          l = (m == NEG_INF ? 0.f : l * expf(m - mn)) + add;
+          for (int i = 0; i < 32; ++i) add += (s[i] != NEG_INF) ? __expf(s[i] - mn) : 0.f;
+          l = (m == NEG_INF ? 0.f : l * __expf(m - mn)) + add;
           m = mn;
         }
       }
@@ -268,10 +269,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(const __grid_
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         const float2 st = stat[c * kRows + rloc];
-        if (st.x != NEG_INF) Ls += st.y * expf(st.x - M);
+        if (st.x != NEG_INF) Ls += st.y * __expf(st.x - M);
       }
       m = M;
-      l = Ls;
+      l = 1.0f / Ls;  // from here on: the reciprocal of the row sum
     }
     // ---- pass 2: exact probabilities, per-key score, P for the tensor cores
     for (int kt = 0; kt < nkt; ++kt) {
@@ -288,7 +289,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(const __grid_
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
         const int key = kt * kKeys + cg * 32 + i;
-        p[i] = (ok && key <= row && key < a.P && row < a.P) ? expf(bf16r(bf16r(s[i]) * a.scale) - m) / l : 0.f;
+        p[i] = (ok && key <= row && key < a.P && row < a.P) ? __expf(bf16r(bf16r(s[i]) * a.scale) - m) * l : 0.f;
       }
       if (a.colmax) {
         // butterfly max across the warp's 32 rows: afterwards lane i holds the maximum of
