@@ -94,58 +94,83 @@ __global__ void add_rmsnorm_kernel(__nv_bfloat16* __restrict__ h, const __nv_bfl
 }
 
 // ---- QKV epilogue -----------------------------------------------------------------
-// Block (row, head) of 64 threads; thread i owns the RoPE pair (i, i + 64).
-__global__ void qkv_epilogue_kernel(const __nv_bfloat16* __restrict__ qkv, int ldq,
-                                    const __nv_bfloat16* __restrict__ bias, const __nv_bfloat16* __restrict__ qnw,
-                                    const __nv_bfloat16* __restrict__ knw, float eps,
-                                    const float* __restrict__ inv_freq, const int* __restrict__ positions,
-                                    const int* __restrict__ write_slot, int rows_per_seq, int Hq, int Hkv, int S,
-                                    __nv_bfloat16* __restrict__ q_out, __nv_bfloat16* __restrict__ kcache,
-                                    __nv_bfloat16* __restrict__ vcache, int* err) {
+// One block (8 warps) per row.  The row's RoPE cos/sin (64 frequencies) are formed once in
+// shared memory; warp w finishes heads w, w + 8, ...; lane l owns the RoPE pairs
+// (l, l + 64) and (l + 32, l + 96) of the head.
+__global__ void __launch_bounds__(256) qkv_epilogue_kernel(
+    const __nv_bfloat16* __restrict__ qkv, int ldq, const __nv_bfloat16* __restrict__ bias,
+    const __nv_bfloat16* __restrict__ qnw, const __nv_bfloat16* __restrict__ knw, float eps,
+    const float* __restrict__ inv_freq, const int* __restrict__ positions, const int* __restrict__ write_slot,
+    int rows_per_seq, int Hq, int Hkv, int S, __nv_bfloat16* __restrict__ q_out, __nv_bfloat16* __restrict__ kcache,
+    __nv_bfloat16* __restrict__ vcache, int* err) {
   pdl_launch_dependents();
   pdl_wait();
-  __shared__ float red[32];
-  const int r = blockIdx.x, hh = blockIdx.y, i = threadIdx.x;
-  const __nv_bfloat16* src = qkv + static_cast<size_t>(r) * ldq + hh * 128;
-  float x0 = __bfloat162float(src[i]);
-  float x1 = __bfloat162float(src[i + 64]);
-  if (bias) {
-    x0 = bf16r(x0 + __bfloat162float(bias[hh * 128 + i]));
-    x1 = bf16r(x1 + __bfloat162float(bias[hh * 128 + i + 64]));
+  __shared__ float cs[64], sn[64];
+  const int r = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (tid < 64) {
+    const float ang = static_cast<float>(positions[r]) * inv_freq[tid];
+    cs[tid] = bf16r(cosf(ang));
+    sn[tid] = bf16r(sinf(ang));
   }
-  const bool is_q = hh < Hq, is_k = !is_q && hh < Hq + Hkv;
-  if (is_q || is_k) {
-    const __nv_bfloat16* nw = is_q ? qnw : knw;
-    if (nw) {  // block-uniform branch
-      const float ss = block_sum(x0 * x0 + x1 * x1, red);
-      const float inv = 1.0f / sqrtf(ss / 128.0f + eps);
-      x0 = bf16r((x0 * inv) * __bfloat162float(nw[i]));
-      x1 = bf16r((x1 * inv) * __bfloat162float(nw[i + 64]));
-    }
-    const float ang = static_cast<float>(positions[r]) * inv_freq[i];
-    const float c = bf16r(cosf(ang)), s = bf16r(sinf(ang));
-    const float y0 = bf16r(bf16r(x0 * c) - bf16r(x1 * s));
-    const float y1 = bf16r(bf16r(x1 * c) + bf16r(x0 * s));
-    x0 = y0;
-    x1 = y1;
-  }
-  if (is_q) {
-    __nv_bfloat16* dst = q_out + (static_cast<size_t>(r) * Hq + hh) * 128;
-    dst[i] = __float2bfloat16_rn(x0);
-    dst[i + 64] = __float2bfloat16_rn(x1);
-    return;
-  }
+  __syncthreads();
   const int slot = write_slot[r];
-  if (slot < 0) return;  // position evicted before its forward: nothing to store
-  if (slot >= S) {
-    set_err(err, kErrIndex);
-    return;
-  }
-  const int kvh = is_k ? hh - Hq : hh - Hq - Hkv;
   const int seq = r / rows_per_seq;
-  __nv_bfloat16* dst = (is_k ? kcache : vcache) + ((static_cast<size_t>(seq) * Hkv + kvh) * S + slot) * 128;
-  dst[i] = __float2bfloat16_rn(x0);
-  dst[i + 64] = __float2bfloat16_rn(x1);
+  const int nh = Hq + 2 * Hkv;
+  for (int hh = warp; hh < nh; hh += 8) {
+    const __nv_bfloat16* src = qkv + static_cast<size_t>(r) * ldq + hh * 128;
+    float x0[2], x1[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int i = lane + 32 * u;
+      x0[u] = __bfloat162float(src[i]);
+      x1[u] = __bfloat162float(src[i + 64]);
+      if (bias) {
+        x0[u] = bf16r(x0[u] + __bfloat162float(bias[hh * 128 + i]));
+        x1[u] = bf16r(x1[u] + __bfloat162float(bias[hh * 128 + i + 64]));
+      }
+    }
+    const bool is_q = hh < Hq, is_k = !is_q && hh < Hq + Hkv;
+    if (is_q || is_k) {
+      const __nv_bfloat16* nw = is_q ? qnw : knw;
+      if (nw) {  // warp-uniform branch: RMSNorm over the head's 128 features
+        const float ss = warp_sum(x0[0] * x0[0] + x1[0] * x1[0] + x0[1] * x0[1] + x1[1] * x1[1]);
+        const float inv = 1.0f / sqrtf(ss / 128.0f + eps);
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int i = lane + 32 * u;
+          x0[u] = bf16r((x0[u] * inv) * __bfloat162float(nw[i]));
+          x1[u] = bf16r((x1[u] * inv) * __bfloat162float(nw[i + 64]));
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int i = lane + 32 * u;
+        const float c = cs[i], sv = sn[i];
+        const float y0 = bf16r(bf16r(x0[u] * c) - bf16r(x1[u] * sv));
+        const float y1 = bf16r(bf16r(x1[u] * c) + bf16r(x0[u] * sv));
+        x0[u] = y0;
+        x1[u] = y1;
+      }
+    }
+    __nv_bfloat16* dst;
+    if (is_q) {
+      dst = q_out + (static_cast<size_t>(r) * Hq + hh) * 128;
+    } else {
+      if (slot < 0) continue;  // position evicted before its forward: nothing to store
+      if (slot >= S) {
+        if (lane == 0) set_err(err, kErrIndex);
+        continue;
+      }
+      const int kvh = is_k ? hh - Hq : hh - Hq - Hkv;
+      dst = (is_k ? kcache : vcache) + ((static_cast<size_t>(seq) * Hkv + kvh) * S + slot) * 128;
+    }
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int i = lane + 32 * u;
+      dst[i] = __float2bfloat16_rn(x0[u]);
+      dst[i + 64] = __float2bfloat16_rn(x1[u]);
+    }
+  }
 }
 
 // ---- SwiGLU: act = bf16(bf16(g * bf16(sigmoid(g))) * u) -------------------------------
@@ -307,8 +332,7 @@ int qkv_epilogue(cudaStream_t st, int rows, int rows_per_seq, int Hq, int Hkv, i
   if (rows <= 0 || rows_per_seq <= 0 || Hq <= 0 || Hkv <= 0 || S <= 0 || ldq < (Hq + 2 * Hkv) * D)
     return fail(kStatusArg, "qkv_epilogue: bad size");
   if ((Hq + 2 * Hkv) > 65535) return fail(kStatusArg, "qkv_epilogue: too many heads");
-  dim3 grid(rows, Hq + 2 * Hkv);
-  const cudaError_t le = launch_pdl(qkv_epilogue_kernel, grid, dim3(64), 0, st, dim3(0), 
+  const cudaError_t le = launch_pdl(qkv_epilogue_kernel, dim3(rows), dim3(256), 0, st, dim3(0),
       static_cast<const __nv_bfloat16*>(qkv), ldq, static_cast<const __nv_bfloat16*>(bias),
       static_cast<const __nv_bfloat16*>(qnw), static_cast<const __nv_bfloat16*>(knw), eps, inv_freq, positions,
       write_slot, rows_per_seq, Hq, Hkv, S, static_cast<__nv_bfloat16*>(q_out), static_cast<__nv_bfloat16*>(kcache),

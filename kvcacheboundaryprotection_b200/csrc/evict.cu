@@ -203,6 +203,19 @@ __device__ KeySlot take_min(int S, uint32_t& taken, KeyF keyf, EligF elig, KeySl
   return w;
 }
 
+// This thread's smallest (key, slot) among its eligible slots not yet taken.
+template <typename KeyF, typename EligF>
+__device__ KeySlot local_min(int S, uint32_t taken, KeyF keyf, EligF elig) {
+  KeySlot best{key_max(), 0x7fffffff};
+  for (int j = 0, i = threadIdx.x; i < S; ++j, i += kEvictThreads) {
+    if ((taken >> j) & 1u) continue;
+    if (!elig(i)) continue;
+    const KeySlot c{keyf(i), i};
+    if (ks_less(c, best)) best = c;
+  }
+  return best;
+}
+
 // Position of the k-th (0-based) set bit of the W-word bitmap; INT_MAX if none.
 // Executed by one full warp.
 __device__ int select_bit_warp(const uint32_t* words, int W, int k) {
@@ -454,9 +467,16 @@ __global__ void __launch_bounds__(kEvictThreads) append_evict_kernel(AppendArgs 
           return policy_key(a.policy, step, s.slot_pos[i], s.insert_step[i], s.last_access[i], s.attn[i],
                             s.max_attn[i], s.cumul[i], s.prefill[i], a.err);
         };
+        // k rounds of block argmin; a thread's local minimum changes only when it owned
+        // the winner, so only that thread rescans its slots
         uint32_t taken = 0;
+        KeySlot mine = local_min(S, taken, pkey, elig);
         for (int r = 0; r < k; ++r) {
-          const KeySlot w = take_min(S, taken, pkey, elig, red_k);
+          const KeySlot w = block_argmin(mine, red_k);
+          if (w.slot != 0x7fffffff && (w.slot % kEvictThreads) == tid) {
+            taken |= 1u << (w.slot / kEvictThreads);
+            mine = local_min(S, taken, pkey, elig);
+          }
           if (tid == 0) s_vict[n_vict] = w.slot;
           ++n_vict;
         }
