@@ -17,12 +17,17 @@
 //           fp32 accumulator in TMEM, two S buffers so the next tile's MMA overlaps this
 //           tile's softmax work); each thread keeps the running max and sum of exp(s - M)
 //           of its row share; the four shares are merged at the end of the pass.
-//   pass 2: S again; p = exp(s - M) / L (the final statistics are known; the exponential
-//           is the fast hardware one, relative error ~1e-6, and 1/L is formed once); the
-//           per-key maximum over the tile's rows (a butterfly max across the warp's 32
-//           rows, then one atomicMax per key and warp) goes to the score; P is written
+//   pass 2: S again; p = exp(s - M) / L (the final statistics are known; exp is the
+//           hardware 2^x of s * log2(e) - M * log2(e), one FFMA and one MUFU op, relative
+//           error ~1e-6 for |s| < 30, and 1/L is formed once); the
+//           per-key maximum over the tile's rows (a warp max reduction per key across
+//           the warp's 32 rows, then one atomicMax per key and warp) goes to the score; P is written
 //           in bf16 hi + lo parts (two MMAs, ~16-bit mantissa; V is exact in bf16) and
 //           O += P.V accumulates in TMEM.
+// The softmax warps' element work is spread over the FP32, integer and MUFU pipes: the
+// bf16 roundings are Veltkamp splits on the FP32 pipe (three instructions each, instead
+// of a conversion on the quarter-rate conversion pipe), packing is a byte permute, and
+// the causal / tail masks are applied only to the blocks that straddle them.
 // Q, K and V tiles arrive by 3-D TMA (128-byte swizzle) in the K-major layout the MMA
 // descriptors describe; P is written by the threads in the same swizzled layout.  V is
 // the MN-major B operand of P.V.  K tiles are double-buffered (the next tile's load
@@ -93,6 +98,27 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
   for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+}
+
+// bf16 round-to-nearest-even of an fp32 value on the FP32 pipe: Veltkamp splitting with
+// sigma = 2^16 + 1 keeps the leading 8 significand bits, rounded to nearest with ties to
+// even (checked bit for bit against the bf16 conversion over whole binades).  The _rn
+// intrinsics keep the three steps from being contracted into an FMA.  Finite |x| < 2^111.
+__device__ __forceinline__ float rnd_bf16(float x) {
+  const float g = __fmul_rn(65537.0f, x);
+  return __fadd_rn(g, __fsub_rn(x, g));
+}
+
+// 2^x (the hardware approximation; -inf gives +0)
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// the upper halves of two fp32 words packed as bf16x2 (a in the low half)
+__device__ __forceinline__ uint32_t hi_halves(float a, float b) {
+  return __byte_perm(__float_as_uint(a), __float_as_uint(b), 0x7632);
 }
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
@@ -228,6 +254,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(const __grid_
     const int rloc = lg * 32 + lane;  // TMEM lane = query row within the tile
     const int row = q0 + rloc;
     const uint32_t lane_base = static_cast<uint32_t>(lg * 32) << 16;
+    const int rmin = q0 + lg * 32;             // this warp's rows: rmin .. rmin + 31
+    const bool rows_in = rmin + 31 < a.P;
+    constexpr float kLog2e = 1.4426950408889634f;
     float m = NEG_INF, l = 0.f;
     // ---- pass 1: row statistics over this warp's columns
     for (int j = 0; j < nkt; ++j) {
@@ -241,19 +270,29 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(const __grid_
       __syncwarp();
       if (lane == 0) mbar_arrive(&sfree[b]);
       if (ok) {
+        const int kb = j * kKeys + cg * 32;
         float mt = NEG_INF;
+        if (kb + 31 <= rmin && rows_in) {  // warp-uniform: no key of the block is masked
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int key = j * kKeys + cg * 32 + i;
-          s[i] = (key <= row && key < a.P) ? bf16r(bf16r(s[i]) * a.scale) : NEG_INF;
-          mt = fmaxf(mt, s[i]);
+          for (int i = 0; i < 32; ++i) {
+            s[i] = rnd_bf16(rnd_bf16(s[i]) * a.scale);
+            mt = fmaxf(mt, s[i]);
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int key = kb + i;
+            s[i] = (key <= row && key < a.P) ? rnd_bf16(rnd_bf16(s[i]) * a.scale) : NEG_INF;
+            mt = fmaxf(mt, s[i]);
+          }
         }
         if (mt != NEG_INF) {
           const float mn = fmaxf(m, mt);
-          float add = 0.f;
+          const float mL = mn * kLog2e;
+          float add[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-          for (int i = 0; i < 32; ++i) add += (s[i] != NEG_INF) ? __expf(s[i] - mn) : 0.f;
-          l = (m == NEG_INF ? 0.f : l * __expf(m - mn)) + add;
+          for (int i = 0; i < 32; ++i) add[i & 3] += ex2(fmaf(s[i], kLog2e, -mL));  // masked: 2^-inf = 0
+          l = l * ex2((m - mn) * kLog2e) + ((add[0] + add[1]) + (add[2] + add[3]));
           m = mn;
         }
       }
@@ -269,11 +308,12 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(const __grid_
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         const float2 st = stat[c * kRows + rloc];
-        if (st.x != NEG_INF) Ls += st.y * __expf(st.x - M);
+        if (st.x != NEG_INF) Ls += st.y * ex2((st.x - M) * kLog2e);
       }
       m = M;
       l = 1.0f / Ls;  // from here on: the reciprocal of the row sum
     }
+    const float mL = m * kLog2e;
     // ---- pass 2: exact probabilities, per-key score, P for the tensor cores
     for (int kt = 0; kt < nkt; ++kt) {
       const int j = nkt + kt, b = j & 1;
@@ -286,26 +326,32 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(const __grid_
       __syncwarp();
       if (lane == 0) mbar_arrive(&sfree[b]);
       float p[32];
+      const int kb = kt * kKeys + cg * 32;
+      if (ok && kb + 31 <= rmin && rows_in) {  // warp-uniform: no key of the block is masked
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const int key = kt * kKeys + cg * 32 + i;
-        p[i] = (ok && key <= row && key < a.P && row < a.P) ? __expf(bf16r(bf16r(s[i]) * a.scale) - m) * l : 0.f;
+        for (int i = 0; i < 32; ++i) p[i] = __fmul_rn(ex2(fmaf(rnd_bf16(rnd_bf16(s[i]) * a.scale), kLog2e, -mL)), l);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int key = kb + i;
+          p[i] = (ok && key <= row && key < a.P && row < a.P)
+                     ? __fmul_rn(ex2(fmaf(rnd_bf16(rnd_bf16(s[i]) * a.scale), kLog2e, -mL)), l)
+                     : 0.f;
+        }
       }
       if (a.colmax) {
-        // butterfly max across the warp's 32 rows: afterwards lane i holds the maximum of
-        // key (tile column cg * 32 + i)
-        float v[32];
+        // per-key maximum over the warp's 32 rows: p >= 0, so its bit pattern orders like
+        // an unsigned integer; lane i keeps key (tile column cg * 32 + i)
+        float v[1];
+        {
+          uint32_t mine = 0;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = p[i];
-#pragma unroll
-        for (int sft = 16; sft >= 1; sft >>= 1) {
-          const bool upper = (lane & sft) != 0;
-#pragma unroll
-          for (int i = 0; i < sft; ++i) {
-            const float send = upper ? v[i] : v[i + sft];
-            const float keep = upper ? v[i + sft] : v[i];
-            v[i] = fmaxf(keep, __shfl_xor_sync(0xffffffffu, send, sft));
+          for (int i = 0; i < 32; ++i) {
+            uint32_t r;
+            asm volatile("redux.sync.max.u32 %0, %1, 0xffffffff;" : "=r"(r) : "r"(__float_as_uint(p[i])));
+            mine = (lane == i) ? r : mine;
           }
+          v[0] = __uint_as_float(mine);
         }
         const int key = kt * kKeys + cg * 32 + lane;
         if (ok && key < a.P && v[0] > 0.f) atomicMax(reinterpret_cast<int*>(a.colmax + key), __float_as_int(v[0]));
@@ -314,9 +360,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(const __grid_
       uint32_t ph[16], pl[16];
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
-        const float h0 = bf16r(p[2 * i]), h1 = bf16r(p[2 * i + 1]);
-        ph[i] = pack_bf16(h0, h1);
-        pl[i] = pack_bf16(p[2 * i] - h0, p[2 * i + 1] - h1);
+        // p = hi + lo: hi rounded to nearest-even, lo = p - hi (exact) truncated to bf16
+        const float h0 = rnd_bf16(p[2 * i]), h1 = rnd_bf16(p[2 * i + 1]);
+        ph[i] = hi_halves(h0, h1);
+        pl[i] = hi_halves(__fsub_rn(p[2 * i], h0), __fsub_rn(p[2 * i + 1], h1));
       }
       // the row's 32 keys into the K-major swizzled A operand: 4 chunks of 8 keys
       const int half = cg >> 1;
