@@ -30,7 +30,7 @@
 // round pushes every CTA's (max, sum) and its O slice r to cluster CTA r (transaction-
 // counted mbarrier).  Each CTA then forms the final max M and sum L, writes its slice
 // of bf16 output, and turns its stored logits into the exact probabilities
-// p = exp(s - M) / L for the per-slot score (max over heads -> atomicMax).  The K/V
+// p = exp(s - M) * (1 / L) for the per-slot score (max over heads -> atomicMax).  The K/V
 // cache is read exactly once, in a single stream.
 //
 // Early streaming: the kernel is launched with programmatic dependent launch, so its
@@ -173,15 +173,10 @@ __global__ void __launch_bounds__(attn_threads(GR), kMinBlocks) decode_attn_scor
     for (int u = 0; u < n_first; ++u) issue(u);
     *n_issued = n_first;
   }
-  if (tid < kConsumers) {
-    const int* spos = p.slot_pos + static_cast<size_t>(b) * S;
-    for (int i = tid; i < nloc; i += kConsumers) {
-      const int slot = t0 * kTile + i;
-      spos_s[i] = slot < S ? spos[slot] : -1;
-    }
-  }
   __syncthreads();
-  cluster_sync_all();  // every peer's barriers are initialised before any st.async
+  // every peer's barriers must be initialised before any st.async: arrive now, wait just
+  // before the exchange, so the tile loop does not wait for the slowest CTA's setup
+  cluster_arrive_release();
 
   // ================================ producer warp =================================
   if (warp == kConsumerWarps) {
@@ -208,7 +203,8 @@ __global__ void __launch_bounds__(attn_threads(GR), kMinBlocks) decode_attn_scor
     }
     __syncwarp();
     if (KVBP_PDL_LATE) pdl_launch_dependents();
-    cluster_sync_all();  // matches the consumers' final cluster barrier
+    cluster_wait_acquire();  // the setup phase (the consumers wait before their exchange)
+    cluster_sync_all();      // matches the consumers' final cluster barrier
     return;
   }
 
@@ -236,8 +232,14 @@ __global__ void __launch_bounds__(attn_threads(GR), kMinBlocks) decode_attn_scor
   const int grp = warp >> 2;
   const int wslot = early ? p.write_slot[b] : -1;  // row of this step's K/V (read after the wait)
 
+  const int* spos_g = p.slot_pos + static_cast<size_t>(b) * S;
   for (int u = grp; u < nt; u += GR) {
     const int st = u % kStages;
+    // slot positions of the warp's rows g and g + 8 of this tile (< 0: free slot), read
+    // while the tile is in flight; lanes t == 0 keep them for the score pass
+    const int lta = u * kTile + r0 + g, ltb = lta + 8;
+    const int pa = t0 * kTile + lta < S ? spos_g[t0 * kTile + lta] : -1;
+    const int pb = t0 * kTile + ltb < S ? spos_g[t0 * kTile + ltb] : -1;
     bool ok_tile = !(*reinterpret_cast<volatile int*>(bad_flag));
     if (ok_tile && !mbar_wait_bounded(&full[st], (u / kStages) & 1)) {
       set_err(p.err, kErrWaitTimeout);
@@ -280,8 +282,11 @@ __global__ void __launch_bounds__(attn_threads(GR), kMinBlocks) decode_attn_scor
           mma_bf16_16816(a0c, x0, x1, x2, x3, qb[kk][0], qb[kk][1]);
       }
       // ---- rounded logits (reference rounding points) -> shared memory ---------------
-      const int lta = u * kTile + r0 + g, ltb = lta + 8;
-      const bool va = spos_s[lta] >= 0, vb = spos_s[ltb] >= 0;
+      const bool va = pa >= 0, vb = pb >= 0;
+      if (t == 0) {
+        spos_s[lta] = pa;
+        spos_s[ltb] = pb;
+      }
       float sa0 = va ? bf16r(bf16r(a0c[0] + a1c[0]) * p.scale) : NEG_INF;
       float sa1 = va ? bf16r(bf16r(a0c[1] + a1c[1]) * p.scale) : NEG_INF;
       float sb0 = vb ? bf16r(bf16r(a0c[2] + a1c[2]) * p.scale) : NEG_INF;
@@ -390,6 +395,7 @@ __global__ void __launch_bounds__(attn_threads(GR), kMinBlocks) decode_attn_scor
     }
   }
   named_bar(1, kConsumers);
+  cluster_wait_acquire();  // every peer is past its setup (barriers initialised)
   // ---- one st.async round: (max, sum) to every peer, O element e to CTA e / per ------
   if (warp == 0 && lane < CS) {
     const uint32_t rbar = mapa_u32(smem_u32(xbar), lane);
@@ -458,13 +464,13 @@ __global__ void __launch_bounds__(attn_threads(GR), kMinBlocks) decode_attn_scor
       orow[e0 + j] = __float2bfloat16_rn(Lh > 0.f ? acc / Lh : 0.f);
     }
   }
-  // per-slot eviction score: max over the group's heads of p = exp(s - M) / L
+  // per-slot eviction score: max over the group's heads of p = exp(s - M) * (1 / L)
   if (!(*reinterpret_cast<volatile int*>(bad_flag))) {
-    float Mh[G], iLh[G];
+    float Mh[G], iLh[G];  // max and 1 / sum per head (0 for a head without valid slots)
 #pragma unroll
     for (int h = 0; h < G; ++h) {
       Mh[h] = finM[h];
-      iLh[h] = finL[h];
+      iLh[h] = finL[h] > 0.f ? 1.0f / finL[h] : 0.f;
     }
     float* sscore = p.step_score + static_cast<size_t>(b) * S;
     for (int i = tid; i < nloc; i += kConsumers) {
@@ -472,7 +478,7 @@ __global__ void __launch_bounds__(attn_threads(GR), kMinBlocks) decode_attn_scor
       float mx = 0.f;
 #pragma unroll
       for (int h = 0; h < G; ++h) {
-        const float pr = iLh[h] > 0.f ? expf(logits[i * 8 + h] - Mh[h]) / iLh[h] : 0.f;
+        const float pr = iLh[h] > 0.f ? expf(logits[i * 8 + h] - Mh[h]) * iLh[h] : 0.f;
         mx = fmaxf(mx, pr);
       }
       if (mx != mx) set_err(p.err, kErrNanScore);

@@ -195,6 +195,13 @@ __device__ __forceinline__ float2 ld_dsmem_f2(uint32_t cluster_addr) {
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
+// the two halves of cluster_sync_all, for work that can run between them
+__device__ __forceinline__ void cluster_arrive_release() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait_acquire() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
 
 // Barrier among the first ``nthreads`` threads of the CTA (named barrier ``id``).
 __device__ __forceinline__ void named_bar(int id, int nthreads) {
