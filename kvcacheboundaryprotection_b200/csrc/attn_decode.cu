@@ -161,26 +161,29 @@ __global__ void __launch_bounds__(attn_threads(GR), kMinBlocks) decode_attn_scor
     }
     mbar_init(xbar, 1);
     *bad_flag = 0;
+    *n_issued = 0;
     fence_barrier_init();
-    if (early) {  // all rows but write_slot's are final: stream before the wait
-      for (int u = 0; u < n_first; ++u) issue(u);
-      *n_issued = n_first;
-    }
-  }
-  if (!KVBP_PDL_LATE) pdl_launch_dependents();
-  pdl_wait();  // q, slot positions and the new K/V row come from earlier kernels
-  if (tid == kConsumers && !early) {
-    for (int u = 0; u < n_first; ++u) issue(u);
-    *n_issued = n_first;
   }
   __syncthreads();
   // every peer's barriers must be initialised before any st.async: arrive now, wait just
   // before the exchange, so the tile loop does not wait for the slowest CTA's setup
   cluster_arrive_release();
+  if (!KVBP_PDL_LATE) pdl_launch_dependents();
 
   // ================================ producer warp =================================
+  // (the first TMA issue of a launch can stall its thread for microseconds, so no other
+  // thread waits for it)
   if (warp == kConsumerWarps) {
     if (lane == 0) {
+      if (early) {  // all rows but write_slot's are final: stream before the wait
+        for (int u = 0; u < n_first; ++u) issue(u);
+        *n_issued = n_first;
+      }
+      pdl_wait();  // the slot positions and this step's K/V row come from earlier kernels
+      if (!early) {
+        for (int u = 0; u < n_first; ++u) issue(u);
+        *n_issued = n_first;
+      }
       for (int u = n_first; u < nt; ++u) {
         const int st = u % kStages;
         if (*reinterpret_cast<volatile int*>(bad_flag)) break;
@@ -209,6 +212,7 @@ __global__ void __launch_bounds__(attn_threads(GR), kMinBlocks) decode_attn_scor
   }
 
   // ================================ consumer warps ================================
+  pdl_wait();  // q, the slot positions and this step's K/V row come from earlier kernels
   if (tid == 0) mbar_expect_tx(xbar, CS * (16 + n_mine) * 4);  // local arrival; completes on the bytes
   const int g = lane >> 2, t = lane & 3;
   uint32_t qb[8][2];
