@@ -159,24 +159,18 @@ __global__ void __launch_bounds__(kThreads) decode_gemm_kernel(const __grid_cons
     }
     flag[0] = 0;
     fence_barrier_init();
-    // weights are constant: stream the first stages before the previous kernel is done
-    for (int u = 0; u < nch && u < kStages; ++u) issue_weights(u);
-  }
-  if (!KVBP_PDL_LATE) pdl_launch_dependents();
-  pdl_wait();  // activations, norm statistics and h belong to earlier kernels
-  if (tid == kConsumers)
-    for (int u = 0; u < nch && u < kStages; ++u) issue_acts(u);
-  if (NORM && tid < 32) {
-    float ss = 0.f;
-    if (tid < M)
-      for (int t = 0; t < a.n_parts; ++t) ss += a.ss_parts[t * 32 + tid];
-    inv_rms[tid] = 1.0f / sqrtf(ss / static_cast<float>(a.K) + a.eps);
   }
   __syncthreads();
+  if (!KVBP_PDL_LATE) pdl_launch_dependents();
 
   // ================================ producer warp =================================
+  // (a TMA issue can stall its thread for microseconds, so no other thread waits for it)
   if (warp == kConsumerWarps) {
     if (lane == 0) {
+      // weights are constant: stream the first stages before the previous kernel is done
+      for (int u = 0; u < nch && u < kStages; ++u) issue_weights(u);
+      pdl_wait();  // the activations belong to earlier kernels
+      for (int u = 0; u < nch && u < kStages; ++u) issue_acts(u);
       int issued = nch < kStages ? nch : kStages;
       for (int u = kStages; u < nch; ++u) {
         const int st = u % kStages;
@@ -206,6 +200,14 @@ __global__ void __launch_bounds__(kThreads) decode_gemm_kernel(const __grid_cons
   }
 
   // ================================ consumer warps ================================
+  pdl_wait();  // activations, norm statistics and h belong to earlier kernels
+  if (NORM && tid < 32) {
+    float ss = 0.f;
+    if (tid < M)
+      for (int t = 0; t < a.n_parts; ++t) ss += a.ss_parts[t * 32 + tid];
+    inv_rms[tid] = 1.0f / sqrtf(ss / static_cast<float>(a.K) + a.eps);
+  }
+  if (NORM) named_bar(1, kConsumers);
   const int g = lane >> 2, t = lane & 3;
   float acc[MT][4][4];
 #pragma unroll
