@@ -50,6 +50,9 @@ constexpr int BK = 128;            // K per stage
 #define KVBP_GEMM_STAGES 3
 #endif
 constexpr int kStages = KVBP_GEMM_STAGES;
+#ifndef KVBP_GEMM_EARLY
+#define KVBP_GEMM_EARLY 3  // weight stages issued before the wait on the previous kernel
+#endif
 constexpr int kConsumerWarps = 4;  // 32 features each
 constexpr int kConsumers = kConsumerWarps * 32;
 constexpr int kThreads = kConsumers + 32;
@@ -168,9 +171,13 @@ __global__ void __launch_bounds__(kThreads) decode_gemm_kernel(const __grid_cons
   if (warp == kConsumerWarps) {
     if (lane == 0) {
       // weights are constant: stream the first stages before the previous kernel is done
-      for (int u = 0; u < nch && u < kStages; ++u) issue_weights(u);
+      constexpr int kEarly = KVBP_GEMM_EARLY < kStages ? KVBP_GEMM_EARLY : kStages;
+      for (int u = 0; u < nch && u < kEarly; ++u) issue_weights(u);
       pdl_wait();  // the activations belong to earlier kernels
-      for (int u = 0; u < nch && u < kStages; ++u) issue_acts(u);
+      for (int u = 0; u < nch && u < kStages; ++u) {
+        if (u >= kEarly) issue_weights(u);
+        issue_acts(u);
+      }
       int issued = nch < kStages ? nch : kStages;
       for (int u = kStages; u < nch; ++u) {
         const int st = u % kStages;
@@ -299,22 +306,35 @@ __global__ void __launch_bounds__(kThreads) decode_gemm_kernel(const __grid_cons
   const int rank = blockIdx.y;  // cluster shape (1, splits, 1): rank == split index
   const int r_lo = (rank * M) / cs, r_hi = ((rank + 1) * M) / cs;
   const uint32_t rt_local = smem_u32(rtile);
+  // The peers' values are all loaded before the first add (one DSMEM round trip instead of
+  // one per peer), then summed in rank order.
   auto sum_pair = [&](int r, int c) -> float2 {  // columns c, c+1 of row r, summed over splits
     if (cs == 1) return *reinterpret_cast<const float2*>(&rtile[r * kRedStride + c]);
     const uint32_t off = static_cast<uint32_t>((r * kRedStride + c) * 4);
-    float2 s = ld_dsmem_f2(mapa_u32(rt_local + off, 0));
-    for (int q = 1; q < cs; ++q) {
-      const float2 v = ld_dsmem_f2(mapa_u32(rt_local + off, q));
-      s.x += v.x;
-      s.y += v.y;
-    }
+    float2 v[kMaxSplits];
+#pragma unroll
+    for (int q = 0; q < kMaxSplits; ++q)
+      if (q < cs) v[q] = ld_dsmem_f2(mapa_u32(rt_local + off, q));
+    float2 s = v[0];
+#pragma unroll
+    for (int q = 1; q < kMaxSplits; ++q)
+      if (q < cs) {
+        s.x += v[q].x;
+        s.y += v[q].y;
+      }
     return s;
   };
   auto sum_one = [&](int r, int c) -> float {
     if (cs == 1) return rtile[r * kRedStride + c];
     const uint32_t off = static_cast<uint32_t>((r * kRedStride + c) * 4);
-    float s = ld_dsmem_f32(mapa_u32(rt_local + off, 0));
-    for (int q = 1; q < cs; ++q) s += ld_dsmem_f32(mapa_u32(rt_local + off, q));
+    float v[kMaxSplits];
+#pragma unroll
+    for (int q = 0; q < kMaxSplits; ++q)
+      if (q < cs) v[q] = ld_dsmem_f32(mapa_u32(rt_local + off, q));
+    float s = v[0];
+#pragma unroll
+    for (int q = 1; q < kMaxSplits; ++q)
+      if (q < cs) s += v[q];
     return s;
   };
   const int nrows = r_hi - r_lo;
