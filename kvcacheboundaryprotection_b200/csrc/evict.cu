@@ -275,9 +275,13 @@ __global__ void __launch_bounds__(kScoreThreads) score_update_kernel(StateArgs s
   mx = block_max_float(mx, red);
   if (threadIdx.x == 0) cta_max = mx;
   cluster_sync_all();
-  float gmx = 0.f;
   const uint32_t local = smem_u32(&cta_max);
-  for (int q = 0; q < CS; ++q) gmx = fmaxf(gmx, ld_dsmem_f32(mapa_u32(local, q)));
+  float pm[8];  // every peer's maximum loaded before the first compare (CS <= 8)
+#pragma unroll
+  for (int q = 0; q < 8; ++q) pm[q] = q < CS ? ld_dsmem_f32(mapa_u32(local, q)) : 0.f;
+  float gmx = 0.f;
+#pragma unroll
+  for (int q = 0; q < 8; ++q) gmx = fmaxf(gmx, pm[q]);
   const float thr = static_cast<float>(0.05 * static_cast<double>(gmx));
   const int step = seq_step[b];
   float* __restrict__ attn = s.attn;
@@ -336,10 +340,8 @@ __global__ void __launch_bounds__(kEvictThreads) append_evict_kernel(AppendArgs 
   pdl_wait();
   extern __shared__ int s_vict[];  // [S] victim slots of this call, in eviction order
   __shared__ int red_i[32];
-  __shared__ float red_f[32];
   __shared__ KeySlot red_k[32];
   __shared__ int sh[8];
-  (void)red_f;
   const int b = blockIdx.x, tid = threadIdx.x;
   const int S = a.st.S;
   SeqState s = a.st.seq(b);
