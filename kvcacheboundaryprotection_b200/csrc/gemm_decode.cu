@@ -215,6 +215,36 @@ __global__ void __launch_bounds__(kThreads) decode_gemm_kernel(const __grid_cons
     inv_rms[tid] = 1.0f / sqrtf(ss / static_cast<float>(a.K) + a.eps);
   }
   if (NORM) named_bar(1, kConsumers);
+  const int rank = blockIdx.y;  // cluster shape (1, splits, 1): rank == split index
+  const int r_lo = (rank * M) / cs, r_hi = ((rank + 1) * M) / cs;
+  const int nrows = r_hi - r_lo;
+  // Epilogue operands that do not depend on the accumulators, fetched for the first two
+  // passes of the epilogue loops while the first stage is in flight (with 16 rows and
+  // 7 splits every pass is covered); later passes load them in the loop.
+  constexpr int kPre = 2;
+  uint32_t pre_h[kPre] = {0u, 0u};                            // RESID: this thread's h pair
+  int pre_pos[kPre] = {0, 0}, pre_slot[kPre] = {-1, -1};     // QKV: the row's position, write slot
+  if (EPI == kResid) {
+#pragma unroll
+    for (int p = 0; p < kPre; ++p) {
+      const int e = p * kConsumers + tid;
+      if (e < nrows * (BN / 2)) {
+        const int r = r_lo + e / (BN / 2), c = 2 * (e % (BN / 2));
+        pre_h[p] = *reinterpret_cast<const uint32_t*>(&a.out[static_cast<size_t>(r) * a.ldo + n0 + c]);
+      }
+    }
+  }
+  if (EPI == kQKV) {
+#pragma unroll
+    for (int p = 0; p < kPre; ++p) {
+      const int e = p * kConsumers + tid;
+      if (e < nrows * 64) {
+        const int r = r_lo + e / 64;
+        if (tile < a.Hq + a.Hkv) pre_pos[p] = a.positions[r];  // q and k heads take RoPE
+        if (tile >= a.Hq) pre_slot[p] = a.write_slot[r];       // k and v heads are stored
+      }
+    }
+  }
   const int g = lane >> 2, t = lane & 3;
   float acc[MT][4][4];
 #pragma unroll
@@ -303,8 +333,6 @@ __global__ void __launch_bounds__(kThreads) decode_gemm_kernel(const __grid_cons
   else named_bar(1, kConsumers);
 
   // ---- reduce this CTA's row slice over the cluster (rank order) and run the epilogue
-  const int rank = blockIdx.y;  // cluster shape (1, splits, 1): rank == split index
-  const int r_lo = (rank * M) / cs, r_hi = ((rank + 1) * M) / cs;
   const uint32_t rt_local = smem_u32(rtile);
   // The peers' values are all loaded before the first add (one DSMEM round trip instead of
   // one per peer), then summed in rank order.
@@ -337,7 +365,6 @@ __global__ void __launch_bounds__(kThreads) decode_gemm_kernel(const __grid_cons
       if (q < cs) s += v[q];
     return s;
   };
-  const int nrows = r_hi - r_lo;
   if (ok) {
     if (EPI == kPlain) {
       for (int e = tid; e < nrows * (BN / 2); e += kConsumers) {
@@ -358,9 +385,10 @@ __global__ void __launch_bounds__(kThreads) decode_gemm_kernel(const __grid_cons
         float ss = 0.f;
         if (e < nrows * (BN / 2)) {
           const int r = r_lo + e / (BN / 2), c = 2 * (e % (BN / 2));
-          const float2 v = sum_pair(r, c);
+          const int pass = e0 / kConsumers;
           uint32_t* hp = reinterpret_cast<uint32_t*>(&a.out[static_cast<size_t>(r) * a.ldo + n0 + c]);
-          const uint32_t hv = *hp;
+          const uint32_t hv = pass == 0 ? pre_h[0] : (pass == 1 ? pre_h[1] : *hp);  // before the DSMEM loads
+          const float2 v = sum_pair(r, c);
           const float x0 = bf16r(bf16lo(hv) + bf16r(v.x));
           const float x1 = bf16r(bf16hi(hv) + bf16r(v.y));
           *hp = pack_bf16(x0, x1);
@@ -451,17 +479,30 @@ __global__ void __launch_bounds__(kThreads) decode_gemm_kernel(const __grid_cons
       const int hh = tile, i = tid & 63;
       const bool is_q = hh < a.Hq, is_k = !is_q && hh < a.Hq + a.Hkv;
       const __nv_bfloat16* nw = is_q ? a.qnw : (is_k ? a.knw : nullptr);
+      // global operands first: the DSMEM loads of the reduction are ordered after them
+      const float fq = (is_q || is_k) ? a.inv_freq[i] : 0.f;
+      const float b0 = a.bias ? __bfloat162float(a.bias[hh * 128 + i]) : 0.f;
+      const float b1 = a.bias ? __bfloat162float(a.bias[hh * 128 + i + 64]) : 0.f;
+      const float nw0 = nw ? __bfloat162float(nw[i]) : 0.f;
+      const float nw1 = nw ? __bfloat162float(nw[i + 64]) : 0.f;
       for (int e0 = 0; e0 < nrows * 64; e0 += kConsumers) {  // two rows per pass
         const int e = e0 + tid;
+        const int pass = e0 / kConsumers;
         const bool live = e < nrows * 64;
         const int r = r_lo + e / 64;
+        int pos = pass == 0 ? pre_pos[0] : pre_pos[1];
+        int slot = pass == 0 ? pre_slot[0] : pre_slot[1];
+        if (live && pass >= kPre) {
+          if (is_q || is_k) pos = a.positions[r];
+          if (!is_q) slot = a.write_slot[r];
+        }
         float x0 = 0.f, x1 = 0.f;
         if (live) {
           x0 = bf16r(sum_one(r, i));  // the GEMM's bf16 output
           x1 = bf16r(sum_one(r, i + 64));
           if (a.bias) {
-            x0 = bf16r(x0 + __bfloat162float(a.bias[hh * 128 + i]));
-            x1 = bf16r(x1 + __bfloat162float(a.bias[hh * 128 + i + 64]));
+            x0 = bf16r(x0 + b0);
+            x1 = bf16r(x1 + b1);
           }
         }
         if (nw) {  // CTA-uniform: RMSNorm over the head's 128 features
@@ -473,12 +514,12 @@ __global__ void __launch_bounds__(kThreads) decode_gemm_kernel(const __grid_cons
           const float tot = red[(warp >> 1) * 2] + red[(warp >> 1) * 2 + 1];
           named_bar(1, kConsumers);  // red is reused by the next pass
           const float inv = 1.0f / sqrtf(tot / 128.0f + a.eps);
-          x0 = bf16r((x0 * inv) * __bfloat162float(nw[i]));
-          x1 = bf16r((x1 * inv) * __bfloat162float(nw[i + 64]));
+          x0 = bf16r((x0 * inv) * nw0);
+          x1 = bf16r((x1 * inv) * nw1);
         }
         if (!live) continue;
         if (is_q || is_k) {
-          const float ang = static_cast<float>(a.positions[r]) * a.inv_freq[i];
+          const float ang = static_cast<float>(pos) * fq;
           const float c = bf16r(cosf(ang)), sn = bf16r(sinf(ang));
           const float y0 = bf16r(bf16r(x0 * c) - bf16r(x1 * sn));
           const float y1 = bf16r(bf16r(x1 * c) + bf16r(x0 * sn));
@@ -489,7 +530,6 @@ __global__ void __launch_bounds__(kThreads) decode_gemm_kernel(const __grid_cons
         if (is_q) {
           dst = a.q_out + (static_cast<size_t>(r) * a.Hq + hh) * 128;
         } else {
-          const int slot = a.write_slot[r];
           if (slot < 0) continue;  // position evicted before its forward: nothing to store
           if (slot >= a.S) {
             set_err(a.err, kErrIndex);
