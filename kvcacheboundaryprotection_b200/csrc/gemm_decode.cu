@@ -367,10 +367,23 @@ __global__ void __launch_bounds__(kThreads) decode_gemm_kernel(const __grid_cons
   };
   if (ok) {
     if (EPI == kPlain) {
-      for (int e = tid; e < nrows * (BN / 2); e += kConsumers) {
-        const int r = r_lo + e / (BN / 2), c = 2 * (e % (BN / 2));
-        const float2 v = sum_pair(r, c);
-        *reinterpret_cast<uint32_t*>(&a.out[static_cast<size_t>(r) * a.ldo + n0 + c]) = pack_bf16(v.x, v.y);
+      // every pass's sums first, then the stores (the lm_head's 1188 tiles run in waves, so
+      // the epilogue is on the critical path)
+      constexpr int kMaxPass = 8 * MT;  // nrows * 64 <= kMaxPass * kConsumers
+      const int nel = nrows * (BN / 2);
+      float2 v[kMaxPass];
+#pragma unroll
+      for (int p = 0; p < kMaxPass; ++p) {
+        const int e = p * kConsumers + tid;
+        if (e < nel) v[p] = sum_pair(r_lo + e / (BN / 2), 2 * (e % (BN / 2)));
+      }
+#pragma unroll
+      for (int p = 0; p < kMaxPass; ++p) {
+        const int e = p * kConsumers + tid;
+        if (e < nel) {
+          const int r = r_lo + e / (BN / 2), c = 2 * (e % (BN / 2));
+          *reinterpret_cast<uint32_t*>(&a.out[static_cast<size_t>(r) * a.ldo + n0 + c]) = pack_bf16(v[p].x, v[p].y);
+        }
       }
     } else if (EPI == kF32) {  // unrounded partial sums (a tensor-parallel shard's share)
       float* of = reinterpret_cast<float*>(a.out);
