@@ -360,8 +360,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(const __grid_
       uint32_t ph[16], pl[16];
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
-        // p = hi + lo: hi rounded to nearest-even, lo = p - hi (exact) truncated to bf16
-        const float h0 = rnd_bf16(p[2 * i]), h1 = rnd_bf16(p[2 * i + 1]);
+        // p = hi + lo: hi = p truncated to bf16 (one mask), lo = p - hi (exact, >= 0)
+        // truncated to bf16; hi + lo is within 2^-16 of p
+        const float h0 = __uint_as_float(__float_as_uint(p[2 * i]) & 0xFFFF0000u);
+        const float h1 = __uint_as_float(__float_as_uint(p[2 * i + 1]) & 0xFFFF0000u);
         ph[i] = hi_halves(h0, h1);
         pl[i] = hi_halves(__fsub_rn(p[2 * i], h0), __fsub_rn(p[2 * i + 1], h1));
       }
