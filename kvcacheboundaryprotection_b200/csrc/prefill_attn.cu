@@ -24,10 +24,11 @@
 //           the warp's 32 rows, then one atomicMax per key and warp) goes to the score; P is written
 //           in bf16 hi + lo parts (two MMAs, ~16-bit mantissa; V is exact in bf16) and
 //           O += P.V accumulates in TMEM.
-// The softmax warps' element work is spread over the FP32, integer and MUFU pipes: the
-// bf16 roundings are Veltkamp splits on the FP32 pipe (three instructions each, instead
-// of a conversion on the quarter-rate conversion pipe), packing is a byte permute, and
-// the causal / tail masks are applied only to the blocks that straddle them.
+// The softmax warps' element work is spread over the FP32, integer, conversion and MUFU
+// pipes: of the two bf16 roundings of a score, the first is a packed conversion (two
+// values per instruction) and the second a Veltkamp split on the FP32 pipe (three
+// instructions), packing is a byte permute, and the causal / tail masks are applied only
+// to the blocks that straddle them.
 // Q, K and V tiles arrive by 3-D TMA (128-byte swizzle) in the K-major layout the MMA
 // descriptors describe; P is written by the threads in the same swizzled layout.  V is
 // the MN-major B operand of P.V.  K tiles are double-buffered (the next tile's load
@@ -119,6 +120,15 @@ __device__ __forceinline__ float ex2(float x) {
 // the upper halves of two fp32 words packed as bf16x2 (a in the low half)
 __device__ __forceinline__ uint32_t hi_halves(float a, float b) {
   return __byte_perm(__float_as_uint(a), __float_as_uint(b), 0x7632);
+}
+
+// bf16 round-to-nearest-even of two fp32 values with one packed conversion instruction
+// (cvt.rn.bf16x2.f32), returned as fp32
+__device__ __forceinline__ void rnd_pair(float& a, float& b) {
+  uint32_t w;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(w) : "f"(b), "f"(a));  // b -> upper half, a -> lower
+  a = __uint_as_float(w << 16);
+  b = __uint_as_float(w & 0xFFFF0000u);
 }
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
@@ -272,17 +282,19 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(const __grid_
       if (ok) {
         const int kb = j * kKeys + cg * 32;
         float mt = NEG_INF;
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) rnd_pair(s[i], s[i + 1]);  // bf16(q.k)
         if (kb + 31 <= rmin && rows_in) {  // warp-uniform: no key of the block is masked
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
-            s[i] = rnd_bf16(rnd_bf16(s[i]) * a.scale);
+            s[i] = rnd_bf16(s[i] * a.scale);
             mt = fmaxf(mt, s[i]);
           }
         } else {
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
             const int key = kb + i;
-            s[i] = (key <= row && key < a.P) ? rnd_bf16(rnd_bf16(s[i]) * a.scale) : NEG_INF;
+            s[i] = (key <= row && key < a.P) ? rnd_bf16(s[i] * a.scale) : NEG_INF;
             mt = fmaxf(mt, s[i]);
           }
         }
@@ -325,17 +337,19 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(const __grid_
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&sfree[b]);
+#pragma unroll
+      for (int i = 0; i < 32; i += 2) rnd_pair(s[i], s[i + 1]);  // bf16(q.k)
       float p[32];
       const int kb = kt * kKeys + cg * 32;
       if (ok && kb + 31 <= rmin && rows_in) {  // warp-uniform: no key of the block is masked
 #pragma unroll
-        for (int i = 0; i < 32; ++i) p[i] = __fmul_rn(ex2(fmaf(rnd_bf16(rnd_bf16(s[i]) * a.scale), kLog2e, -mL)), l);
+        for (int i = 0; i < 32; ++i) p[i] = __fmul_rn(ex2(fmaf(rnd_bf16(s[i] * a.scale), kLog2e, -mL)), l);
       } else {
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           const int key = kb + i;
           p[i] = (ok && key <= row && key < a.P && row < a.P)
-                     ? __fmul_rn(ex2(fmaf(rnd_bf16(rnd_bf16(s[i]) * a.scale), kLog2e, -mL)), l)
+                     ? __fmul_rn(ex2(fmaf(rnd_bf16(s[i] * a.scale), kLog2e, -mL)), l)
                      : 0.f;
         }
       }
