@@ -24,11 +24,10 @@
 //           the warp's 32 rows, then one atomicMax per key and warp) goes to the score; P is written
 //           in bf16 hi + lo parts (two MMAs, ~16-bit mantissa; V is exact in bf16) and
 //           O += P.V accumulates in TMEM.
-// The softmax warps' element work is spread over the FP32, integer, conversion and MUFU
-// pipes: of the two bf16 roundings of a score, the first is a packed conversion (two
-// values per instruction) and the second a Veltkamp split on the FP32 pipe (three
-// instructions), packing is a byte permute, and the causal / tail masks are applied only
-// to the blocks that straddle them.
+// The softmax warps' element work is kept to few instructions per score: both bf16
+// roundings of a score are packed conversions (cvt.rn.bf16x2.f32, two values per
+// instruction), exp is one FFMA + ex2, P's hi part is a mask, packing is a byte permute,
+// and the causal / tail masks are applied only to the blocks that straddle them.
 // Q, K and V tiles arrive by 3-D TMA (128-byte swizzle) in the K-major layout the MMA
 // descriptors describe; P is written by the threads in the same swizzled layout.  V is
 // the MN-major B operand of P.V.  K tiles are double-buffered (the next tile's load
@@ -99,15 +98,6 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
   for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-}
-
-// bf16 round-to-nearest-even of an fp32 value on the FP32 pipe: Veltkamp splitting with
-// sigma = 2^16 + 1 keeps the leading 8 significand bits, rounded to nearest with ties to
-// even (checked bit for bit against the bf16 conversion over whole binades).  The _rn
-// intrinsics keep the three steps from being contracted into an FMA.  Finite |x| < 2^111.
-__device__ __forceinline__ float rnd_bf16(float x) {
-  const float g = __fmul_rn(65537.0f, x);
-  return __fadd_rn(g, __fsub_rn(x, g));
 }
 
 // 2^x (the hardware approximation; -inf gives +0)
@@ -284,17 +274,20 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(const __grid_
         float mt = NEG_INF;
 #pragma unroll
         for (int i = 0; i < 32; i += 2) rnd_pair(s[i], s[i + 1]);  // bf16(q.k)
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {  // bf16(bf16(q.k) * scale)
+          s[i] *= a.scale;
+          s[i + 1] *= a.scale;
+          rnd_pair(s[i], s[i + 1]);
+        }
         if (kb + 31 <= rmin && rows_in) {  // warp-uniform: no key of the block is masked
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            s[i] = rnd_bf16(s[i] * a.scale);
-            mt = fmaxf(mt, s[i]);
-          }
+          for (int i = 0; i < 32; ++i) mt = fmaxf(mt, s[i]);
         } else {
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
             const int key = kb + i;
-            s[i] = (key <= row && key < a.P) ? rnd_bf16(s[i] * a.scale) : NEG_INF;
+            s[i] = (key <= row && key < a.P) ? s[i] : NEG_INF;
             mt = fmaxf(mt, s[i]);
           }
         }
@@ -339,17 +332,23 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(const __grid_
       if (lane == 0) mbar_arrive(&sfree[b]);
 #pragma unroll
       for (int i = 0; i < 32; i += 2) rnd_pair(s[i], s[i + 1]);  // bf16(q.k)
+#pragma unroll
+      for (int i = 0; i < 32; i += 2) {  // bf16(bf16(q.k) * scale)
+        s[i] *= a.scale;
+        s[i + 1] *= a.scale;
+        rnd_pair(s[i], s[i + 1]);
+      }
       float p[32];
       const int kb = kt * kKeys + cg * 32;
       if (ok && kb + 31 <= rmin && rows_in) {  // warp-uniform: no key of the block is masked
 #pragma unroll
-        for (int i = 0; i < 32; ++i) p[i] = __fmul_rn(ex2(fmaf(rnd_bf16(s[i] * a.scale), kLog2e, -mL)), l);
+        for (int i = 0; i < 32; ++i) p[i] = __fmul_rn(ex2(fmaf(s[i], kLog2e, -mL)), l);
       } else {
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           const int key = kb + i;
           p[i] = (ok && key <= row && key < a.P && row < a.P)
-                     ? __fmul_rn(ex2(fmaf(rnd_bf16(s[i] * a.scale), kLog2e, -mL)), l)
+                     ? __fmul_rn(ex2(fmaf(s[i], kLog2e, -mL)), l)
                      : 0.f;
         }
       }
