@@ -24,10 +24,11 @@
 //           the warp's 32 rows, then one atomicMax per key and warp) goes to the score; P is written
 //           in bf16 hi + lo parts (two MMAs, ~16-bit mantissa; V is exact in bf16) and
 //           O += P.V accumulates in TMEM.
-// The softmax warps' element work is kept to few instructions per score: both bf16
-// roundings of a score are packed conversions (cvt.rn.bf16x2.f32, two values per
-// instruction), exp is one FFMA + ex2, P's hi part is a mask, packing is a byte permute,
-// and the causal / tail masks are applied only to the blocks that straddle them.
+// The softmax warps' element work is kept to few instructions per score: a pair of
+// scores takes one packed conversion (cvt.rn.bf16x2.f32) and one packed bf16 multiply by
+// the scale (the exact product rounded once, = bf16(bf16(q.k) * bf16(1/sqrt(128)))), exp
+// is one FFMA + ex2, P's hi part is a mask, packing is a byte permute, and the causal /
+// tail masks are applied only to the blocks that straddle them.
 // Q, K and V tiles arrive by 3-D TMA (128-byte swizzle) in the K-major layout the MMA
 // descriptors describe; P is written by the threads in the same swizzled layout.  V is
 // the MN-major B operand of P.V.  K tiles are double-buffered (the next tile's load
@@ -112,11 +113,13 @@ __device__ __forceinline__ uint32_t hi_halves(float a, float b) {
   return __byte_perm(__float_as_uint(a), __float_as_uint(b), 0x7632);
 }
 
-// bf16 round-to-nearest-even of two fp32 values with one packed conversion instruction
-// (cvt.rn.bf16x2.f32), returned as fp32
-__device__ __forceinline__ void rnd_pair(float& a, float& b) {
+// bf16(bf16(a) * scale), bf16(bf16(b) * scale) for fp32 a, b: one packed conversion and
+// one packed bf16 multiply (the exact product of two bf16 values is rounded once to
+// nearest-even), returned as fp32
+__device__ __forceinline__ void rnd_scaled_pair(float& a, float& b, uint32_t scale2) {
   uint32_t w;
   asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(w) : "f"(b), "f"(a));  // b -> upper half, a -> lower
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(w) : "r"(w), "r"(scale2));
   a = __uint_as_float(w << 16);
   b = __uint_as_float(w & 0xFFFF0000u);
 }
@@ -257,6 +260,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(const __grid_
     const int rmin = q0 + lg * 32;             // this warp's rows: rmin .. rmin + 31
     const bool rows_in = rmin + 31 < a.P;
     constexpr float kLog2e = 1.4426950408889634f;
+    const uint32_t scale2 = (__float_as_uint(a.scale) >> 16) * 0x10001u;  // bf16(scale) in both halves
     float m = NEG_INF, l = 0.f;
     // ---- pass 1: row statistics over this warp's columns
     for (int j = 0; j < nkt; ++j) {
@@ -273,13 +277,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(const __grid_
         const int kb = j * kKeys + cg * 32;
         float mt = NEG_INF;
 #pragma unroll
-        for (int i = 0; i < 32; i += 2) rnd_pair(s[i], s[i + 1]);  // bf16(q.k)
-#pragma unroll
-        for (int i = 0; i < 32; i += 2) {  // bf16(bf16(q.k) * scale)
-          s[i] *= a.scale;
-          s[i + 1] *= a.scale;
-          rnd_pair(s[i], s[i + 1]);
-        }
+        for (int i = 0; i < 32; i += 2) rnd_scaled_pair(s[i], s[i + 1], scale2);  // bf16(bf16(q.k) * scale)
         if (kb + 31 <= rmin && rows_in) {  // warp-uniform: no key of the block is masked
 #pragma unroll
           for (int i = 0; i < 32; ++i) mt = fmaxf(mt, s[i]);
@@ -331,13 +329,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(const __grid_
       __syncwarp();
       if (lane == 0) mbar_arrive(&sfree[b]);
 #pragma unroll
-      for (int i = 0; i < 32; i += 2) rnd_pair(s[i], s[i + 1]);  // bf16(q.k)
-#pragma unroll
-      for (int i = 0; i < 32; i += 2) {  // bf16(bf16(q.k) * scale)
-        s[i] *= a.scale;
-        s[i + 1] *= a.scale;
-        rnd_pair(s[i], s[i + 1]);
-      }
+      for (int i = 0; i < 32; i += 2) rnd_scaled_pair(s[i], s[i + 1], scale2);  // bf16(bf16(q.k) * scale)
       float p[32];
       const int kb = kt * kKeys + cg * 32;
       if (ok && kb + 31 <= rmin && rows_in) {  // warp-uniform: no key of the block is masked
