@@ -299,11 +299,12 @@ class CappedKVEngine:
     @staticmethod
     def _pick_splits(N: int, K: int, sms: int = 148) -> int:
         """Split K so that the grid holds about 256 CTAs (N / 128 column tiles per split,
-        at most 7 CTAs per cluster): measured best on B200 for the 7B decode shapes
-        (q/k/v 7, o and down 7, gate/up and lm_head 1)."""
+        at most 8 CTAs per cluster): measured best on B200 for the 7B decode shapes
+        (q/k/v 7, o and down 8, gate/up and lm_head 1; q/k/v at 8 and o at 9 or 10 were
+        slower, o and down at 8 faster than at 7)."""
         tiles = max(1, N // 128)
         want = (256 * sms // 148) // tiles
-        return max(1, min(want, K // 128, 7))
+        return max(1, min(want, K // 128, 8))
 
     @property
     def stream(self) -> int:
