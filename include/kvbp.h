@@ -269,7 +269,9 @@ int kvbp_decode_gemm_allreduce(kvbp_stream_t stream, int32_t M, int32_t N, int32
 int kvbp_pack_weight(kvbp_stream_t stream, int32_t N, int32_t K, const void* src, void* dst);
 int kvbp_unpack_weight(kvbp_stream_t stream, int32_t N, int32_t K, const void* src, void* dst);
 
-/* Greedy sampling: first index of the row maximum (numpy.argmax), kv_coupled_generator.py:344. */
+/* Greedy sampling: first index of the row maximum (numpy.argmax), kv_coupled_generator.py:344.
+ * logits [rows][ld] bf16, 16-byte aligned with ld a multiple of 8 (else status 1, nothing
+ * launched); rows <= 65535. */
 int kvbp_argmax(kvbp_stream_t stream, int32_t rows, int32_t vocab, int64_t ld, const void* logits, int32_t* out_ids);
 
 /* Greedy sampling over a vocabulary shard (tensor parallelism): keys_out[r] encodes the

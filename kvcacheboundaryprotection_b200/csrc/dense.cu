@@ -208,19 +208,23 @@ __device__ __forceinline__ bool arg_better(float av, int ai, float bv, int bi) {
   return av > bv || (av == bv && ai < bi);
 }
 
+// Grid (CS, rows), a cluster of CS CTAs per row: CTA c scans vectors [c, c + 1) * nvec / CS
+// of the row, and cluster rank 0 reduces the CTAs' winners over distributed shared memory.
 __global__ void argmax_kernel(const __nv_bfloat16* __restrict__ logits, long long ld, int V, int* __restrict__ out,
                               long long* __restrict__ keys, int index_offset) {
   pdl_launch_dependents();
   pdl_wait();
   __shared__ float sv[32];
   __shared__ int si[32];
-  const int r = blockIdx.x;
+  __shared__ float cta_v;  // this CTA's winner, read by cluster rank 0
+  __shared__ int cta_i;
+  const int r = blockIdx.y, CS = gridDim.x, c = blockIdx.x;
   const __nv_bfloat16* row = logits + r * ld;
   float bv = -__int_as_float(0x7f800000);
   int bi = 0x7fffffff;
   const int nvec = V / 8;
-  for (int j = threadIdx.x; j < nvec; j += blockDim.x) {
-    const uint4 w = reinterpret_cast<const uint4*>(row)[j];
+  const uint4* rv = reinterpret_cast<const uint4*>(row);
+  auto visit = [&](const uint4 w, int j) {  // the 8 logits of vector j
     const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
@@ -229,11 +233,25 @@ __global__ void argmax_kernel(const __nv_bfloat16* __restrict__ logits, long lon
       if (arg_better(a, ia, bv, bi)) bv = a, bi = ia;
       if (arg_better(b, ia + 1, bv, bi)) bv = b, bi = ia + 1;
     }
+  };
+  // four independent loads in flight per thread (the winner does not depend on the order
+  // in which candidates are visited: larger value, then smaller index)
+  const int v1 = static_cast<int>((static_cast<long long>(c + 1) * nvec) / CS);
+  int j = static_cast<int>((static_cast<long long>(c) * nvec) / CS) + threadIdx.x;
+  const int stride = blockDim.x;
+  for (; j + 3 * stride < v1; j += 4 * stride) {
+    uint4 w[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) w[q] = rv[j + q * stride];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) visit(w[q], j + q * stride);
   }
-  for (int j = nvec * 8 + threadIdx.x; j < V; j += blockDim.x) {
-    const float a = __bfloat162float(row[j]);
-    if (arg_better(a, j, bv, bi)) bv = a, bi = j;
-  }
+  for (; j < v1; j += stride) visit(rv[j], j);
+  if (c == CS - 1)
+    for (int k = nvec * 8 + threadIdx.x; k < V; k += stride) {
+      const float a = __bfloat162float(row[k]);
+      if (arg_better(a, k, bv, bi)) bv = a, bi = k;
+    }
 #pragma unroll
   for (int o = 16; o; o >>= 1) {
     const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
@@ -253,18 +271,28 @@ __global__ void argmax_kernel(const __nv_bfloat16* __restrict__ logits, long lon
       const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
       if (arg_better(ov, oi, bv, bi)) bv = ov, bi = oi;
     }
-    if (lane == 0) {
-      if (out) out[r] = bi;
-      if (keys) {
-        // (value, lowest index) as one integer: the largest key over vocabulary shards is
-        // the global first maximum
-        uint32_t u = __float_as_uint(bv);
-        u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-        const uint32_t idx = static_cast<uint32_t>(bi + index_offset);
-        keys[r] = static_cast<long long>((static_cast<unsigned long long>(u) << 32) | (0xFFFFFFFFu - idx));
-      }
+    if (lane == 0) cta_v = bv, cta_i = bi;
+  }
+  if (CS > 1) cluster_sync_all();  // every CTA's winner is in its shared memory
+  if (threadIdx.x == 0 && c == 0) {
+    bv = cta_v;
+    bi = cta_i;
+    for (int q = 1; q < CS; ++q) {
+      const float ov = ld_dsmem_f32(mapa_u32(smem_u32(&cta_v), q));
+      const int oi = __float_as_int(ld_dsmem_f32(mapa_u32(smem_u32(&cta_i), q)));
+      if (arg_better(ov, oi, bv, bi)) bv = ov, bi = oi;
+    }
+    if (out) out[r] = bi;
+    if (keys) {
+      // (value, lowest index) as one integer: the largest key over vocabulary shards is
+      // the global first maximum
+      uint32_t u = __float_as_uint(bv);
+      u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+      const uint32_t idx = static_cast<uint32_t>(bi + index_offset);
+      keys[r] = static_cast<long long>((static_cast<unsigned long long>(u) << 32) | (0xFFFFFFFFu - idx));
     }
   }
+  if (CS > 1) cluster_sync_all();  // no CTA leaves while rank 0 may still read its winner
 }
 
 __global__ void key_to_token_kernel(const long long* __restrict__ keys, int rows, int* __restrict__ tokens) {
@@ -358,12 +386,20 @@ int silu_mul(cudaStream_t st, int rows, int F, const void* gu, void* act) {
   return check_launch("silu_mul", le);
 }
 
+// CTAs per row: one per 2048 16-byte vectors, 1..8 (a portable cluster)
+static int argmax_cluster(int V) {
+  int cs = (V / 8) / 2048;
+  return cs < 1 ? 1 : (cs > 8 ? 8 : cs);
+}
+
 int argmax_rows(cudaStream_t st, int rows, int V, long long ld, const void* logits, int* out) {
   if (!logits || !out) return fail(kStatusArg, "argmax: null pointer");
   if (rows <= 0 || V <= 0 || ld < V) return fail(kStatusArg, "argmax: bad size");
   if ((ld % 8) || (reinterpret_cast<uintptr_t>(logits) & 15))
     return fail(kStatusArg, "argmax: rows must be 16-byte aligned (ld % 8 == 0)");
-  const cudaError_t le = launch_pdl(argmax_kernel, dim3(rows), dim3(1024), 0, st, dim3(0),
+  if (rows > 65535) return fail(kStatusArg, "argmax: %d rows exceed 65535", rows);
+  const int cs = argmax_cluster(V);
+  const cudaError_t le = launch_pdl(argmax_kernel, dim3(cs, rows), dim3(512), 0, st, cs > 1 ? dim3(cs, 1, 1) : dim3(0),
                                     static_cast<const __nv_bfloat16*>(logits), ld, V, out,
                                     static_cast<long long*>(nullptr), 0);
   return check_launch("argmax", le);
@@ -375,7 +411,9 @@ int argmax_key(cudaStream_t st, int rows, int V, long long ld, const void* logit
   if (rows <= 0 || V <= 0 || ld < V || index_offset < 0) return fail(kStatusArg, "argmax_key: bad size");
   if ((ld % 8) || (reinterpret_cast<uintptr_t>(logits) & 15))
     return fail(kStatusArg, "argmax_key: rows must be 16-byte aligned (ld % 8 == 0)");
-  const cudaError_t le = launch_pdl(argmax_kernel, dim3(rows), dim3(1024), 0, st, dim3(0),
+  if (rows > 65535) return fail(kStatusArg, "argmax_key: %d rows exceed 65535", rows);
+  const int cs = argmax_cluster(V);
+  const cudaError_t le = launch_pdl(argmax_kernel, dim3(cs, rows), dim3(512), 0, st, cs > 1 ? dim3(cs, 1, 1) : dim3(0),
                                     static_cast<const __nv_bfloat16*>(logits), ld, V, static_cast<int*>(nullptr),
                                     keys, index_offset);
   return check_launch("argmax_key", le);

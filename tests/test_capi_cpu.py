@@ -60,6 +60,7 @@ def test_host_validation_rejects_bad_arguments(L):
     st = L.kvbp_decode_attn_score(None, 1, 18, 2, 128, 64, 16, 16, 16, 16, None, 16, 16, None)
     assert st == 2  # group of 9 heads unsupported
     assert L.kvbp_argmax(None, 1, 100, 50, 16, 16) == 1  # ld < vocab
+    assert L.kvbp_argmax(None, 1, 100, 101, 16, 16) == 1  # rows not 16-byte aligned (ld % 8 != 0)
     cfg = capi.EvictCfg(0, 8, 0, 1, 25, 25, 1)
     n = C.c_int32()
     assert L.kvbp_prefill_select(None, 1, 100, C.byref(cfg), None, 16, 16, 10, C.byref(n), None) == 1

@@ -1,0 +1,45 @@
+"""Greedy sampling kernel (kvbp_argmax) against numpy.argmax's rule, the reference's
+sampler (kv_coupled_generator.py:337-344): the first index of the maximum, the first NaN
+if any, on bf16 logits of the full Qwen2.5 vocabulary (several CTAs per row, reduced over
+a thread-block cluster) and on ragged row lengths with padded rows."""
+
+import pytest
+import torch
+
+from kvcacheboundaryprotection_b200 import capi
+
+pytestmark = pytest.mark.gpu
+
+
+def _first_argmax(x: torch.Tensor) -> list:
+    out = []
+    for row in x.float().cpu():
+        nan = torch.nonzero(torch.isnan(row))
+        if nan.numel():
+            out.append(int(nan[0]))
+            continue
+        out.append(int(torch.nonzero(row == row.max())[0]))
+    return out
+
+
+@pytest.mark.parametrize("B,V", [(16, 152064), (3, 4097), (5, 8), (1, 1), (2, 40000)])
+def test_argmax_first_maximum(B, V):
+    g = torch.Generator(device="cuda").manual_seed(V)
+    ld = (V + 7) // 8 * 8  # rows must start on 16-byte boundaries
+    buf = torch.randn(B, ld, generator=g, device="cuda").to(torch.bfloat16)
+    buf[:, V:] = 100.0  # padding past the vocabulary is never a candidate
+    logits = buf[:, :V]
+    if B > 1 and V > 64:
+        logits[1, V - 1] = 30.0
+        logits[1, 7] = 30.0  # tie: the lower index wins
+        logits[0] = -2.0     # all equal: index 0
+    if B > 2 and V > 64:
+        logits[2, 40] = float("nan")  # a NaN wins
+        logits[2, 3] = 50.0
+    out = torch.empty(B, dtype=torch.int32, device="cuda")
+    L = capi.lib()
+    st = torch.cuda.current_stream().cuda_stream
+    for _ in range(2):  # the result does not depend on an earlier call
+        capi.check(L.kvbp_argmax(st, B, V, ld, buf.data_ptr(), out.data_ptr()), "argmax")
+        torch.cuda.synchronize()
+        assert out.tolist() == _first_argmax(logits)
