@@ -43,3 +43,26 @@ def test_argmax_first_maximum(B, V):
         capi.check(L.kvbp_argmax(st, B, V, ld, buf.data_ptr(), out.data_ptr()), "argmax")
         torch.cuda.synchronize()
         assert out.tolist() == _first_argmax(logits)
+
+
+def test_argmax_keys_over_shards_match_full_row():
+    # vocabulary shards long enough to be split over a cluster of CTAs per row
+    g = torch.Generator(device="cuda").manual_seed(11)
+    B, per, shards = 4, 40000, 3
+    V = per * shards
+    logits = torch.randn(B, V, generator=g, device="cuda").to(torch.bfloat16)
+    logits[1, per + 5] = logits[1, 2 * per + 9] = 40.0  # tie across shards
+    logits[2, per - 1] = logits[2, per - 2] = 40.0      # tie at the end of a shard
+    L = capi.lib()
+    st = torch.cuda.current_stream().cuda_stream
+    keys = torch.full((B,), torch.iinfo(torch.int64).min, dtype=torch.int64, device="cuda")
+    for r in range(shards):
+        k = torch.empty(B, dtype=torch.int64, device="cuda")
+        part = logits[:, r * per : (r + 1) * per].contiguous()
+        capi.check(L.kvbp_argmax_key(st, B, per, per, part.data_ptr(), r * per, k.data_ptr()), "argmax_key")
+        torch.maximum(keys, k, out=keys)
+    tok = torch.empty(B, dtype=torch.int32, device="cuda")
+    capi.check(L.kvbp_key_to_token(st, B, keys.data_ptr(), tok.data_ptr()), "key_to_token")
+    torch.cuda.synchronize()
+    assert tok.tolist() == _first_argmax(logits)
+    assert tok[1].item() == per + 5 and tok[2].item() == per - 2
