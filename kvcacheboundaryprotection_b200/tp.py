@@ -177,6 +177,18 @@ def allreduce_buffer_bytes(world: int, M: int, N: int, splits: int) -> int:
     return (flags + 255) // 256 * 256 + 2 * world * M * N * 4
 
 
+def allreduce_splits(cfg: ModelConfig, world: int) -> dict:
+    """Split-K factors of the row-parallel o and down GEMMs under tensor parallelism.  The
+    fused allreduce pairs the same (tile, row slice) on every rank, so every rank uses one
+    split count (their K differs when the shards are uneven): the smallest of the ranks'
+    single-GPU choices, and at most 7 -- every split adds a row slice of flags and peer
+    stores to the allreduce (7B at TP=2: 4725 tok/s with 7, 4476 with 8)."""
+    k_of = {"o": lambda p: len(p.q_heads) * cfg.head_dim, "down": lambda p: p.ffn_hi - p.ffn_lo}
+    return {name: min(min(CappedKVEngine._pick_splits(cfg.hidden, k(tp_plan(cfg, world, r))), 7)
+                      for r in range(world))
+            for name, k in k_of.items()}
+
+
 class TPEngine(CappedKVEngine):
     """One rank of a tensor-parallel decode.  ``weights`` is the FULL weight dict (it is
     sharded here) or this rank's prebuilt ``FusedWeights``.  ``collective`` performs the
@@ -199,13 +211,7 @@ class TPEngine(CappedKVEngine):
         super().__init__(lcfg, weights, **kw)
         self.part = torch.zeros(self.B, cfg.hidden, dtype=torch.float32, device=self.dev)
         self.keys = torch.zeros(self.B, dtype=torch.int64, device=self.dev)
-        # the fused allreduce pairs the same (tile, row slice) on every rank: use one split
-        # count for o and down across ranks (their K differs when the shards are uneven).
-        # At most 7: every split adds a row slice of flags and peer stores to the allreduce
-        # (7B at TP=2: 4725 tok/s with 7, 4476 with 8).
-        for name, k_of in (("o", lambda p: len(p.q_heads) * cfg.head_dim), ("down", lambda p: p.ffn_hi - p.ffn_lo)):
-            self.splits[name] = min(min(self._pick_splits(cfg.hidden, k_of(tp_plan(cfg, plan.world, r))), 7)
-                                    for r in range(plan.world))
+        self.splits.update(allreduce_splits(cfg, plan.world))
         self.symm = None
         if fused_allreduce and plan.world > 1:
             sp = max(self.splits["o"], self.splits["down"])

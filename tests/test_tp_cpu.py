@@ -73,3 +73,19 @@ def test_sharded_projections_sum_to_the_full_ones(world):
     assert torch.allclose(o_sum, o_full, atol=1e-4)
     assert torch.allclose(d_sum, d_full, atol=1e-4)
     assert torch.allclose(torch.cat(logits, 1), x @ w["lm_head"].t(), atol=1e-4)
+
+
+def test_split_k_choices():
+    # single GPU: about 256 CTAs per GEMM, at most 8 per cluster
+    from kvcacheboundaryprotection_b200.engine import CappedKVEngine
+
+    cfg = get_config("qwen2.5-7b")
+    H, F, V = cfg.hidden, cfg.ffn, cfg.vocab
+    qkv_n = (cfg.n_heads + 2 * cfg.n_kv_heads) * cfg.head_dim
+    pick = CappedKVEngine._pick_splits
+    assert [pick(qkv_n, H), pick(H, H), pick(2 * F, H), pick(H, F), pick(V, H)] == [7, 8, 1, 8, 1]
+    # tensor parallel: one count for every rank, at most 7 (fused allreduce)
+    from kvcacheboundaryprotection_b200.tp import allreduce_splits
+
+    assert allreduce_splits(cfg, 2) == {"o": 7, "down": 7}
+    assert allreduce_splits(cfg, 8) == {"o": 3, "down": 7}  # 3 or 4 query heads per rank
