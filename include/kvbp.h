@@ -179,8 +179,10 @@ int kvbp_prefill_compact(kvbp_stream_t stream, const kvbp_state* st, int32_t P, 
  * assigns it (XLA pre-allocates most of the GPU, so a cudaMalloc of its own can fail).
  * Limit: batch * prompt <= 1,048,576 positions, else KVBP_ERR_ARG.  The array costs
  * 1 MiB on every GPU that loads the library, until the process exits.  The first call
- * on a device looks up the array's device address (with that device current); make that
- * first call before any stream capture.  All calls share the array: calls that overlap
+ * in a CUDA context looks up the array's device address (with that context current) and
+ * caches it under the context's unique ID, so a context made after cudaDeviceReset or a
+ * non-primary context gets its own lookup; make that first call before any stream
+ * capture.  All calls share the array: calls that overlap
  * on the GPU (e.g. on two streams) race; calls on one stream are ordered and safe.  Each
  * call rewrites every flag it uses, so no clearing is needed. */
 int kvbp_prefill_evict_noalloc(kvbp_stream_t stream, const kvbp_state* st, int32_t P, const kvbp_evict_cfg* cfg,
@@ -247,9 +249,11 @@ int kvbp_decode_qkv_gemm(kvbp_stream_t stream, int32_t M, int32_t n_heads, int32
  * of every rank of the group (peer_bases[q] = rank q's buffer, mapped into this process;
  * a device array), and each tile is finished as h = bf16(h + bf16(sum over ranks, in
  * rank order)) with ss_out as in epilogue 1 -- identical on every rank.  Buffer layout
- * (buffer_bytes each): u32 flags [2][world][N/128][splits], then at the next 256-byte
- * boundary fp32 [2][world][M][N]; the flags are zeroed (and the ranks synchronised)
- * before a run.  call_index (0..254) numbers the allreduces of one step (parity =
+ * (buffer_bytes each): u32 flags [2][world][1024] (word tile * 16 + split of each
+ * (parity, source rank) row; N <= 8192), then fp32 [2][world][M][N] at byte offset
+ * 8192 * world.  The flag area does not depend on the call's split count or N, so calls
+ * with different splits share one buffer safely.  The flags are zeroed (and the ranks
+ * synchronised) before a run.  call_index (0..254) numbers the allreduces of one step (parity =
  * call_index & 1 double-buffers the receive area) and *epoch must differ between steps
  * (flags hold epoch * 256 + call_index + 1).  Every rank must make the same calls in the
  * same order; waits are bounded (KVBP_DEV_PEER_TIMEOUT).  One rank per GPU: the ranks'

@@ -943,36 +943,66 @@ int kvbp_gather_kv(kvbp_stream_t stream, const void* src_k, const void* src_v, v
 // per-position victim flags that sit between kvbp_prefill_select and kvbp_prefill_compact.
 // This variant keeps them in a fixed array that every GPU loading the library holds until
 // the process exits.
+#include <cuda.h>
+
 #include <mutex>
 
 namespace {
 
 constexpr long long kNoAllocMaxPositions = 1LL << 20;  // batch * prompt flags (1 MiB)
-constexpr int kNoAllocMaxDevices = 64;
+constexpr int kNoAllocCacheEntries = 64;
 
 __device__ __align__(256) uint8_t g_prefill_victim_scratch[kNoAllocMaxPositions];
 
+// Cache of the array's device address per CUDA context.  A context's ID (cuCtxGetId) is
+// unique for the life of the process, so a context created after cudaDeviceReset, or a
+// non-primary context on the same device, never picks up a stale address.
+struct NoAllocEntry {
+  unsigned long long ctx_id;
+  uint8_t* ptr;
+};
 std::mutex g_noalloc_mu;
-uint8_t* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+NoAllocEntry g_noalloc_cache[kNoAllocCacheEntries] = {};
+int g_noalloc_used = 0;
 
-// Device address of the scratch array on the current device.  In host code the array's
-// name is only a host-side stand-in, so the address is looked up once per device (with
-// that device current) and cached.
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long*);
+
+template <typename Fn>
+Fn driver_fn(const char* name) {
+  void* ptr = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPoint(name, &ptr, cudaEnableDefault, &q) == cudaSuccess && q == cudaDriverEntryPointSuccess)
+    return reinterpret_cast<Fn>(ptr);
+  return nullptr;
+}
+
+// Device address of the scratch array in the current context.  In host code the array's
+// name is only a host-side stand-in, so the address is looked up with the context current
+// (cudaGetSymbolAddress) and cached under the context's ID.
 int noalloc_scratch(uint8_t** out) {
   int dev = -1;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return kvbp::fail(kvbp::kStatusCuda, "kvbp_prefill_evict_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
-  if (dev < 0 || dev >= kNoAllocMaxDevices)
-    return kvbp::fail(kvbp::kStatusUnsupported, "kvbp_prefill_evict_noalloc: device %d beyond %d", dev, kNoAllocMaxDevices);
+  static CtxGetCurrentFn get_ctx = driver_fn<CtxGetCurrentFn>("cuCtxGetCurrent");
+  static CtxGetIdFn get_id = driver_fn<CtxGetIdFn>("cuCtxGetId");
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  // no context current yet on this thread: the lookup below initialises one, uncached
+  const bool have_id = get_ctx && get_id && get_ctx(&ctx) == CUDA_SUCCESS && ctx && get_id(ctx, &id) == CUDA_SUCCESS;
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (!g_noalloc_ptr[dev]) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_prefill_victim_scratch);
-    if (e != cudaSuccess || !p)
-      return kvbp::fail(kvbp::kStatusCuda, "kvbp_prefill_evict_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
-    g_noalloc_ptr[dev] = static_cast<uint8_t*>(p);
-  }
-  *out = g_noalloc_ptr[dev];
+  if (have_id)
+    for (int i = 0; i < g_noalloc_used; ++i)
+      if (g_noalloc_cache[i].ctx_id == id) {
+        *out = g_noalloc_cache[i].ptr;
+        return kvbp::kStatusOk;
+      }
+  void* p = nullptr;
+  e = cudaGetSymbolAddress(&p, g_prefill_victim_scratch);
+  if (e != cudaSuccess || !p)
+    return kvbp::fail(kvbp::kStatusCuda, "kvbp_prefill_evict_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+  if (have_id && g_noalloc_used < kNoAllocCacheEntries) g_noalloc_cache[g_noalloc_used++] = {id, static_cast<uint8_t*>(p)};
+  *out = static_cast<uint8_t*>(p);
   return kvbp::kStatusOk;
 }
 

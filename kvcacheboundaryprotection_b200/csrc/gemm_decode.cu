@@ -89,18 +89,18 @@ struct Args {
   __nv_bfloat16* kcache;  // [M][Hkv][S][128]
   __nv_bfloat16* vcache;
   // RESID + ALLREDUCE epilogue: every rank's symmetric buffer holds
-  //   flags u32 [2][world][N/128][splits], then (256-byte aligned) recv f32 [2][world][M][N]
+  //   flags u32 [2][world][kArFlagSlots] (slot = tile * kMaxSplits + split), then
+  //   recv f32 [2][world][M][N].  The flag area's size depends on the world size only, so
+  //   calls with different split counts or widths never overlap each other's flags.
   const unsigned long long* peers;  // [world] base address of each rank's buffer (device array)
   int world, rank, call;            // call: index of this allreduce within the step (parity = call & 1)
   const int* epoch;                 // device counter that differs between steps
 };
 
-__host__ __device__ inline size_t ar_flag_words(int world, int tiles, int splits) {
-  return static_cast<size_t>(2) * world * tiles * splits;
-}
-__host__ __device__ inline size_t ar_recv_offset(int world, int tiles, int splits) {
-  return (ar_flag_words(world, tiles, splits) * 4 + 255) / 256 * 256;
-}
+constexpr int kArMaxTiles = 64;                         // N <= 8192
+constexpr int kArFlagSlots = kArMaxTiles * kMaxSplits;  // per (parity, source rank)
+__host__ __device__ inline size_t ar_flag_words(int world) { return static_cast<size_t>(2) * world * kArFlagSlots; }
+__host__ __device__ inline size_t ar_recv_offset(int world) { return ar_flag_words(world) * 4; }  // 256-byte multiple
 
 __device__ __forceinline__ void st_release_sys_u32(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -419,10 +419,10 @@ __global__ void __launch_bounds__(kThreads) decode_gemm_kernel(const __grid_cons
         if (rank == 0 && r >= M) a.ss_out[tile * 32 + r] = 0.f;
       }
     } else if (EPI == kResidAR) {
-      const int W = a.world, tiles = gridDim.x;
+      const int W = a.world;
       const int par = a.call & 1;
       const uint32_t v = static_cast<uint32_t>(*a.epoch) * 256u + static_cast<uint32_t>(a.call) + 1u;
-      const size_t roff = ar_recv_offset(W, tiles, cs);
+      const size_t roff = ar_recv_offset(W);
       // 1. this rank's rows of the tile into every rank's receive buffer (slot `rank`)
       for (int e = tid; e < nrows * (BN / 2); e += kConsumers) {
         const int r = r_lo + e / (BN / 2), c = 2 * (e % (BN / 2));
@@ -433,12 +433,12 @@ __global__ void __launch_bounds__(kThreads) decode_gemm_kernel(const __grid_cons
       }
       __threadfence_system();
       named_bar(1, kConsumers);
-      const size_t fslot = (static_cast<size_t>(tile) * cs + blockIdx.y);
+      const size_t fslot = static_cast<size_t>(tile) * kMaxSplits + blockIdx.y;
       if (tid < W)
-        st_release_sys_u32(reinterpret_cast<uint32_t*>(a.peers[tid]) + (static_cast<size_t>(par) * W + a.rank) * tiles * cs + fslot, v);
+        st_release_sys_u32(reinterpret_cast<uint32_t*>(a.peers[tid]) + (static_cast<size_t>(par) * W + a.rank) * kArFlagSlots + fslot, v);
       // 2. every rank's rows of this slice have landed here
       if (tid < W) {
-        const uint32_t* f = reinterpret_cast<const uint32_t*>(a.peers[a.rank]) + (static_cast<size_t>(par) * W + tid) * tiles * cs + fslot;
+        const uint32_t* f = reinterpret_cast<const uint32_t*>(a.peers[a.rank]) + (static_cast<size_t>(par) * W + tid) * kArFlagSlots + fslot;
         uint32_t spins = 0;
         while (ld_acquire_sys_u32(f) != v) {
           if (++spins > (1u << 24)) {
@@ -698,7 +698,8 @@ int decode_gemm_allreduce(cudaStream_t stream, int M, int N, int K, const void* 
   if (!h || !ss_out || !peers || !epoch) return fail(kStatusArg, "decode_gemm_allreduce: null pointer");
   if (world < 1 || world > 64 || rank < 0 || rank >= world || call < 0 || call > 254)
     return fail(kStatusArg, "decode_gemm_allreduce: bad world %d / rank %d / call %d", world, rank, call);
-  if (N <= 0 || N % BN || splits < 1 || splits > kMaxSplits) return fail(kStatusArg, "decode_gemm_allreduce: bad size");
+  if (N <= 0 || N % BN || N / BN > kArMaxTiles || splits < 1 || splits > kMaxSplits)
+    return fail(kStatusArg, "decode_gemm_allreduce: bad size (N %d, splits %d)", N, splits);
   {
     // the ranks' CTAs wait on each other: every CTA of the grid must be resident at once
     const int MT = M > 16 ? 2 : 1;
@@ -725,7 +726,7 @@ int decode_gemm_allreduce(cudaStream_t stream, int M, int N, int K, const void* 
       return fail(kStatusUnsupported, "decode_gemm_allreduce: %d column tiles but only %d clusters of %d resident",
                   N / BN, clusters, splits);
   }
-  const size_t need = ar_recv_offset(world, N / BN, splits) + static_cast<size_t>(2) * world * M * N * 4;
+  const size_t need = ar_recv_offset(world) + static_cast<size_t>(2) * world * M * N * 4;
   if (buffer_bytes < 0 || static_cast<size_t>(buffer_bytes) < need)
     return fail(kStatusArg, "decode_gemm_allreduce: symmetric buffer of %lld bytes < %zu needed", buffer_bytes, need);
   if (reinterpret_cast<uintptr_t>(h) & 3) return fail(kStatusArg, "decode_gemm_allreduce: h rows must be 4-byte aligned");

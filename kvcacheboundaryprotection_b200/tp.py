@@ -171,10 +171,26 @@ class SymmetricBuffer:
         dist.barrier(group=self.group)
 
 
-def allreduce_buffer_bytes(world: int, M: int, N: int, splits: int) -> int:
+AR_MAX_TILES = 64  # N <= 8192 columns per fused-allreduce GEMM
+AR_MAX_SPLITS = 16
+AR_FLAG_SLOTS = AR_MAX_TILES * AR_MAX_SPLITS  # flag words per (parity, source rank)
+
+
+def allreduce_flag_word(world: int, parity: int, src_rank: int, tile: int, split: int) -> int:
+    """Index of the u32 flag that ``src_rank`` raises for (tile, split) of a call of this
+    parity, in every rank's symmetric buffer: the same for every split count and width."""
+    assert 0 <= tile < AR_MAX_TILES and 0 <= split < AR_MAX_SPLITS and 0 <= src_rank < world
+    return (parity * world + src_rank) * AR_FLAG_SLOTS + tile * AR_MAX_SPLITS + split
+
+
+def allreduce_recv_offset(world: int) -> int:
+    """Byte offset of the fp32 receive area [2][world][M][N] (after the flags)."""
+    return 2 * world * AR_FLAG_SLOTS * 4
+
+
+def allreduce_buffer_bytes(world: int, M: int, N: int) -> int:
     """Size of the symmetric buffer kvbp_decode_gemm_allreduce needs (include/kvbp.h)."""
-    flags = 2 * world * (N // 128) * splits * 4
-    return (flags + 255) // 256 * 256 + 2 * world * M * N * 4
+    return allreduce_recv_offset(world) + 2 * world * M * N * 4
 
 
 def allreduce_splits(cfg: ModelConfig, world: int) -> dict:
@@ -214,8 +230,7 @@ class TPEngine(CappedKVEngine):
         self.splits.update(allreduce_splits(cfg, plan.world))
         self.symm = None
         if fused_allreduce and plan.world > 1:
-            sp = max(self.splits["o"], self.splits["down"])
-            self.symm = SymmetricBuffer(allreduce_buffer_bytes(plan.world, self.B, cfg.hidden, sp), self.dev)
+            self.symm = SymmetricBuffer(allreduce_buffer_bytes(plan.world, self.B, cfg.hidden), self.dev)
 
     def _allreduce_gemm(self, name, K, w, x, ldx, call, ss_out) -> None:
         c = self.cfg

@@ -66,3 +66,31 @@ def test_argmax_keys_over_shards_match_full_row():
     torch.cuda.synchronize()
     assert tok.tolist() == _first_argmax(logits)
     assert tok[1].item() == per + 5 and tok[2].item() == per - 2
+
+
+def test_argmax_keys_signed_zero_and_nan_across_shards():
+    """numpy.argmax ranks -0.0 and +0.0 equal (the lower index wins) and returns the first
+    NaN whatever its sign: the sharded keys must agree when those cases span shards."""
+    B, per, shards = 3, 40000, 3
+    V = per * shards
+    g = torch.Generator(device="cuda").manual_seed(5)
+    logits = -(torch.rand(B, V, generator=g, device="cuda") + 0.5).to(torch.bfloat16)
+    bits = logits.view(torch.int16)
+    logits[0, 10] = -0.0        # shard 0: negative zero first ...
+    logits[0, per + 2] = 0.0    # ... shard 1: positive zero later -> index 10
+    logits[1, 3] = 40.0
+    bits[1, 2 * per + 7] = -64  # 0xFFC0: a negative NaN in shard 2 wins over the finite 40
+    bits[2, per + 1] = -64      # negative NaN in shard 1 ...
+    bits[2, 100] = 0x7FC0       # ... but a positive NaN comes first in shard 0
+    L = capi.lib()
+    st = torch.cuda.current_stream().cuda_stream
+    keys = torch.full((B,), torch.iinfo(torch.int64).min, dtype=torch.int64, device="cuda")
+    for r in range(shards):
+        k = torch.empty(B, dtype=torch.int64, device="cuda")
+        part = logits[:, r * per : (r + 1) * per].contiguous()
+        capi.check(L.kvbp_argmax_key(st, B, per, per, part.data_ptr(), r * per, k.data_ptr()), "argmax_key")
+        torch.maximum(keys, k, out=keys)
+    tok = torch.empty(B, dtype=torch.int32, device="cuda")
+    capi.check(L.kvbp_key_to_token(st, B, keys.data_ptr(), tok.data_ptr()), "key_to_token")
+    torch.cuda.synchronize()
+    assert tok.tolist() == _first_argmax(logits) == [10, 2 * per + 7, 100]

@@ -89,3 +89,30 @@ def test_split_k_choices():
 
     assert allreduce_splits(cfg, 2) == {"o": 7, "down": 7}
     assert allreduce_splits(cfg, 8) == {"o": 3, "down": 7}  # 3 or 4 query heads per rank
+
+
+def test_allreduce_flag_layout_is_independent_of_the_call():
+    """The o and down fused-allreduce GEMMs share one symmetric buffer with different
+    split counts (7B at TP=8: 3 and 7).  Every (parity, source rank, tile, split) flag word
+    is distinct, all flags lie before the receive area, and the receive area's offset
+    depends on the world size only."""
+    from kvcacheboundaryprotection_b200.tp import (AR_MAX_SPLITS, AR_MAX_TILES, allreduce_buffer_bytes,
+                                                   allreduce_flag_word, allreduce_recv_offset, allreduce_splits)
+
+    cfg = get_config("qwen2.5-7b")
+    world = 8
+    sp = allreduce_splits(cfg, world)
+    assert sp["o"] != sp["down"]  # the case that used to overlap
+    tiles = cfg.hidden // 128
+    words = {}
+    for call, name in enumerate(("o", "down")):  # o = even call index, down = odd
+        for src in range(world):
+            for t in range(tiles):
+                for s in range(sp[name]):
+                    wd = allreduce_flag_word(world, call & 1, src, t, s)
+                    assert wd not in words, (name, src, t, s, words.get(wd))
+                    words[wd] = (name, src, t, s)
+    roff = allreduce_recv_offset(world)
+    assert max(words) * 4 + 4 <= roff and roff % 256 == 0
+    assert allreduce_flag_word(world, 1, world - 1, AR_MAX_TILES - 1, AR_MAX_SPLITS - 1) * 4 + 4 == roff
+    assert allreduce_buffer_bytes(world, 16, cfg.hidden) == roff + 2 * world * 16 * cfg.hidden * 4
