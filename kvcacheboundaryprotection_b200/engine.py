@@ -12,14 +12,21 @@ One decode step is::
 
     kvbp_append_evict   new position -> lowest free slot; cadence eviction
     kvbp_embed
-    L x [ kvbp_add_rmsnorm, GEMM qkv, kvbp_qkv_rope_scatter, kvbp_decode_attn_score,
-          GEMM o, kvbp_add_rmsnorm, GEMM gate|up, kvbp_silu_mul, GEMM down ]
-    kvbp_add_rmsnorm (final), GEMM lm_head, kvbp_argmax
+    kvbp_row_sumsq
+    L x [ kvbp_decode_qkv_gemm   (RMSNorm prologue; bias, q/k norm, RoPE, K/V slot store)
+          kvbp_decode_attn_score (attention over the slots + per-slot score)
+          kvbp_decode_gemm o     (residual epilogue)
+          kvbp_decode_gemm gu    (RMSNorm prologue, SwiGLU epilogue)
+          kvbp_decode_gemm down  (residual epilogue) ]
+    kvbp_decode_gemm lm_head (final RMSNorm prologue), kvbp_argmax
     kvbp_score_update
 
 Every step-dependent value (step counter, positions, slots) lives on the device, so
-one captured CUDA graph replays every step.  The GEMMs are cuBLAS (torch.mm) with
-bf16 output and float32 accumulation; everything else is this package's kernels.
+one captured CUDA graph replays every step.  The decode GEMMs are this package's
+weight-streaming sm_100a kernels over packed weights (``gemm="kvbp"``, the default);
+``gemm="cublas"`` runs them as torch.mm with bf16 output and float32 accumulation,
+with standalone norm / RoPE / SwiGLU kernels around them.  The prefill projections are
+cuBLAS either way.
 
 The reference computes the same step in ``KVCoupledQwen35Generator`` (host loop,
 ``src/counterfact_kv_eviction/kv_coupled_generator.py:336-516``) around
@@ -173,6 +180,11 @@ class FusedWeights:
             biggest = max(L[k].numel() for L in self.layers for k in self.PACKED)
             self._scratch = torch.empty(max(n, biggest), dtype=torch.bfloat16, device=w.device)
         return unpack_weight(w, self._scratch[:n].view(w.shape))
+
+    def streamed_bytes(self, batch: int) -> int:
+        """Weight bytes one decode step reads: every matrix, bias and norm, the lm_head in
+        full, but only ``batch`` rows of the embedding table (a lookup, not a stream)."""
+        return self.nbytes() - 2 * self.embed_w.numel() + 2 * batch * self.cfg.hidden
 
     def nbytes(self) -> int:
         n = self.embed_w.numel() + (0 if self.lm_w is self.embed_w else self.lm_w.numel()) + self.final_norm.numel()

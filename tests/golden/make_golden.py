@@ -18,8 +18,13 @@ Fixtures:
 * ``e2e_parity_qwen2.json`` -- the reference generator driven by the numpy forward
   (``oracle.model``) on the small ``parity-qwen2`` decoder, greedy, with per-step
   logit summaries (used by the GPU parity test).
+* ``e2e_tiny_qwen2_lru.json`` -- the same at the CPU-runnable plumbing configuration:
+  the 4-layer ``tiny-qwen2`` decoder (hidden 1024, 8/2 heads, vocab 151936), a
+  1024-token prompt, LRU, capacity 256, max-cache-len 2048, protect-frac 0.10,
+  evict-every 8, 128 greedy tokens.
 
-Usage:  python tests/golden/make_golden.py [--ref /root/reference] [--only NAME]
+Usage:  python tests/golden/make_golden.py --ref REFERENCE_DIR [--only NAME]
+        (or set KVBP_REFERENCE to the reference project's directory)
 """
 
 from __future__ import annotations
@@ -27,6 +32,7 @@ from __future__ import annotations
 import argparse
 import importlib.util
 import json
+import os
 import sys
 from pathlib import Path
 
@@ -269,15 +275,19 @@ def make_e2e(ref: Path, preset: str, n_prompt: int, cap: int, max_cache: int, ma
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("KVBP_REFERENCE"),
+                    help="the reference project's directory (default: $KVBP_REFERENCE)")
     ap.add_argument("--only", default=None)
     a = ap.parse_args()
+    if not a.ref:
+        ap.error("give --ref or set KVBP_REFERENCE")
     ref = Path(a.ref)
     jobs = {
         "policy_kats.json": lambda: make_policy_kats(ref),
         "generator_kats.json": lambda: make_generator_kats(ref),
         "e2e_parity_qwen2.json": lambda: make_e2e(ref, "parity-qwen2", 300, 64, 512, 40, "lru"),
         "e2e_parity_qwen2_h2o.json": lambda: make_e2e(ref, "parity-qwen2", 300, 64, 512, 40, "h2o_faithful"),
+        "e2e_tiny_qwen2_lru.json": lambda: make_e2e(ref, "tiny-qwen2", 1024, 256, 2048, 128, "lru"),
     }
     for fname, fn in jobs.items():
         if a.only and a.only != fname:
