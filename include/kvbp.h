@@ -57,6 +57,7 @@ typedef struct CUstream_st* kvbp_stream_t; /* == cudaStream_t */
 #define KVBP_POLICY_ADAKV 5
 #define KVBP_POLICY_QUEST 6
 #define KVBP_POLICY_STREAMINGLLM 7
+#define KVBP_POLICY_RANDOM 8 /* victims sampled on the host: kvbp_append_evict_listed */
 
 const char* kvbp_version(void);
 const char* kvbp_last_error(void);
@@ -148,17 +149,36 @@ int kvbp_score_update(kvbp_stream_t stream, const kvbp_state* st, const int32_t*
  * (kv_coupled_generator.py:549-604).  Outputs cur_pos[b] (position to forward) and
  * write_slot[b] (its slot, -1 if evicted at this step); appends victims to
  * evlog [B][evcap] (evcount [B]); logs tokens[b] into token_log[B][log_steps] and the
- * retained count into retained_log[B][log_steps+1] when those are non-NULL. */
+ * retained count into retained_log[B][log_steps+1] when those are non-NULL.
+ * KVBP_POLICY_RANDOM is rejected here (KVBP_ERR_ARG): use kvbp_append_evict_listed. */
 int kvbp_append_evict(kvbp_stream_t stream, const kvbp_state* st, const kvbp_evict_cfg* cfg, int32_t* seq_step,
                       int32_t* next_pos, int32_t* cur_pos, int32_t* write_slot, const int32_t* tokens,
                       int32_t* token_log, int32_t log_steps, int32_t* evlog, int32_t* evcount, int32_t evcap,
                       int32_t* retained_log, int32_t* dev_err);
 
+/* K3 with the victims chosen on the host -- the random policy's path.
+ * RandomEvictionPolicy (src/counterfact_kv_eviction/policies.py:1553-1582) draws its
+ * victims with Python's random.Random(42).sample over the eligible keys in dict order,
+ * so they are computed by the host (bit-exact with the reference's generator) and
+ * handed in here.  Same as kvbp_append_evict, except that at a cadence step the victims
+ * are victim_pos[b][0..victim_count[b]) (absolute positions, in eviction order, each
+ * retained after this step's append; victim_pos is [B][victim_stride]) instead of the
+ * kernel's protection + top-k; the hard-capacity guardrail (kv_coupled_generator.py:
+ * 588-604) still runs after them.  Unknown or repeated positions are skipped
+ * (KVBP_DEV_INDEX for unknown).  Off-cadence steps ignore the list. */
+int kvbp_append_evict_listed(kvbp_stream_t stream, const kvbp_state* st, const kvbp_evict_cfg* cfg,
+                             int32_t* seq_step, int32_t* next_pos, int32_t* cur_pos, int32_t* write_slot,
+                             const int32_t* tokens, int32_t* token_log, int32_t log_steps, int32_t* evlog,
+                             int32_t* evcount, int32_t evcap, int32_t* retained_log, const int32_t* victim_pos,
+                             const int32_t* victim_count, int32_t victim_stride, int32_t* dev_err);
+
 /* K3 at step 0 -- victim selection over the P prompt positions after prefill
  * (kv_coupled_generator.py:229-239 with force_if_over_capacity).  scores [B][P] are the
  * prefill per-key scores (NULL = zeros, as for LRU).  Writes victim [B][P] flags and the
  * policy victims, in eviction order, to evlog [B][evcap][0..n).  *n_policy_victims
- * receives n (identical for every sequence). */
+ * receives n (identical for every sequence).  KVBP_POLICY_RANDOM is rejected
+ * (KVBP_ERR_ARG): its step-0 victims come from the host, which writes the flags and the
+ * eviction-ordered log itself and calls kvbp_prefill_compact. */
 int kvbp_prefill_select(kvbp_stream_t stream, int32_t B, int32_t P, const kvbp_evict_cfg* cfg, const float* scores,
                         uint8_t* victim, int32_t* evlog, int32_t evcap, int32_t* n_policy_victims,
                         int32_t* dev_err);

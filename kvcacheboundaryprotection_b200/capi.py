@@ -36,6 +36,7 @@ POLICY_IDS = {
     "adakv": 5,
     "quest": 6,
     "streamingllm": 7,
+    "random": 8,  # victims sampled on the host, applied by kvbp_append_evict_listed
 }
 
 
@@ -88,6 +89,10 @@ SIGNATURES = {
     "kvbp_append_evict": (
         C.c_int,
         [P, C.POINTER(State), C.POINTER(EvictCfg), P, P, P, P, P, P, I32, P, P, I32, P, P],
+    ),
+    "kvbp_append_evict_listed": (
+        C.c_int,
+        [P, C.POINTER(State), C.POINTER(EvictCfg), P, P, P, P, P, P, I32, P, P, I32, P, P, P, I32, P],
     ),
     "kvbp_prefill_select": (C.c_int, [P, I32, I32, C.POINTER(EvictCfg), P, P, P, I32, C.POINTER(C.c_int32), P]),
     "kvbp_prefill_compact": (

@@ -43,6 +43,7 @@ int kvbp_policy_id(const char* name) {
       {"adakv", KVBP_POLICY_ADAKV},
       {"quest", KVBP_POLICY_QUEST},
       {"streamingllm", KVBP_POLICY_STREAMINGLLM},
+      {"random", KVBP_POLICY_RANDOM},
   };
   for (const auto& e : table)
     if (strcmp(e.n, name) == 0) return e.id;

@@ -324,6 +324,10 @@ struct AppendArgs {
   int evcap;
   int* retained_log;    // [B][log_steps + 1] retained count after step s (may be null)
   int* err;
+  // victims chosen on the host (the random policy): [B][ext_stride] positions, ext_n [B]
+  const int* ext_pos;
+  const int* ext_n;
+  int ext_stride;
 };
 
 __device__ void log_victim(const AppendArgs& a, int b, int pos) {
@@ -420,7 +424,33 @@ __global__ void __launch_bounds__(kEvictThreads) append_evict_kernel(AppendArgs 
     }
     __syncthreads();
     int k = 0;
-    if (!none && k_req > 0) {
+    if (a.ext_pos) {
+      // victims listed by the host, in its order: look up each position's slot
+      int nl = a.ext_n[b];
+      nl = nl < a.ext_stride ? nl : a.ext_stride;
+      for (int j = 0; j < nl; ++j) {
+        const int p = a.ext_pos[static_cast<size_t>(b) * a.ext_stride + j];
+        int hit = 0x7fffffff;
+        for (int i = tid; i < S; i += kEvictThreads)
+          if (s.slot_pos[i] == p && p >= 0) {
+            hit = i;
+            break;
+          }
+        const int sl = block_min_int(hit, red_i);
+        if (tid == 0) {
+          bool dup = false;
+          for (int q = 0; q < n_vict; ++q) dup |= s_vict[q] == sl;
+          if (sl == 0x7fffffff)
+            set_err(a.err, kErrIndex);
+          else if (!dup)
+            s_vict[n_vict] = sl;
+          sh[5] = (sl != 0x7fffffff && !dup) ? 1 : 0;
+        }
+        __syncthreads();
+        n_vict += sh[5];
+        __syncthreads();
+      }
+    } else if (!none && k_req > 0) {
       auto elig = [&](int i) {
         const int p = s.slot_pos[i];
         return p >= 0 && p >= thr_lo && p < thr_hi;
@@ -733,6 +763,10 @@ int append_evict(cudaStream_t stream, const AppendArgs& a) {
     return fail(kStatusArg, "append_evict: bad argument");
   if (a.C <= 0 || a.E <= 0) return fail(kStatusArg, "append_evict: capacity and evict_every must be > 0");
   if (a.policy < 0 || a.policy >= kPolicyCount) return fail(kStatusArg, "append_evict: unknown policy %d", a.policy);
+  if (a.policy == kPolicyRandom && !a.ext_pos)
+    return fail(kStatusArg, "append_evict: the random policy's victims come from the host (kvbp_append_evict_listed)");
+  if (a.ext_pos && (!a.ext_n || a.ext_stride <= 0))
+    return fail(kStatusArg, "append_evict_listed: victim_count and victim_stride > 0 are required");
   if (a.st.S > kEvictThreads * kMaxPerThread)
     return fail(kStatusUnsupported, "append_evict: %d slots exceed %d", a.st.S, kEvictThreads * kMaxPerThread);
   if (a.n_prefix < 0 || a.n_suffix < 0) return fail(kStatusArg, "append_evict: negative protection size");
@@ -813,12 +847,16 @@ int kvbp_score_update(kvbp_stream_t stream, const kvbp_state* st, const int32_t*
   return kvbp::score_update(reinterpret_cast<cudaStream_t>(stream), to_state(st), seq_step, step_score, dev_err);
 }
 
-int kvbp_append_evict(kvbp_stream_t stream, const kvbp_state* st, const kvbp_evict_cfg* cfg, int32_t* seq_step,
-                      int32_t* next_pos, int32_t* cur_pos, int32_t* write_slot, const int32_t* tokens,
-                      int32_t* token_log, int32_t log_steps, int32_t* evlog, int32_t* evcount, int32_t evcap,
-                      int32_t* retained_log, int32_t* dev_err) {
+static int append_evict_common(kvbp_stream_t stream, const kvbp_state* st, const kvbp_evict_cfg* cfg,
+                               int32_t* seq_step, int32_t* next_pos, int32_t* cur_pos, int32_t* write_slot,
+                               const int32_t* tokens, int32_t* token_log, int32_t log_steps, int32_t* evlog,
+                               int32_t* evcount, int32_t evcap, int32_t* retained_log, const int32_t* victim_pos,
+                               const int32_t* victim_count, int32_t victim_stride, int32_t* dev_err) {
   if (!st || !cfg) return kvbp::fail(kvbp::kStatusArg, "append_evict: null state/config");
   kvbp::AppendArgs a{};
+  a.ext_pos = victim_pos;
+  a.ext_n = victim_count;
+  a.ext_stride = victim_stride;
   a.st = to_state(st);
   a.C = cfg->capacity;
   a.E = cfg->evict_every;
@@ -842,12 +880,32 @@ int kvbp_append_evict(kvbp_stream_t stream, const kvbp_state* st, const kvbp_evi
   return kvbp::append_evict(reinterpret_cast<cudaStream_t>(stream), a);
 }
 
+int kvbp_append_evict(kvbp_stream_t stream, const kvbp_state* st, const kvbp_evict_cfg* cfg, int32_t* seq_step,
+                      int32_t* next_pos, int32_t* cur_pos, int32_t* write_slot, const int32_t* tokens,
+                      int32_t* token_log, int32_t log_steps, int32_t* evlog, int32_t* evcount, int32_t evcap,
+                      int32_t* retained_log, int32_t* dev_err) {
+  return append_evict_common(stream, st, cfg, seq_step, next_pos, cur_pos, write_slot, tokens, token_log, log_steps,
+                             evlog, evcount, evcap, retained_log, nullptr, nullptr, 0, dev_err);
+}
+
+int kvbp_append_evict_listed(kvbp_stream_t stream, const kvbp_state* st, const kvbp_evict_cfg* cfg,
+                             int32_t* seq_step, int32_t* next_pos, int32_t* cur_pos, int32_t* write_slot,
+                             const int32_t* tokens, int32_t* token_log, int32_t log_steps, int32_t* evlog,
+                             int32_t* evcount, int32_t evcap, int32_t* retained_log, const int32_t* victim_pos,
+                             const int32_t* victim_count, int32_t victim_stride, int32_t* dev_err) {
+  if (!victim_pos) return kvbp::fail(kvbp::kStatusArg, "append_evict_listed: victim_pos is required");
+  return append_evict_common(stream, st, cfg, seq_step, next_pos, cur_pos, write_slot, tokens, token_log, log_steps,
+                             evlog, evcount, evcap, retained_log, victim_pos, victim_count, victim_stride, dev_err);
+}
+
 int kvbp_prefill_select(kvbp_stream_t stream, int32_t B, int32_t P, const kvbp_evict_cfg* cfg, const float* scores,
                         uint8_t* victim, int32_t* evlog, int32_t evcap, int32_t* n_policy_victims,
                         int32_t* dev_err) {
   if (!cfg || !n_policy_victims) return kvbp::fail(kvbp::kStatusArg, "prefill_select: null config/output");
   if (cfg->policy < 0 || cfg->policy >= kvbp::kPolicyCount)
     return kvbp::fail(kvbp::kStatusArg, "prefill_select: unknown policy %d", cfg->policy);
+  if (cfg->policy == kvbp::kPolicyRandom)
+    return kvbp::fail(kvbp::kStatusArg, "prefill_select: the random policy's victims come from the host");
   if (P <= 0 || cfg->capacity <= 0) return kvbp::fail(kvbp::kStatusArg, "prefill_select: bad size");
   // _maybe_evict(step=0, force_if_over_capacity=True): evict_count = max(0, P - C)
   const int C = cfg->capacity;

@@ -62,7 +62,8 @@ enum PolicyId : int {
   kPolicyAdaKV = 5,
   kPolicyQuest = 6,
   kPolicyStreamingLLM = 7,
-  kPolicyCount = 8,
+  kPolicyRandom = 8,  // victims sampled on the host (kvbp_append_evict_listed)
+  kPolicyCount = 9,
 };
 
 }  // namespace kvbp

@@ -206,6 +206,7 @@ class CappedKVEngine:
         device: Optional[torch.device] = None,
         kv_heads: Optional[List[int]] = None,
         gemm: str = "kvbp",
+        host_policy=None,
     ):
         if cfg.head_dim != 128:
             raise ValueError("only head_dim 128 is supported")
@@ -218,6 +219,13 @@ class CappedKVEngine:
         if evict.regime not in ("decode", "prefill"):
             raise ValueError("eviction_regime must be 'decode' or 'prefill'")
         lib()  # fail loudly when the CUDA library is missing
+        # a policy that draws its victims on the host (the random policy) through the
+        # reference's select_evictions protocol; the device applies them
+        self.host_policy = host_policy
+        if (capi.POLICY_IDS.get(evict.policy) == capi.POLICY_IDS["random"]) != (host_policy is not None):
+            raise ValueError("the random policy needs its policy object (host_policy), and only it")
+        if host_policy is not None and int(batch) != 1:
+            raise ValueError("a host-selected policy consumes one random stream sequence after sequence: batch must be 1")
         self.dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         if self.dev.type != "cuda":
             raise ValueError("CappedKVEngine runs on CUDA devices only")
@@ -277,6 +285,9 @@ class CappedKVEngine:
         self.retained_log = z(B, self.max_new + 1)
         self.evlog = z(B, self.evcap)
         self.evcount = z(B)
+        if self.host_policy is not None:  # victims listed by the host at cadence steps
+            self.ext_pos = z(B, S)
+            self.ext_n = z(B)
         self.dev_err = z(1)
         H, F, V = c.hidden, c.ffn, c.vocab
         self.h = z(B, H, dt=bf)
@@ -416,18 +427,39 @@ class CappedKVEngine:
         self._select_and_compact(P, scores, pre_k, pre_v)
         check(L.kvbp_argmax(st, B, c.vocab, c.vocab, _ptr(self.logits), _ptr(self.tokens)), "argmax")
 
+    def _host_victims(self, retained_sorted: List[int], evict_count: int, step: int) -> List[int]:
+        """One ``_maybe_evict`` policy call on the host (kv_coupled_generator.py:563-577):
+        blocks keyed by str(position) in ascending position order."""
+        blocks = {str(p): None for p in retained_sorted}
+        out, seen = [], set()
+        for key in self.host_policy.select_evictions(blocks, evict_count, step):
+            p = int(key)
+            if p in blocks and p not in seen:
+                seen.add(p)
+                out.append(p)
+        return out
+
     def _select_and_compact(self, P, scores, pre_k=None, pre_v=None) -> None:
         L, st = lib(), self.stream
         victim = torch.zeros(self.B, P, dtype=torch.uint8, device=self.dev)
         self.evlog.zero_()
         nvict = capi.C.c_int32()
-        check(
-            L.kvbp_prefill_select(
-                st, self.B, P, capi.C.byref(self._cfg), _ptr(scores), _ptr(victim), _ptr(self.evlog), self.evcap,
-                capi.C.byref(nvict), _ptr(self.dev_err),
-            ),
-            "prefill_select",
-        )
+        if self.host_policy is not None:
+            # step 0 (force_if_over_capacity): evict_count = P - capacity, victims in the
+            # policy's order, then the compaction's hard-capacity guardrail
+            vict = self._host_victims(list(range(P)), max(0, P - self.ev.capacity), 0)
+            if vict:
+                victim[0, torch.tensor(vict, dtype=torch.long, device=self.dev)] = 1
+                self.evlog[0, : len(vict)] = torch.tensor(vict, dtype=torch.int32, device=self.dev)
+            nvict.value = len(vict)
+        else:
+            check(
+                L.kvbp_prefill_select(
+                    st, self.B, P, capi.C.byref(self._cfg), _ptr(scores), _ptr(victim), _ptr(self.evlog), self.evcap,
+                    capi.C.byref(nvict), _ptr(self.dev_err),
+                ),
+                "prefill_select",
+            )
         self.gather_src = torch.empty(self.B, self.S, dtype=torch.int32, device=self.dev)
         self.retained_log.zero_()
         check(
@@ -469,6 +501,9 @@ class CappedKVEngine:
 
     # ------------------------------------------------------------------ decode
     def _append_evict(self) -> None:
+        if self.host_policy is not None:
+            self._append_evict_listed()
+            return
         check(
             lib().kvbp_append_evict(
                 self.stream, capi.C.byref(self._state), capi.C.byref(self._cfg), _ptr(self.seq_step),
@@ -477,6 +512,31 @@ class CappedKVEngine:
                 _ptr(self.retained_log), _ptr(self.dev_err),
             ),
             "append_evict",
+        )
+
+    def _append_evict_listed(self) -> None:
+        """Decode-step bookkeeping with host-drawn victims: at a cadence step the host
+        reads the retained positions (plus the one this step appends), runs the policy
+        call and lists its victims; the kernel appends, frees them and applies the
+        hard-capacity guardrail.  Synchronises with the device every step."""
+        step = int(self.seq_step[0].item()) + 1
+        n = 0
+        if self.ev.regime == "decode" and step % self.ev.evict_every == 0:
+            sp = self.slot_pos[0].cpu().numpy()
+            retained = sorted(sp[sp >= 0].tolist() + [int(self.next_pos[0].item())])
+            vict = self._host_victims(retained, max(0, len(retained) - self.ev.capacity), step)
+            n = len(vict)
+            if n:
+                self.ext_pos[0, :n] = torch.tensor(vict, dtype=torch.int32, device=self.dev)
+        self.ext_n.fill_(n)
+        check(
+            lib().kvbp_append_evict_listed(
+                self.stream, capi.C.byref(self._state), capi.C.byref(self._cfg), _ptr(self.seq_step),
+                _ptr(self.next_pos), _ptr(self.cur_pos), _ptr(self.write_slot), _ptr(self.tokens),
+                _ptr(self.token_log), self.max_new, _ptr(self.evlog), _ptr(self.evcount), self.evcap,
+                _ptr(self.retained_log), _ptr(self.ext_pos), _ptr(self.ext_n), self.S, _ptr(self.dev_err),
+            ),
+            "append_evict_listed",
         )
 
     def _gemm(self, name, epi, N, K, w, x, ldx, out, ldo, norm_w=None, ss_in=None, n_parts=0, ss_out=None):
@@ -580,6 +640,8 @@ class CappedKVEngine:
 
     def capture(self) -> None:
         """Capture one full decode step (append/evict + forward + sample + score) as a graph."""
+        if self.host_policy is not None:
+            raise ValueError("a host-selected policy synchronises every step: run eager steps, not a graph")
         s = torch.cuda.Stream(self.dev)
         s.wait_stream(torch.cuda.current_stream(self.dev))
         # cuBLAS creates its handle and workspace lazily; do that outside the capture

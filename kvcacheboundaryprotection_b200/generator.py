@@ -25,7 +25,7 @@ import torch
 
 from .config import ModelConfig
 from .engine import CappedKVEngine, EvictionSpec, FusedWeights
-from .policies import kernel_policy_name
+from .policies import host_selected, kernel_policy_name
 
 
 @dataclass
@@ -139,14 +139,23 @@ class KVCoupledQwen35Generator:
         if any(len(x) != P for x in batch_input_ids):
             raise ValueError("generate_batch needs prompts of equal length")
         B = len(batch_input_ids)
+        host_pol = self.policy if host_selected(self.policy) else None
+        if host_pol is not None and B > 1:
+            # one random stream consumed sequence after sequence, as the reference's loop does
+            return [
+                self.generate_batch([ids], max_new_tokens, eos_token_ids, temperature, rng,
+                                    None if forced_tokens is None else forced_tokens[b : b + 1])[0]
+                for b, ids in enumerate(batch_input_ids)
+            ]
         eng = CappedKVEngine(
             self.model.cfg, self.model.weights, batch=B, evict=self.spec, max_prompt_len=P,
-            max_new_tokens=max(1, max_new_tokens), device=self.model.device,
+            max_new_tokens=max(1, max_new_tokens), device=self.model.device, host_policy=host_pol,
         )
         self.last_engine = eng
         ids = torch.tensor(np.asarray(batch_input_ids, np.int64), dtype=torch.int32)
         dev = self.model.device
-        host_loop = bool(eos_token_ids) or (temperature > 0.0 and rng is not None) or forced_tokens is not None
+        host_loop = (bool(eos_token_ids) or (temperature > 0.0 and rng is not None) or forced_tokens is not None
+                     or host_pol is not None)
 
         torch.cuda.synchronize(dev)
         t0 = time.perf_counter()

@@ -1,7 +1,11 @@
 """Policy objects with the reference's names and constructor arguments.
 
-They carry configuration only: victim selection runs on the GPU in
-``kvbp_append_evict`` / ``kvbp_prefill_select``.  Names, defaults and the protection
+The scored policies carry configuration only: their victim selection runs on the GPU in
+``kvbp_append_evict`` / ``kvbp_prefill_select``.  ``RandomEvictionPolicy`` is the
+exception: its victims are Python ``random.Random(seed).sample`` draws over the eligible
+keys, so it (and ``ProtectedPolicyWrapper`` around it) selects on the host through the
+reference's ``select_evictions(blocks, evict_count, step)`` protocol and the engine
+hands the victims to ``kvbp_append_evict_listed``.  Names, defaults and the protection
 wrapper follow ``src/counterfact_kv_eviction/policies.py`` and
 ``scripts/run_v3_jax.py:102-136,500-527``.  ``"attention-mass"`` is accepted as the
 name of the pure cumulative-attention-mass policy (``h2o_faithful``).
@@ -9,10 +13,11 @@ name of the pure cumulative-attention-mass policy (``h2o_faithful``).
 
 from __future__ import annotations
 
-from dataclasses import dataclass
-from typing import Any
+import random
+from dataclasses import dataclass, field
+from typing import Any, Dict, List
 
-from .capi import POLICY_IDS
+from .capi import POLICY_IDS, protection_sizes
 
 
 @dataclass
@@ -70,8 +75,32 @@ class StreamingSinkLikePolicy:
     name: str = "streaming_sink_like"
 
 
+@dataclass
+class RandomEvictionPolicy:
+    """Uniform random eviction (policies.py:1553-1582).  One ``random.Random(seed)`` stream
+    per policy object, consumed across calls (and across the sequences a generator decodes
+    with this object, one after another); each call samples ``min(evict_count, len(blocks))``
+    keys in the blocks' order.  The draws must be Python's own to match the reference bit
+    for bit, so this runs on the host."""
+
+    seed: int = 42
+    name: str = "random"
+    _rng: random.Random = field(init=False, repr=False, compare=False)
+
+    def __post_init__(self) -> None:
+        self._rng = random.Random(self.seed)
+
+    def select_evictions(self, blocks: Dict[str, Any], evict_count: int, step: int) -> List[str]:
+        k = min(max(0, int(evict_count)), len(blocks))
+        if k <= 0:
+            return []
+        return self._rng.sample(list(blocks.keys()), k)
+
+
 class ProtectedPolicyWrapper:
-    """Excludes the lowest/highest retained positions from eviction (run_v3_jax.py:102-136)."""
+    """Excludes the lowest/highest retained positions from eviction (run_v3_jax.py:102-136).
+    The scored policies apply it on the GPU from (prefix_frac, suffix_frac, capacity);
+    ``select_evictions`` is the host form, used around host-side inner policies."""
 
     def __init__(self, inner_policy: Any, prefix_frac: float = 0.10, suffix_frac: float = 0.10, capacity: int = 0):
         self.inner = inner_policy
@@ -79,6 +108,24 @@ class ProtectedPolicyWrapper:
         self.prefix_frac = prefix_frac
         self.suffix_frac = suffix_frac
         self.capacity = capacity
+
+    def select_evictions(self, blocks: Dict[str, Any], evict_count: int, step: int) -> List[str]:
+        if evict_count <= 0 or not blocks:
+            return []
+        cap = self.capacity if self.capacity > 0 else len(blocks)
+        n_pre, n_suf = protection_sizes(cap, self.prefix_frac, self.suffix_frac)
+        ordered = sorted(int(k) for k in blocks)
+        protected = {str(p) for p in ordered[:n_pre]}
+        protected.update(str(p) for p in ordered[-n_suf:])  # n_suf == 0: the whole list
+        eligible = {k: v for k, v in blocks.items() if k not in protected}
+        if not eligible:
+            return []
+        return self.inner.select_evictions(eligible, min(evict_count, len(eligible)), step)
+
+
+def host_selected(policy: Any) -> bool:
+    """True when the (possibly wrapped) policy picks its victims on the host."""
+    return isinstance(getattr(policy, "inner", policy), RandomEvictionPolicy)
 
 
 def policy_from_name(name: str, capacity: int) -> Any:
@@ -93,6 +140,7 @@ def policy_from_name(name: str, capacity: int) -> Any:
         "snapkv_faithful": SnapKVFaithfulPolicy,
         "adakv": AdaKVPolicy,
         "quest": QUESTPolicy,
+        "random": RandomEvictionPolicy,
     }
     if name == "streamingllm":
         return StreamingSinkLikePolicy(sink_size=4, recent_window_size=max(0, capacity - 4))

@@ -12,6 +12,7 @@ components fall back to *string* order ("100" < "11" < "9").
 
 from __future__ import annotations
 
+import random
 from dataclasses import dataclass, field
 from typing import Callable, Dict, List, Optional, Sequence
 
@@ -31,6 +32,7 @@ GLOBAL_POLICIES = (
     "adakv",
     "quest",
     "streamingllm",
+    "random",
 )
 
 
@@ -100,9 +102,17 @@ def smallest(positions: Sequence[int], k: int, key: Callable[[int], tuple]) -> L
     return sorted(positions, key=key)[:k]
 
 
-def inner_select(policy: str, positions: Sequence[int], m: Meta, k: int, step: int, capacity: int) -> List[int]:
+def inner_select(policy: str, positions: Sequence[int], m: Meta, k: int, step: int, capacity: int,
+                 rng: Optional[random.Random] = None) -> List[int]:
     """One call of the unwrapped policy's ``select_evictions``."""
     policy = canonical(policy)
+    if policy == "random":
+        # RandomEvictionPolicy (policies.py:1553-1582): the policy's own Random(42) stream,
+        # ``sample`` over the candidate keys in the order given (ascending positions)
+        k = min(max(0, k), len(positions))
+        if k <= 0:
+            return []
+        return [int(x) for x in rng.sample([str(p) for p in positions], k)]
     if policy == "streamingllm":
         # StreamingSinkLikePolicy(sink_size=4, recent_window_size=max(0, capacity-4)),
         # policies.py:1221-1264 with the CLI's construction at run_v3_jax.py:504-507.
@@ -138,10 +148,15 @@ class PolicySpec:
     protect: bool = False
     prefix_frac: float = 0.10
     suffix_frac: float = 0.10
+    rng: Optional[random.Random] = field(default=None, init=False, repr=False)
+
+    def __post_init__(self) -> None:
+        if canonical(self.name) == "random":  # one stream per policy object, seed 42
+            self.rng = random.Random(42)
 
     def select(self, positions: Sequence[int], m: Meta, evict_count: int, step: int) -> List[int]:
         if not self.protect:
-            return inner_select(self.name, positions, m, evict_count, step, self.capacity)
+            return inner_select(self.name, positions, m, evict_count, step, self.capacity, self.rng)
         if evict_count <= 0 or not positions:
             return []
         cap = self.capacity if self.capacity > 0 else len(positions)
@@ -154,7 +169,7 @@ class PolicySpec:
         eligible = [p for p in positions if p not in prot]
         if not eligible:
             return []
-        return inner_select(self.name, eligible, m, min(evict_count, len(eligible)), step, self.capacity)
+        return inner_select(self.name, eligible, m, min(evict_count, len(eligible)), step, self.capacity, self.rng)
 
 
 def hard_cap(retained: Sequence[int], m: Meta, overflow: int) -> List[int]:

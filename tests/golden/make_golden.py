@@ -65,10 +65,11 @@ def _policy_factory(P, name: str, capacity: int):
         "adakv": lambda: P.AdaKVPolicy(),
         "quest": lambda: P.QUESTPolicy(),
         "streamingllm": lambda: P.StreamingSinkLikePolicy(sink_size=4, recent_window_size=max(0, capacity - 4)),
+        "random": lambda: P.RandomEvictionPolicy(),
     }[name]()
 
 
-POLICIES = ["lru", "h2o_faithful", "h2o", "snapkv", "snapkv_faithful", "adakv", "quest", "streamingllm"]
+POLICIES = ["lru", "h2o_faithful", "h2o", "snapkv", "snapkv_faithful", "adakv", "quest", "streamingllm", "random"]
 
 
 def _rand_meta(rng, n_pos_max: int, n_live: int, step: int, tie_level: int):
@@ -180,6 +181,10 @@ GEN_CASES = [
     ("prefill_regime", "lru", 120, 40, 8, 20, (0.10, 0.10), 2, "prefill", 14),
     ("lru_1024_256", "lru", 1024, 256, 8, 128, (0.10, 0.10), 2, "decode", 15),
     ("h2of_1024_256", "h2o_faithful", 1024, 256, 8, 128, (0.10, 0.10), 2, "decode", 16),
+    ("random_p160_c40", "random", 160, 40, 8, 30, (0.10, 0.10), 2, "decode", 17),
+    ("random_noprot_e4", "random", 120, 40, 4, 25, None, 2, "decode", 18),
+    ("random_tiny_cap_hardcap", "random", 60, 6, 8, 30, (0.10, 0.10), 2, "decode", 19),
+    ("random_1024_256", "random", 1024, 256, 8, 64, (0.10, 0.10), 2, "decode", 20),
 ]
 
 

@@ -36,7 +36,7 @@ def test_version_and_policy_ids(L):
     assert b"sm_100a" in L.kvbp_version()
     assert capi.policy_id("lru") == 0
     assert capi.policy_id("attention-mass") == capi.policy_id("h2o_faithful") == 1
-    assert L.kvbp_policy_id(b"random") == -1
+    assert L.kvbp_policy_id(b"random") == 8 and L.kvbp_policy_id(b"no_such_policy") == -1
     with pytest.raises(ValueError):
         capi.policy_id("adakv_faithful")
 

@@ -17,6 +17,7 @@ import pytest
 import torch
 
 from kvcacheboundaryprotection_b200 import build, capi
+from kvcacheboundaryprotection_b200.policies import ProtectedPolicyWrapper, RandomEvictionPolicy
 from oracle.generator import generate, slot_count
 from oracle.policies import PolicySpec
 from oracle.stub_model import StubScoreModel
@@ -57,14 +58,35 @@ class Driver:
     def st(self):
         return torch.cuda.current_stream().cuda_stream
 
-    def prefill(self, P, scores):
+    def prefill(self, P, scores, host=None):
         victim = torch.zeros(self.B, P, dtype=torch.uint8, device="cuda")
         n = C.c_int32()
         sc = None if scores is None else torch.as_tensor(scores, dtype=torch.float32, device="cuda").reshape(self.B, P).contiguous()
-        capi.check(self.L.kvbp_prefill_select(self.st, self.B, P, C.byref(self.cfg), None if sc is None else sc.data_ptr(), victim.data_ptr(), self.evlog.data_ptr(), self.evcap, C.byref(n), self.err.data_ptr()), "select")
+        if host is not None:  # random policy: the host's victims, in its order (one sequence)
+            vict = [int(k) for k in host.select_evictions({str(p): None for p in range(P)}, max(0, P - self.cfg.capacity), 0)]
+            if vict:
+                victim[0, torch.tensor(vict, device="cuda")] = 1
+                self.evlog[0, : len(vict)] = torch.tensor(vict, dtype=torch.int32, device="cuda")
+            n.value = len(vict)
+        else:
+            capi.check(self.L.kvbp_prefill_select(self.st, self.B, P, C.byref(self.cfg), None if sc is None else sc.data_ptr(), victim.data_ptr(), self.evlog.data_ptr(), self.evcap, C.byref(n), self.err.data_ptr()), "select")
         gsrc = torch.empty(self.B, self.S, dtype=torch.int32, device="cuda")
         capi.check(self.L.kvbp_prefill_compact(self.st, C.byref(self.state), P, self.cfg.capacity, n.value, victim.data_ptr(), None if sc is None else sc.data_ptr(), gsrc.data_ptr(), self.evlog.data_ptr(), self.evcap, self.evcount.data_ptr(), self.seq_step.data_ptr(), self.next_pos.data_ptr(), self.retained_log.data_ptr(), self.max_new, self.step_score.data_ptr(), self.err.data_ptr()), "compact")
         return gsrc
+
+    def append_evict_listed(self, host):
+        """Cadence victims drawn by the host policy over the retained positions plus the
+        one this step appends (one sequence), then the listed-victims kernel."""
+        step = int(self.seq_step[0].item()) + 1
+        pos, cnt = torch.zeros(self.B, self.S, dtype=torch.int32, device="cuda"), torch.zeros(self.B, dtype=torch.int32, device="cuda")
+        if step % self.cfg.evict_every == 0 and self.cfg.decode_regime:
+            sp = self.slot_pos[0].cpu().numpy()
+            live = sorted(sp[sp >= 0].tolist() + [int(self.next_pos[0].item())])
+            vict = [int(k) for k in host.select_evictions({str(p): None for p in live}, max(0, len(live) - self.cfg.capacity), step)]
+            if vict:
+                pos[0, : len(vict)] = torch.tensor(vict, dtype=torch.int32, device="cuda")
+            cnt[0] = len(vict)
+        capi.check(self.L.kvbp_append_evict_listed(self.st, C.byref(self.state), C.byref(self.cfg), self.seq_step.data_ptr(), self.next_pos.data_ptr(), self.cur_pos.data_ptr(), self.write_slot.data_ptr(), self.tokens.data_ptr(), self.token_log.data_ptr(), self.max_new, self.evlog.data_ptr(), self.evcount.data_ptr(), self.evcap, self.retained_log.data_ptr(), pos.data_ptr(), cnt.data_ptr(), self.S, self.err.data_ptr()), "append_evict_listed")
 
     def append_evict(self):
         capi.check(self.L.kvbp_append_evict(self.st, C.byref(self.state), C.byref(self.cfg), self.seq_step.data_ptr(), self.next_pos.data_ptr(), self.cur_pos.data_ptr(), self.write_slot.data_ptr(), self.tokens.data_ptr(), self.token_log.data_ptr(), self.max_new, self.evlog.data_ptr(), self.evcount.data_ptr(), self.evcap, self.retained_log.data_ptr(), self.err.data_ptr()), "append_evict")
@@ -96,11 +118,16 @@ def test_eviction_kernels_match_reference_trace(case):
     cfg = capi.EvictCfg(cap, E, capi.policy_id(case["policy"]), int(case["protect"] is not None), n_pre, n_suf, int(case["regime"] == "decode"))
     S = slot_count(cap, E, max_new, case["regime"])
     D = Driver(1, S, (P + max_new + 2 + 31) // 32, P + max_new + 2, max_new, cfg)
-    pre = o.meta.prefill[:P] if case["policy"] != "lru" else None
-    D.prefill(P, pre)
+    host = None
+    if case["policy"] == "random":  # victims drawn on the host with the package's policy objects
+        host = RandomEvictionPolicy()
+        if case["protect"]:
+            host = ProtectedPolicyWrapper(host, *case["protect"], cap)
+    pre = o.meta.prefill[:P] if case["policy"] not in ("lru", "random") else None
+    D.prefill(P, pre, host)
     assert D.slot_pos[0].cpu().numpy().tolist() == o.slot_tables[0].tolist()
     for s in range(1, max_new + 1):
-        D.append_evict()
+        D.append_evict_listed(host) if host is not None else D.append_evict()
         assert D.slot_pos[0].cpu().numpy().tolist() == o.slot_tables[s].tolist(), f"slot table after step {s}"
         if s == max_new:
             break
@@ -155,3 +182,35 @@ def test_step0_scored_policies_large_prompt(policy):
     want = want + hard_cap(rest, m, len(rest) - cap)
     n = int(D.evcount[0].item())
     assert D.evlog[0, :n].cpu().numpy().tolist() == want
+
+
+def test_random_policy_is_rejected_without_a_victim_list():
+    cfg = capi.EvictCfg(32, 8, capi.policy_id("random"), 1, 4, 4, 1)
+    D = Driver(1, 40, 8, 200, 8, cfg)
+    with pytest.raises(capi.KVBPError, match="host"):
+        D.append_evict()
+    with pytest.raises(capi.KVBPError, match="host"):
+        D.prefill(100, None)
+
+
+def test_random_policy_generator_end_to_end_matches_reference_trace():
+    """The drop-in generator with the random policy (host-drawn victims, device slot
+    path) reproduces the reference generator's trace of the same policy: victims are
+    independent of the model's scores except through the hard-capacity guardrail, which
+    these settings never reach."""
+    from kvcacheboundaryprotection_b200.config import get_config
+    from kvcacheboundaryprotection_b200.generator import CappedKVModel, KVCoupledQwen35Generator
+    from kvcacheboundaryprotection_b200.weights import init_weights
+
+    case = next(c for c in CASES if c["name"] == "random_p160_c40")
+    cfg = get_config("parity-qwen2").with_(vocab=128 * 8)
+    model = CappedKVModel(cfg, init_weights(cfg, seed=0), device="cuda")
+    pol = ProtectedPolicyWrapper(RandomEvictionPolicy(), 0.10, 0.10, case["capacity"])
+    gen = KVCoupledQwen35Generator(model, None, pol, case["capacity"], case["evict_every"], cfg.n_kv_heads)
+    res = gen.generate_with_kv_control(case["prompt"], case["max_new_tokens"])
+    assert res.positions_evicted == case["positions_evicted"]
+    assert res.retained_counts_by_step == case["retained_counts_by_step"]
+    assert res.policy_call_steps == case["policy_call_steps"]
+    # the policy object's stream continues across calls, as in the reference
+    res2 = gen.generate_with_kv_control(case["prompt"], case["max_new_tokens"])
+    assert res2.positions_evicted != res.positions_evicted
