@@ -14,8 +14,15 @@ One step = one decode step of every sequence (slot append + cadence eviction,
 28-layer forward, greedy argmax, score update), replayed from one CUDA graph.
 Inputs are larger than L2 (15 GB of weights are streamed every step).
 
-Multi-GPU: one process per GPU, sequences sharded data-parallel with no collective
-(weak scaling: 16 sequences per GPU); time = max over ranks of the device time.
+Multi-GPU: one process per GPU.  The headline at N > 1 decodes the same 16 sequences
+tensor-parallel over KV-head groups (strong scaling; o/down allreduce fused into the
+GEMMs over NVLink, score and argmax allreduce-MAX by NCCL) and checks it ("tp_check":
+bit-identical state on every rank, and logits / victims against one GPU decoding the
+same state).  Beside it: "data_parallel" (16 independent sequences per GPU, no
+collective, weak scaling) and "configs" -- the Qwen2.5-3B-arch workload (32 sequences
+per GPU, capacity 256, LRU, data parallel) and the Qwen3-4B-arch single 65536-token
+sequence (capacity 4096, LRU, tensor parallel over its 8 KV heads).  Time = max over
+ranks of the device time.
 
 Run ``--impl reference`` for the CPU reference arm (the oracle port of the
 reference's decode step timed on the host cores).
@@ -42,14 +49,16 @@ WORKLOADS = {
     # name: preset, batch, capacity, prompt, policy, multi-GPU parallelism
     # (dp: independent sequences shard with no data-path collective -- every rank decodes
     #  its own `batch` sequences, weak scaling; tp: one decode of `batch` sequences over
-    #  all ranks' KV-head groups, strong scaling).  The 7B workload's line is data
-    #  parallel; its tensor-parallel decode is measured beside it ("tensor_parallel").
-    "qwen2.5-7b": ("qwen2.5-7b", 16, 1024, 32768, "attention-mass", "dp"),
+    #  all ranks' KV-head groups, strong scaling).  The 7B workload is tensor parallel at
+    #  N > 1 (its configuration names tensor parallelism over KV-head groups); its
+    #  data-parallel decode is measured beside it ("data_parallel").
+    "qwen2.5-7b": ("qwen2.5-7b", 16, 1024, 32768, "attention-mass", "tp"),
     "qwen2.5-3b": ("qwen2.5-3b", 32, 256, 2048, "lru", "dp"),
     "qwen3-4b": ("qwen3-4b", 1, 4096, 65536, "lru", "tp"),
     "tiny-qwen2": ("tiny-qwen2", 1, 256, 1024, "lru", "dp"),
 }
-ALSO_TP = {"qwen2.5-7b"}
+ALSO_DP = {"qwen2.5-7b"}
+OTHER_CONFIGS = ("qwen2.5-3b", "qwen3-4b")  # measured beside the 7B headline (--no-configs skips)
 METRIC = "decode tok/s (Qwen2.5-7B arch, cap 1024) at 1/2/4/8 B200; kernel HBM GB/s"
 
 
@@ -65,6 +74,8 @@ def parse():
     ap.add_argument("--parallel", default="auto", choices=["auto", "tp", "dp"],
                     help="multi-GPU scheme (auto: the workload's own, see WORKLOADS)")
     ap.add_argument("--no-micro", action="store_true", help="skip the operator microbench sweep")
+    ap.add_argument("--no-configs", action="store_true", help="skip the other workloads measured beside the headline")
+    ap.add_argument("--no-check", action="store_true", help="skip the tensor-parallel correctness check")
     ap.add_argument("--nccl-allreduce", action="store_true",
                     help="tensor parallelism: reduce the o/down partials with NCCL instead of the fused NVLink GEMM")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
@@ -145,81 +156,19 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------------ ours
-def run_tp_side(a, rank, world, local_rank):
-    """Tensor-parallel decode of the workload's sequences over all ranks (one decode of
-    `batch` sequences per step, KV-head groups sharded), K graph replays timed with
-    device events (max over ranks)."""
+def _build_engine(workload, tp, rank, world, dev, B, n_new, seed_rank):
+    """The workload's engine on this rank: tensor-parallel (TPEngine over all ranks'
+    KV-head groups, the same synthetic post-prefill state on every rank) or one GPU's
+    independent sequences (CappedKVEngine, its own seeded state)."""
     import torch
-    import torch.distributed as dist
 
-    from kvcacheboundaryprotection_b200.config import get_config
-    from kvcacheboundaryprotection_b200.engine import EvictionSpec, FusedWeights
-    from kvcacheboundaryprotection_b200.tp import TPEngine, local_config, shard_weights, tp_plan
-    from kvcacheboundaryprotection_b200.weights import init_weights
-
-    dev = torch.device("cuda", local_rank)
-    preset, B0, C, P, policy, _ = WORKLOADS[a.workload]
-    B = a.batch or B0
-    cfg = get_config(preset)
-    K, W = a.steps, a.warmup
-    plan = tp_plan(cfg, world, rank)
-    weights = init_weights(cfg, seed=0, device=dev)
-    fw = FusedWeights(local_config(cfg, plan), shard_weights(cfg, weights, plan), dev)
-    del weights
-    torch.cuda.empty_cache()
-    eng = TPEngine(cfg, fw, plan=plan, fused_allreduce=not a.nccl_allreduce, batch=B,
-                   evict=EvictionSpec(policy, C, 8, True, 0.10, 0.10), max_prompt_len=P, max_new_tokens=W + K + 16,
-                   device=dev)
-    eng.synthetic_prefill(P, seed=1234)
-    eng.capture()
-    for _ in range(W):
-        eng.run_step()
-    torch.cuda.synchronize()
-    dist.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(K):
-        eng.run_step()
-    e1.record()
-    torch.cuda.synchronize()
-    t = torch.tensor([e0.elapsed_time(e1)], device=dev)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = float(t.item())
-    eng.check_device_errors()
-    eng.graph = None
-    del eng
-    torch.cuda.empty_cache()
-    return {
-        "parallelism": f"tp{world}",
-        "value": round(B * K / (ms / 1000.0), 2),
-        "unit": "tok/s",
-        "ms_per_step": round(ms / K, 4),
-        "scaling": "strong",
-        "global_batch": B,
-        "allreduce": "nccl" if a.nccl_allreduce else "fused NVLink GEMM epilogue (o, down) + NCCL (score, argmax)",
-    }
-
-
-def run_ours(a, rank, world, local_rank):
-    import torch
-    import torch.distributed as dist
-
-    from kvcacheboundaryprotection_b200 import build as kbuild
     from kvcacheboundaryprotection_b200.config import get_config
     from kvcacheboundaryprotection_b200.engine import CappedKVEngine, EvictionSpec, FusedWeights
     from kvcacheboundaryprotection_b200.weights import init_weights
 
-    kbuild.build()
-    dev = torch.device("cuda", local_rank)
-    torch.cuda.set_device(dev)
-    preset, B0, C, P, policy, par = WORKLOADS[a.workload]
-    par = par if a.parallel == "auto" else a.parallel
-    tp = world > 1 and par == "tp"
-    B = a.batch or B0
+    preset, _, C, P, policy, _ = WORKLOADS[workload]
     cfg = get_config(preset)
-    K, W = a.steps, a.warmup
     spec = EvictionSpec(policy, C, 8, True, 0.10, 0.10)
-    n_new = W + K + a.e2e_steps + 16
     weights = init_weights(cfg, seed=0, device=dev)
     if tp:
         from kvcacheboundaryprotection_b200.tp import TPEngine, local_config, shard_weights, tp_plan
@@ -228,26 +177,47 @@ def run_ours(a, rank, world, local_rank):
         fw = FusedWeights(local_config(cfg, plan), shard_weights(cfg, weights, plan), dev)
         del weights
         torch.cuda.empty_cache()
-        eng = TPEngine(cfg, fw, plan=plan, fused_allreduce=not a.nccl_allreduce, batch=B, evict=spec,
-                       max_prompt_len=P, max_new_tokens=n_new, device=dev)
-        eng.synthetic_prefill(P, seed=1234)  # the same state on every rank
+        eng = TPEngine(cfg, fw, plan=plan, fused_allreduce=True, batch=B, evict=spec, max_prompt_len=P,
+                       max_new_tokens=n_new, device=dev)
+        eng.synthetic_prefill(P, seed=1234)
     else:
         fw = FusedWeights(cfg, weights, dev)
         del weights
         torch.cuda.empty_cache()
         eng = CappedKVEngine(cfg, fw, batch=B, evict=spec, max_prompt_len=P, max_new_tokens=n_new, device=dev)
-        eng.synthetic_prefill(P, seed=1234 + rank)
+        eng.synthetic_prefill(P, seed=1234 + seed_rank)
     torch.cuda.synchronize()
+    return cfg, eng, fw
+
+
+def decode_run(a, workload, par, rank, world, local_rank, *, steps, warmup, full=True):
+    """Decode throughput of one workload: K graph replays timed with device events
+    between barriers, max over ranks.  ``par``: "tp" (one decode of the workload's
+    sequences over all ranks, strong scaling) or "dp" (each rank decodes its own
+    sequences, no data-path collective, weak scaling).  With ``full`` also the end-to-end
+    number through host buffers and clocks; always the per-kernel table and rooflines."""
+    import torch
+    import torch.distributed as dist
+
+    dev = torch.device("cuda", local_rank)
+    preset, B0, C, P, policy, _ = WORKLOADS[workload]
+    tp = world > 1 and par == "tp"
+    B = (a.batch or B0) if workload == a.workload else B0
+    K, W = steps, warmup
+    n_new = W + K + (a.e2e_steps if full else 0) + 16
+    cfg, eng, fw = _build_engine(workload, tp, rank, world, dev, B, n_new, rank)
     eng.capture()
     for _ in range(W):
         eng.run_step()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    cvd = [x for x in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if x.strip().isdigit()]
-    clocks = ClockSampler(int(cvd[local_rank]) if len(cvd) > local_rank else local_rank)
-    clocks.start()
-    time.sleep(0.3)
+    clocks = None
+    if full:
+        cvd = [x for x in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if x.strip().isdigit()]
+        clocks = ClockSampler(int(cvd[local_rank]) if len(cvd) > local_rank else local_rank)
+        clocks.start()
+        time.sleep(0.3)
     torch.cuda.synchronize()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
@@ -256,7 +226,7 @@ def run_ours(a, rank, world, local_rank):
         eng.run_step()
     e1.record()
     torch.cuda.synchronize()
-    ck = clocks.stop()
+    ck = clocks.stop() if clocks else None
     ms = e0.elapsed_time(e1)
     if world > 1:
         t = torch.tensor([ms], device=dev)
@@ -267,31 +237,37 @@ def run_ours(a, rank, world, local_rank):
     value = seqs * K / (ms / 1000.0)
     eng.check_device_errors()
 
-    # ---- end to end through host buffers: host feeds each step's tokens and reads them back
-    import torch as T
+    e2e = None
+    if full:
+        # end to end through host buffers: the host feeds each step's tokens and reads them back
+        pin_in = torch.empty(B, dtype=torch.int32, pin_memory=True)
+        pin_out = torch.empty(B, dtype=torch.int32, pin_memory=True)
+        pin_in.copy_(eng.tokens.cpu())
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(a.e2e_steps):
+            eng.tokens.copy_(pin_in, non_blocking=True)
+            eng.run_step()
+            pin_out.copy_(eng.tokens, non_blocking=True)
+            torch.cuda.current_stream().synchronize()
+            pin_in.copy_(pin_out)
+        e2e_s = time.perf_counter() - t0
+        if world > 1:
+            t = torch.tensor([e2e_s], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e2e_s = float(t.item())
+        e2e = {
+            "value": round(seqs * a.e2e_steps / e2e_s, 2),
+            "unit": "tok/s",
+            "h2d_bytes_per_step": 4 * B,
+            "d2h_bytes_per_step": 4 * B,
+            "how": "host copies each step's token ids in from pinned memory, replays the step, reads the sampled ids back and synchronises",
+        }
 
-    pin_in = T.empty(B, dtype=T.int32, pin_memory=True)
-    pin_out = T.empty(B, dtype=T.int32, pin_memory=True)
-    pin_in.copy_(eng.tokens.cpu())
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    t0 = time.perf_counter()
-    for _ in range(a.e2e_steps):
-        eng.tokens.copy_(pin_in, non_blocking=True)
-        eng.run_step()
-        pin_out.copy_(eng.tokens, non_blocking=True)
-        torch.cuda.current_stream().synchronize()
-        pin_in.copy_(pin_out)
-    e2e_s = time.perf_counter() - t0
-    if world > 1:
-        t = torch.tensor([e2e_s], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_s = float(t.item())
-    e2e = seqs * a.e2e_steps / e2e_s
-
-    # ---- live per-kernel timing (eager instrumented steps) and the roofline
-    km = measure_kernels_in_step(eng, steps=3)
+    # ---- live per-kernel timing (the step's launches of each kind replayed as a burst)
+    km = measure_kernels_in_step(eng, steps=2)
     hbm, tf, peak_kind = peaks()
     avg_valid = C + 3.5  # retained slots per (sequence, kv head): C .. C+E-1 over a cadence
     kbytes = kernel_algorithmic_bytes(eng.cfg, B, avg_valid)  # this rank's shapes
@@ -321,7 +297,6 @@ def run_ours(a, rank, world, local_rank):
     lc = eng.cfg
     step_bytes = fw.streamed_bytes(B) + cfg.n_layers * algorithmic_attn_bytes(B, lc.n_heads, lc.n_kv_heads, avg_valid)
     step_ms = ms / K
-    gpu_launches = K * launches_per_step(cfg)
     out = {
         "metric": METRIC,
         "value": round(value, 2),
@@ -345,16 +320,8 @@ def run_ours(a, rank, world, local_rank):
             "prompt_len": P,
             "policy": policy,
             "parallelism": f"tp{world}" if tp else f"dp{world}",
-            "allreduce": ("nccl" if a.nccl_allreduce else "fused NVLink GEMM epilogue (o, down) + NCCL (score, argmax)")
-            if tp else None,
+            "allreduce": "fused NVLink GEMM epilogue (o, down) + NCCL (score, argmax)" if tp else None,
             "l2": "inputs larger than L2 (all weights streamed every step)",
-        },
-        "e2e": {
-            "value": round(e2e, 2),
-            "unit": "tok/s",
-            "h2d_bytes_per_step": 4 * B,
-            "d2h_bytes_per_step": 4 * B,
-            "how": "host copies each step's token ids in from pinned memory, replays the step, reads the sampled ids back and synchronises",
         },
         "roofline": roofline_of(dominant),
         "roofline_attention": roofline_of("attention"),
@@ -363,19 +330,100 @@ def run_ours(a, rank, world, local_rank):
             "bytes_per_step": int(step_bytes),
             "achieved_gbs": round(step_bytes / (step_ms * 1e-3) / 1e9, 1),
             "frac": round(step_bytes / (step_ms * 1e-3) / 1e9 / hbm, 4),
-            "note": "bytes one decode step must read (every weight matrix and the lm_head; B rows of the embedding "
-                    "table; K/V, q, out) / measured step time (all kernels own sm_100a)",
+            "note": "bytes one decode step must read on one GPU (every weight matrix and the lm_head of this rank; "
+                    "B rows of the embedding table; K/V, q, out) / measured step time (all kernels own sm_100a)",
         },
-        "gpu_launches": gpu_launches,
-        "clocks": ck,
+        "gpu_launches": K * launches_per_step(cfg, tp),
     }
+    if e2e:
+        out["e2e"] = e2e
+    if ck:
+        out["clocks"] = ck
     return out, eng, fw
 
 
-def launches_per_step(cfg) -> int:
+def _checksum(t):
+    """Order-sensitive integer digest of a tensor's bytes (for cross-rank identity)."""
+    import torch
+
+    b = t.contiguous().view(torch.uint8).to(torch.int64)
+    w = torch.arange(b.numel(), device=b.device, dtype=torch.int64) % 65521 + 1
+    return int((b * w).sum().item())
+
+
+def tp_check(a, workload, rank, world, local_rank, eng, steps=9):
+    """Correctness of the tensor-parallel run (the fused NVLink allreduce included).
+
+    1. After the timed steps every rank must hold bit-identical token logs, eviction
+       logs and counts, slot tables, float64 cumulative scores and residual streams
+       (the allreduce sums the ranks' partials in rank order on every rank).
+    2. From a fresh synthetic state, ``steps`` teacher-forced steps of the tensor-parallel
+       engine against one GPU decoding the same state with the full weights
+       (CappedKVEngine): each rank's vocabulary shard of the logits within 2e-2 of the
+       single-GPU logits, identical slot tables, and the victims of the cadence step."""
+    import torch
+    import torch.distributed as dist
+
+    from kvcacheboundaryprotection_b200.engine import CappedKVEngine, EvictionSpec, FusedWeights
+    from kvcacheboundaryprotection_b200.weights import init_weights
+
+    dev = torch.device("cuda", local_rank)
+    names = ["token_log", "evlog", "evcount", "slot_pos", "cumul", "h", "tokens", "retained_log"]
+    mine = torch.tensor([_checksum(getattr(eng, n)) for n in names], dtype=torch.int64, device=dev)
+    allv = [torch.empty_like(mine) for _ in range(world)]
+    dist.all_gather(allv, mine)
+    differ = [names[i] for i in range(len(names)) if any(int(v[i]) != int(allv[0][i]) for v in allv)]
+
+    preset, B0, C, P, policy, _ = WORKLOADS[workload]
+    B = (a.batch or B0) if workload == a.workload else B0
+    cfg = eng.full_cfg
+    ref = CappedKVEngine(cfg, FusedWeights(cfg, init_weights(cfg, seed=0, device=dev), dev), batch=B,
+                         evict=EvictionSpec(policy, C, 8, True, 0.10, 0.10), max_prompt_len=P,
+                         max_new_tokens=steps + 4, device=dev)
+    torch.cuda.empty_cache()
+    ref.synthetic_prefill(P, seed=4321)
+    eng.synthetic_prefill(P, seed=4321)  # the same full state; this rank keeps its heads
+    lo, hi = eng.plan.vocab_lo, eng.plan.vocab_hi
+    worst, agree, slots_same = 0.0, 0, True
+    for _ in range(steps):
+        eng.tokens.copy_(ref.tokens)
+        ref.decode_step_launches()
+        eng.decode_step_launches()
+        torch.cuda.synchronize()
+        worst = max(worst, float((eng.logits.float() - ref.logits[:, lo:hi].float()).abs().max().item()))
+        slots_same &= bool(torch.equal(eng.slot_pos, ref.slot_pos))
+        agree += int(torch.equal(eng.tokens, ref.tokens))
+    ev_same = bool(torch.equal(eng.evcount, ref.evcount)) and bool(torch.equal(eng.evlog, ref.evlog))
+    eng.check_device_errors()
+    ref.check_device_errors()
+    del ref
+    torch.cuda.empty_cache()
+    w = torch.tensor([worst], device=dev)
+    dist.all_reduce(w, op=dist.ReduceOp.MAX)
+    ok_flags = torch.tensor([int(slots_same), int(ev_same), agree], device=dev)
+    dist.all_reduce(ok_flags, op=dist.ReduceOp.MIN)
+    worst = float(w.item())
+    slots_same, ev_same, agree = bool(ok_flags[0]), bool(ok_flags[1]), int(ok_flags[2])
+    ok = not differ and worst <= 2e-2 and slots_same and ev_same
+    return {
+        "status": "ok" if ok else "FAILED",
+        "ranks_identical": not differ,
+        "ranks_differ_in": differ,
+        "vs_1gpu_steps": steps,
+        "vs_1gpu_max_logit_diff": round(worst, 5),
+        "vs_1gpu_steps_all_tokens_equal": agree,
+        "vs_1gpu_slot_tables_identical": slots_same,
+        "vs_1gpu_victims_identical": ev_same,
+        "how": "bit-identical state across ranks after the timed steps; then teacher-forced steps from one fresh "
+               "state against a single-GPU engine with the full weights (logit tolerance 2e-2)",
+    }
+
+
+def launches_per_step(cfg, tp: bool = False) -> int:
     # own kernels: append_evict, embed, row_sumsq, per layer (q/k/v GEMM, attention, o GEMM,
-    # gate/up GEMM, down GEMM), lm_head GEMM, argmax, score_update
-    return 1 + 1 + 1 + cfg.n_layers * 5 + 1 + 1 + 1
+    # gate/up GEMM, down GEMM), lm_head GEMM, argmax (tensor parallel: argmax_key +
+    # key_to_token), score_update; NCCL's own kernels are not counted
+    return 1 + 1 + 1 + cfg.n_layers * 5 + 1 + (2 if tp else 1) + 1
 
 
 def algorithmic_attn_bytes(B, Hq, Hkv, valid_slots):
@@ -1056,18 +1104,43 @@ def main():
         from datetime import timedelta
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local_rank))
-    out, eng, fw = run_ours(a, rank, world, local_rank)
+    from kvcacheboundaryprotection_b200 import build as kbuild
+
+    kbuild.build()
+    torch.cuda.set_device(local_rank)
+    par = WORKLOADS[a.workload][5] if a.parallel == "auto" else a.parallel
+    out, eng, fw = decode_run(a, a.workload, par, rank, world, local_rank, steps=a.steps, warmup=a.warmup)
+    if world > 1 and par == "tp" and not a.no_check:
+        eng.graph = None
+        out["tp_check"] = tp_check(a, a.workload, rank, world, local_rank, eng)
     eng.graph = None  # a graph holding NCCL calls goes before the process group
-    del eng
+    del eng, fw
     torch.cuda.empty_cache()
-    if world > 1 and a.parallel == "auto" and a.workload in ALSO_TP:
-        del fw
+    side_k, side_w = min(a.steps, 20), min(a.warmup, 3)
+    if world > 1 and a.parallel == "auto" and a.workload in ALSO_DP:
+        r, e, f = decode_run(a, a.workload, "dp", rank, world, local_rank, steps=side_k, warmup=side_w, full=False)
+        e.graph = None
+        del e, f
         torch.cuda.empty_cache()
-        out["tensor_parallel"] = run_tp_side(a, rank, world, local_rank)
+        out["data_parallel"] = {k: r[k] for k in ("value", "unit", "ms_per_step", "scaling", "config", "roofline",
+                                                  "step_roofline")}
+    if not a.no_configs and a.workload == "qwen2.5-7b" and a.batch is None:
+        out["configs"] = {}
+        for w in OTHER_CONFIGS:
+            wpar = WORKLOADS[w][5]
+            r, e, f = decode_run(a, w, wpar, rank, world, local_rank, steps=side_k, warmup=side_w, full=False)
+            entry = {k: r[k] for k in ("value", "unit", "ms_per_step", "scaling", "config", "roofline",
+                                       "roofline_attention", "step_roofline", "kernels")}
+            if world > 1 and wpar == "tp" and not a.no_check:
+                e.graph = None
+                entry["tp_check"] = tp_check(a, w, rank, world, local_rank, e)
+            e.graph = None
+            del e, f
+            torch.cuda.empty_cache()
+            out["configs"][w] = entry
+    fw = None
     if rank == 0 and world == 1:
         if not a.no_micro:
-            del fw
-            torch.cuda.empty_cache()
             out["kernel_microbench"] = run_microbench()
             out["gemm_microbench"] = run_gemm_microbench(WORKLOADS[a.workload][0])
             preset, B0, C0 = WORKLOADS[a.workload][:3]
