@@ -288,10 +288,15 @@ __global__ void argmax_kernel(const __nv_bfloat16* __restrict__ logits, long lon
       // the global first maximum.  -0 becomes +0 (numpy ranks them equal, so the lower
       // index must decide) and every NaN one positive NaN above +inf (numpy.argmax takes
       // the first NaN, whatever its sign or payload).
+      // The value's bits are mapped to an order-preserving unsigned word, then the top
+      // bit is flipped so that the keys also order correctly as SIGNED int64 (the
+      // allreduce-MAX compares int64): a shard whose maximum is negative ranks below one
+      // whose maximum is positive.
       uint32_t u = __float_as_uint(bv);
       if (bv != bv) u = 0x7fc00000u;
       else if (u == 0x80000000u) u = 0u;
       u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+      u ^= 0x80000000u;
       const uint32_t idx = static_cast<uint32_t>(bi + index_offset);
       keys[r] = static_cast<long long>((static_cast<unsigned long long>(u) << 32) | (0xFFFFFFFFu - idx));
     }
