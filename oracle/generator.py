@@ -1,10 +1,10 @@
 """Restatement of the reference's global-mask decode/eviction loop (test infrastructure).
 
 Follows ``KVCoupledQwen35Generator.generate_with_kv_control`` and ``_maybe_evict``
-(``src/counterfact_kv_eviction/kv_coupled_generator.py:135-604``) for policies that
-rank positions globally (the per-KV-head faithful policies are not covered).  The
-model is any callable with the JAX adapter's signature
-(``src/counterfact_kv_eviction/jax_inference.py:1575-1583``).
+(``src/counterfact_kv_eviction/kv_coupled_generator.py:135-604``), including the per-KV-head
+mode of the faithful / native Ada-KV and QUEST policies (:216-325 at step 0, :373-433 in
+the decode loop, signal updates :470-497).  The model is any callable with the JAX
+adapter's signature (``src/counterfact_kv_eviction/jax_inference.py:1575-1583``).
 
 On top of the reference behaviour it tracks the slot layout that the CUDA path
 defines, since the reference keeps a position-indexed cache and has no slots:
@@ -23,7 +23,8 @@ from typing import Any, Dict, List, Optional, Sequence
 
 import numpy as np
 
-from .policies import Meta, PolicySpec, canonical, hard_cap
+from .policies import (PER_HEAD_POLICIES, Meta, PolicySpec, canonical, hard_cap, per_head_uses_current,
+                       protection_sizes, select_per_head_retention, union_trim)
 
 
 @dataclass
@@ -45,6 +46,13 @@ class OracleResult:
     # logits row used for sampling at each step (float32), when recorded
     step_logits: List[np.ndarray] = field(default_factory=list)
     meta: Optional[Meta] = None
+    faithful_union_retained_max: int = 0
+    faithful_union_overflow_max: int = 0
+    faithful_union_overflow_steps: int = 0
+    # per-head mode: the (n_kv_heads, positions) keep mask after each step's selection
+    head_keep: Optional[np.ndarray] = None
+    # per-head mode, per decode forward: the (n_kv_heads, n_pos) signal rows it produced
+    step_head_scores: List[np.ndarray] = field(default_factory=list)
 
 
 class SlotTable:
@@ -134,6 +142,39 @@ def generate(
     step_logits: List[np.ndarray] = []
     slots = SlotTable(n_slots or slot_count(cap, evict_every, max_new_tokens, regime))
 
+    # per-KV-head mode (AdaKV / QUEST faithful and native), kv_coupled_generator.py:115-133
+    per_head = canonical(policy.name) in PER_HEAD_POLICIES
+    use_cur = per_head and per_head_uses_current(policy.name)
+    ph_cumul = ph_cur = ph_keep = None
+    ph_ready = False
+    n_pref = n_suff = 0
+    if per_head and policy.protect:
+        n_pref, n_suff = protection_sizes(cap, policy.prefix_frac, policy.suffix_frac)
+    if per_head and n_kv_heads > 0:
+        ph_cumul = np.zeros((n_kv_heads, n_alloc), np.float64)
+        ph_cur = np.zeros((n_kv_heads, n_alloc), np.float32)
+        ph_keep = np.ones((n_kv_heads, n_alloc), bool)
+    union_stats = [0, 0, 0]  # retained max, overflow max, overflow steps
+    step_head_scores: List[np.ndarray] = []
+
+    def per_head_select(step: int) -> List[int]:
+        """One per-head policy call + union trim; returns the evicted positions (ascending)."""
+        signal = ph_cur if use_cur else ph_cumul
+        rmask = retained[:n_pos]
+        keep = select_per_head_retention(policy.name, signal[:, :n_pos], rmask.tolist(), cap, n_pref, n_suff)
+        n_union = int(keep.any(axis=0).sum())
+        union_stats[0] = max(union_stats[0], n_union)
+        union_stats[1] = max(union_stats[1], max(0, n_union - cap))
+        union_stats[2] += int(n_union > cap)
+        union = union_trim(keep, signal[:, :n_pos], rmask, cap, n_pref, n_suff)
+        ph_keep[:, :n_pos] = keep
+        out_v = [p for p in range(n_pos) if retained[p] and not union[p]]
+        for p in out_v:
+            retained[p] = False
+        evicted.extend(out_v)
+        calls.append(step)
+        return out_v
+
     # --- prefill (kv_coupled_generator.py:160-209) ---------------------------------
     need_attn = canonical(getattr(policy, "name", "")) != "lru"
     out = model(input_ids=list(input_ids), output_attentions=need_attn, use_cache=True)
@@ -168,7 +209,26 @@ def generate(
         evicted.extend(out_v)
         return out_v
 
-    evict(0, True)
+    if not per_head:
+        evict(0, True)
+    elif n_prompt > cap and ph_keep is not None:
+        # step 0 per head: the first attention output seeds head 0's signal
+        # (kv_coupled_generator.py:240-271: a (1, 1, 1, N) prefill array gives one row)
+        raw = out.attentions
+        if raw is not None and len(raw) > 0:
+            arr = np.asarray(raw[0], np.float32)
+            if arr.ndim == 4:
+                arr = arr[0, :, -1, :]
+            if arr.ndim == 2:
+                hh, cc = min(arr.shape[0], n_kv_heads), min(arr.shape[1], n_prompt)
+                if hh > 0 and cc > 0:
+                    ph_cumul[:hh, :cc] += arr[:hh, :cc]
+                    ph_cur[:hh, :cc] = arr[:hh, :cc]
+                    ph_ready = True
+        if not use_cur or ph_ready:
+            per_head_select(0)
+    if ph_keep is not None and evicted:
+        ph_keep[:, evicted] = False
     slots.compact(np.flatnonzero(retained[:n_pos]).tolist())
     slot_tables.append(slots.pos.copy())
     counts.append(int(retained[:n_pos].sum()))
@@ -202,7 +262,13 @@ def generate(
         meta.access_count[new_pos] = 1
         slots.assign(new_pos)
 
-        vict = evict(step, False) if regime == "decode" else []
+        cadence = step % evict_every == 0
+        if per_head and cadence and regime == "decode" and ph_keep is not None and (not use_cur or ph_ready):
+            vict = per_head_select(step)
+        else:
+            vict = evict(step, False) if regime == "decode" else []
+        if ph_keep is not None and vict:
+            ph_keep[:, vict] = False
         for p in vict:
             slots.release(p)
         victims_by_step.append(vict)
@@ -212,7 +278,9 @@ def generate(
         if step == max_new_tokens:
             break
 
-        if n_kv_heads > 0:
+        if per_head and ph_keep is not None:
+            mask_arg = ph_keep[:, :n_pos].astype(np.float32)
+        elif n_kv_heads > 0:
             mask_arg = np.broadcast_to(retained[:n_pos].astype(np.float32), (n_kv_heads, n_pos)).copy()
         else:
             mask_arg = [1.0 if r else 0.0 for r in retained[:n_pos]]
@@ -222,7 +290,20 @@ def generate(
         past = out.past_key_values
         last_logits = np.asarray(out.logits, np.float32)
 
-        ks = _per_key_max(out.attentions, n_pos)[:n_pos].astype(np.float32)
+        if per_head and out.attentions is not None and len(out.attentions) > 0:
+            # per-head scores (Hq, C); rows 0..n_kv_heads-1 feed the per-head signals
+            # (kv_coupled_generator.py:470-497: the first n_kv_heads QUERY heads)
+            arr = np.asarray(out.attentions[0], np.float32)
+            if ph_cumul is not None and arr.ndim == 2:
+                hh, cc = min(arr.shape[0], n_kv_heads), min(arr.shape[1], n_pos)
+                ph_cumul[:hh, :cc] += arr[:hh, :cc]
+                ph_cur[:, :n_pos] = 0.0
+                ph_cur[:hh, :cc] = arr[:hh, :cc]
+                ph_ready = cc > 0
+                step_head_scores.append(arr[:hh, :n_pos].copy())
+            ks = arr.max(axis=0)[:n_pos].astype(np.float32)
+        else:
+            ks = _per_key_max(out.attentions, n_pos)[:n_pos].astype(np.float32)
         if ks.size:
             step_scores.append(ks.copy())
             rm = retained[:n_pos]
@@ -249,4 +330,9 @@ def generate(
         step_scores=step_scores,
         step_logits=step_logits,
         meta=meta,
+        faithful_union_retained_max=union_stats[0],
+        faithful_union_overflow_max=union_stats[1],
+        faithful_union_overflow_steps=union_stats[2],
+        head_keep=None if ph_keep is None else ph_keep[:, :n_pos].copy(),
+        step_head_scores=step_head_scores,
     )

@@ -90,8 +90,10 @@ def _key_fn(policy: str, m: Meta, step: int) -> Callable[[int], tuple]:
         return lambda p: (float(m.prefill[p]), int(m.last_access[p]), str(p))
     if policy == "adakv":  # AdaKVPolicy alpha=0.5, policies.py:1375-1412
         return lambda p: (float(m.cumul[p]) + 0.5 * float(m.max_attn[p]), int(m.last_access[p]), str(p))
-    if policy == "quest":  # policies.py:1415-1449
+    if policy in ("quest", "quest_faithful", "quest_native"):  # policies.py:1415-1449, fallback :1467-1478
         return lambda p: (float(m.attn[p]), int(m.last_access[p]), str(p))
+    if policy in ("adakv_faithful", "adakv_native"):  # global fallback, policies.py:1600-1612
+        return lambda p: (float(m.cumul[p]), int(m.last_access[p]), str(p))
     raise ValueError(f"unknown policy {policy!r}")
 
 
@@ -178,3 +180,106 @@ def hard_cap(retained: Sequence[int], m: Meta, overflow: int) -> List[int]:
         return []
     order = sorted(retained, key=lambda p: (int(m.last_access[p]), int(m.insert_step[p]), int(p)))
     return order[:overflow]
+
+
+# ---- per-KV-head ("faithful" / "native") policies -----------------------------------
+# AdaKVFaithfulPolicy / AdaKVNativePolicy (policies.py:1585-1672, helpers :69-178) and
+# QUESTFaithfulPolicy / QUESTNativePolicy (:1452-1551).  Each KV head keeps its own top-k
+# positions by a per-head signal; the generator evicts what no head keeps.
+PER_HEAD_POLICIES = ("adakv_faithful", "adakv_native", "quest_faithful", "quest_native")
+
+
+def per_head_uses_current(name: str) -> bool:
+    """QUEST ranks by the latest step's per-head attention, Ada-KV by the cumulative one."""
+    return canonical(name).startswith("quest")
+
+
+def _prefix_suffix(retained: np.ndarray, n_prefix: int, n_suffix: int) -> np.ndarray:
+    """Positions 0..n_prefix-1 and the n_suffix highest retained positions."""
+    prot = np.zeros(retained.shape[0], bool)
+    prot[:n_prefix] = True
+    if n_suffix > 0:
+        live = np.flatnonzero(retained)
+        if live.size:
+            prot[live[-n_suffix:]] = True
+    return prot
+
+
+def adakv_budgets(head_attn: np.ndarray, budget: int, native: bool) -> np.ndarray:
+    """Per-head budgets (policies.py:95-125): the same budget for every head (native), or a
+    shared budget split by inverse attention entropy, each head at least 1."""
+    H = head_attn.shape[0]
+    if budget <= 0 or H <= 0:
+        return np.zeros(H, dtype=int)
+    if native:
+        return np.full(H, budget, dtype=int)
+    total = budget * H
+    probs = head_attn / np.maximum(head_attn.sum(axis=1, keepdims=True), 1e-12)
+    ent = -np.sum(probs * np.log(np.maximum(probs, 1e-12)), axis=1)
+    inv = 1.0 / np.maximum(ent, 1e-6)
+    out = np.maximum(np.round(inv / inv.sum() * total).astype(int), 1)
+    while out.sum() > total:
+        out[np.argmax(out)] -= 1
+    while out.sum() < total:
+        out[np.argmin(out)] += 1
+    return out
+
+
+def select_per_head_retention(name: str, signal: np.ndarray, retention_mask: Sequence[bool], capacity: int,
+                              n_prefix: int, n_suffix: int) -> np.ndarray:
+    """(n_kv_heads, n_positions) keep mask of one per-head policy call."""
+    name = canonical(name)
+    H, n = signal.shape
+    retained = np.array(list(retention_mask)[:n], dtype=bool)
+    prot_raw = _prefix_suffix(retained, n_prefix, n_suffix)
+    if name.startswith("adakv"):
+        prot = prot_raw & retained
+        budget = max(0, int(capacity) - int(prot.sum()))
+        evictable_mask = retained & ~prot
+    else:  # quest: the budget counts the raw protected set
+        prot = prot_raw & retained
+        budget = max(0, int(capacity) - int(prot_raw.sum()))
+        evictable_mask = retained & ~prot_raw
+    keep = np.tile(prot, (H, 1))
+    if budget <= 0:
+        return keep
+    ev = np.flatnonzero(evictable_mask)
+    if ev.size == 0:
+        return keep
+    if name.startswith("adakv"):
+        budgets = adakv_budgets(signal[:, ev], budget, native=(name == "adakv_native"))
+    else:
+        budgets = np.full(H, budget, dtype=int)
+    for h in range(H):
+        b_h = min(int(budgets[h]), ev.size)
+        if b_h >= ev.size:
+            keep[h, ev] = True
+            continue
+        top = np.argpartition(signal[h, ev], -b_h)[-b_h:]
+        keep[h, ev[top]] = True
+    return keep
+
+
+def union_trim(keep: np.ndarray, signal: np.ndarray, retained: np.ndarray, capacity: int, n_prefix: int,
+               n_suffix: int) -> np.ndarray:
+    """Global retention = union of the heads' keep masks, trimmed to capacity by fewest
+    votes then lowest summed signal (kv_coupled_generator.py:398-427); modifies ``keep``."""
+    union = keep.any(axis=0)
+    n_union = int(union.sum())
+    if n_union > capacity:
+        n = keep.shape[1]
+        prot = np.zeros(n, bool)
+        prot[:n_prefix] = True
+        if n_suffix > 0:
+            live = np.flatnonzero(retained[:n])
+            if live.size >= n_suffix:
+                prot[live[-n_suffix:]] = True
+        cand = np.flatnonzero(union & ~prot)
+        if cand.size:
+            votes = keep[:, cand].sum(axis=0).astype(np.float64)
+            attn = signal[:, cand].sum(axis=0)
+            order = np.lexsort((attn, votes))
+            trim = cand[order[: min(n_union - capacity, cand.size)]]
+            union[trim] = False
+            keep[:, trim] = False
+    return union

@@ -66,6 +66,10 @@ def _policy_factory(P, name: str, capacity: int):
         "quest": lambda: P.QUESTPolicy(),
         "streamingllm": lambda: P.StreamingSinkLikePolicy(sink_size=4, recent_window_size=max(0, capacity - 4)),
         "random": lambda: P.RandomEvictionPolicy(),
+        "adakv_faithful": lambda: P.AdaKVFaithfulPolicy(),
+        "adakv_native": lambda: P.AdaKVNativePolicy(),
+        "quest_faithful": lambda: P.QUESTFaithfulPolicy(),
+        "quest_native": lambda: P.QUESTNativePolicy(),
     }[name]()
 
 
@@ -185,6 +189,16 @@ GEN_CASES = [
     ("random_noprot_e4", "random", 120, 40, 4, 25, None, 2, "decode", 18),
     ("random_tiny_cap_hardcap", "random", 60, 6, 8, 30, (0.10, 0.10), 2, "decode", 19),
     ("random_1024_256", "random", 1024, 256, 8, 64, (0.10, 0.10), 2, "decode", 20),
+    # per-KV-head policies (n_kv_heads > 0 selects the generator's per-head mode)
+    ("adakv_faithful", "adakv_faithful", 160, 40, 8, 30, (0.10, 0.10), 2, "decode", 21),
+    ("adakv_native", "adakv_native", 160, 40, 8, 30, (0.10, 0.10), 2, "decode", 22),
+    ("quest_faithful", "quest_faithful", 160, 40, 8, 30, (0.10, 0.10), 2, "decode", 23),
+    ("quest_native", "quest_native", 160, 40, 8, 30, (0.10, 0.10), 2, "decode", 24),
+    ("adakv_faithful_noprot", "adakv_faithful", 120, 32, 4, 25, None, 2, "decode", 25),
+    ("quest_faithful_e1_short_prompt", "quest_faithful", 30, 40, 1, 20, (0.10, 0.10), 2, "decode", 26),
+    ("adakv_faithful_1024_256", "adakv_faithful", 1024, 256, 8, 64, (0.10, 0.10), 2, "decode", 27),
+    ("quest_faithful_prefill_regime", "quest_faithful", 120, 40, 8, 20, (0.10, 0.10), 2, "prefill", 28),
+    ("adakv_native_tight", "adakv_native", 200, 24, 8, 40, (0.05, 0.05), 2, "decode", 29),
 ]
 
 
@@ -221,6 +235,9 @@ def make_generator_kats(ref: Path) -> dict:
                 "policy_call_steps": res.policy_call_steps,
                 "retained_counts_by_step": res.retained_counts_by_step,
                 "prefill_position_count": res.prefill_position_count,
+                "faithful_union_retained_max": res.faithful_union_retained_max,
+                "faithful_union_overflow_max": res.faithful_union_overflow_max,
+                "faithful_union_overflow_steps": res.faithful_union_overflow_steps,
             }
         )
     return {"source": "reference KVCoupledQwen35Generator + oracle.stub_model.StubScoreModel", "cases": out}

@@ -1,4 +1,5 @@
-"""Oracle decode/eviction loop vs. traces of the reference generator (same stub model)."""
+"""Oracle decode/eviction loop vs. traces of the reference generator (same stub model), global
+and per-KV-head policies."""
 
 import json
 import os
@@ -29,7 +30,8 @@ def test_generator_trace(case):
         n_kv_heads=case["n_kv_heads"], regime=case["regime"],
     )
     for key in ("generated_token_ids", "eviction_count", "positions_retained", "positions_evicted",
-                "retention_mask", "policy_call_steps", "retained_counts_by_step", "prefill_position_count"):
+                "retention_mask", "policy_call_steps", "retained_counts_by_step", "prefill_position_count",
+                "faithful_union_retained_max", "faithful_union_overflow_max", "faithful_union_overflow_steps"):
         assert getattr(res, key) == case[key], key
 
 
