@@ -164,13 +164,38 @@ int kvbp_append_evict(kvbp_stream_t stream, const kvbp_state* st, const kvbp_evi
  * are victim_pos[b][0..victim_count[b]) (absolute positions, in eviction order, each
  * retained after this step's append; victim_pos is [B][victim_stride]) instead of the
  * kernel's protection + top-k; the hard-capacity guardrail (kv_coupled_generator.py:
- * 588-604) still runs after them.  Unknown or repeated positions are skipped
- * (KVBP_DEV_INDEX for unknown).  Off-cadence steps ignore the list. */
+ * 588-604) still runs after them unless flags has KVBP_LISTED_NO_HARDCAP.  Unknown or
+ * repeated positions are skipped (KVBP_DEV_INDEX for unknown).  Off-cadence steps ignore
+ * the list.  The per-KV-head policies use the same path: their selection (per-head top-k,
+ * union, trim by votes then signal, kv_coupled_generator.py:373-433) lists the positions
+ * no head keeps, with KVBP_LISTED_NO_HARDCAP (that branch of the reference has no
+ * guardrail). */
+#define KVBP_LISTED_NO_HARDCAP 1
 int kvbp_append_evict_listed(kvbp_stream_t stream, const kvbp_state* st, const kvbp_evict_cfg* cfg,
                              int32_t* seq_step, int32_t* next_pos, int32_t* cur_pos, int32_t* write_slot,
                              const int32_t* tokens, int32_t* token_log, int32_t log_steps, int32_t* evlog,
                              int32_t* evcount, int32_t evcap, int32_t* retained_log, const int32_t* victim_pos,
-                             const int32_t* victim_count, int32_t victim_stride, int32_t* dev_err);
+                             const int32_t* victim_count, int32_t victim_stride, int32_t flags, int32_t* dev_err);
+
+/* K1 with per-KV-head retention (faithful Ada-KV / QUEST, kv_coupled_generator.py:
+ * 436-447 builds the per-head mask, jax_inference.py:1534-1573 applies it per KV head).
+ * As kvbp_decode_attn_score, and: head_keep [B][Hkv][S] u8 -- slot s is visible to kv
+ * head h only when head_keep[b][h][s] != 0 (and slot_pos >= 0); head_score [B][Hkv][S]
+ * float (non-negative on entry) is max-accumulated with query head r's probability for
+ * r < Hkv: the rows of the per-head (Hq, C) attention output the reference's generator
+ * takes as its per-head signals (kv_coupled_generator.py:470-492).  Pass the same buffer
+ * for every layer to get the max over layers (jax_inference.py:1666-1673). */
+int kvbp_decode_attn_score_heads(kvbp_stream_t stream, int32_t B, int32_t Hq, int32_t Hkv, int32_t head_dim,
+                                 int32_t S, const void* q, const void* kcache, const void* vcache,
+                                 const int32_t* slot_pos, const int32_t* write_slot, const uint8_t* head_keep,
+                                 void* out, float* step_score, float* head_score, int32_t* dev_err);
+
+/* Per-head signal update after a step's forward (kv_coupled_generator.py:482-492):
+ * head_cumul [B][Hkv][S] float64 += head_score (the slot write_slot[b] names starts from
+ * 0: it holds this step's new position), head_current = head_score, then head_score is
+ * cleared. */
+int kvbp_head_signal_update(kvbp_stream_t stream, int32_t B, int32_t Hkv, int32_t S, const int32_t* write_slot,
+                            float* head_score, double* head_cumul, float* head_current, int32_t* dev_err);
 
 /* K3 at step 0 -- victim selection over the P prompt positions after prefill
  * (kv_coupled_generator.py:229-239 with force_if_over_capacity).  scores [B][P] are the
@@ -266,19 +291,19 @@ int kvbp_decode_qkv_gemm(kvbp_stream_t stream, int32_t M, int32_t n_heads, int32
 
 /* Tensor-parallel row-parallel projection with the allreduce fused in: this rank's
  * partial Y = X . W^T (fp32, W packed) is pushed tile by tile into the symmetric buffer
- * of every rank of the group (peer_bases[q] = rank q's buffer, mapped into this process;
- * a device array), and each tile is finished as h = bf16(h + bf16(sum over ranks, in
- * rank order)) with ss_out as in epilogue 1 -- identical on every rank.  Buffer layout
- * (buffer_bytes each): u32 flags [2][world][1024] (word tile * 16 + split of each
- * (parity, source rank) row; N <= 8192), then fp32 [2][world][M][N] at byte offset
- * 8192 * world.  The flag area does not depend on the call's split count or N, so calls
- * with different splits share one buffer safely.  The flags are zeroed (and the ranks
- * synchronised) before a run.  call_index (0..254) numbers the allreduces of one step (parity =
- * call_index & 1 double-buffers the receive area) and *epoch must differ between steps
- * (flags hold epoch * 256 + call_index + 1).  Every rank must make the same calls in the
- * same order; waits are bounded (KVBP_DEV_PEER_TIMEOUT).  One rank per GPU: the ranks'
- * kernels wait on each other and must run concurrently; the call is rejected when the
- * whole grid cannot be resident at once. */
+ * of every other rank of the group (peer_bases[q] = rank q's buffer, mapped into this
+ * process; a device array), and each tile is finished as h = bf16(h + bf16(sum over
+ * ranks, in rank order)) with ss_out as in epilogue 1 -- identical on every rank.  Each
+ * fp32 value travels with a tag in the same 8 bytes (16-byte slots {x, tag, y, tag} per
+ * column pair), so receivers spin on the data itself: no fences or flag round trips.
+ * Buffer layout (buffer_bytes each, >= 2 * world * M * N * 8): slots
+ * [2 (call_index & 1)][world (source rank)][M][N / 2]; N <= 8192.  The buffer is zeroed
+ * (and the ranks synchronised) before a run.  call_index (0..254) numbers the allreduces
+ * of one step and *epoch must differ between steps (tags are epoch * 256 + call_index +
+ * 1).  Every rank must make the same calls in the same order; waits are bounded
+ * (KVBP_DEV_PEER_TIMEOUT).  One rank per GPU: the ranks' kernels wait on each other and
+ * must run concurrently; the call is rejected when the whole grid cannot be resident at
+ * once. */
 int kvbp_decode_gemm_allreduce(kvbp_stream_t stream, int32_t M, int32_t N, int32_t K, const void* w_packed,
                                const void* x, int32_t ldx, void* h, float* ss_out, int32_t splits,
                                const uint64_t* peer_bases, int32_t world, int32_t rank, int32_t call_index,

@@ -15,6 +15,7 @@ from typing import Optional
 LIB_PATH = Path(__file__).resolve().parent / "lib" / "libkvbp.so"
 
 KVBP_OK = 0
+LISTED_NO_HARDCAP = 1
 DEV_ERRORS = {
     1: "no free KV slot",
     2: "NaN score",
@@ -92,8 +93,10 @@ SIGNATURES = {
     ),
     "kvbp_append_evict_listed": (
         C.c_int,
-        [P, C.POINTER(State), C.POINTER(EvictCfg), P, P, P, P, P, P, I32, P, P, I32, P, P, P, I32, P],
+        [P, C.POINTER(State), C.POINTER(EvictCfg), P, P, P, P, P, P, I32, P, P, I32, P, P, P, I32, I32, P],
     ),
+    "kvbp_decode_attn_score_heads": (C.c_int, [P, I32, I32, I32, I32, I32, P, P, P, P, P, P, P, P, P, P]),
+    "kvbp_head_signal_update": (C.c_int, [P, I32, I32, I32, P, P, P, P, P]),
     "kvbp_prefill_select": (C.c_int, [P, I32, I32, C.POINTER(EvictCfg), P, P, P, I32, C.POINTER(C.c_int32), P]),
     "kvbp_prefill_compact": (
         C.c_int,

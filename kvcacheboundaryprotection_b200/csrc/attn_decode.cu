@@ -91,6 +91,11 @@ struct AttnArgs {
   const int* write_slot;   // [B] or null: see "Early streaming"
   __nv_bfloat16* out;      // [B, Hq, D]
   float* step_score;       // [B, S], non-negative; atomicMax target
+  // per-KV-head retention (Ada-KV / QUEST faithful): slot s is visible to kv head h only
+  // when head_keep[b][h][s] != 0 (null: every valid slot); head_score[b][r][s] receives the
+  // max over calls of query head r's probability for r < Hkv (null: not kept)
+  const uint8_t* head_keep;
+  float* head_score;
   int* err;
   int B, Hq, Hkv, S;
   int tiles;       // ceil(S / 64)
@@ -242,8 +247,13 @@ __global__ void __launch_bounds__(attn_threads(GR), kMinBlocks) decode_attn_scor
     // slot positions of the warp's rows g and g + 8 of this tile (< 0: free slot), read
     // while the tile is in flight; lanes t == 0 keep them for the score pass
     const int lta = u * kTile + r0 + g, ltb = lta + 8;
-    const int pa = t0 * kTile + lta < S ? spos_g[t0 * kTile + lta] : -1;
-    const int pb = t0 * kTile + ltb < S ? spos_g[t0 * kTile + ltb] : -1;
+    int pa = t0 * kTile + lta < S ? spos_g[t0 * kTile + lta] : -1;
+    int pb = t0 * kTile + ltb < S ? spos_g[t0 * kTile + ltb] : -1;
+    if (p.head_keep) {  // a slot this kv head does not retain counts as free for it
+      const uint8_t* hk = p.head_keep + static_cast<size_t>(pair) * S + t0 * kTile;
+      if (pa >= 0 && !hk[lta]) pa = -1;
+      if (pb >= 0 && !hk[ltb]) pb = -1;
+    }
     bool ok_tile = !(*reinterpret_cast<volatile int*>(bad_flag));
     if (ok_tile && !mbar_wait_bounded(&full[st], (u / kStages) & 1)) {
       set_err(p.err, kErrWaitTimeout);
@@ -477,6 +487,8 @@ __global__ void __launch_bounds__(attn_threads(GR), kMinBlocks) decode_attn_scor
       iLh[h] = finL[h] > 0.f ? 1.0f / finL[h] : 0.f;
     }
     float* sscore = p.step_score + static_cast<size_t>(b) * S;
+    // query heads kvh * G + h below Hkv also feed the per-head signal rows
+    float* hrow = p.head_score ? p.head_score + (static_cast<size_t>(b) * p.Hkv + kvh * G) * S : nullptr;
     for (int i = tid; i < nloc; i += kConsumers) {
       if (spos_s[i] < 0) continue;
       float mx = 0.f;
@@ -484,6 +496,8 @@ __global__ void __launch_bounds__(attn_threads(GR), kMinBlocks) decode_attn_scor
       for (int h = 0; h < G; ++h) {
         const float pr = iLh[h] > 0.f ? expf(logits[i * 8 + h] - Mh[h]) * iLh[h] : 0.f;
         mx = fmaxf(mx, pr);
+        if (hrow && kvh * G + h < p.Hkv)
+          atomicMax(reinterpret_cast<int*>(&hrow[static_cast<size_t>(h) * S + t0 * kTile + i]), __float_as_int(pr));
       }
       if (mx != mx) set_err(p.err, kErrNanScore);
       atomicMax(reinterpret_cast<int*>(&sscore[t0 * kTile + i]), __float_as_int(mx));
@@ -560,7 +574,7 @@ static cudaError_t launch_g(cudaStream_t stream, const CUtensorMap& km, const CU
 
 int decode_attn_score(cudaStream_t stream, int B, int Hq, int Hkv, int D, int S, const void* q, const void* kcache,
                       const void* vcache, const int* slot_pos, const int* write_slot, void* out, float* step_score,
-                      int* err, int cluster_override) {
+                      int* err, int cluster_override, const uint8_t* head_keep, float* head_score) {
   if (!q || !kcache || !vcache || !slot_pos || !out || !step_score)
     return fail(kStatusArg, "decode_attn_score: null pointer");
   if (D != kD) return fail(kStatusUnsupported, "decode_attn_score: head_dim %d unsupported (only 128)", D);
@@ -604,6 +618,8 @@ int decode_attn_score(cudaStream_t stream, int B, int Hq, int Hkv, int D, int S,
   a.write_slot = write_slot;
   a.out = static_cast<__nv_bfloat16*>(out);
   a.step_score = step_score;
+  a.head_keep = head_keep;
+  a.head_score = head_score;
   a.err = err;
   a.B = B;
   a.Hq = Hq;
@@ -651,7 +667,18 @@ extern "C" int kvbp_decode_attn_score(kvbp_stream_t stream, int32_t B, int32_t H
                                       const int32_t* slot_pos, const int32_t* write_slot, void* out,
                                       float* step_score, int32_t* dev_err) {
   return kvbp::decode_attn_score(reinterpret_cast<cudaStream_t>(stream), B, Hq, Hkv, head_dim, S, q, kcache, vcache,
-                                 slot_pos, write_slot, out, step_score, dev_err, 0);
+                                 slot_pos, write_slot, out, step_score, dev_err, 0, nullptr, nullptr);
+}
+
+extern "C" int kvbp_decode_attn_score_heads(kvbp_stream_t stream, int32_t B, int32_t Hq, int32_t Hkv,
+                                            int32_t head_dim, int32_t S, const void* q, const void* kcache,
+                                            const void* vcache, const int32_t* slot_pos, const int32_t* write_slot,
+                                            const uint8_t* head_keep, void* out, float* step_score,
+                                            float* head_score, int32_t* dev_err) {
+  if (!head_keep || !head_score)
+    return kvbp::fail(kvbp::kStatusArg, "decode_attn_score_heads: head_keep and head_score are required");
+  return kvbp::decode_attn_score(reinterpret_cast<cudaStream_t>(stream), B, Hq, Hkv, head_dim, S, q, kcache, vcache,
+                                 slot_pos, write_slot, out, step_score, dev_err, 0, head_keep, head_score);
 }
 
 // Same as kvbp_decode_attn_score with an explicit cluster size (CTAs per sequence and
@@ -661,5 +688,5 @@ extern "C" int kvbp_decode_attn_score_cs(kvbp_stream_t stream, int32_t B, int32_
                                          const int32_t* slot_pos, const int32_t* write_slot, void* out,
                                          float* step_score, int32_t* dev_err, int32_t cluster) {
   return kvbp::decode_attn_score(reinterpret_cast<cudaStream_t>(stream), B, Hq, Hkv, head_dim, S, q, kcache, vcache,
-                                 slot_pos, write_slot, out, step_score, dev_err, cluster);
+                                 slot_pos, write_slot, out, step_score, dev_err, cluster, nullptr, nullptr);
 }

@@ -328,6 +328,7 @@ struct AppendArgs {
   const int* ext_pos;
   const int* ext_n;
   int ext_stride;
+  int no_hardcap;  // listed victims only: skip the hard-capacity guardrail (per-head mode has none)
 };
 
 __device__ void log_victim(const AppendArgs& a, int b, int pos) {
@@ -526,7 +527,7 @@ __global__ void __launch_bounds__(kEvictThreads) append_evict_kernel(AppendArgs 
     }
     __syncthreads();
     // ---- hard-capacity guardrail ------------------------------------------------
-    const int overflow = (R - n_vict) - a.C;
+    const int overflow = a.no_hardcap ? 0 : (R - n_vict) - a.C;
     if (overflow > 0) {
       auto live = [&](int i) { return s.slot_pos[i] >= 0; };
       auto hkey = [&](int i) { return hardcap_key(s.slot_pos[i], s.insert_step[i], s.last_access[i]); };
@@ -758,6 +759,38 @@ int score_update(cudaStream_t stream, const StateArgs& st, const int* seq_step, 
   return check_launch("score_update");
 }
 
+// per-head signals of the faithful Ada-KV / QUEST policies (kv_coupled_generator.py:
+// 470-492): cumulative (float64 sum over steps) and current (this step's) attention of
+// query heads 0..Hkv-1, per slot.  The slot that received this step's new position
+// starts from zero (a fresh position's signal in the reference); head_score is cleared.
+__global__ void head_signal_update_kernel(int Hkv, int S, const int* __restrict__ write_slot,
+                                          float* __restrict__ head_score, double* __restrict__ head_cumul,
+                                          float* __restrict__ head_current) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int b = blockIdx.y;
+  const int ws = write_slot[b];
+  const size_t base = static_cast<size_t>(b) * Hkv * S;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < Hkv * S; i += gridDim.x * blockDim.x) {
+    const float q = head_score[base + i];
+    const double prev = (i % S) == ws ? 0.0 : head_cumul[base + i];
+    head_cumul[base + i] = __dadd_rn(prev, static_cast<double>(q));
+    head_current[base + i] = q;
+    head_score[base + i] = 0.f;
+  }
+}
+
+int head_signal_update(cudaStream_t stream, int B, int Hkv, int S, const int* write_slot, float* head_score,
+                       double* head_cumul, float* head_current, int* err) {
+  (void)err;
+  const int n = Hkv * S;
+  dim3 grid((n + 255) / 256 < 64 ? (n + 255) / 256 : 64, B);
+  cudaError_t e = launch_pdl(head_signal_update_kernel, grid, dim3(256), 0, stream, dim3(0), Hkv, S, write_slot,
+                             head_score, head_cumul, head_current);
+  if (e != cudaSuccess) return fail(kStatusCuda, "head_signal_update launch: %s", cudaGetErrorString(e));
+  return check_launch("head_signal_update");
+}
+
 int append_evict(cudaStream_t stream, const AppendArgs& a) {
   if (!state_ok(a.st) || !a.seq_step || !a.next_pos || !a.cur_pos || !a.write_slot || !a.evlog || !a.evcount)
     return fail(kStatusArg, "append_evict: bad argument");
@@ -851,12 +884,14 @@ static int append_evict_common(kvbp_stream_t stream, const kvbp_state* st, const
                                int32_t* seq_step, int32_t* next_pos, int32_t* cur_pos, int32_t* write_slot,
                                const int32_t* tokens, int32_t* token_log, int32_t log_steps, int32_t* evlog,
                                int32_t* evcount, int32_t evcap, int32_t* retained_log, const int32_t* victim_pos,
-                               const int32_t* victim_count, int32_t victim_stride, int32_t* dev_err) {
+                               const int32_t* victim_count, int32_t victim_stride, int32_t flags,
+                               int32_t* dev_err) {
   if (!st || !cfg) return kvbp::fail(kvbp::kStatusArg, "append_evict: null state/config");
   kvbp::AppendArgs a{};
   a.ext_pos = victim_pos;
   a.ext_n = victim_count;
   a.ext_stride = victim_stride;
+  a.no_hardcap = (flags & KVBP_LISTED_NO_HARDCAP) ? 1 : 0;
   a.st = to_state(st);
   a.C = cfg->capacity;
   a.E = cfg->evict_every;
@@ -885,17 +920,27 @@ int kvbp_append_evict(kvbp_stream_t stream, const kvbp_state* st, const kvbp_evi
                       int32_t* token_log, int32_t log_steps, int32_t* evlog, int32_t* evcount, int32_t evcap,
                       int32_t* retained_log, int32_t* dev_err) {
   return append_evict_common(stream, st, cfg, seq_step, next_pos, cur_pos, write_slot, tokens, token_log, log_steps,
-                             evlog, evcount, evcap, retained_log, nullptr, nullptr, 0, dev_err);
+                             evlog, evcount, evcap, retained_log, nullptr, nullptr, 0, 0, dev_err);
 }
 
 int kvbp_append_evict_listed(kvbp_stream_t stream, const kvbp_state* st, const kvbp_evict_cfg* cfg,
                              int32_t* seq_step, int32_t* next_pos, int32_t* cur_pos, int32_t* write_slot,
                              const int32_t* tokens, int32_t* token_log, int32_t log_steps, int32_t* evlog,
                              int32_t* evcount, int32_t evcap, int32_t* retained_log, const int32_t* victim_pos,
-                             const int32_t* victim_count, int32_t victim_stride, int32_t* dev_err) {
+                             const int32_t* victim_count, int32_t victim_stride, int32_t flags, int32_t* dev_err) {
   if (!victim_pos) return kvbp::fail(kvbp::kStatusArg, "append_evict_listed: victim_pos is required");
   return append_evict_common(stream, st, cfg, seq_step, next_pos, cur_pos, write_slot, tokens, token_log, log_steps,
-                             evlog, evcount, evcap, retained_log, victim_pos, victim_count, victim_stride, dev_err);
+                             evlog, evcount, evcap, retained_log, victim_pos, victim_count, victim_stride, flags,
+                             dev_err);
+}
+
+int kvbp_head_signal_update(kvbp_stream_t stream, int32_t B, int32_t Hkv, int32_t S, const int32_t* write_slot,
+                            float* head_score, double* head_cumul, float* head_current, int32_t* dev_err) {
+  if (!head_score || !head_cumul || !head_current || !write_slot)
+    return kvbp::fail(kvbp::kStatusArg, "head_signal_update: null pointer");
+  if (B <= 0 || Hkv <= 0 || S <= 0 || B > 65535) return kvbp::fail(kvbp::kStatusArg, "head_signal_update: bad size");
+  return kvbp::head_signal_update(reinterpret_cast<cudaStream_t>(stream), B, Hkv, S, write_slot, head_score,
+                                  head_cumul, head_current, dev_err);
 }
 
 int kvbp_prefill_select(kvbp_stream_t stream, int32_t B, int32_t P, const kvbp_evict_cfg* cfg, const float* scores,

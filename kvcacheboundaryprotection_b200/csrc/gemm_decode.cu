@@ -88,26 +88,30 @@ struct Args {
   __nv_bfloat16* q_out;   // [M][Hq][128]
   __nv_bfloat16* kcache;  // [M][Hkv][S][128]
   __nv_bfloat16* vcache;
-  // RESID + ALLREDUCE epilogue: every rank's symmetric buffer holds
-  //   flags u32 [2][world][kArFlagSlots] (slot = tile * kMaxSplits + split), then
-  //   recv f32 [2][world][M][N].  The flag area's size depends on the world size only, so
-  //   calls with different split counts or widths never overlap each other's flags.
+  // RESID + ALLREDUCE epilogue: every rank's symmetric buffer holds the receive area
+  //   [2 (call parity)][world (source rank)][M][N / 2] 16-byte slots {x, tag, y, tag}.
+  //   Its layout depends on the world size, M and N only, never on the split count.
   const unsigned long long* peers;  // [world] base address of each rank's buffer (device array)
   int world, rank, call;            // call: index of this allreduce within the step (parity = call & 1)
   const int* epoch;                 // device counter that differs between steps
 };
 
-constexpr int kArMaxTiles = 64;                         // N <= 8192
-constexpr int kArFlagSlots = kArMaxTiles * kMaxSplits;  // per (parity, source rank)
-__host__ __device__ inline size_t ar_flag_words(int world) { return static_cast<size_t>(2) * world * kArFlagSlots; }
-__host__ __device__ inline size_t ar_recv_offset(int world) { return ar_flag_words(world) * 4; }  // 256-byte multiple
-
-__device__ __forceinline__ void st_release_sys_u32(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+constexpr int kArMaxTiles = 64;  // N <= 8192
+__host__ __device__ inline size_t ar_buffer_bytes(int world, int M, int N) {
+  return static_cast<size_t>(2) * world * M * N * 8;
 }
-__device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+
+__device__ __forceinline__ void st_relaxed_sys_v4(uint4* p, uint4 v) {
+  asm volatile("st.relaxed.sys.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z),
+               "r"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ uint4 ld_relaxed_sys_v4(const uint4* p) {
+  uint4 v;
+  asm volatile("ld.relaxed.sys.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p)
+               : "memory");
   return v;
 }
 
@@ -419,48 +423,55 @@ __global__ void __launch_bounds__(kThreads) decode_gemm_kernel(const __grid_cons
         if (rank == 0 && r >= M) a.ss_out[tile * 32 + r] = 0.f;
       }
     } else if (EPI == kResidAR) {
+      // Low-latency allreduce: every fp32 partial travels with its tag in the same 8 bytes
+      // ({x, tag, y, tag} per column pair, one 16-byte store per peer), so a receiver
+      // spins on the data itself -- no fences, no separate flags.  Each rank sums the
+      // ranks' values in rank order, so every rank holds the same bits.
       const int W = a.world;
       const int par = a.call & 1;
-      const uint32_t v = static_cast<uint32_t>(*a.epoch) * 256u + static_cast<uint32_t>(a.call) + 1u;
-      const size_t roff = ar_recv_offset(W);
-      // 1. this rank's rows of the tile into every rank's receive buffer (slot `rank`)
+      const uint32_t tag = static_cast<uint32_t>(*a.epoch) * 256u + static_cast<uint32_t>(a.call) + 1u;
+      const int np = a.N / 2;  // column pairs per row
+      auto slot = [&](int q, int src, int r, int c) {  // rank q's 16-byte slot for (src, r, pair c/2)
+        return reinterpret_cast<uint4*>(a.peers[q]) + ((static_cast<size_t>(par) * W + src) * M + r) * np + (n0 + c) / 2;
+      };
+      // 1. this rank's rows of the tile into every peer's receive area
       for (int e = tid; e < nrows * (BN / 2); e += kConsumers) {
         const int r = r_lo + e / (BN / 2), c = 2 * (e % (BN / 2));
         const float2 val = sum_pair(r, c);
-        const size_t off = ((static_cast<size_t>(par) * W + a.rank) * M + r) * a.N + n0 + c;
+        const uint4 pk = make_uint4(__float_as_uint(val.x), tag, __float_as_uint(val.y), tag);
         for (int q = 0; q < W; ++q)
-          *reinterpret_cast<float2*>(reinterpret_cast<float*>(a.peers[q] + roff) + off) = val;
+          if (q != a.rank) st_relaxed_sys_v4(slot(q, a.rank, r, c), pk);
       }
-      __threadfence_system();
-      named_bar(1, kConsumers);
-      const size_t fslot = static_cast<size_t>(tile) * kMaxSplits + blockIdx.y;
-      if (tid < W)
-        st_release_sys_u32(reinterpret_cast<uint32_t*>(a.peers[tid]) + (static_cast<size_t>(par) * W + a.rank) * kArFlagSlots + fslot, v);
-      // 2. every rank's rows of this slice have landed here
-      if (tid < W) {
-        const uint32_t* f = reinterpret_cast<const uint32_t*>(a.peers[a.rank]) + (static_cast<size_t>(par) * W + tid) * kArFlagSlots + fslot;
-        uint32_t spins = 0;
-        while (ld_acquire_sys_u32(f) != v) {
-          if (++spins > (1u << 24)) {
-            set_err(a.err, kErrPeerTimeout);
-            break;
-          }
-          if (spins > 64) __nanosleep(128);
-        }
-      }
-      named_bar(1, kConsumers);
-      // 3. sum the ranks' partials in rank order, residual add, sums of squares
-      const float* recv = reinterpret_cast<const float*>(a.peers[a.rank] + roff);
+      // 2. every rank's value, summed in rank order; residual add, sums of squares
       for (int e0 = 0; e0 < nrows * (BN / 2); e0 += kConsumers) {
         const int e = e0 + tid;
         float ss = 0.f;
         if (e < nrows * (BN / 2)) {
           const int r = r_lo + e / (BN / 2), c = 2 * (e % (BN / 2));
-          float2 sum = __ldcg(reinterpret_cast<const float2*>(recv + ((static_cast<size_t>(par) * W + 0) * M + r) * a.N + n0 + c));
-          for (int q = 1; q < W; ++q) {
-            const float2 t2 = __ldcg(reinterpret_cast<const float2*>(recv + ((static_cast<size_t>(par) * W + q) * M + r) * a.N + n0 + c));
-            sum.x += t2.x;
-            sum.y += t2.y;
+          const float2 own = sum_pair(r, c);
+          float2 sum = make_float2(0.f, 0.f);
+          for (int q = 0; q < W; ++q) {
+            float2 v = own;
+            if (q != a.rank) {
+              const uint4* src = slot(a.rank, q, r, c);
+              uint4 got = ld_relaxed_sys_v4(src);
+              uint32_t spins = 0;
+              while (got.y != tag || got.w != tag) {
+                if (++spins > (1u << 22)) {
+                  set_err(a.err, kErrPeerTimeout);
+                  break;
+                }
+                if (spins > 32) __nanosleep(64);
+                got = ld_relaxed_sys_v4(src);
+              }
+              v = make_float2(__uint_as_float(got.x), __uint_as_float(got.z));
+            }
+            if (q == 0) {
+              sum = v;
+            } else {
+              sum.x += v.x;
+              sum.y += v.y;
+            }
           }
           uint32_t* hp = reinterpret_cast<uint32_t*>(&a.out[static_cast<size_t>(r) * a.ldo + n0 + c]);
           const uint32_t hv = *hp;
@@ -726,7 +737,7 @@ int decode_gemm_allreduce(cudaStream_t stream, int M, int N, int K, const void* 
       return fail(kStatusUnsupported, "decode_gemm_allreduce: %d column tiles but only %d clusters of %d resident",
                   N / BN, clusters, splits);
   }
-  const size_t need = ar_recv_offset(world) + static_cast<size_t>(2) * world * M * N * 4;
+  const size_t need = ar_buffer_bytes(world, M, N);
   if (buffer_bytes < 0 || static_cast<size_t>(buffer_bytes) < need)
     return fail(kStatusArg, "decode_gemm_allreduce: symmetric buffer of %lld bytes < %zu needed", buffer_bytes, need);
   if (reinterpret_cast<uintptr_t>(h) & 3) return fail(kStatusArg, "decode_gemm_allreduce: h rows must be 4-byte aligned");

@@ -50,7 +50,10 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
 
 int decode_attn_score(cudaStream_t stream, int B, int Hq, int Hkv, int D, int S, const void* q, const void* kcache,
                       const void* vcache, const int* slot_pos, const int* write_slot, void* out, float* step_score,
-                      int* err, int cluster_override);
+                      int* err, int cluster_override, const uint8_t* head_keep, float* head_score);
+
+int head_signal_update(cudaStream_t stream, int B, int Hkv, int S, const int* write_slot, float* head_score,
+                       double* head_cumul, float* head_current, int* err);
 
 // Policy identifiers understood by the eviction kernels.
 enum PolicyId : int {

@@ -221,11 +221,18 @@ class CappedKVEngine:
         lib()  # fail loudly when the CUDA library is missing
         # a policy that draws its victims on the host (the random policy) through the
         # reference's select_evictions protocol; the device applies them
+        from .policies import per_head as _is_per_head
+
         self.host_policy = host_policy
-        if (capi.POLICY_IDS.get(evict.policy) == capi.POLICY_IDS["random"]) != (host_policy is not None):
-            raise ValueError("the random policy needs its policy object (host_policy), and only it")
+        self.per_head = host_policy is not None and _is_per_head(host_policy)
+        if evict.policy == "random" and host_policy is None:
+            raise ValueError("the random policy needs its policy object (host_policy)")
+        if host_policy is not None and not (self.per_head or evict.policy == "random"):
+            raise ValueError("host_policy is for the random and the per-KV-head policies only")
         if host_policy is not None and int(batch) != 1:
-            raise ValueError("a host-selected policy consumes one random stream sequence after sequence: batch must be 1")
+            raise ValueError("a host-selected policy runs one sequence per engine: batch must be 1")
+        inner = getattr(host_policy, "inner", host_policy)
+        self.head_uses_current = self.per_head and inner.name.startswith("quest")
         self.dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         if self.dev.type != "cuda":
             raise ValueError("CappedKVEngine runs on CUDA devices only")
@@ -288,6 +295,15 @@ class CappedKVEngine:
         if self.host_policy is not None:  # victims listed by the host at cadence steps
             self.ext_pos = z(B, S)
             self.ext_n = z(B)
+        if self.per_head:  # per-KV-head retention masks and signals, slot-indexed
+            Hkv = c.n_kv_heads
+            self.head_keep = torch.ones(B, Hkv, S, dtype=torch.uint8, device=d)
+            self.head_score = z(B, Hkv, S, dt=f32)
+            self.head_cumul = z(B, Hkv, S, dt=torch.float64)
+            self.head_current = z(B, Hkv, S, dt=f32)
+            self.head_ready = False
+            self.union_stats = [0, 0, 0]  # retained max, overflow max, overflow steps
+            self.head_call_steps: List[int] = []
         self.dev_err = z(1)
         H, F, V = c.hidden, c.ffn, c.vocab
         self.h = z(B, H, dt=bf)
@@ -376,6 +392,9 @@ class CappedKVEngine:
         pre_k = torch.empty(c.n_layers, B, Hkv, P, D, dtype=torch.bfloat16, device=d)
         pre_v = torch.empty_like(pre_k)
         scores = torch.zeros(B, P, dtype=torch.float32, device=d) if need_scores else None
+        # per-head mode seeds head 0 with the FIRST layer's per-key max only: the generator
+        # reads attentions[0] of the prefill output (kv_coupled_generator.py:244-262)
+        self.prefill_head_seed = torch.zeros(B, P, dtype=torch.float32, device=d) if self.per_head else None
         positions = torch.arange(P, dtype=torch.int32, device=d)
         H = c.hidden
         for b in range(B):
@@ -401,6 +420,8 @@ class CappedKVEngine:
                 att = self._prefill_attention(q, kb, vb, need_scores, lcol)
                 if need_scores:
                     torch.maximum(colmax, lcol, out=colmax)
+                    if li == 0 and self.prefill_head_seed is not None:
+                        self.prefill_head_seed[b].copy_(lcol)
                 o = torch.mm(att, self.fw.rowmajor(Lw["w_o"]).t())
                 check(L.kvbp_add_rmsnorm(st, P, H, _ptr(h), _ptr(o), _ptr(Lw["post_norm"]), _ptr(x), c.eps), "rmsnorm")
                 gu = torch.mm(x, self.fw.rowmajor(Lw["w_gu"]).t())
@@ -434,7 +455,7 @@ class CappedKVEngine:
         out, seen = [], set()
         for key in self.host_policy.select_evictions(blocks, evict_count, step):
             p = int(key)
-            if p in blocks and p not in seen:
+            if str(p) in blocks and p not in seen:
                 seen.add(p)
                 out.append(p)
         return out
@@ -444,7 +465,14 @@ class CappedKVEngine:
         victim = torch.zeros(self.B, P, dtype=torch.uint8, device=self.dev)
         self.evlog.zero_()
         nvict = capi.C.c_int32()
-        if self.host_policy is not None:
+        head_state = None
+        if self.per_head:
+            vict, head_state = self._per_head_step0(P, scores)
+            if vict:
+                victim[0, torch.tensor(vict, dtype=torch.long, device=self.dev)] = 1
+                self.evlog[0, : len(vict)] = torch.tensor(vict, dtype=torch.int32, device=self.dev)
+            nvict.value = len(vict)
+        elif self.host_policy is not None:
             # step 0 (force_if_over_capacity): evict_count = P - capacity, victims in the
             # policy's order, then the compaction's hard-capacity guardrail
             vict = self._host_victims(list(range(P)), max(0, P - self.ev.capacity), 0)
@@ -470,6 +498,8 @@ class CappedKVEngine:
             ),
             "prefill_compact",
         )
+        if self.per_head:
+            self._per_head_load(head_state)
         if pre_k is not None:
             c = self.cfg
             check(
@@ -493,6 +523,7 @@ class CappedKVEngine:
         P = int(prompt_len)
         scores = torch.rand(self.B, P, generator=g, device=self.dev, dtype=torch.float32)
         need_scores = capi.POLICY_IDS[self.ev.policy] != 0
+        self.prefill_head_seed = None  # per-head mode: the scores stand in for layer 0's
         self._select_and_compact(P, scores if need_scores else None)
         for t in (self.kc, self.vc):
             for li in range(t.shape[0]):
@@ -501,6 +532,9 @@ class CappedKVEngine:
 
     # ------------------------------------------------------------------ decode
     def _append_evict(self) -> None:
+        if self.per_head:
+            self._append_evict_per_head()
+            return
         if self.host_policy is not None:
             self._append_evict_listed()
             return
@@ -513,6 +547,121 @@ class CappedKVEngine:
             ),
             "append_evict",
         )
+
+    # ------------------------------------------------------------------ per-KV-head mode
+    def _per_head_call(self, signal: np.ndarray, retained: np.ndarray, step: int):
+        """One per-head policy call and the union trim (kv_coupled_generator.py:383-433);
+        returns (keep (Hkv, n), union (n,))."""
+        from .policies import union_trim
+
+        inner = getattr(self.host_policy, "inner", self.host_policy)
+        C = self.ev.capacity
+        keep = inner.select_per_head_retention(signal, retained.tolist(), C, n_protected=self.n_prefix,
+                                               n_suffix_protected=self.n_suffix, orig_prompt_len=self.prompt_len)
+        n_union = int(keep.any(axis=0).sum())
+        st = self.union_stats
+        st[0] = max(st[0], n_union)
+        st[1] = max(st[1], max(0, n_union - C))
+        st[2] += int(n_union > C)
+        union = union_trim(keep, signal, retained, C, self.n_prefix, self.n_suffix)
+        self.head_call_steps.append(step)
+        return keep, union
+
+    def _per_head_step0(self, P: int, scores):
+        """Step 0 in per-head mode (kv_coupled_generator.py:216-325): when the prompt
+        exceeds the capacity, the prefill score seeds head 0's signals and one per-head
+        call picks the victims (no global policy call otherwise)."""
+        Hkv = self.cfg.n_kv_heads
+        self.head_ready = False
+        self.head_call_steps = []
+        self.union_stats = [0, 0, 0]
+        if P <= self.ev.capacity:
+            return [], None
+        seed = (self.prefill_head_seed if getattr(self, "prefill_head_seed", None) is not None else scores)
+        seed = np.zeros(P, np.float32) if seed is None else seed[0].float().cpu().numpy()[:P]
+        cumul = np.zeros((Hkv, P), np.float64)
+        cumul[:1, :P] += seed[None, :]
+        cur = np.zeros((Hkv, P), np.float32)
+        cur[:1, :P] = seed[None, :]
+        self.head_ready = True
+        keep, union = self._per_head_call(cur if self.head_uses_current else cumul, np.ones(P, bool), 0)
+        return [p for p in range(P) if not union[p]], (keep, cumul, cur)
+
+    def _per_head_load(self, head_state) -> None:
+        """Slot-indexed per-head state after the step-0 compaction."""
+        self.head_keep.fill_(1)
+        self.head_cumul.zero_()
+        self.head_current.zero_()
+        self.head_score.zero_()
+        if head_state is None:
+            return
+        keep, cumul, cur = head_state
+        sp = self.slot_pos[0].cpu().numpy()
+        ok = sp >= 0
+        kk = np.ones(keep.shape[:1] + sp.shape, np.uint8)
+        kk[:, ok] = keep[:, sp[ok]]
+        self.head_keep[0].copy_(torch.from_numpy(kk))
+        cu = np.zeros(kk.shape, np.float64)
+        cu[:, ok] = cumul[:, sp[ok]]
+        self.head_cumul[0].copy_(torch.from_numpy(cu))
+        cr = np.zeros(kk.shape, np.float32)
+        cr[:, ok] = cur[:, sp[ok]]
+        self.head_current[0].copy_(torch.from_numpy(cr))
+
+    def _append_evict_per_head(self) -> None:
+        """Decode-step bookkeeping in per-head mode.  At a cadence step the host builds the
+        position-indexed signals from the device's per-slot ones, runs the per-head call
+        and the union trim, and the kernel frees the positions no head keeps (no guardrail,
+        as in the reference); then every slot's keep row is written for the next forward.
+        If the signal is not ready yet (QUEST before any forward), the reference falls back
+        to its global policy call, which is the device's QUEST key."""
+        step = int(self.seq_step[0].item()) + 1
+        cadence = self.ev.regime == "decode" and step % self.ev.evict_every == 0
+        if not cadence or (self.head_uses_current and not self.head_ready):
+            check(
+                lib().kvbp_append_evict(
+                    self.stream, capi.C.byref(self._state), capi.C.byref(self._cfg), _ptr(self.seq_step),
+                    _ptr(self.next_pos), _ptr(self.cur_pos), _ptr(self.write_slot), _ptr(self.tokens),
+                    _ptr(self.token_log), self.max_new, _ptr(self.evlog), _ptr(self.evcount), self.evcap,
+                    _ptr(self.retained_log), _ptr(self.dev_err),
+                ),
+                "append_evict",
+            )
+            if cadence:  # global fallback call: freed slots become visible to every head
+                self.head_call_steps.append(step)
+                free = self.slot_pos[0] < 0
+                self.head_keep[0][:, free] = 1
+            return
+        sp = self.slot_pos[0].cpu().numpy()
+        new_pos = int(self.next_pos[0].item())
+        n = new_pos + 1
+        ok = sp >= 0
+        retained = np.zeros(n, bool)
+        retained[sp[ok]] = True
+        retained[new_pos] = True
+        src = (self.head_current if self.head_uses_current else self.head_cumul)[0].cpu().numpy()
+        signal = np.zeros((src.shape[0], n), src.dtype)
+        signal[:, sp[ok]] = src[:, ok]
+        keep, union = self._per_head_call(signal, retained, step)
+        vict = [p for p in range(n) if retained[p] and not union[p]]
+        if vict:
+            self.ext_pos[0, : len(vict)] = torch.tensor(vict, dtype=torch.int32, device=self.dev)
+        self.ext_n.fill_(len(vict))
+        check(
+            lib().kvbp_append_evict_listed(
+                self.stream, capi.C.byref(self._state), capi.C.byref(self._cfg), _ptr(self.seq_step),
+                _ptr(self.next_pos), _ptr(self.cur_pos), _ptr(self.write_slot), _ptr(self.tokens),
+                _ptr(self.token_log), self.max_new, _ptr(self.evlog), _ptr(self.evcount), self.evcap,
+                _ptr(self.retained_log), _ptr(self.ext_pos), _ptr(self.ext_n), self.S, capi.LISTED_NO_HARDCAP,
+                _ptr(self.dev_err),
+            ),
+            "append_evict_listed",
+        )
+        sp2 = self.slot_pos[0].cpu().numpy()
+        ok2 = sp2 >= 0
+        kk = np.ones((keep.shape[0], sp2.shape[0]), np.uint8)
+        kk[:, ok2] = keep[:, sp2[ok2]]
+        self.head_keep[0].copy_(torch.from_numpy(kk))
 
     def _append_evict_listed(self) -> None:
         """Decode-step bookkeeping with host-drawn victims: at a cadence step the host
@@ -534,7 +683,7 @@ class CappedKVEngine:
                 self.stream, capi.C.byref(self._state), capi.C.byref(self._cfg), _ptr(self.seq_step),
                 _ptr(self.next_pos), _ptr(self.cur_pos), _ptr(self.write_slot), _ptr(self.tokens),
                 _ptr(self.token_log), self.max_new, _ptr(self.evlog), _ptr(self.evcount), self.evcap,
-                _ptr(self.retained_log), _ptr(self.ext_pos), _ptr(self.ext_n), self.S, _ptr(self.dev_err),
+                _ptr(self.retained_log), _ptr(self.ext_pos), _ptr(self.ext_n), self.S, 0, _ptr(self.dev_err),
             ),
             "append_evict_listed",
         )
@@ -575,19 +724,33 @@ class CappedKVEngine:
                 ),
                 "decode_qkv_gemm",
             )
-            check(
-                L.kvbp_decode_attn_score(
-                    st, B, c.n_heads, c.n_kv_heads, D, self.S, _ptr(self.q), _ptr(self.kc[li]), _ptr(self.vc[li]),
-                    _ptr(self.slot_pos), _ptr(self.write_slot), _ptr(self.attn_out), _ptr(self.step_score),
-                    _ptr(self.dev_err),
-                ),
-                "decode_attn_score",
-            )
+            self._attention(li)
             self._gemm("o", 1, H, c.n_heads * D, Lw["w_o"], self.attn_out, c.n_heads * D, self.h, H, ss_out=self.ss_b)
             self._gemm("gu", 2, 2 * F, H, Lw["w_gu"], self.h, H, self.act, F, Lw["post_norm"], self.ss_b, nt_h)
             self._gemm("down", 1, H, F, Lw["w_down"], self.act, F, self.h, H, ss_out=self.ss_a)
             ss_in, n_in = self.ss_a, nt_h
         self._gemm("lm", 0, c.vocab, H, self.lm_w, self.h, H, self.logits, c.vocab, self.final_norm, ss_in, n_in)
+
+    def _attention(self, li: int) -> None:
+        c, L = self.cfg, lib()
+        if self.per_head:
+            check(
+                L.kvbp_decode_attn_score_heads(
+                    self.stream, self.B, c.n_heads, c.n_kv_heads, c.head_dim, self.S, _ptr(self.q), _ptr(self.kc[li]),
+                    _ptr(self.vc[li]), _ptr(self.slot_pos), _ptr(self.write_slot), _ptr(self.head_keep),
+                    _ptr(self.attn_out), _ptr(self.step_score), _ptr(self.head_score), _ptr(self.dev_err),
+                ),
+                "decode_attn_score_heads",
+            )
+            return
+        check(
+            L.kvbp_decode_attn_score(
+                self.stream, self.B, c.n_heads, c.n_kv_heads, c.head_dim, self.S, _ptr(self.q), _ptr(self.kc[li]),
+                _ptr(self.vc[li]), _ptr(self.slot_pos), _ptr(self.write_slot), _ptr(self.attn_out),
+                _ptr(self.step_score), _ptr(self.dev_err),
+            ),
+            "decode_attn_score",
+        )
 
     def _forward_cublas(self) -> None:
         """Forward the token of every sequence at cur_pos, writing its K/V to write_slot."""
@@ -606,14 +769,7 @@ class CappedKVEngine:
                 ),
                 "qkv_rope_scatter",
             )
-            check(
-                L.kvbp_decode_attn_score(
-                    st, B, c.n_heads, c.n_kv_heads, D, self.S, _ptr(self.q), _ptr(self.kc[li]), _ptr(self.vc[li]),
-                    _ptr(self.slot_pos), _ptr(self.write_slot), _ptr(self.attn_out), _ptr(self.step_score),
-                    _ptr(self.dev_err),
-                ),
-                "decode_attn_score",
-            )
+            self._attention(li)
             torch.mm(self.attn_out, Lw["w_o"].t(), out=self.o)
             check(L.kvbp_add_rmsnorm(st, B, H, _ptr(self.h), _ptr(self.o), _ptr(Lw["post_norm"]), _ptr(self.x), c.eps), "rmsnorm")
             torch.mm(self.x, Lw["w_gu"].t(), out=self.gu)
@@ -627,6 +783,14 @@ class CappedKVEngine:
         L, st, c = lib(), self.stream, self.cfg
         check(L.kvbp_argmax(st, self.B, c.vocab, c.vocab, _ptr(self.logits), _ptr(self.tokens)), "argmax")
         check(L.kvbp_score_update(st, capi.C.byref(self._state), _ptr(self.seq_step), _ptr(self.step_score), _ptr(self.dev_err)), "score_update")
+        self._head_signal_update()
+
+    def _head_signal_update(self) -> None:
+        if self.per_head:
+            check(lib().kvbp_head_signal_update(self.stream, self.B, self.cfg.n_kv_heads, self.S, _ptr(self.write_slot),
+                                                _ptr(self.head_score), _ptr(self.head_cumul), _ptr(self.head_current),
+                                                _ptr(self.dev_err)), "head_signal_update")
+            self.head_ready = True
 
     def decode_step_launches(self, *, forward: bool = True, sample: bool = True) -> None:
         """Enqueue one decode step (no host synchronisation)."""
@@ -637,6 +801,7 @@ class CappedKVEngine:
                 self._sample_and_score()
             else:
                 check(lib().kvbp_score_update(self.stream, capi.C.byref(self._state), _ptr(self.seq_step), _ptr(self.step_score), _ptr(self.dev_err)), "score_update")
+                self._head_signal_update()
 
     def capture(self) -> None:
         """Capture one full decode step (append/evict + forward + sample + score) as a graph."""

@@ -240,7 +240,10 @@ class KVCoupledQwen35Generator:
         n_pos = P + stop
         mask = np.ones(n_pos, bool)
         mask[evicted] = False
-        calls = [0] + ([s for s in range(1, stop + 1) if s % E == 0] if self.eviction_regime == "decode" else [])
+        if getattr(eng, "per_head", False):  # the per-head branch records only the calls it made
+            calls = [s for s in eng.head_call_steps if s <= stop]
+        else:
+            calls = [0] + ([s for s in range(1, stop + 1) if s % E == 0] if self.eviction_regime == "decode" else [])
         gen = [int(t) for t in prompt] + [int(t) for t in tokens]
         if eos_tok is not None:
             gen.append(int(eos_tok))
@@ -265,4 +268,6 @@ class KVCoupledQwen35Generator:
             decode_step_p50_ms=p50,
             decode_step_p95_ms=p95,
             decode_step_p99_ms=p99,
+            **({"faithful_union_retained_max": eng.union_stats[0], "faithful_union_overflow_max": eng.union_stats[1],
+                "faithful_union_overflow_steps": eng.union_stats[2]} if getattr(eng, "per_head", False) else {}),
         )

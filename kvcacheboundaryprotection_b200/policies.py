@@ -15,7 +15,9 @@ from __future__ import annotations
 
 import random
 from dataclasses import dataclass, field
-from typing import Any, Dict, List
+from typing import Any, Dict, List, Sequence
+
+import numpy as np
 
 from .capi import POLICY_IDS, protection_sizes
 
@@ -123,9 +125,162 @@ class ProtectedPolicyWrapper:
         return self.inner.select_evictions(eligible, min(evict_count, len(eligible)), step)
 
 
+# ---- per-KV-head policies -------------------------------------------------------------
+# Each KV head keeps its own top-k positions by a per-head signal; the generator evicts
+# what no head keeps.  The selection is numpy on the host, with the reference's numpy
+# operations in the same order (np.argpartition's choice among equal signals -- e.g. the
+# all-zero rows of heads 1.. at step 0 -- is part of the result), over signals the GPU
+# accumulates per slot; the GPU applies the per-head masks in attention and frees the
+# victims' slots.
+
+
+def _protected(retained: np.ndarray, n_prefix: int, n_suffix: int) -> np.ndarray:
+    """Positions 0..n_prefix-1 and the n_suffix highest retained positions."""
+    prot = np.zeros(retained.shape[0], dtype=bool)
+    prot[:n_prefix] = True
+    if n_suffix > 0:
+        live = np.where(retained)[0]
+        if len(live) > 0:
+            prot[live[-n_suffix:]] = True
+    return prot
+
+
+def _top_b_per_head(signal: np.ndarray, evictable: np.ndarray, budgets, keep: np.ndarray) -> None:
+    for h in range(signal.shape[0]):
+        b_h = min(int(budgets[h]), len(evictable))
+        if b_h >= len(evictable):
+            keep[h, evictable] = True
+            continue
+        top = np.argpartition(signal[h, evictable], -b_h)[-b_h:]
+        keep[h, evictable[top]] = True
+
+
+@dataclass
+class AdaKVFaithfulPolicy:
+    """Ada-KV with per-head budgets (policies.py:1585-1642, :95-178): a shared budget of
+    (capacity - protected) per head is split across heads by inverse attention entropy
+    of the cumulative per-head signal; each head keeps its top-B_h."""
+
+    name: str = "adakv_faithful"
+    static_suffix_mode: bool = False
+    native_per_head = False
+
+    def __post_init__(self):
+        if self.static_suffix_mode:
+            raise ValueError("static_suffix_mode is not supported on the GPU path")
+
+    def _budgets(self, head_attn: np.ndarray, budget: int) -> np.ndarray:
+        H = head_attn.shape[0]
+        if budget <= 0 or H <= 0:
+            return np.zeros(H, dtype=int)
+        if self.native_per_head:
+            return np.full(H, budget, dtype=int)
+        total = budget * H
+        row = np.maximum(head_attn.sum(axis=1, keepdims=True), 1e-12)
+        probs = head_attn / row
+        ent = -np.sum(probs * np.log(np.maximum(probs, 1e-12)), axis=1)
+        inv = 1.0 / np.maximum(ent, 1e-6)
+        b = np.maximum(np.round(inv / inv.sum() * total).astype(int), 1)
+        while b.sum() > total:
+            b[np.argmax(b)] -= 1
+        while b.sum() < total:
+            b[np.argmin(b)] += 1
+        return b
+
+    def select_per_head_retention(self, per_head_cumul_attn: np.ndarray, retention_mask: Sequence[bool],
+                                  capacity: int, n_protected: int = 0, n_suffix_protected: int = 0,
+                                  orig_prompt_len: int = 0) -> np.ndarray:
+        H, n = per_head_cumul_attn.shape
+        retained = np.array(list(retention_mask)[:n], dtype=bool)
+        prot = _protected(retained, n_protected, n_suffix_protected) & retained
+        keep = np.tile(prot, (H, 1))
+        budget = max(0, int(capacity) - int(prot.sum()))
+        ev = np.where(retained & ~prot)[0]
+        if budget <= 0 or len(ev) == 0:
+            return keep
+        _top_b_per_head(per_head_cumul_attn, ev, self._budgets(per_head_cumul_attn[:, ev], budget), keep)
+        return keep
+
+
+@dataclass
+class AdaKVNativePolicy(AdaKVFaithfulPolicy):
+    """Ada-KV with the full unprotected budget for every head (policies.py:1645-1672)."""
+
+    name: str = "adakv_native"
+    native_per_head = True
+
+
+@dataclass
+class QUESTFaithfulPolicy:
+    """QUEST per head (policies.py:1452-1538): each head keeps its top (capacity -
+    protected) positions by the latest step's per-head attention."""
+
+    name: str = "quest_faithful"
+    static_suffix_mode: bool = False
+
+    def __post_init__(self):
+        if self.static_suffix_mode:
+            raise ValueError("static_suffix_mode is not supported on the GPU path")
+
+    def select_per_head_retention(self, per_head_attn: np.ndarray, retention_mask: Sequence[bool], capacity: int,
+                                  n_protected: int = 0, n_suffix_protected: int = 0,
+                                  orig_prompt_len: int = 0) -> np.ndarray:
+        H, n = per_head_attn.shape
+        retained = np.array(list(retention_mask)[:n], dtype=bool)
+        prot = _protected(retained, n_protected, n_suffix_protected)
+        keep = np.tile(prot & retained, (H, 1))
+        budget = max(0, int(capacity) - int(prot.sum()))  # the raw protected count
+        ev = np.where(retained & ~prot)[0]
+        if budget <= 0 or len(ev) == 0:
+            return keep
+        _top_b_per_head(per_head_attn, ev, [budget] * H, keep)
+        return keep
+
+
+@dataclass
+class QUESTNativePolicy(QUESTFaithfulPolicy):
+    """Named alias of QUESTFaithfulPolicy (policies.py:1541-1550)."""
+
+    name: str = "quest_native"
+
+
+def union_trim(keep: np.ndarray, signal: np.ndarray, retained: np.ndarray, capacity: int, n_prefix: int,
+               n_suffix: int) -> np.ndarray:
+    """Global retention = the heads' union, trimmed to ``capacity`` by fewest votes, then
+    lowest summed signal, outside the prefix/suffix (kv_coupled_generator.py:398-427).
+    Clears trimmed positions in ``keep`` too; returns the union."""
+    union = keep.any(axis=0)
+    n_union = int(union.sum())
+    if n_union > capacity:
+        n = keep.shape[1]
+        prot = np.zeros(n, dtype=bool)
+        prot[:n_prefix] = True
+        if n_suffix > 0:
+            live = np.where(retained[:n])[0]
+            if len(live) >= n_suffix:
+                prot[live[-n_suffix:]] = True
+        cand = np.where(union & ~prot)[0]
+        if len(cand) > 0:
+            votes = keep[:, cand].sum(axis=0).astype(np.float64)
+            attn = signal[:, cand].sum(axis=0)
+            order = np.lexsort((attn, votes))
+            trim = cand[order[: min(n_union - capacity, len(cand))]]
+            union[trim] = False
+            keep[:, trim] = False
+    return union
+
+
+PER_HEAD_CLASSES = (AdaKVFaithfulPolicy, QUESTFaithfulPolicy)
+
+
+def per_head(policy: Any) -> bool:
+    """True for the per-KV-head (faithful / native) Ada-KV and QUEST policies."""
+    return isinstance(getattr(policy, "inner", policy), PER_HEAD_CLASSES)
+
+
 def host_selected(policy: Any) -> bool:
     """True when the (possibly wrapped) policy picks its victims on the host."""
-    return isinstance(getattr(policy, "inner", policy), RandomEvictionPolicy)
+    return isinstance(getattr(policy, "inner", policy), RandomEvictionPolicy) or per_head(policy)
 
 
 def policy_from_name(name: str, capacity: int) -> Any:
@@ -141,6 +296,10 @@ def policy_from_name(name: str, capacity: int) -> Any:
         "adakv": AdaKVPolicy,
         "quest": QUESTPolicy,
         "random": RandomEvictionPolicy,
+        "adakv_faithful": AdaKVFaithfulPolicy,
+        "adakv_native": AdaKVNativePolicy,
+        "quest_faithful": QUESTFaithfulPolicy,
+        "quest_native": QUESTNativePolicy,
     }
     if name == "streamingllm":
         return StreamingSinkLikePolicy(sink_size=4, recent_window_size=max(0, capacity - 4))
@@ -153,6 +312,10 @@ def kernel_policy_name(policy: Any, capacity: int) -> str:
     """Canonical kernel policy name of a (possibly wrapped) policy object."""
     inner = getattr(policy, "inner", policy)
     name = inner.name
+    if isinstance(inner, QUESTFaithfulPolicy):
+        return "quest"  # the device key of its global fallback call (policies.py:1467-1478)
+    if isinstance(inner, AdaKVFaithfulPolicy):
+        return "quest"  # never called globally: the cumulative signal always exists
     if name == "streaming_sink_like":
         if getattr(inner, "sink_size", 4) != 4 or getattr(inner, "recent_window_size", capacity - 4) != max(0, capacity - 4):
             raise ValueError("streamingllm on the GPU path uses sink_size=4, recent_window_size=capacity-4")

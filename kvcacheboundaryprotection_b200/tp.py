@@ -171,26 +171,17 @@ class SymmetricBuffer:
         dist.barrier(group=self.group)
 
 
-AR_MAX_TILES = 64  # N <= 8192 columns per fused-allreduce GEMM
-AR_MAX_SPLITS = 16
-AR_FLAG_SLOTS = AR_MAX_TILES * AR_MAX_SPLITS  # flag words per (parity, source rank)
-
-
-def allreduce_flag_word(world: int, parity: int, src_rank: int, tile: int, split: int) -> int:
-    """Index of the u32 flag that ``src_rank`` raises for (tile, split) of a call of this
-    parity, in every rank's symmetric buffer: the same for every split count and width."""
-    assert 0 <= tile < AR_MAX_TILES and 0 <= split < AR_MAX_SPLITS and 0 <= src_rank < world
-    return (parity * world + src_rank) * AR_FLAG_SLOTS + tile * AR_MAX_SPLITS + split
-
-
-def allreduce_recv_offset(world: int) -> int:
-    """Byte offset of the fp32 receive area [2][world][M][N] (after the flags)."""
-    return 2 * world * AR_FLAG_SLOTS * 4
+def allreduce_slot(world: int, M: int, N: int, parity: int, src_rank: int, row: int, col: int) -> int:
+    """Byte offset, in every rank's symmetric buffer, of the 16-byte slot {x, tag, y, tag}
+    that ``src_rank`` writes for (row, columns col & ~1, col | 1) in a call of this parity."""
+    assert 0 <= src_rank < world and 0 <= row < M and 0 <= col < N and parity in (0, 1)
+    return (((parity * world + src_rank) * M + row) * (N // 2) + col // 2) * 16
 
 
 def allreduce_buffer_bytes(world: int, M: int, N: int) -> int:
-    """Size of the symmetric buffer kvbp_decode_gemm_allreduce needs (include/kvbp.h)."""
-    return allreduce_recv_offset(world) + 2 * world * M * N * 4
+    """Size of the symmetric buffer kvbp_decode_gemm_allreduce needs (include/kvbp.h):
+    [2 parities][world source ranks][M][N / 2] slots of 16 bytes."""
+    return 2 * world * M * N * 8
 
 
 def allreduce_splits(cfg: ModelConfig, world: int) -> dict:

@@ -86,7 +86,7 @@ class Driver:
             if vict:
                 pos[0, : len(vict)] = torch.tensor(vict, dtype=torch.int32, device="cuda")
             cnt[0] = len(vict)
-        capi.check(self.L.kvbp_append_evict_listed(self.st, C.byref(self.state), C.byref(self.cfg), self.seq_step.data_ptr(), self.next_pos.data_ptr(), self.cur_pos.data_ptr(), self.write_slot.data_ptr(), self.tokens.data_ptr(), self.token_log.data_ptr(), self.max_new, self.evlog.data_ptr(), self.evcount.data_ptr(), self.evcap, self.retained_log.data_ptr(), pos.data_ptr(), cnt.data_ptr(), self.S, self.err.data_ptr()), "append_evict_listed")
+        capi.check(self.L.kvbp_append_evict_listed(self.st, C.byref(self.state), C.byref(self.cfg), self.seq_step.data_ptr(), self.next_pos.data_ptr(), self.cur_pos.data_ptr(), self.write_slot.data_ptr(), self.tokens.data_ptr(), self.token_log.data_ptr(), self.max_new, self.evlog.data_ptr(), self.evcount.data_ptr(), self.evcap, self.retained_log.data_ptr(), pos.data_ptr(), cnt.data_ptr(), self.S, 0, self.err.data_ptr()), "append_evict_listed")
 
     def append_evict(self):
         capi.check(self.L.kvbp_append_evict(self.st, C.byref(self.state), C.byref(self.cfg), self.seq_step.data_ptr(), self.next_pos.data_ptr(), self.cur_pos.data_ptr(), self.write_slot.data_ptr(), self.tokens.data_ptr(), self.token_log.data_ptr(), self.max_new, self.evlog.data_ptr(), self.evcount.data_ptr(), self.evcap, self.retained_log.data_ptr(), self.err.data_ptr()), "append_evict")
@@ -106,7 +106,12 @@ def _spec(case):
     return PolicySpec(case["policy"], case["capacity"], prot is not None, *(prot or (0.0, 0.0)))
 
 
-@pytest.mark.parametrize("case", CASES, ids=[c["name"] for c in CASES])
+PER_HEAD = ("adakv_faithful", "adakv_native", "quest_faithful", "quest_native")
+GLOBAL_CASES = [c for c in CASES if c["policy"] not in PER_HEAD]
+PER_HEAD_CASES = [c for c in CASES if c["policy"] in PER_HEAD]
+
+
+@pytest.mark.parametrize("case", GLOBAL_CASES, ids=[c["name"] for c in GLOBAL_CASES])
 def test_eviction_kernels_match_reference_trace(case):
     P, cap, E, max_new = case["n_prompt"], case["capacity"], case["evict_every"], case["max_new_tokens"]
     model = StubScoreModel(vocab=97, n_heads=4, n_kv_heads=2, n_layers=2, max_cache_len=P + max_new + 8, seed=case["seed"])
@@ -214,3 +219,68 @@ def test_random_policy_generator_end_to_end_matches_reference_trace():
     # the policy object's stream continues across calls, as in the reference
     res2 = gen.generate_with_kv_control(case["prompt"], case["max_new_tokens"])
     assert res2.positions_evicted != res.positions_evicted
+
+
+@pytest.mark.parametrize("case", PER_HEAD_CASES, ids=[c["name"] for c in PER_HEAD_CASES])
+def test_per_head_policies_match_reference_trace(case):
+    """Per-KV-head Ada-KV / QUEST through the engine's own per-head path: host selection
+    over the device's per-slot signals, listed victims freed on the device, per-head keep
+    masks written back -- with the oracle's per-step scores injected into step_score and
+    head_score, so victims, slot tables, calls and union statistics must be identical to
+    the reference generator's trace."""
+    from kvcacheboundaryprotection_b200.config import get_config
+    from kvcacheboundaryprotection_b200.engine import CappedKVEngine, EvictionSpec
+    from kvcacheboundaryprotection_b200.policies import policy_from_name
+    from kvcacheboundaryprotection_b200.weights import init_weights
+
+    P, cap, E, max_new = case["n_prompt"], case["capacity"], case["evict_every"], case["max_new_tokens"]
+    mk = lambda: StubScoreModel(vocab=97, n_heads=4, n_kv_heads=2, n_layers=2, max_cache_len=P + max_new + 8,  # noqa: E731
+                                seed=case["seed"])
+    o = generate(mk(), _spec(case), case["prompt"], max_new, evict_every=E, n_kv_heads=case["n_kv_heads"],
+                 regime=case["regime"])
+    assert o.positions_evicted == case["positions_evicted"]  # oracle == reference
+    pre = mk()(input_ids=case["prompt"], output_attentions=True, use_cache=True).attentions
+    layer0 = np.asarray(pre[0], np.float32).reshape(-1)[:P]
+    cfg = get_config("parity-qwen2").with_(n_layers=1, vocab=1024)
+    assert (cfg.n_heads, cfg.n_kv_heads) == (4, 2)
+    pol = policy_from_name(case["policy"], cap)
+    prot = case["protect"]
+    if prot:
+        pol = ProtectedPolicyWrapper(pol, *prot, cap)
+    spec = EvictionSpec("quest", cap, E, prot is not None, *(prot or (0.0, 0.0)), regime=case["regime"],
+                        protect_capacity=cap)
+    eng = CappedKVEngine(cfg, init_weights(cfg, seed=0), batch=1, evict=spec, max_prompt_len=P, max_new_tokens=max_new,
+                         host_policy=pol)
+    assert eng.per_head and eng.S == slot_count(cap, E, max_new, case["regime"])
+    eng.prefill_head_seed = torch.from_numpy(layer0).cuda()[None]
+    eng._select_and_compact(P, torch.from_numpy(o.meta.prefill[:P].copy()).cuda()[None])
+    eng.prompt_len = P
+    assert eng.slot_pos[0].cpu().numpy().tolist() == o.slot_tables[0].tolist()
+    heads = iter(o.step_head_scores)
+    for s in range(1, max_new + 1):
+        eng._append_evict()
+        assert eng.slot_pos[0].cpu().numpy().tolist() == o.slot_tables[s].tolist(), f"slot table after step {s}"
+        if s == max_new:
+            break
+        sp = eng.slot_pos[0].cpu().numpy()
+        ok = sp >= 0
+        sc = np.zeros(eng.S, np.float32)
+        sc[ok] = o.step_scores[s - 1][sp[ok]]
+        eng.step_score[0].copy_(torch.from_numpy(sc))
+        hs = next(heads)
+        hsc = np.zeros((2, eng.S), np.float32)
+        hsc[:, ok] = hs[:, sp[ok]]
+        eng.head_score[0].copy_(torch.from_numpy(hsc))
+        eng._sample_and_score()
+    torch.cuda.synchronize()
+    eng.check_device_errors()
+    n = int(eng.evcount[0].item())
+    assert eng.evlog[0, :n].cpu().numpy().tolist() == case["positions_evicted"]
+    assert [P] + eng.retained_log[0].cpu().numpy().tolist() == case["retained_counts_by_step"]
+    assert eng.head_call_steps == case["policy_call_steps"]
+    assert eng.union_stats == [case["faithful_union_retained_max"], case["faithful_union_overflow_max"],
+                               case["faithful_union_overflow_steps"]]
+    sp = eng.slot_pos[0].cpu().numpy()
+    ok = sp >= 0
+    keep = eng.head_keep[0].cpu().numpy()[:, ok].astype(bool)
+    assert (keep == o.head_keep[:, sp[ok]]).all()

@@ -91,28 +91,24 @@ def test_split_k_choices():
     assert allreduce_splits(cfg, 8) == {"o": 3, "down": 7}  # 3 or 4 query heads per rank
 
 
-def test_allreduce_flag_layout_is_independent_of_the_call():
+def test_allreduce_slots_are_independent_of_the_call():
     """The o and down fused-allreduce GEMMs share one symmetric buffer with different
-    split counts (7B at TP=8: 3 and 7).  Every (parity, source rank, tile, split) flag word
-    is distinct, all flags lie before the receive area, and the receive area's offset
-    depends on the world size only."""
-    from kvcacheboundaryprotection_b200.tp import (AR_MAX_SPLITS, AR_MAX_TILES, allreduce_buffer_bytes,
-                                                   allreduce_flag_word, allreduce_recv_offset, allreduce_splits)
+    split counts (7B at TP=8: 3 and 7).  Every (parity, source rank, row, column pair) has
+    its own 16-byte slot inside the buffer; o (even call index) and down (odd) never share
+    one, whatever their split counts, and the layout does not depend on the split count."""
+    from kvcacheboundaryprotection_b200.tp import allreduce_buffer_bytes, allreduce_slot, allreduce_splits
 
     cfg = get_config("qwen2.5-7b")
-    world = 8
+    world, M, N = 8, 16, cfg.hidden
     sp = allreduce_splits(cfg, world)
     assert sp["o"] != sp["down"]  # the case that used to overlap
-    tiles = cfg.hidden // 128
-    words = {}
-    for call, name in enumerate(("o", "down")):  # o = even call index, down = odd
+    size = allreduce_buffer_bytes(world, M, N)
+    seen = set()
+    for parity in (0, 1):
         for src in range(world):
-            for t in range(tiles):
-                for s in range(sp[name]):
-                    wd = allreduce_flag_word(world, call & 1, src, t, s)
-                    assert wd not in words, (name, src, t, s, words.get(wd))
-                    words[wd] = (name, src, t, s)
-    roff = allreduce_recv_offset(world)
-    assert max(words) * 4 + 4 <= roff and roff % 256 == 0
-    assert allreduce_flag_word(world, 1, world - 1, AR_MAX_TILES - 1, AR_MAX_SPLITS - 1) * 4 + 4 == roff
-    assert allreduce_buffer_bytes(world, 16, cfg.hidden) == roff + 2 * world * 16 * cfg.hidden * 4
+            offs = [allreduce_slot(world, M, N, parity, src, r, c) for r in range(M) for c in range(0, N, 2)]
+            assert len(set(offs)) == len(offs)
+            assert all(o % 16 == 0 and 0 <= o and o + 16 <= size for o in offs)
+            assert not (seen & set(offs))
+            seen |= set(offs)
+    assert len(seen) * 16 == size
