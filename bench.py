@@ -561,9 +561,13 @@ NCU_TRAFFIC = {
 # ------------------------------------------------------------------------ microbench
 def run_microbench(cap_list=(256, 1024, 4096), policies=("lru", "attention-mass"), fracs=(0.10, 0.05), iters=20):
     """Operator microbench: one fused decode attention + eviction step for 64 sequences,
-    8 kv heads x group 4, head_dim 128 (slot append + cadence eviction, K/V scatter,
-    attention + per-slot score, score update).  Each timed step is preceded by an L2
-    flush (a 512 MB read, which leaves no dirty lines behind) outside the CUDA-event pair."""
+    8 kv heads x group 4, head_dim 128.  The step is two launches: kvbp_append_evict (slot
+    append + cadence protection / top-k / hard cap) and kvbp_decode_attn_score_update
+    (scatter of the new K/V row into its slot, attention + per-slot score, and the score
+    update by the last CTA of each sequence); q and the new K/V rows are the operator's
+    inputs.  "unfused_step_us" times the same step as four launches (append, q/k RoPE +
+    K/V scatter, attention, score update).  Each timed step is preceded by an L2 flush (a
+    512 MB read, which leaves no dirty lines behind) outside the CUDA-event pair."""
     import ctypes as C_
 
     import torch
@@ -595,6 +599,15 @@ def run_microbench(cap_list=(256, 1024, 4096), policies=("lru", "attention-mass"
                 attn_out = torch.empty_like(q)
                 inv = torch.from_numpy(inv_freq_table(D, 1e6)).to(dev)
                 err = torch.zeros(1, dtype=torch.int32, device=dev)
+                qf = (torch.randn(B, Hq, D, generator=g, device=dev) / math.sqrt(D)).to(torch.bfloat16)
+                knew = torch.randn(B, Hkv, D, generator=g, device=dev).to(torch.bfloat16)
+                vnew = torch.randn(B, Hkv, D, generator=g, device=dev).to(torch.bfloat16)
+                counter = torch.zeros(B, dtype=torch.int32, device=dev)
+
+                def fused_step():
+                    s = torch.cuda.current_stream().cuda_stream
+                    check(L.kvbp_append_evict(s, C_.byref(st["state"]), C_.byref(cfg), st["seq_step"].data_ptr(), st["next_pos"].data_ptr(), st["cur_pos"].data_ptr(), st["write_slot"].data_ptr(), None, None, 0, st["evlog"].data_ptr(), st["evcount"].data_ptr(), st["evcap"], None, err.data_ptr()), "append")
+                    check(L.kvbp_decode_attn_score_update(s, B, Hq, Hkv, D, S, qf.data_ptr(), knew.data_ptr(), vnew.data_ptr(), kc.data_ptr(), vc.data_ptr(), st["slot_pos"].data_ptr(), st["write_slot"].data_ptr(), attn_out.data_ptr(), st["step_score"].data_ptr(), C_.byref(st["state"]), st["seq_step"].data_ptr(), counter.data_ptr(), err.data_ptr()), "attn_update")
 
                 def step(ev=None):
                     s = torch.cuda.current_stream().cuda_stream
@@ -609,25 +622,36 @@ def run_microbench(cap_list=(256, 1024, 4096), policies=("lru", "attention-mass"
                     check(L.kvbp_score_update(s, C_.byref(st["state"]), st["seq_step"].data_ptr(), st["step_score"].data_ptr(), err.data_ptr()), "score")
                     mark(4)
 
-                for _ in range(3):
-                    step()
-                gr = torch.cuda.CUDAGraph()
-                side = torch.cuda.Stream()
-                side.wait_stream(torch.cuda.current_stream())
-                with torch.cuda.stream(side):
-                    with torch.cuda.graph(gr, stream=side):
-                        step()
-                torch.cuda.current_stream().wait_stream(side)
-                tot = 0.0
+                def graph_of(fn):
+                    for _ in range(3):
+                        fn()
+                    gr_ = torch.cuda.CUDAGraph()
+                    side = torch.cuda.Stream()
+                    side.wait_stream(torch.cuda.current_stream())
+                    with torch.cuda.stream(side):
+                        with torch.cuda.graph(gr_, stream=side):
+                            fn()
+                    torch.cuda.current_stream().wait_stream(side)
+                    return gr_
+
+                def timed_replays(gr_):
+                    t = 0.0
+                    for it in range(iters):
+                        flush.sum()
+                        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                        e0.record()
+                        gr_.replay()
+                        e1.record()
+                        torch.cuda.synchronize()
+                        t += e0.elapsed_time(e1)
+                    return t
+
+                gr = graph_of(fused_step)
+                tot = timed_replays(gr)
+                del gr
+                gr = graph_of(step)
+                tot_unfused = timed_replays(gr)
                 attn_only = 0.0
-                for it in range(iters):
-                    flush.sum()
-                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                    e0.record()
-                    gr.replay()
-                    e1.record()
-                    torch.cuda.synchronize()
-                    tot += e0.elapsed_time(e1)
                 # attention kernel alone (same L2 discipline)
                 s_ = torch.cuda.current_stream().cuda_stream
                 for it in range(iters):
@@ -651,6 +675,7 @@ def run_microbench(cap_list=(256, 1024, 4096), policies=("lru", "attention-mass"
                 if int(err.item()):
                     raise RuntimeError("device error in microbench: " + str(capi.decode_dev_errors(int(err.item()))))
                 us = tot / iters * 1000
+                us_unfused = tot_unfused / iters * 1000
                 valid = C + E / 2
                 byts = micro_bytes(B, Hq, Hkv, valid, E)
                 ab = algorithmic_attn_bytes(B, Hq, Hkv, valid)
@@ -663,6 +688,9 @@ def run_microbench(cap_list=(256, 1024, 4096), policies=("lru", "attention-mass"
                         "step_us": round(us, 2),
                         "step_gbs": round(byts / (us * 1e-6) / 1e9, 1),
                         "step_frac": round(byts / (us * 1e-6) / 1e9 / hbm, 4),
+                        "launches": 2,
+                        "unfused_step_us": round(us_unfused, 2),
+                        "unfused_step_frac": round(byts / (us_unfused * 1e-6) / 1e9 / hbm, 4),
                         "attn_us": round(aus, 2),
                         "attn_gbs": round(ab / (aus * 1e-6) / 1e9, 1),
                         "attn_frac": round(ab / (aus * 1e-6) / 1e9 / hbm, 4),

@@ -111,6 +111,23 @@ int kvbp_decode_attn_score(kvbp_stream_t stream, int32_t B, int32_t Hq, int32_t 
                            const void* q, const void* kcache, const void* vcache, const int32_t* slot_pos,
                            const int32_t* write_slot, void* out, float* step_score, int32_t* dev_err);
 
+/* K4 + K1 + K2 fused -- one layer's decode attention that also scatters this step's new
+ * K/V row and, as the last kernel of the step to touch the scores, runs the per-step score
+ * update (kv_coupled_generator.py:504-516).  As kvbp_decode_attn_score, and:
+ *  - k_new / v_new [B][Hkv][128] bf16 (16-byte aligned; both NULL = the row is already in
+ *    the cache): stored into slot write_slot[b] (< 0: not stored) and used in place of the
+ *    cache row in this call (jax_inference.py:1011-1012);
+ *  - st, seq_step: the score update's state; the last CTA to finish each sequence updates
+ *    attn / max_attn / cumul / last_access / access_count of its valid slots from the
+ *    completed step_score (pass the layer that completes the max over layers: the last)
+ *    and clears step_score, as kvbp_score_update does;
+ *  - seq_counter [B] int32, all zero before the first call; the kernel leaves it zero. */
+int kvbp_decode_attn_score_update(kvbp_stream_t stream, int32_t B, int32_t Hq, int32_t Hkv, int32_t head_dim,
+                                  int32_t S, const void* q, const void* k_new, const void* v_new, void* kcache,
+                                  void* vcache, const int32_t* slot_pos, const int32_t* write_slot, void* out,
+                                  float* step_score, const kvbp_state* st, const int32_t* seq_step,
+                                  int32_t* seq_counter, int32_t* dev_err);
+
 /* K5 -- causal prefill attention of one sequence and layer on the tcgen05 tensor cores,
  * with the per-key score.  q [P][Hq][128] bf16 (after RoPE), kcache/vcache
  * [Hkv][P][128] bf16 (16-byte aligned), out [P][Hq][128] bf16 = the attention output

@@ -96,6 +96,10 @@ SIGNATURES = {
         [P, C.POINTER(State), C.POINTER(EvictCfg), P, P, P, P, P, P, I32, P, P, I32, P, P, P, I32, I32, P],
     ),
     "kvbp_decode_attn_score_heads": (C.c_int, [P, I32, I32, I32, I32, I32, P, P, P, P, P, P, P, P, P, P]),
+    "kvbp_decode_attn_score_update": (
+        C.c_int,
+        [P, I32, I32, I32, I32, I32, P, P, P, P, P, P, P, P, P, C.POINTER(State), P, P, P],
+    ),
     "kvbp_head_signal_update": (C.c_int, [P, I32, I32, I32, P, P, P, P, P]),
     "kvbp_prefill_select": (C.c_int, [P, I32, I32, C.POINTER(EvictCfg), P, P, P, I32, C.POINTER(C.c_int32), P]),
     "kvbp_prefill_compact": (

@@ -96,6 +96,17 @@ struct AttnArgs {
   // max over calls of query head r's probability for r < Hkv (null: not kept)
   const uint8_t* head_keep;
   float* head_score;
+  // fused scatter: this step's K/V row [B][Hkv][128] (null: already in the cache)
+  const __nv_bfloat16* knew;
+  const __nv_bfloat16* vnew;
+  // fused score update (null upd_last: none): the last CTA to finish a sequence runs K2
+  float* upd_attn;
+  float* upd_maxa;
+  double* upd_cumul;
+  int* upd_last;
+  int* upd_cnt;
+  const int* seq_step;
+  int* seq_counter;  // [B], zero between launches
   int* err;
   int B, Hq, Hkv, S;
   int tiles;       // ceil(S / 64)
@@ -261,15 +272,23 @@ __global__ void __launch_bounds__(attn_threads(GR), kMinBlocks) decode_attn_scor
       ok_tile = false;
     }
     ok_tile = __all_sync(0xffffffffu, ok_tile);  // warp-uniform: the tile's mma/ldmatrix are warp-wide
-    if (ok_tile && u < n_first && wslot >= 0 && wslot < S) {
-      // a tile staged before the wait may hold a stale copy of this step's row: the warp
-      // that owns the row (rows r0..r0+15 of the tile) reloads it, K by lanes 0-15 and V by
-      // lanes 16-31, one 16-byte chunk each, at the 128-byte-swizzled position
+    if (ok_tile && (u < n_first || p.knew) && wslot >= 0 && wslot < S) {
+      // a tile staged before the wait may hold a stale copy of this step's row (and with a
+      // fused scatter every tile may): the warp that owns the row (rows r0..r0+15 of the
+      // tile) writes it into the staged tile, K by lanes 0-15 and V by lanes 16-31, one
+      // 16-byte chunk each, at the 128-byte-swizzled position -- from the cache, or from
+      // knew/vnew, which it also stores into the cache for the next steps
       const int lr = wslot - (t0 + u) * kTile;
       if (lr >= r0 && lr < r0 + 16) {
         const int half = lane >> 4, ch = lane & 15, box = ch >> 3, c = ch & 7;
-        const __nv_bfloat16* src = (half ? p.vc : p.kc) + (static_cast<size_t>(pair) * S + wslot) * kD + ch * 8;
-        const uint4 v = __ldcg(reinterpret_cast<const uint4*>(src));
+        __nv_bfloat16* crow = const_cast<__nv_bfloat16*>(half ? p.vc : p.kc) + (static_cast<size_t>(pair) * S + wslot) * kD + ch * 8;
+        uint4 v;
+        if (p.knew) {
+          v = __ldg(reinterpret_cast<const uint4*>((half ? p.vnew : p.knew) + static_cast<size_t>(pair) * kD + ch * 8));
+          *reinterpret_cast<uint4*>(crow) = v;
+        } else {
+          v = __ldcg(reinterpret_cast<const uint4*>(crow));
+        }
         uint8_t* dst = ring + st * kStageBytes + half * kHalfBytes + box * kBoxBytes + lr * 128 + ((c ^ (lr & 7)) << 4);
         *reinterpret_cast<uint4*>(dst) = v;
         fence_proxy_async_smem();  // the stage is refilled by TMA later
@@ -503,6 +522,47 @@ __global__ void __launch_bounds__(attn_threads(GR), kMinBlocks) decode_attn_scor
       atomicMax(reinterpret_cast<int*>(&sscore[t0 * kTile + i]), __float_as_int(mx));
     }
   }
+  if (p.upd_last) {
+    // fused score update (kv_coupled_generator.py:504-516): the last of the sequence's
+    // CTAs (every kv head, every cluster rank) to finish updates all of its slots
+    __threadfence();  // this CTA's score maxima are visible before it counts itself
+    named_bar(1, kConsumers);
+    int* last_flag = flags + 2;
+    if (tid == 0) *last_flag = atomicAdd(&p.seq_counter[b], 1) == static_cast<int>(gridDim.x * gridDim.y) - 1;
+    named_bar(1, kConsumers);
+    if (*last_flag) {
+      __threadfence();
+      const float* sc_all = p.step_score + static_cast<size_t>(b) * S;
+      float mx = 0.f;
+      for (int i = tid; i < S; i += kConsumers)
+        if (spos_g[i] >= 0) mx = fmaxf(mx, __ldcg(&sc_all[i]));
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      if (lane == 0) escr[warp] = mx;
+      named_bar(1, kConsumers);
+      float gmx = 0.f;
+      for (int w = 0; w < kConsumerWarps; ++w) gmx = fmaxf(gmx, escr[w]);
+      const float thr = static_cast<float>(0.05 * static_cast<double>(gmx));
+      const int step = p.seq_step[b];
+      const size_t o0 = static_cast<size_t>(b) * S;
+      float* scw = p.step_score + o0;
+      for (int i = tid; i < S; i += kConsumers) {
+        const float ks = __ldcg(&scw[i]);
+        if (spos_g[i] >= 0) {
+          if (ks != ks) set_err(p.err, kErrNanScore);
+          p.upd_attn[o0 + i] = ks;
+          p.upd_maxa[o0 + i] = fmaxf(p.upd_maxa[o0 + i], ks);
+          p.upd_cumul[o0 + i] = __dadd_rn(p.upd_cumul[o0 + i], static_cast<double>(ks));
+          if (ks > thr) {
+            p.upd_last[o0 + i] = step;
+            p.upd_cnt[o0 + i] += 1;
+          }
+        }
+        scw[i] = 0.f;
+      }
+      if (tid == 0) p.seq_counter[b] = 0;
+    }
+  }
   __syncwarp();
   cluster_sync_all();  // no CTA leaves while a peer may still target its shared memory
 }
@@ -574,7 +634,7 @@ static cudaError_t launch_g(cudaStream_t stream, const CUtensorMap& km, const CU
 
 int decode_attn_score(cudaStream_t stream, int B, int Hq, int Hkv, int D, int S, const void* q, const void* kcache,
                       const void* vcache, const int* slot_pos, const int* write_slot, void* out, float* step_score,
-                      int* err, int cluster_override, const uint8_t* head_keep, float* head_score) {
+                      int* err, int cluster_override, const AttnExtra& x) {
   if (!q || !kcache || !vcache || !slot_pos || !out || !step_score)
     return fail(kStatusArg, "decode_attn_score: null pointer");
   if (D != kD) return fail(kStatusUnsupported, "decode_attn_score: head_dim %d unsupported (only 128)", D);
@@ -618,8 +678,23 @@ int decode_attn_score(cudaStream_t stream, int B, int Hq, int Hkv, int D, int S,
   a.write_slot = write_slot;
   a.out = static_cast<__nv_bfloat16*>(out);
   a.step_score = step_score;
-  a.head_keep = head_keep;
-  a.head_score = head_score;
+  a.head_keep = x.head_keep;
+  a.head_score = x.head_score;
+  a.knew = static_cast<const __nv_bfloat16*>(x.knew);
+  a.vnew = static_cast<const __nv_bfloat16*>(x.vnew);
+  a.upd_attn = x.upd_attn;
+  a.upd_maxa = x.upd_maxa;
+  a.upd_cumul = x.upd_cumul;
+  a.upd_last = x.upd_last;
+  a.upd_cnt = x.upd_cnt;
+  a.seq_step = x.seq_step;
+  a.seq_counter = x.seq_counter;
+  if ((a.knew || a.vnew) && !(a.knew && a.vnew && write_slot))
+    return fail(kStatusArg, "decode_attn_score: k_new and v_new need each other and write_slot");
+  if (a.knew && ((reinterpret_cast<uintptr_t>(a.knew) | reinterpret_cast<uintptr_t>(a.vnew)) & 15))
+    return fail(kStatusArg, "decode_attn_score: k_new / v_new must be 16-byte aligned");
+  if (a.upd_last && !(a.upd_attn && a.upd_maxa && a.upd_cumul && a.upd_cnt && a.seq_step && a.seq_counter))
+    return fail(kStatusArg, "decode_attn_score: the fused score update needs every state array");
   a.err = err;
   a.B = B;
   a.Hq = Hq;
@@ -667,7 +742,31 @@ extern "C" int kvbp_decode_attn_score(kvbp_stream_t stream, int32_t B, int32_t H
                                       const int32_t* slot_pos, const int32_t* write_slot, void* out,
                                       float* step_score, int32_t* dev_err) {
   return kvbp::decode_attn_score(reinterpret_cast<cudaStream_t>(stream), B, Hq, Hkv, head_dim, S, q, kcache, vcache,
-                                 slot_pos, write_slot, out, step_score, dev_err, 0, nullptr, nullptr);
+                                 slot_pos, write_slot, out, step_score, dev_err, 0, kvbp::AttnExtra{});
+}
+
+extern "C" int kvbp_decode_attn_score_update(kvbp_stream_t stream, int32_t B, int32_t Hq, int32_t Hkv,
+                                             int32_t head_dim, int32_t S, const void* q, const void* k_new,
+                                             const void* v_new, void* kcache, void* vcache,
+                                             const int32_t* slot_pos, const int32_t* write_slot, void* out,
+                                             float* step_score, const kvbp_state* st, const int32_t* seq_step,
+                                             int32_t* seq_counter, int32_t* dev_err) {
+  if (!st || !seq_step || !seq_counter)
+    return kvbp::fail(kvbp::kStatusArg, "decode_attn_score_update: state, seq_step and seq_counter are required");
+  if (st->B != B || st->S != S || st->slot_pos != slot_pos)
+    return kvbp::fail(kvbp::kStatusArg, "decode_attn_score_update: state does not match B / S / slot_pos");
+  kvbp::AttnExtra x;
+  x.knew = k_new;
+  x.vnew = v_new;
+  x.upd_attn = st->attn;
+  x.upd_maxa = st->max_attn;
+  x.upd_cumul = st->cumul;
+  x.upd_last = st->last_access;
+  x.upd_cnt = st->access_count;
+  x.seq_step = seq_step;
+  x.seq_counter = seq_counter;
+  return kvbp::decode_attn_score(reinterpret_cast<cudaStream_t>(stream), B, Hq, Hkv, head_dim, S, q, kcache, vcache,
+                                 slot_pos, write_slot, out, step_score, dev_err, 0, x);
 }
 
 extern "C" int kvbp_decode_attn_score_heads(kvbp_stream_t stream, int32_t B, int32_t Hq, int32_t Hkv,
@@ -677,8 +776,11 @@ extern "C" int kvbp_decode_attn_score_heads(kvbp_stream_t stream, int32_t B, int
                                             float* head_score, int32_t* dev_err) {
   if (!head_keep || !head_score)
     return kvbp::fail(kvbp::kStatusArg, "decode_attn_score_heads: head_keep and head_score are required");
+  kvbp::AttnExtra x;
+  x.head_keep = head_keep;
+  x.head_score = head_score;
   return kvbp::decode_attn_score(reinterpret_cast<cudaStream_t>(stream), B, Hq, Hkv, head_dim, S, q, kcache, vcache,
-                                 slot_pos, write_slot, out, step_score, dev_err, 0, head_keep, head_score);
+                                 slot_pos, write_slot, out, step_score, dev_err, 0, x);
 }
 
 // Same as kvbp_decode_attn_score with an explicit cluster size (CTAs per sequence and
@@ -688,5 +790,5 @@ extern "C" int kvbp_decode_attn_score_cs(kvbp_stream_t stream, int32_t B, int32_
                                          const int32_t* slot_pos, const int32_t* write_slot, void* out,
                                          float* step_score, int32_t* dev_err, int32_t cluster) {
   return kvbp::decode_attn_score(reinterpret_cast<cudaStream_t>(stream), B, Hq, Hkv, head_dim, S, q, kcache, vcache,
-                                 slot_pos, write_slot, out, step_score, dev_err, cluster, nullptr, nullptr);
+                                 slot_pos, write_slot, out, step_score, dev_err, cluster, kvbp::AttnExtra{});
 }

@@ -48,9 +48,23 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
+// Optional parts of the decode attention launch (all null: attention + per-slot score).
+struct AttnExtra {
+  const uint8_t* head_keep = nullptr;  // per-KV-head retention [B][Hkv][S]
+  float* head_score = nullptr;         // per-head signal rows [B][Hkv][S]
+  const void* knew = nullptr;          // fused scatter of this step's K/V row [B][Hkv][128]
+  const void* vnew = nullptr;
+  float* upd_attn = nullptr;           // fused score update: the kvbp_state arrays
+  float* upd_maxa = nullptr;
+  double* upd_cumul = nullptr;
+  int* upd_last = nullptr;
+  int* upd_cnt = nullptr;
+  const int* seq_step = nullptr;
+  int* seq_counter = nullptr;
+};
 int decode_attn_score(cudaStream_t stream, int B, int Hq, int Hkv, int D, int S, const void* q, const void* kcache,
                       const void* vcache, const int* slot_pos, const int* write_slot, void* out, float* step_score,
-                      int* err, int cluster_override, const uint8_t* head_keep, float* head_score);
+                      int* err, int cluster_override, const AttnExtra& extra);
 
 int head_signal_update(cudaStream_t stream, int B, int Hkv, int S, const int* write_slot, float* head_score,
                        double* head_cumul, float* head_current, int* err);

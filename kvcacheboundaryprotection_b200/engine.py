@@ -283,6 +283,7 @@ class CappedKVEngine:
         self.prefill_s = z(B, S, dt=f32)
         self.posmap = z(B, self.W, dt=torch.int32)
         self.step_score = z(B, S, dt=f32)
+        self.seq_counter = z(B)  # arrivals per sequence of the fused score update (zero between launches)
         self.seq_step = z(B)
         self.next_pos = z(B)
         self.cur_pos = z(B)
@@ -731,8 +732,24 @@ class CappedKVEngine:
             ss_in, n_in = self.ss_a, nt_h
         self._gemm("lm", 0, c.vocab, H, self.lm_w, self.h, H, self.logits, c.vocab, self.final_norm, ss_in, n_in)
 
+    @property
+    def fused_score_update(self) -> bool:
+        """The last layer's attention runs the per-step score update (no separate launch)."""
+        return not self.per_head and type(self) is CappedKVEngine
+
     def _attention(self, li: int) -> None:
         c, L = self.cfg, lib()
+        if li == c.n_layers - 1 and self.fused_score_update:
+            check(
+                L.kvbp_decode_attn_score_update(
+                    self.stream, self.B, c.n_heads, c.n_kv_heads, c.head_dim, self.S, _ptr(self.q), None, None,
+                    _ptr(self.kc[li]), _ptr(self.vc[li]), _ptr(self.slot_pos), _ptr(self.write_slot),
+                    _ptr(self.attn_out), _ptr(self.step_score), capi.C.byref(self._state), _ptr(self.seq_step),
+                    _ptr(self.seq_counter), _ptr(self.dev_err),
+                ),
+                "decode_attn_score_update",
+            )
+            return
         if self.per_head:
             check(
                 L.kvbp_decode_attn_score_heads(
@@ -782,7 +799,8 @@ class CappedKVEngine:
     def _sample_and_score(self) -> None:
         L, st, c = lib(), self.stream, self.cfg
         check(L.kvbp_argmax(st, self.B, c.vocab, c.vocab, _ptr(self.logits), _ptr(self.tokens)), "argmax")
-        check(L.kvbp_score_update(st, capi.C.byref(self._state), _ptr(self.seq_step), _ptr(self.step_score), _ptr(self.dev_err)), "score_update")
+        if not self.fused_score_update:
+            check(L.kvbp_score_update(st, capi.C.byref(self._state), _ptr(self.seq_step), _ptr(self.step_score), _ptr(self.dev_err)), "score_update")
         self._head_signal_update()
 
     def _head_signal_update(self) -> None:
@@ -800,7 +818,8 @@ class CappedKVEngine:
             if sample:
                 self._sample_and_score()
             else:
-                check(lib().kvbp_score_update(self.stream, capi.C.byref(self._state), _ptr(self.seq_step), _ptr(self.step_score), _ptr(self.dev_err)), "score_update")
+                if not self.fused_score_update:
+                    check(lib().kvbp_score_update(self.stream, capi.C.byref(self._state), _ptr(self.seq_step), _ptr(self.step_score), _ptr(self.dev_err)), "score_update")
                 self._head_signal_update()
 
     def capture(self) -> None:

@@ -183,3 +183,74 @@ def test_early_streaming_with_write_slot_matches_plain(cluster):
     # and the written rows really are part of the attention (the reference agrees)
     ref_out, ref_score = torch_reference(q, outs[1][2], vc_i, slot_pos)
     assert (outs[0][0].float() - ref_out).abs().max().item() <= 1.6e-2
+
+
+def _state(B, S, pos, seed):
+    """kvbp_state arrays with seeded metadata for the score update."""
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    d = "cuda"
+    st = {
+        "slot_pos": pos.clone(),
+        "insert_step": torch.randint(0, 5, (B, S), generator=g, device=d, dtype=torch.int32),
+        "last_access": torch.randint(0, 9, (B, S), generator=g, device=d, dtype=torch.int32),
+        "access_count": torch.randint(1, 9, (B, S), generator=g, device=d, dtype=torch.int32),
+        "attn": torch.rand(B, S, generator=g, device=d),
+        "max_attn": torch.rand(B, S, generator=g, device=d),
+        "cumul": torch.rand(B, S, generator=g, device=d, dtype=torch.float64) * 3,
+        "prefill": torch.rand(B, S, generator=g, device=d),
+        "posmap": torch.zeros(B, 64, dtype=torch.int32, device=d),
+    }
+    s = capi.State(B, S, 64, *[st[k].data_ptr() for k in ("slot_pos", "insert_step", "last_access", "access_count",
+                                                        "attn", "max_attn", "cumul", "prefill", "posmap")])
+    return st, s
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,S", [(64, 32, 8, 264), (16, 28, 4, 1032), (3, 8, 2, 4104)])
+def test_fused_scatter_and_score_update_equal_separate_launches(B, Hq, Hkv, S):
+    """kvbp_decode_attn_score_update (new K/V row stored by the attention kernel, score
+    update by the last CTA of each sequence) gives bit for bit the state of the separate
+    launches: the row copied into the cache, kvbp_decode_attn_score, kvbp_score_update --
+    on two calls in a row (the per-sequence arrival counters reset themselves)."""
+    import ctypes as C
+
+    L = capi.lib()
+    stream = torch.cuda.current_stream().cuda_stream
+    q, kc, vc, pos = make_case(B, Hq, Hkv, S, 0.2, seed=S)
+    g = torch.Generator(device="cuda").manual_seed(7)
+    knew = torch.randn(B, Hkv, 128, generator=g, device="cuda").to(torch.bfloat16)
+    vnew = torch.randn(B, Hkv, 128, generator=g, device="cuda").to(torch.bfloat16)
+    ws = torch.randint(0, S, (B,), generator=g, device="cuda", dtype=torch.int32)
+    ws[0] = -1  # a sequence whose new position was evicted before its forward
+    pos[torch.arange(B, device="cuda")[1:], ws[1:].long()] = 10 ** 6  # the written slots hold the new position
+    seq_step = torch.full((B,), 9, dtype=torch.int32, device="cuda")
+    kc_a, vc_a, kc_b, vc_b = kc.clone(), vc.clone(), kc.clone(), vc.clone()
+    sa, state_a = _state(B, S, pos, 1)
+    sb, state_b = _state(B, S, pos, 1)
+    counter = torch.zeros(B, dtype=torch.int32, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    for rep in range(2):
+        out_a, out_b = torch.empty_like(q), torch.empty_like(q)
+        sc_a = torch.zeros(B, S, device="cuda")
+        sc_b = torch.zeros(B, S, device="cuda")
+        for b in range(1, B):  # separate: the scatter, attention, score update
+            kc_a[b, :, ws[b]] = knew[b]
+            vc_a[b, :, ws[b]] = vnew[b]
+        capi.check(L.kvbp_decode_attn_score(stream, B, Hq, Hkv, 128, S, q.data_ptr(), kc_a.data_ptr(), vc_a.data_ptr(),
+                                            pos.data_ptr(), ws.data_ptr(), out_a.data_ptr(), sc_a.data_ptr(),
+                                            err.data_ptr()), "attn")
+        capi.check(L.kvbp_score_update(stream, C.byref(state_a), seq_step.data_ptr(), sc_a.data_ptr(), err.data_ptr()),
+                   "score_update")
+        capi.check(L.kvbp_decode_attn_score_update(stream, B, Hq, Hkv, 128, S, q.data_ptr(), knew.data_ptr(),
+                                                   vnew.data_ptr(), kc_b.data_ptr(), vc_b.data_ptr(), pos.data_ptr(),
+                                                   ws.data_ptr(), out_b.data_ptr(), sc_b.data_ptr(), C.byref(state_b),
+                                                   seq_step.data_ptr(), counter.data_ptr(), err.data_ptr()), "fused")
+        torch.cuda.synchronize()
+        assert int(err.item()) == 0, capi.decode_dev_errors(int(err.item()))
+        assert torch.equal(out_a, out_b)
+        assert torch.equal(kc_a, kc_b) and torch.equal(vc_a, vc_b)
+        for k in ("attn", "max_attn", "cumul", "last_access", "access_count"):
+            assert torch.equal(sa[k], sb[k]), k
+        assert not sc_b.any() and not sc_a.any()
+        assert not counter.any()
+        knew, vnew = vnew, knew  # second call: other rows
+        seq_step += 1
