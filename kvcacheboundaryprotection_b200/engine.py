@@ -338,13 +338,23 @@ class CappedKVEngine:
 
     @staticmethod
     def _pick_splits(N: int, K: int, sms: int = 148) -> int:
-        """Split K so that the grid holds about 256 CTAs (N / 128 column tiles per split,
-        at most 8 CTAs per cluster): measured best on B200 for the 7B decode shapes
-        (q/k/v 7, o and down 8, gate/up and lm_head 1; q/k/v at 8 and o at 9 or 10 were
-        slower, o and down at 8 faster than at 7)."""
+        """Split-K factor (CTAs per 128-column tile, one thread-block cluster) of a decode
+        GEMM with N / 128 column tiles and K / 128 k-blocks, from a burst sweep of every
+        per-rank shape of the 7B and Qwen3-4B decoders at 1, 2, 4 and 8 GPUs on B200:
+        * >= 2 tiles per SM: no split (the grid already fills two CTAs per SM);
+        * >= ~2/3 tile per SM: the split whose whole waves of 2 CTAs per SM carry the most
+          work per wave -- a grid a few CTAs past a whole wave leaves them as a slow tail
+          (149 tiles: 3 splits, not 2);
+        * fewer tiles: about 210 CTAs in all, at most 16 per cluster."""
         tiles = max(1, N // 128)
-        want = (256 * sms // 148) // tiles
-        return max(1, min(want, K // 128, 8))
+        kc = max(1, K // 128)
+        slots = 2 * sms
+        if tiles >= slots:
+            return 1
+        if tiles * 3 >= slots:
+            cands = range(1, min(4, kc) + 1)
+            return min(cands, key=lambda s: (math.ceil(tiles * s / slots) / s, s))
+        return max(1, min(round(210 * sms / 148 / tiles), 16, kc))
 
     @property
     def stream(self) -> int:

@@ -184,16 +184,13 @@ def allreduce_buffer_bytes(world: int, M: int, N: int) -> int:
     return 2 * world * M * N * 8
 
 
-def allreduce_splits(cfg: ModelConfig, world: int) -> dict:
-    """Split-K factors of the row-parallel o and down GEMMs under tensor parallelism.  The
-    fused allreduce pairs the same (tile, row slice) on every rank, so every rank uses one
-    split count (their K differs when the shards are uneven): the smallest of the ranks'
-    single-GPU choices, and at most 7 -- every split adds a row slice of flags and peer
-    stores to the allreduce (7B at TP=2: 4725 tok/s with 7, 4476 with 8)."""
-    k_of = {"o": lambda p: len(p.q_heads) * cfg.head_dim, "down": lambda p: p.ffn_hi - p.ffn_lo}
-    return {name: min(min(CappedKVEngine._pick_splits(cfg.hidden, k(tp_plan(cfg, world, r))), 7)
-                      for r in range(world))
-            for name, k in k_of.items()}
+def allreduce_splits(cfg: ModelConfig, world: int, rank: int = 0) -> dict:
+    """Split-K factors of this rank's row-parallel o and down GEMMs under tensor
+    parallelism: the single-GPU rule on the rank's own K.  The fused allreduce pairs
+    values by (source rank, row, column) only, so the ranks need not agree on them."""
+    p = tp_plan(cfg, world, rank)
+    return {"o": CappedKVEngine._pick_splits(cfg.hidden, len(p.q_heads) * cfg.head_dim),
+            "down": CappedKVEngine._pick_splits(cfg.hidden, p.ffn_hi - p.ffn_lo)}
 
 
 class TPEngine(CappedKVEngine):
@@ -218,7 +215,7 @@ class TPEngine(CappedKVEngine):
         super().__init__(lcfg, weights, **kw)
         self.part = torch.zeros(self.B, cfg.hidden, dtype=torch.float32, device=self.dev)
         self.keys = torch.zeros(self.B, dtype=torch.int64, device=self.dev)
-        self.splits.update(allreduce_splits(cfg, plan.world))
+        self.splits.update(allreduce_splits(cfg, plan.world, plan.rank))
         self.symm = None
         if fused_allreduce and plan.world > 1:
             self.symm = SymmetricBuffer(allreduce_buffer_bytes(plan.world, self.B, cfg.hidden), self.dev)

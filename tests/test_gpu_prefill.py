@@ -57,7 +57,8 @@ def _run(q, k, v, colmax):
     return out
 
 
-@pytest.mark.parametrize("P,Hq,Hkv", [(1, 4, 2), (100, 4, 1), (128, 7, 1), (300, 8, 2), (640, 28, 4)])
+@pytest.mark.parametrize("P,Hq,Hkv", [(1, 4, 2), (100, 4, 1), (128, 7, 1), (300, 8, 2), (640, 28, 4), (1024, 8, 2),
+                                      (4096, 28, 4), (8192, 8, 1)])
 def test_prefill_attention_matches_torch(P, Hq, Hkv):
     g = torch.Generator(device="cuda").manual_seed(P + Hq)
     q = torch.randn(P, Hq, 128, generator=g, device="cuda").to(torch.bfloat16)

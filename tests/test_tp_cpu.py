@@ -76,19 +76,22 @@ def test_sharded_projections_sum_to_the_full_ones(world):
 
 
 def test_split_k_choices():
-    # single GPU: about 256 CTAs per GEMM, at most 8 per cluster
+    """The split rule reproduces the burst sweep's best (or within a few %) choices."""
     from kvcacheboundaryprotection_b200.engine import CappedKVEngine
 
     cfg = get_config("qwen2.5-7b")
     H, F, V = cfg.hidden, cfg.ffn, cfg.vocab
     qkv_n = (cfg.n_heads + 2 * cfg.n_kv_heads) * cfg.head_dim
     pick = CappedKVEngine._pick_splits
-    assert [pick(qkv_n, H), pick(H, H), pick(2 * F, H), pick(H, F), pick(V, H)] == [7, 8, 1, 8, 1]
-    # tensor parallel: one count for every rank, at most 7 (fused allreduce)
+    assert [pick(qkv_n, H), pick(H, H), pick(2 * F, H), pick(H, F), pick(V, H)] == [6, 8, 1, 8, 1]
+    assert pick(128 * 148, H) == 2       # 148 tiles: exactly two CTAs per SM
+    assert pick(128 * 149, H) == 3       # 149 tiles: 2 splits would leave a 2-CTA tail
+    assert pick(768, H) == 16            # 6 tiles (q/k/v at TP=8)
+    # tensor parallel: each rank picks for its own shard
     from kvcacheboundaryprotection_b200.tp import allreduce_splits
 
-    assert allreduce_splits(cfg, 2) == {"o": 7, "down": 7}
-    assert allreduce_splits(cfg, 8) == {"o": 3, "down": 7}  # 3 or 4 query heads per rank
+    assert allreduce_splits(cfg, 2) == {"o": 8, "down": 8}
+    assert allreduce_splits(cfg, 8, 0) == {"o": 4, "down": 8}  # 4 query heads on rank 0
 
 
 def test_allreduce_slots_are_independent_of_the_call():
