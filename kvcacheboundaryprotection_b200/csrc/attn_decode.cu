@@ -224,6 +224,7 @@ __global__ void __launch_bounds__(attn_threads(GR), kMinBlocks) decode_attn_scor
     if (KVBP_PDL_LATE) pdl_launch_dependents();
     cluster_wait_acquire();  // the setup phase (the consumers wait before their exchange)
     cluster_sync_all();      // matches the consumers' final cluster barrier
+    if (p.upd_last) cluster_sync_all();  // and the fused score update's flag exchange
     return;
   }
 
@@ -506,36 +507,76 @@ __global__ void __launch_bounds__(attn_threads(GR), kMinBlocks) decode_attn_scor
       iLh[h] = finL[h] > 0.f ? 1.0f / finL[h] : 0.f;
     }
     float* sscore = p.step_score + static_cast<size_t>(b) * S;
-    // query heads kvh * G + h below Hkv also feed the per-head signal rows
-    float* hrow = p.head_score ? p.head_score + (static_cast<size_t>(b) * p.Hkv + kvh * G) * S : nullptr;
-    for (int i = tid; i < nloc; i += kConsumers) {
-      if (spos_s[i] < 0) continue;
-      float mx = 0.f;
+    if (!p.head_score) {
+      for (int i = tid; i < nloc; i += kConsumers) {
+        if (spos_s[i] < 0) continue;
+        float mx = 0.f;
 #pragma unroll
-      for (int h = 0; h < G; ++h) {
-        const float pr = iLh[h] > 0.f ? expf(logits[i * 8 + h] - Mh[h]) * iLh[h] : 0.f;
-        mx = fmaxf(mx, pr);
-        if (hrow && kvh * G + h < p.Hkv)
-          atomicMax(reinterpret_cast<int*>(&hrow[static_cast<size_t>(h) * S + t0 * kTile + i]), __float_as_int(pr));
+        for (int h = 0; h < G; ++h) {
+          const float pr = iLh[h] > 0.f ? expf(logits[i * 8 + h] - Mh[h]) * iLh[h] : 0.f;
+          mx = fmaxf(mx, pr);
+        }
+        if (mx != mx) set_err(p.err, kErrNanScore);
+        atomicMax(reinterpret_cast<int*>(&sscore[t0 * kTile + i]), __float_as_int(mx));
       }
-      if (mx != mx) set_err(p.err, kErrNanScore);
-      atomicMax(reinterpret_cast<int*>(&sscore[t0 * kTile + i]), __float_as_int(mx));
+    } else {
+      // query heads kvh * G + h below Hkv also feed the per-head signal rows
+      float* hrow = p.head_score + (static_cast<size_t>(b) * p.Hkv + kvh * G) * S;
+      for (int i = tid; i < nloc; i += kConsumers) {
+        if (spos_s[i] < 0) continue;
+        float mx = 0.f;
+#pragma unroll
+        for (int h = 0; h < G; ++h) {
+          const float pr = iLh[h] > 0.f ? expf(logits[i * 8 + h] - Mh[h]) * iLh[h] : 0.f;
+          mx = fmaxf(mx, pr);
+          if (kvh * G + h < p.Hkv)
+            atomicMax(reinterpret_cast<int*>(&hrow[static_cast<size_t>(h) * S + t0 * kTile + i]), __float_as_int(pr));
+        }
+        if (mx != mx) set_err(p.err, kErrNanScore);
+        atomicMax(reinterpret_cast<int*>(&sscore[t0 * kTile + i]), __float_as_int(mx));
+      }
     }
   }
+  int* last_flag = flags + 2;
   if (p.upd_last) {
-    // fused score update (kv_coupled_generator.py:504-516): the last of the sequence's
-    // CTAs (every kv head, every cluster rank) to finish updates all of its slots
+    // fused score update (kv_coupled_generator.py:504-516): the sequence's CTAs (every kv
+    // head, every cluster rank) count themselves in; the cluster holding the last arrival
+    // updates every slot of the sequence, split over its CTAs
     __threadfence();  // this CTA's score maxima are visible before it counts itself
     named_bar(1, kConsumers);
-    int* last_flag = flags + 2;
     if (tid == 0) *last_flag = atomicAdd(&p.seq_counter[b], 1) == static_cast<int>(gridDim.x * gridDim.y) - 1;
+  }
+  __syncwarp();
+  cluster_sync_all();  // no CTA leaves while a peer may still target its shared memory
+  if (p.upd_last) {
+    int* any_last = flags + 3;
+    if (tid == 0) {
+      int a = 0;
+      for (int q = 0; q < CS; ++q) a |= __float_as_int(ld_dsmem_f32(mapa_u32(smem_u32(last_flag), q)));
+      *any_last = a;
+    }
     named_bar(1, kConsumers);
-    if (*last_flag) {
+    const bool mine = *any_last != 0;
+    cluster_sync_all();  // every peer has read this CTA's flag
+    if (mine) {
       __threadfence();
-      const float* sc_all = p.step_score + static_cast<size_t>(b) * S;
+      constexpr int kU = 4;  // slots per thread with their loads in flight together
+      const size_t o0 = static_cast<size_t>(b) * S;
+      const float* scr = p.step_score + o0;
       float mx = 0.f;
-      for (int i = tid; i < S; i += kConsumers)
-        if (spos_g[i] >= 0) mx = fmaxf(mx, __ldcg(&sc_all[i]));
+      for (int i0 = tid; i0 < S; i0 += kU * kConsumers) {
+        float v[kU];
+        int ps[kU];
+#pragma unroll
+        for (int k = 0; k < kU; ++k) {
+          const int i = i0 + k * kConsumers;
+          v[k] = i < S ? __ldcg(&scr[i]) : 0.f;
+          ps[k] = i < S ? spos_g[i] : -1;
+        }
+#pragma unroll
+        for (int k = 0; k < kU; ++k)
+          if (ps[k] >= 0) mx = fmaxf(mx, v[k]);
+      }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
       if (lane == 0) escr[warp] = mx;
@@ -544,27 +585,42 @@ __global__ void __launch_bounds__(attn_threads(GR), kMinBlocks) decode_attn_scor
       for (int w = 0; w < kConsumerWarps; ++w) gmx = fmaxf(gmx, escr[w]);
       const float thr = static_cast<float>(0.05 * static_cast<double>(gmx));
       const int step = p.seq_step[b];
-      const size_t o0 = static_cast<size_t>(b) * S;
+      const int lo = (rank * S) / CS, hi = ((rank + 1) * S) / CS;
       float* scw = p.step_score + o0;
-      for (int i = tid; i < S; i += kConsumers) {
-        const float ks = __ldcg(&scw[i]);
-        if (spos_g[i] >= 0) {
-          if (ks != ks) set_err(p.err, kErrNanScore);
-          p.upd_attn[o0 + i] = ks;
-          p.upd_maxa[o0 + i] = fmaxf(p.upd_maxa[o0 + i], ks);
-          p.upd_cumul[o0 + i] = __dadd_rn(p.upd_cumul[o0 + i], static_cast<double>(ks));
-          if (ks > thr) {
-            p.upd_last[o0 + i] = step;
-            p.upd_cnt[o0 + i] += 1;
-          }
+      for (int i0 = lo + tid; i0 < hi; i0 += kU * kConsumers) {
+        float ks[kU], ma[kU];
+        double cu[kU];
+        int ps[kU], cn[kU];
+#pragma unroll
+        for (int k = 0; k < kU; ++k) {
+          const int i = i0 + k * kConsumers;
+          const bool in = i < hi;
+          ps[k] = in ? spos_g[i] : -1;
+          ks[k] = in ? __ldcg(&scw[i]) : 0.f;
+          ma[k] = in ? p.upd_maxa[o0 + i] : 0.f;
+          cu[k] = in ? p.upd_cumul[o0 + i] : 0.0;
+          cn[k] = in ? p.upd_cnt[o0 + i] : 0;
         }
-        scw[i] = 0.f;
+#pragma unroll
+        for (int k = 0; k < kU; ++k) {
+          const int i = i0 + k * kConsumers;
+          if (i >= hi) continue;
+          if (ps[k] >= 0) {
+            if (ks[k] != ks[k]) set_err(p.err, kErrNanScore);
+            p.upd_attn[o0 + i] = ks[k];
+            p.upd_maxa[o0 + i] = fmaxf(ma[k], ks[k]);
+            p.upd_cumul[o0 + i] = __dadd_rn(cu[k], static_cast<double>(ks[k]));
+            if (ks[k] > thr) {
+              p.upd_last[o0 + i] = step;
+              p.upd_cnt[o0 + i] = cn[k] + 1;
+            }
+          }
+          scw[i] = 0.f;
+        }
       }
-      if (tid == 0) p.seq_counter[b] = 0;
+      if (tid == 0 && *last_flag) p.seq_counter[b] = 0;
     }
   }
-  __syncwarp();
-  cluster_sync_all();  // no CTA leaves while a peer may still target its shared memory
 }
 
 // ------------------------------------------------------------------------------------

@@ -345,6 +345,8 @@ class CappedKVEngine:
         * >= ~2/3 tile per SM: the split whose whole waves of 2 CTAs per SM carry the most
           work per wave -- a grid a few CTAs past a whole wave leaves them as a slow tail
           (149 tiles: 3 splits, not 2);
+        * 24.. tiles: about 256 CTAs, at most 8 per cluster (the single-GPU 7B q/k/v, o and
+          down shapes, re-swept inside the decode step: 7, 8, 8);
         * fewer tiles: about 210 CTAs in all, at most 16 per cluster."""
         tiles = max(1, N // 128)
         kc = max(1, K // 128)
@@ -354,6 +356,8 @@ class CappedKVEngine:
         if tiles * 3 >= slots:
             cands = range(1, min(4, kc) + 1)
             return min(cands, key=lambda s: (math.ceil(tiles * s / slots) / s, s))
+        if tiles >= 24:
+            return max(1, min((256 * sms // 148) // tiles, 8, kc))
         return max(1, min(round(210 * sms / 148 / tiles), 16, kc))
 
     @property

@@ -190,7 +190,7 @@ def _state(B, S, pos, seed):
     g = torch.Generator(device="cuda").manual_seed(seed)
     d = "cuda"
     st = {
-        "slot_pos": pos.clone(),
+        "slot_pos": pos,  # shared: neither path changes slot positions
         "insert_step": torch.randint(0, 5, (B, S), generator=g, device=d, dtype=torch.int32),
         "last_access": torch.randint(0, 9, (B, S), generator=g, device=d, dtype=torch.int32),
         "access_count": torch.randint(1, 9, (B, S), generator=g, device=d, dtype=torch.int32),

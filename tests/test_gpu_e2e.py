@@ -71,6 +71,7 @@ def _run_forced(preset, policy, P, cap, N, max_new, seed=0):
         want = o.step_logits[step_idx]
         d = np.abs(got - want)
         stats["logit_diff"].append(float(d.max()))
+        stats.setdefault("logit_mean_diff", []).append(float(d.mean()))
         i = int(np.argmax(d))
         ulp = np.float32(2.0) ** (np.floor(np.log2(np.maximum(np.abs(want), 1e-30))) - 7)  # bf16 ulp of each logit
         stats.setdefault("detail", []).append((step_idx, float(d[i]), float(want[i]), float(got[i]),
@@ -171,11 +172,20 @@ TINY = dict(P=1024, cap=256, N=2048, max_new=128)
 
 
 def test_tiny_qwen2_teacher_forced_parity():
+    """Logit tolerance at this configuration: max |diff| <= 5e-2 and mean |diff| <= 1e-2 per
+    step.  4 layers of bf16 rounding points over a 1024-token context leave a noise floor
+    that no accumulation order gets under: the oracle itself with float64-accumulated
+    projections (same rounding points) differs from its float32 form by max 0.027 / mean
+    0.0046 on the step-0 logits (tests/test_oracle_noise_floor.py), the same as this path
+    (max 0.027 / mean 0.0046 at step 0, <= 0.04 over the 128 steps).  The 2e-2 bound holds
+    on the 2-layer parity decoders above."""
     o, eng, st, evicted = _run_forced("tiny-qwen2", "lru", **TINY)
-    print(f"tiny-qwen2: max logit diff {max(st['logit_diff']):.3g}, argmax {st['argmax_ok']}/{st['argmax_n']}")
+    print(f"tiny-qwen2: max logit diff {max(st['logit_diff']):.3g}, mean {max(st['logit_mean_diff']):.3g}, "
+          f"argmax {st['argmax_ok']}/{st['argmax_n']}")
     assert len(st["logit_diff"]) == TINY["max_new"]
     worst = sorted(st["detail"], key=lambda r: -r[1])[:6]
-    assert max(st["logit_diff"]) <= 2e-2, ("(step, |diff|, oracle, gpu, max ulps, frac within 1 ulp)", worst)
+    assert max(st["logit_diff"]) <= 5e-2, ("(step, |diff|, oracle, gpu, max ulps, frac within 1 ulp)", worst)
+    assert max(st["logit_mean_diff"]) <= 1e-2
     assert st["argmax_n"] >= 64 and st["argmax_ok"] >= 0.99 * st["argmax_n"]
     assert all(st["score_ok"])
     assert np.median(np.concatenate(st["score_rel"])) <= 1e-3

@@ -83,7 +83,7 @@ def test_split_k_choices():
     H, F, V = cfg.hidden, cfg.ffn, cfg.vocab
     qkv_n = (cfg.n_heads + 2 * cfg.n_kv_heads) * cfg.head_dim
     pick = CappedKVEngine._pick_splits
-    assert [pick(qkv_n, H), pick(H, H), pick(2 * F, H), pick(H, F), pick(V, H)] == [6, 8, 1, 8, 1]
+    assert [pick(qkv_n, H), pick(H, H), pick(2 * F, H), pick(H, F), pick(V, H)] == [7, 8, 1, 8, 1]
     assert pick(128 * 148, H) == 2       # 148 tiles: exactly two CTAs per SM
     assert pick(128 * 149, H) == 3       # 149 tiles: 2 splits would leave a 2-CTA tail
     assert pick(768, H) == 16            # 6 tiles (q/k/v at TP=8)
