@@ -115,7 +115,9 @@ struct AttnArgs {
   float scale;     // bfloat16(1/sqrt(D)) as float
 };
 
-template <int G, int GR>
+// X: the optional parts (per-head keep masks and scores, fused scatter, fused score
+// update) are compiled in; the plain kernel (X = false) carries none of their code.
+template <int G, int GR, bool X>
 __global__ void __launch_bounds__(attn_threads(GR), kMinBlocks) decode_attn_score_kernel(const __grid_constant__ CUtensorMap kmap,
                                                                      const __grid_constant__ CUtensorMap vmap,
                                                                      const AttnArgs p) {
@@ -224,7 +226,7 @@ __global__ void __launch_bounds__(attn_threads(GR), kMinBlocks) decode_attn_scor
     if (KVBP_PDL_LATE) pdl_launch_dependents();
     cluster_wait_acquire();  // the setup phase (the consumers wait before their exchange)
     cluster_sync_all();      // matches the consumers' final cluster barrier
-    if (p.upd_last) cluster_sync_all();  // and the fused score update's flag exchange
+    if (X && p.upd_last) cluster_sync_all();  // and the fused score update's flag exchange
     return;
   }
 
@@ -261,7 +263,7 @@ __global__ void __launch_bounds__(attn_threads(GR), kMinBlocks) decode_attn_scor
     const int lta = u * kTile + r0 + g, ltb = lta + 8;
     int pa = t0 * kTile + lta < S ? spos_g[t0 * kTile + lta] : -1;
     int pb = t0 * kTile + ltb < S ? spos_g[t0 * kTile + ltb] : -1;
-    if (p.head_keep) {  // a slot this kv head does not retain counts as free for it
+    if (X && p.head_keep) {  // a slot this kv head does not retain counts as free for it
       const uint8_t* hk = p.head_keep + static_cast<size_t>(pair) * S + t0 * kTile;
       if (pa >= 0 && !hk[lta]) pa = -1;
       if (pb >= 0 && !hk[ltb]) pb = -1;
@@ -273,7 +275,7 @@ __global__ void __launch_bounds__(attn_threads(GR), kMinBlocks) decode_attn_scor
       ok_tile = false;
     }
     ok_tile = __all_sync(0xffffffffu, ok_tile);  // warp-uniform: the tile's mma/ldmatrix are warp-wide
-    if (ok_tile && (u < n_first || p.knew) && wslot >= 0 && wslot < S) {
+    if (ok_tile && (u < n_first || (X && p.knew)) && wslot >= 0 && wslot < S) {
       // a tile staged before the wait may hold a stale copy of this step's row (and with a
       // fused scatter every tile may): the warp that owns the row (rows r0..r0+15 of the
       // tile) writes it into the staged tile, K by lanes 0-15 and V by lanes 16-31, one
@@ -284,7 +286,7 @@ __global__ void __launch_bounds__(attn_threads(GR), kMinBlocks) decode_attn_scor
         const int half = lane >> 4, ch = lane & 15, box = ch >> 3, c = ch & 7;
         __nv_bfloat16* crow = const_cast<__nv_bfloat16*>(half ? p.vc : p.kc) + (static_cast<size_t>(pair) * S + wslot) * kD + ch * 8;
         uint4 v;
-        if (p.knew) {
+        if (X && p.knew) {
           v = __ldg(reinterpret_cast<const uint4*>((half ? p.vnew : p.knew) + static_cast<size_t>(pair) * kD + ch * 8));
           *reinterpret_cast<uint4*>(crow) = v;
         } else {
@@ -507,7 +509,7 @@ __global__ void __launch_bounds__(attn_threads(GR), kMinBlocks) decode_attn_scor
       iLh[h] = finL[h] > 0.f ? 1.0f / finL[h] : 0.f;
     }
     float* sscore = p.step_score + static_cast<size_t>(b) * S;
-    if (!p.head_score) {
+    if (!X || !p.head_score) {
       for (int i = tid; i < nloc; i += kConsumers) {
         if (spos_s[i] < 0) continue;
         float mx = 0.f;
@@ -538,7 +540,7 @@ __global__ void __launch_bounds__(attn_threads(GR), kMinBlocks) decode_attn_scor
     }
   }
   int* last_flag = flags + 2;
-  if (p.upd_last) {
+  if (X && p.upd_last) {
     // fused score update (kv_coupled_generator.py:504-516): the sequence's CTAs (every kv
     // head, every cluster rank) count themselves in; the cluster holding the last arrival
     // updates every slot of the sequence, split over its CTAs
@@ -548,7 +550,7 @@ __global__ void __launch_bounds__(attn_threads(GR), kMinBlocks) decode_attn_scor
   }
   __syncwarp();
   cluster_sync_all();  // no CTA leaves while a peer may still target its shared memory
-  if (p.upd_last) {
+  if (X && p.upd_last) {
     int* any_last = flags + 3;
     if (tid == 0) {
       int a = 0;
@@ -677,12 +679,13 @@ static int choose_cluster(int pairs, int tiles, int sms, int max_nloc_tiles) {
 template <int G, int GR>
 static cudaError_t launch_g(cudaStream_t stream, const CUtensorMap& km, const CUtensorMap& vm, const AttnArgs& a,
                             int smem) {
-  auto kern = decode_attn_score_kernel<G, GR>;
-  static int configured_smem = 0;
-  if (smem > configured_smem) {
+  const bool x = a.head_keep || a.head_score || a.knew || a.upd_last;
+  auto kern = x ? decode_attn_score_kernel<G, GR, true> : decode_attn_score_kernel<G, GR, false>;
+  static int configured_smem[2] = {0, 0};  // per kernel (plain, with the optional parts)
+  if (smem > configured_smem[x]) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    configured_smem = smem;
+    configured_smem[x] = smem;
   }
   return launch_pdl(kern, dim3(a.cluster, a.Hkv, a.B), dim3(attn_threads(GR)), smem, stream, dim3(a.cluster, 1, 1), km,
                     vm, a);
