@@ -817,6 +817,55 @@ def run_attn_microbench(preset="qwen2.5-7b", B=16, C=1024, E=8, layers=8, iters=
             "peak_gbs": hbm, "peak_kind": peak_kind}
 
 
+def planted_prompt(vocab: int, P: int, seed: int = 0, span: int = 16):
+    """Uniform-random token ids with one key span: tokens [r, r + span) copied to the last
+    ``span`` positions (r uniform), the synthetic stand-in for a needle-in-a-haystack prompt."""
+    rng = np.random.default_rng(seed)
+    ids = rng.integers(0, vocab, P)
+    r = int(rng.integers(0, P - 2 * span))
+    ids[P - span:] = ids[r : r + span]
+    return ids
+
+
+def run_prefill_e2e(workload="qwen2.5-7b", batch=1):
+    """Step 0 of the workload end to end through CappedKVEngine.prefill: prompt forward
+    (cuBLAS projections, tcgen05 causal attention with the per-key score), the forced
+    eviction down to the capacity, compaction into the slot cache and the first greedy
+    token, for ``batch`` prompts with a planted key span.  Reported apart from the decode
+    metric (which excludes prefill, as the reference's decode_step_* fields do)."""
+    import torch
+
+    from kvcacheboundaryprotection_b200.config import get_config
+    from kvcacheboundaryprotection_b200.engine import CappedKVEngine, EvictionSpec, FusedWeights
+    from kvcacheboundaryprotection_b200.weights import init_weights
+
+    preset, _, C, P, policy, _ = WORKLOADS[workload]
+    cfg = get_config(preset)
+    dev = torch.device("cuda")
+    fw = FusedWeights(cfg, init_weights(cfg, seed=0, device=dev), dev)
+    eng = CappedKVEngine(cfg, fw, batch=batch, evict=EvictionSpec(policy, C, 8, True, 0.10, 0.10), max_prompt_len=P,
+                         max_new_tokens=8, device=dev)
+    ids = torch.tensor(np.stack([planted_prompt(cfg.vocab, P, seed=b) for b in range(batch)]), dtype=torch.int32)
+    eng.prefill(ids)  # warm-up of the same shapes
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.perf_counter()
+    e0.record()
+    eng.prefill(ids)
+    e1.record()
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    ms = e0.elapsed_time(e1)
+    eng.check_device_errors()
+    out = {"workload": f"{preset}, {batch} x {P}-token prompt with a planted 16-token key span, capacity {C}, {policy}",
+           "ms": round(ms, 1), "wall_ms": round(wall * 1000, 1), "prefill_tok_s": round(batch * P / (ms / 1000), 1),
+           "retained_after_step0": int((eng.slot_pos[0] >= 0).sum().item()),
+           "how": "CUDA events around CappedKVEngine.prefill (after one warm-up prefill of the same shapes)"}
+    del eng, fw
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_prefill_microbench(preset="qwen2.5-7b", P=8192, iters=3):
     """Operator microbench of kvbp_prefill_attn_score (tcgen05 causal prefill attention
     with the per-key score) for one layer of one sequence at the preset's heads.
@@ -1216,6 +1265,7 @@ def main():
             preset, B0, C0 = WORKLOADS[a.workload][:3]
             out["attn_microbench"] = run_attn_microbench(preset, a.batch or B0, C0)
             out["prefill_microbench"] = run_prefill_microbench(preset, 8192)
+            out["prefill_e2e"] = run_prefill_e2e(a.workload)
         if not a.no_cpu:
             times, sample, threads = cpu_reference_step_times(a.workload, 3, 1, budget_s=20.0)
             v = 1.0 / (sum(times) / len(times))
