@@ -355,6 +355,17 @@ int kvbp_key_to_token(kvbp_stream_t stream, int32_t rows, const int64_t* keys, i
 int kvbp_residual_add(kvbp_stream_t stream, int32_t rows, int32_t hidden, void* h, const float* delta,
                       float* ss_out);
 
+/* Lossy int8 demotion of cache rows (online_credit_generator.py:643-704,
+ * _demote_kv_positions): for every layer and kv head, the K and V rows of slots
+ * slots[b][0..counts[b]) (slots is [B][stride]; < 0 or >= S sets KVBP_DEV_INDEX) of the
+ * caches [layers][B][Hkv][S][128] bf16 get an absmax int8 round trip in place, with the
+ * reference's bf16 arithmetic: scale = bf16(max|x| / 127), q = clip(round-half-even(
+ * bf16(x / max(scale, bf16(1e-10)))), -127, 127), x = bf16(q * scale).  Slots are
+ * the caller's map of the positions to demote (slot_pos); skipping positions already
+ * demoted is the caller's bookkeeping, as in the reference. */
+int kvbp_demote_int8(kvbp_stream_t stream, void* kcache, void* vcache, int32_t layers, int32_t B, int32_t Hkv,
+                     int32_t S, const int32_t* slots, int32_t stride, const int32_t* counts, int32_t* dev_err);
+
 #ifdef __cplusplus
 }
 #endif

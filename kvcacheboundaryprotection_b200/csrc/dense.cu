@@ -444,6 +444,62 @@ int residual_add(cudaStream_t st, int rows, int H, void* h, const float* delta, 
   return check_launch("residual_add", le);
 }
 
+// ---- lossy int8 demotion of cache rows (online_credit_generator.py:643-704) ----------
+// Per (layer, sequence, kv head, slot) row of K and of V: absmax int8 round trip with the
+// reference's bf16 arithmetic -- every op computed in fp32 and rounded to bf16:
+//   scale = bf16(max|x| / 127), q = clip(round_half_even(bf16(x / max(scale, bf16(1e-10)))),
+//   -127, 127), x' = bf16(q * scale).  One warp per row, four elements per lane.
+__global__ void demote_int8_kernel(__nv_bfloat16* __restrict__ kc, __nv_bfloat16* __restrict__ vc, int B, int Hkv,
+                                   int S, const int* __restrict__ slots, int stride, const int* __restrict__ counts,
+                                   int* err) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int layer = blockIdx.z, b = blockIdx.y;
+  const int n = counts[b] < stride ? counts[b] : stride;
+  const int rows = n * Hkv * 2;
+  const float tiny = bf16r(1e-10f);
+  for (int r = blockIdx.x * (blockDim.x >> 5) + warp; r < rows; r += gridDim.x * (blockDim.x >> 5)) {
+    const int which = r % 2, h = (r / 2) % Hkv, j = r / (2 * Hkv);
+    const int slot = slots[static_cast<size_t>(b) * stride + j];
+    if (slot < 0 || slot >= S) {
+      if (lane == 0) set_err(err, kErrIndex);
+      continue;
+    }
+    __nv_bfloat16* row = (which ? vc : kc) + (((static_cast<size_t>(layer) * B + b) * Hkv + h) * S + slot) * 128;
+    uint2 raw = *reinterpret_cast<const uint2*>(row + lane * 4);
+    float x[4] = {bf16lo(raw.x), bf16hi(raw.x), bf16lo(raw.y), bf16hi(raw.y)};
+    float amax = fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fmaxf(fabsf(x[2]), fabsf(x[3])));
+#pragma unroll
+    for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float scale = bf16r(amax / 127.0f);
+    const float den = fmaxf(scale, tiny);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float q = fminf(fmaxf(rintf(bf16r(x[i] / den)), -127.0f), 127.0f);
+      x[i] = bf16r(q * scale);
+    }
+    raw.x = pack_bf16(x[0], x[1]);
+    raw.y = pack_bf16(x[2], x[3]);
+    *reinterpret_cast<uint2*>(row + lane * 4) = raw;
+  }
+}
+
+int demote_int8(cudaStream_t st, void* kc, void* vc, int layers, int B, int Hkv, int S, const int* slots, int stride,
+                const int* counts, int* err) {
+  if (!kc || !vc || !slots || !counts) return fail(kStatusArg, "demote_int8: null pointer");
+  if (layers <= 0 || B <= 0 || Hkv <= 0 || S <= 0 || stride <= 0 || layers > 65535 || B > 65535)
+    return fail(kStatusArg, "demote_int8: bad size");
+  if ((reinterpret_cast<uintptr_t>(kc) | reinterpret_cast<uintptr_t>(vc)) & 7)
+    return fail(kStatusArg, "demote_int8: caches must be 8-byte aligned");
+  const int rows = stride * Hkv * 2;
+  const int blocks = (rows + 7) / 8 < 64 ? (rows + 7) / 8 : 64;
+  const cudaError_t le = launch_pdl(demote_int8_kernel, dim3(blocks, B, layers), dim3(256), 0, st, dim3(0),
+                                    static_cast<__nv_bfloat16*>(kc), static_cast<__nv_bfloat16*>(vc), B, Hkv, S, slots,
+                                    stride, counts, err);
+  return check_launch("demote_int8", le);
+}
+
 }  // namespace kvbp
 
 // ------------------------------------------------------------------------------------
@@ -484,6 +540,12 @@ int kvbp_argmax_key(kvbp_stream_t stream, int32_t rows, int32_t vocab, int64_t l
 int kvbp_key_to_token(kvbp_stream_t stream, int32_t rows, const int64_t* keys, int32_t* tokens) {
   return kvbp::key_to_token(reinterpret_cast<cudaStream_t>(stream), rows, reinterpret_cast<const long long*>(keys),
                             tokens);
+}
+
+int kvbp_demote_int8(kvbp_stream_t stream, void* kcache, void* vcache, int32_t layers, int32_t B, int32_t Hkv,
+                     int32_t S, const int32_t* slots, int32_t stride, const int32_t* counts, int32_t* dev_err) {
+  return kvbp::demote_int8(reinterpret_cast<cudaStream_t>(stream), kcache, vcache, layers, B, Hkv, S, slots, stride,
+                           counts, dev_err);
 }
 
 int kvbp_residual_add(kvbp_stream_t stream, int32_t rows, int32_t hidden, void* h, const float* delta,

@@ -66,6 +66,8 @@ int decode_attn_score(cudaStream_t stream, int B, int Hq, int Hkv, int D, int S,
                       const void* vcache, const int* slot_pos, const int* write_slot, void* out, float* step_score,
                       int* err, int cluster_override, const AttnExtra& extra);
 
+int demote_int8(cudaStream_t st, void* kc, void* vc, int layers, int B, int Hkv, int S, const int* slots, int stride,
+                const int* counts, int* err);
 int head_signal_update(cudaStream_t stream, int B, int Hkv, int S, const int* write_slot, float* head_score,
                        double* head_cumul, float* head_current, int* err);
 

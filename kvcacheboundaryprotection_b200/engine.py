@@ -871,6 +871,38 @@ class CappedKVEngine:
         self._append_evict()
         self.step += 1
 
+    def demote_positions(self, positions) -> List[List[int]]:
+        """Lossy int8 round trip of the K/V of retained positions, every layer and kv head
+        (the online-credit generator's demotion, online_credit_generator.py:643-704).
+        ``positions[b]`` lists sequence b's positions; positions already demoted, or not
+        retained, are skipped.  Returns the positions demoted now, per sequence."""
+        if len(positions) != self.B:
+            raise ValueError("one position list per sequence")
+        if not hasattr(self, "demoted"):
+            self.demoted = [set() for _ in range(self.B)]
+        sp = self.slot_pos.cpu().numpy()
+        done, rows = [], []
+        for b in range(self.B):
+            where = {int(p): s for s, p in enumerate(sp[b]) if p >= 0}
+            new = [int(p) for p in positions[b] if int(p) in where and int(p) not in self.demoted[b]]
+            new = list(dict.fromkeys(new))
+            self.demoted[b].update(new)
+            done.append(new)
+            rows.append([where[p] for p in new])
+        stride = max(1, max(len(r) for r in rows))
+        slots = torch.full((self.B, stride), -1, dtype=torch.int32)
+        for b, r in enumerate(rows):
+            slots[b, : len(r)] = torch.tensor(r, dtype=torch.int32)
+        counts = torch.tensor([len(r) for r in rows], dtype=torch.int32)
+        if int(counts.sum()):
+            slots_d, counts_d = slots.to(self.dev), counts.to(self.dev)
+            c = self.cfg
+            check(lib().kvbp_demote_int8(self.stream, _ptr(self.kc), _ptr(self.vc), c.n_layers, self.B, c.n_kv_heads,
+                                         self.S, _ptr(slots_d), stride, _ptr(counts_d), _ptr(self.dev_err)),
+                  "demote_int8")
+            torch.cuda.current_stream(self.dev).synchronize()
+        return done
+
     def check_device_errors(self) -> None:
         word = int(self.dev_err.item())
         if word:

@@ -275,3 +275,15 @@ def weight_names(cfg: OracleConfig) -> List[str]:
     if not cfg.tie_embed:
         names.append("lm_head")
     return names
+
+
+def int8_roundtrip(rows: np.ndarray) -> np.ndarray:
+    """Lossy int8 demotion of K/V rows (last axis = head_dim), restating
+    ``_demote_kv_positions`` (src/counterfact_kv_eviction/online_credit_generator.py:
+    676-691): per row absmax scale, round-half-even, clip to [-127, 127], dequantise --
+    each op on bfloat16 values, computed in float32 and rounded to bfloat16."""
+    x = rnd(np.asarray(rows, F32))
+    scale = rnd(np.abs(x).max(axis=-1, keepdims=True) / F32(127.0))
+    den = np.maximum(scale, rnd(np.array([1e-10], F32))[0])
+    q = np.clip(np.round(rnd(x / den)), F32(-127.0), F32(127.0))
+    return rnd(q * scale)

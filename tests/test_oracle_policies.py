@@ -62,3 +62,23 @@ def test_attention_mass_alias():
     a = PolicySpec("attention-mass", 20, True).select(list(range(50)), m, 10, 3)
     b = PolicySpec("h2o_faithful", 20, True).select(list(range(50)), m, 10, 3)
     assert a == b
+
+
+def test_int8_roundtrip_restatement():
+    """The oracle's int8 demotion: zero rows stay zero, the row maximum maps to +-127 * scale,
+    every value is a multiple of the scale, and re-demotion is nearly idempotent."""
+    import numpy as np
+
+    from oracle.bf16 import rnd
+    from oracle.model import int8_roundtrip
+
+    rng = np.random.default_rng(0)
+    x = rnd(rng.standard_normal((6, 128)).astype(np.float32) * 3)
+    x[2] = 0.0
+    y = int8_roundtrip(x)
+    assert (y[2] == 0).all()
+    scale = rnd(np.abs(x).max(axis=-1, keepdims=True) / np.float32(127))
+    q = y / np.where(scale == 0, 1, scale)
+    assert np.abs(q).max() <= 127.0 * (1 + 2 ** -8)  # q * scale is rounded to bf16
+    assert np.allclose(np.abs(y).max(axis=-1), (127 * scale[:, 0]), rtol=1e-2)
+    assert np.abs(int8_roundtrip(y) - y).max() <= np.abs(y).max() * 2 ** -7
