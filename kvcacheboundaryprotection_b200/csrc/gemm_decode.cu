@@ -49,7 +49,10 @@ constexpr int BK = 128;            // K per stage
 #ifndef KVBP_GEMM_STAGES
 #define KVBP_GEMM_STAGES 3
 #endif
-constexpr int kStages = KVBP_GEMM_STAGES;
+constexpr int kStagesM16 = KVBP_GEMM_STAGES;
+// ring depth per activation height: with 32 rows (MT = 2) a third 40 KiB stage would leave
+// room for one CTA per SM only; two stages keep two CTAs per SM
+__host__ __device__ constexpr int stages_for(int MT) { return MT == 1 ? kStagesM16 : 2; }
 #ifndef KVBP_GEMM_EARLY
 #define KVBP_GEMM_EARLY 3  // weight stages issued before the wait on the previous kernel
 #endif
@@ -120,6 +123,7 @@ __global__ void __launch_bounds__(kThreads) decode_gemm_kernel(const __grid_cons
                                                                const Args a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  constexpr int kStages = stages_for(MT);
   constexpr int kABox = MT * 16 * 128;  // one 64-wide k box of the activation chunk
   constexpr int kStageBytes = kWBytes + 2 * kABox;
   static_assert(MT * 16 * kRedStride * 4 <= kStages * kStageBytes, "partial tile must fit in the ring");
@@ -614,6 +618,7 @@ static EncodeTiledFnG encode_fn_g() {
 
 static int gemm_smem_bytes(int MT) {
   using namespace gemm;
+  const int kStages = stages_for(MT);
   return kStages * (kWBytes + MT * 16 * BK * 2) + kStages * BK * 2 + (32 + 2 * 32) * 4 + 16 + 2 * kStages * 8 + 1024;
 }
 
