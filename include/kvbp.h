@@ -326,6 +326,18 @@ int kvbp_decode_gemm_allreduce(kvbp_stream_t stream, int32_t M, int32_t N, int32
                                const uint64_t* peer_bases, int32_t world, int32_t rank, int32_t call_index,
                                const int32_t* epoch, int64_t buffer_bytes, int32_t* dev_err);
 
+/* Prefill projection on the tcgen05 tensor cores: out = X[M][K] . W[N][K]^T for the
+ * prompt rows of every sequence at once (the q/k/v, o, gate/up and down products of
+ * _forward_jittable over the prompt, jax_inference.py:949-956,1081,1095-1107 as the
+ * prefill branch :1684-1790 runs them).  w_packed is W in the kvbp_pack_weight layout
+ * (read directly, no unpacking); x [M][ldx] bf16 (ldx >= K, a multiple of 8, 16-byte
+ * aligned); bf16 output rounded from fp32 accumulators.  Epilogue 0: out [M][ldo] =
+ * bf16(acc).  Epilogue 2 (SwiGLU, gate/up interleaved in blocks of 64 rows as for
+ * kvbp_decode_gemm): out [M][ldo] holds the N/2 features bf16(bf16(g * bf16(sigmoid(g)))
+ * * u) (jax_inference.py:702-704,1103-1107).  N, K multiples of 128. */
+int kvbp_prefill_gemm(kvbp_stream_t stream, int32_t epilogue, int32_t M, int32_t N, int32_t K, const void* w_packed,
+                      const void* x, int32_t ldx, void* out, int32_t ldo, int32_t* dev_err);
+
 /* Converts a row-major bf16 weight W[N][K] (N, K multiples of 128) to the decode GEMM's
  * packed layout and back: each 128-row x 128-column block becomes one contiguous 32 KiB
  * run of two 128 x 64 halves whose 16-byte chunks are XOR-swizzled by row (chunk

@@ -21,7 +21,7 @@ CSRC = PKG / "csrc"
 LIB_DIR = PKG / "lib"
 LIB = LIB_DIR / "libkvbp.so"
 INCLUDE = PKG.parent / "include"
-SOURCES = ["capi.cu", "attn_decode.cu", "dense.cu", "evict.cu", "gemm_decode.cu", "prefill_attn.cu"]
+SOURCES = ["capi.cu", "attn_decode.cu", "dense.cu", "evict.cu", "gemm_decode.cu", "prefill_attn.cu", "prefill_gemm.cu"]
 HEADERS = ["common.cuh", "kvbp_internal.h"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

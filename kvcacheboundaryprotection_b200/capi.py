@@ -126,6 +126,7 @@ SIGNATURES = {
     "kvbp_key_to_token": (C.c_int, [P, I32, P, P]),
     "kvbp_residual_add": (C.c_int, [P, I32, I32, P, P, P]),
     "kvbp_demote_int8": (C.c_int, [P, P, P, I32, I32, I32, I32, P, I32, P, P]),
+    "kvbp_prefill_gemm": (C.c_int, [P, I32, I32, I32, I32, P, P, I32, P, I32, P]),
     "kvbp_unpack_weight": (C.c_int, [P, I32, I32, P, P]),
 }
 EXTRA_SIGNATURES = {

@@ -1,0 +1,312 @@
+// Prefill projections on the 5th-generation tensor cores (tcgen05 + TMEM):
+// Y[M][N] = X[M][K] . W[N][K]^T with bf16 operands and fp32 accumulation, for the prompt
+// rows of every sequence at once (the q/k/v, o, gate/up and down products of
+// _forward_jittable over the prompt, jax_inference.py:949-956,1081,1095-1107, as the
+// prefill branch :1684-1790 runs them).
+//
+// W is the decode GEMM's packed layout (kvbp_pack_weight): each 128-row x 128-column
+// block is two 128 x 64 halves, each half the 128-byte-swizzled K-major image the MMA
+// reads -- so a B tile is a 1-D bulk copy per half, no repacking.  X is row-major; its
+// 128 x 64 tiles arrive by 2-D TMA with the same 128-byte swizzle.
+//
+// One CTA per 128-row x BN-column output tile (BN = 256: two packed blocks, or 128),
+// warp-specialised:
+//   warp 0  TMA / bulk producer over a 4-stage ring (A 16 KiB + B BN/128 x 16 KiB);
+//   warp 1  allocates BN TMEM columns and issues tcgen05.mma (M = 128, N = BN, K = 16,
+//           four per 64-wide stage) from one thread, committing each stage back to the
+//           producer and the last one to the epilogue;
+//   warps 2-5  epilogue: TMEM -> registers (each warp its 32-lane quarter) -> bf16.
+// Epilogues: plain (out = bf16(acc)), and SwiGLU for the interleaved gate/up weights
+// (rows 64t..64t+63 of block t are gate features, the next 64 the matching up ones):
+// act = bf16(bf16(g * bf16(sigmoid(g))) * u) with g, u the bf16 GEMM outputs
+// (jax_inference.py:702-704,1103-1107), so the 2F-wide gate/up product never reaches HBM.
+#include "common.cuh"
+#include "kvbp_internal.h"
+
+namespace kvbp {
+namespace pg {
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;  // one swizzle atom of K per stage
+constexpr int kStages = 4;
+constexpr int kHalf = 128 * 128;  // bytes of one 128 x 64 bf16 tile (16 KiB)
+constexpr int kThreads = 6 * 32;
+
+__device__ __forceinline__ uint64_t sdesc(uint32_t saddr) {
+  // K-major, 128-byte swizzle: 8-row core groups 1024 B apart (SBO), LBO unused (16 B)
+  return static_cast<uint64_t>((saddr >> 4) & 0x3FFF) | (static_cast<uint64_t>(1) << 16) |
+         (static_cast<uint64_t>(1024 >> 4) << 32) | (static_cast<uint64_t>(1) << 46) | (static_cast<uint64_t>(2) << 61);
+}
+
+// kind::f16 instruction descriptor: D f32, A/B bf16, both K-major, M x N
+__host__ __device__ constexpr uint32_t idesc(int M, int N) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(N >> 3) << 17) |
+         (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t id, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+      "l"(da), "l"(db), "r"(id), "r"(acc));
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+struct Args {
+  const __nv_bfloat16* w;  // packed [N/128][K/128][2][128][64]
+  __nv_bfloat16* out;      // plain: [M][ldo] (columns n); SwiGLU: [M][ldo] (features n / 2)
+  int ldo;
+  int M, N, K;
+  int swiglu;
+  int* err;
+};
+
+template <int BN>
+__global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_constant__ CUtensorMap xmap,
+                                                                  const Args a) {
+  constexpr int kNB = BN / 128;               // packed blocks per tile
+  constexpr int kStage = kHalf * (1 + kNB);   // A + B bytes per stage
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(base + kStages * kStage);
+  uint64_t* empty = full + kStages;
+  uint64_t* accfull = empty + kStages;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(accfull + 1);
+  int* bad = reinterpret_cast<int*>(tslot + 1);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tn = blockIdx.x, tm = blockIdx.y;
+  const int m0 = tm * kBM;
+  const int kc = a.K / 128;      // packed k-blocks
+  const int nk = a.K / kBK;      // 64-wide stages
+  const int nblk = a.N / 128;
+
+  if (tid == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accfull, 1);
+    *bad = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tslot)), "r"(BN));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+  auto healthy = [&]() { return !*reinterpret_cast<volatile int*>(bad); };
+  auto wait_or_fail = [&](uint64_t* bar, uint32_t ph) {
+    if (!mbar_wait_bounded(bar, ph)) {
+      set_err(a.err, kErrWaitTimeout);
+      atomicExch(bad, 1);
+      return false;
+    }
+    return true;
+  };
+
+  if (warp == 0) {
+    // =========================== producer =============================================
+    if (lane == 0) {
+      prefetch_tmap(&xmap);
+      int issued = 0;
+      for (int u = 0; u < nk && healthy(); ++u) {
+        const int st = u % kStages;
+        if (u >= kStages && !wait_or_fail(&empty[st], ((u / kStages) - 1) & 1)) break;
+        uint8_t* sA = base + st * kStage;
+        mbar_expect_tx(&full[st], kStage);
+        tma_load_2d(sA, &xmap, &full[st], u * kBK, m0);
+        for (int b = 0; b < kNB; ++b) {
+          const int blk = tn * kNB + b;
+          const __nv_bfloat16* src =
+              a.w + ((static_cast<size_t>(blk) * kc + (u >> 1)) * 2 + (u & 1)) * (128 * 64);
+          bulk_load(sA + kHalf * (1 + b), src, kHalf, &full[st]);
+        }
+        issued = u + 1;
+      }
+      if (!healthy()) {  // let the copies in flight land before the CTA can exit
+        for (int u = (issued > kStages ? issued - kStages : 0); u < issued; ++u)
+          mbar_wait_bounded(&full[u % kStages], (u / kStages) & 1, 1u << 16);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // =========================== MMA issue ============================================
+    if (lane == 0) {
+      constexpr uint32_t id = idesc(kBM, BN);
+      for (int u = 0; u < nk; ++u) {
+        const int st = u % kStages;
+        if (!wait_or_fail(&full[st], (u / kStages) & 1)) break;
+        tc_fence_after();
+        const uint32_t sA = smem_u32(base + st * kStage);
+        const uint32_t sB = sA + kHalf;
+#pragma unroll
+        for (int ks = 0; ks < kBK / 16; ++ks)
+          mma_bf16(tmem, sdesc(sA + ks * 32), sdesc(sB + ks * 32), id, (u > 0 || ks > 0) ? 1u : 0u);
+        mma_commit(&empty[st]);
+      }
+      mma_commit(accfull);  // every MMA issued so far is complete when this arrives
+    }
+    __syncwarp();
+  } else {
+    // =========================== epilogue =============================================
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
+    const int row = m0 + q * 32 + lane;
+    const bool ok = wait_or_fail(accfull, 0);
+    tc_fence_after();
+    if (__all_sync(0xffffffffu, ok && healthy())) {
+      if (!a.swiglu) {
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          float v[32];
+          tmem_ld32(tmem + lane_base + c, v);
+          const int n = tn * BN + c;
+          if (row < a.M && n < a.N) {
+            uint4* dst = reinterpret_cast<uint4*>(a.out + static_cast<size_t>(row) * a.ldo + n);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              dst[i] = make_uint4(pack_bf16(v[8 * i], v[8 * i + 1]), pack_bf16(v[8 * i + 2], v[8 * i + 3]),
+                                  pack_bf16(v[8 * i + 4], v[8 * i + 5]), pack_bf16(v[8 * i + 6], v[8 * i + 7]));
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int b = 0; b < kNB; ++b) {
+#pragma unroll 1
+          for (int j = 0; j < 64; j += 32) {  // 32 gate columns and the matching 32 up columns
+            float gv[32], uv[32];
+            tmem_ld32(tmem + lane_base + b * 128 + j, gv);
+            tmem_ld32(tmem + lane_base + b * 128 + 64 + j, uv);
+            const int f = (tn * kNB + b) * 64 + j;  // feature index
+            if (row < a.M) {
+              uint32_t pk[16];
+#pragma unroll
+              for (int i = 0; i < 32; i += 2) {
+                float r2[2];
+#pragma unroll
+                for (int t = 0; t < 2; ++t) {
+                  const float g = bf16r(gv[i + t]);
+                  const float up = bf16r(uv[i + t]);
+                  const float sig = bf16r(1.0f / (1.0f + expf(-g)));
+                  r2[t] = bf16r(g * sig) * up;
+                }
+                pk[i / 2] = pack_bf16(r2[0], r2[1]);
+              }
+              uint4* dst = reinterpret_cast<uint4*>(a.out + static_cast<size_t>(row) * a.ldo + f);
+#pragma unroll
+              for (int i = 0; i < 4; ++i) dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+            }
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN));
+}
+
+}  // namespace pg
+
+using EncodeTiledFnG = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFnG encode_fn_g() {
+  static EncodeTiledFnG fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFnG>(ptr);
+  }
+  return fn;
+}
+
+template <int BN>
+static cudaError_t launch_pg(cudaStream_t stream, const CUtensorMap& xm, const pg::Args& a, int grid_n) {
+  constexpr int smem = pg::kStages * pg::kHalf * (1 + BN / 128) + 1024 + 256;
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(pg::prefill_gemm_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         smem);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  dim3 grid(grid_n, (a.M + pg::kBM - 1) / pg::kBM);
+  pg::prefill_gemm_kernel<BN><<<grid, pg::kThreads, smem, stream>>>(xm, a);
+  return cudaGetLastError();
+}
+
+int prefill_gemm(cudaStream_t stream, int epilogue, int M, int N, int K, const void* w, const void* x, int ldx,
+                 void* out, int ldo, int* err) {
+  if (!w || !x || !out) return fail(kStatusArg, "prefill_gemm: null pointer");
+  if (epilogue != 0 && epilogue != 2) return fail(kStatusUnsupported, "prefill_gemm: epilogue %d (plain 0, SwiGLU 2)", epilogue);
+  if (M <= 0 || N <= 0 || K <= 0 || N % 128 || K % 128) return fail(kStatusArg, "prefill_gemm: bad size");
+  if ((M + pg::kBM - 1) / pg::kBM > 65535) return fail(kStatusArg, "prefill_gemm: too many rows");
+  if (ldx < K || ldx % 8 || ldo % 8) return fail(kStatusArg, "prefill_gemm: ldx / ldo must be >= K and multiples of 8");
+  if (ldo < (epilogue == 2 ? N / 2 : N)) return fail(kStatusArg, "prefill_gemm: ldo too small");
+  if ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out)) & 15)
+    return fail(kStatusArg, "prefill_gemm: pointers must be 16-byte aligned");
+  EncodeTiledFnG enc = encode_fn_g();
+  if (!enc) return fail(kStatusCuda, "cuTensorMapEncodeTiled unavailable");
+  CUtensorMap xm;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(M)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ldx) * 2};
+  cuuint32_t box[2] = {64, pg::kBM};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(&xm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(x), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(kStatusCuda, "prefill_gemm: tensor map failed (%d)", static_cast<int>(r));
+  pg::Args a;
+  a.w = static_cast<const __nv_bfloat16*>(w);
+  a.out = static_cast<__nv_bfloat16*>(out);
+  a.ldo = ldo;
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.swiglu = epilogue == 2;
+  a.err = err;
+  const bool wide = (N / 128) % 2 == 0;
+  cudaError_t e = wide ? launch_pg<256>(stream, xm, a, N / 256) : launch_pg<128>(stream, xm, a, N / 128);
+  if (e != cudaSuccess) return fail(kStatusCuda, "prefill_gemm launch: %s", cudaGetErrorString(e));
+  return kStatusOk;
+}
+
+}  // namespace kvbp
+
+#include "../../include/kvbp.h"
+
+extern "C" int kvbp_prefill_gemm(kvbp_stream_t stream, int32_t epilogue, int32_t M, int32_t N, int32_t K,
+                                 const void* w_packed, const void* x, int32_t ldx, void* out, int32_t ldo,
+                                 int32_t* dev_err) {
+  return kvbp::prefill_gemm(reinterpret_cast<cudaStream_t>(stream), epilogue, M, N, K, w_packed, x, ldx, out, ldo,
+                            dev_err);
+}

@@ -412,6 +412,14 @@ class CappedKVEngine:
         self.prefill_head_seed = torch.zeros(B, P, dtype=torch.float32, device=d) if self.per_head else None
         positions = torch.arange(P, dtype=torch.int32, device=d)
         H = c.hidden
+        if self.gemm == "kvbp":
+            # own tcgen05 projections over the prompt rows of several sequences at once
+            group = max(1, min(B, self.PREFILL_ROWS // P))
+            for g0 in range(0, B, group):
+                self._prefill_group(ids[g0 : g0 + group], g0, pre_k, pre_v, scores, need_scores, positions)
+            self._select_and_compact(P, scores, pre_k, pre_v)
+            check(L.kvbp_argmax(st, B, c.vocab, c.vocab, _ptr(self.logits), _ptr(self.tokens)), "argmax")
+            return
         for b in range(B):
             h = torch.empty(P, H, dtype=torch.bfloat16, device=d)
             check(L.kvbp_embed(st, P, c.vocab, H, _ptr(self.embed_w), _ptr(ids[b]), _ptr(h), _ptr(self.dev_err)), "embed")
@@ -462,6 +470,73 @@ class CappedKVEngine:
                 scores[b] = colmax
         self._select_and_compact(P, scores, pre_k, pre_v)
         check(L.kvbp_argmax(st, B, c.vocab, c.vocab, _ptr(self.logits), _ptr(self.tokens)), "argmax")
+
+    PREFILL_ROWS = 65536  # prompt rows forwarded together by the tcgen05 prefill path
+
+    def _prefill_group(self, ids, b0, pre_k, pre_v, scores, need_scores, positions) -> None:
+        """Prompt forward of sequences b0 .. b0 + n - 1 (ids [n, P]) with every projection on
+        the tcgen05 prefill GEMM over all n * P rows at once (packed weights read directly,
+        the gate/up product finished as SwiGLU in its epilogue); RoPE + K/V scatter for all
+        rows in one launch; causal attention with the per-key score per sequence."""
+        c, d, st, L = self.cfg, self.dev, self.stream, lib()
+        n, P = ids.shape
+        R, H, D, Hkv = n * P, c.hidden, c.head_dim, c.n_kv_heads
+        bf = torch.bfloat16
+        flat = ids.reshape(-1).contiguous()
+        pos = positions.repeat(n).contiguous()
+        err = _ptr(self.dev_err)
+
+        def gemm(epi, N, K, w, x, out):
+            check(L.kvbp_prefill_gemm(st, epi, R, N, K, _ptr(w), _ptr(x), x.stride(0), _ptr(out), out.stride(0), err),
+                  "prefill_gemm")
+
+        h = torch.empty(R, H, dtype=bf, device=d)
+        check(L.kvbp_embed(st, R, c.vocab, H, _ptr(self.embed_w), _ptr(flat), _ptr(h), err), "embed")
+        x = torch.empty_like(h)
+        qkv = torch.empty(R, c.qkv_dim, dtype=bf, device=d)
+        q = torch.empty(R, c.n_heads, D, dtype=bf, device=d)
+        att = torch.empty(R, c.n_heads * D, dtype=bf, device=d)
+        o = torch.empty(R, H, dtype=bf, device=d)
+        act = torch.empty(R, c.ffn, dtype=bf, device=d)
+        delta = None
+        colmax = torch.zeros(n, P, dtype=torch.float32, device=d) if need_scores else None
+        for li, Lw in enumerate(self.layers):
+            check(L.kvbp_add_rmsnorm(st, R, H, _ptr(h), _ptr(delta), _ptr(Lw["in_norm"]), _ptr(x), c.eps), "rmsnorm")
+            gemm(0, c.qkv_dim, H, Lw["w_qkv"], x, qkv)
+            kc, vc = pre_k[li, b0 : b0 + n], pre_v[li, b0 : b0 + n]
+            check(
+                L.kvbp_qkv_rope_scatter(
+                    st, R, P, c.n_heads, Hkv, D, P, _ptr(qkv), c.qkv_dim, _ptr(Lw["b_qkv"]), _ptr(Lw["q_norm"]),
+                    _ptr(Lw["k_norm"]), c.eps, _ptr(self.inv_freq), _ptr(pos), _ptr(pos), _ptr(q), _ptr(kc), _ptr(vc),
+                    err,
+                ),
+                "qkv_rope_scatter",
+            )
+            for j in range(n):
+                lcol = torch.zeros(P, dtype=torch.float32, device=d) if need_scores else None
+                att[j * P : (j + 1) * P] = self._prefill_attention(q[j * P : (j + 1) * P], kc[j], vc[j], need_scores,
+                                                                    lcol)
+                if need_scores:
+                    torch.maximum(colmax[j], lcol, out=colmax[j])
+                    if li == 0 and self.prefill_head_seed is not None:
+                        self.prefill_head_seed[b0 + j].copy_(lcol)
+            gemm(0, H, c.n_heads * D, Lw["w_o"], att, o)
+            check(L.kvbp_add_rmsnorm(st, R, H, _ptr(h), _ptr(o), _ptr(Lw["post_norm"]), _ptr(x), c.eps), "rmsnorm")
+            gemm(2, 2 * c.ffn, H, Lw["w_gu"], x, act)
+            delta = o  # o is free again: the down projection lands there
+            gemm(0, H, c.ffn, Lw["w_down"], act, delta)
+        last = torch.arange(n, device=d) * P + (P - 1)
+        hl = h[last].contiguous()
+        dl = delta[last].contiguous()
+        xl = torch.empty_like(hl)
+        check(L.kvbp_add_rmsnorm(st, n, H, _ptr(hl), _ptr(dl), _ptr(self.final_norm), _ptr(xl), c.eps), "rmsnorm")
+        check(
+            L.kvbp_decode_gemm(st, 0, n, c.vocab, H, _ptr(self.lm_w), _ptr(xl), H, None, 0, None, c.eps,
+                               _ptr(self.logits[b0 : b0 + n]), c.vocab, None, self.splits["lm"], err),
+            "decode_gemm[lm]",
+        )
+        if need_scores:
+            scores[b0 : b0 + n] = colmax
 
     def _host_victims(self, retained_sorted: List[int], evict_count: int, step: int) -> List[int]:
         """One ``_maybe_evict`` policy call on the host (kv_coupled_generator.py:563-577):
