@@ -3,7 +3,7 @@ same op: out = bf16(X . W^T) with fp32 accumulation, W read from the packed layo
 
 Tolerance: the fp32 sum runs in another order (tensor-core K steps of 16 vs. the
 reference GEMM), so an output may land on the neighbouring bf16 value: >= 99 % of the
-elements bit-identical, the rest within 2 bf16 ulps.  The SwiGLU epilogue applies the
+elements bit-identical, the rest within 2 bf16 ulps (1e-4 absolute near zero).  The SwiGLU epilogue applies the
 reference's rounding points to the bf16 gate / up outputs (as the decode GEMM does)."""
 
 import pytest
@@ -21,11 +21,15 @@ def _lib():
 
 
 def _check(got, want):
+    """>= 99 % bit-identical; the rest within 2 bf16 ulps, or within 1e-4 absolute where the
+    sum cancels to a value far below its terms (outputs are O(1) here; the fp32 sum of
+    hundreds of O(0.02) terms carries ~1e-6 of absolute rounding, a large relative error
+    on a result near zero)."""
     got, want = got.float(), want.float()
     d = (got - want).abs()
-    ulp = torch.finfo(torch.bfloat16).eps * want.abs().clamp_min(1e-30)
+    ulp = torch.finfo(torch.bfloat16).eps * want.abs()
     assert (d == 0).float().mean().item() >= 0.99, (d == 0).float().mean().item()
-    assert (d <= 2 * ulp + 1e-30).all(), d.max().item()
+    assert (d <= 2 * ulp + 1e-4).all(), d.max().item()
 
 
 def _run(epi, x, wp, N, out_cols):
