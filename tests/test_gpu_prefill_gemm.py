@@ -56,18 +56,28 @@ def test_prefill_gemm_plain(M, N, K):
 
 @pytest.mark.parametrize("M,F,K", [(200, 1024, 512), (1024, 2816, 1024), (777, 18944 // 4, 3584)])
 def test_prefill_gemm_swiglu(M, F, K):
+    """The SwiGLU epilogue applies act = bf16(bf16(g * bf16(sigmoid(g))) * u) to the kernel's own
+    bf16 gate / up outputs: against the plain epilogue's outputs of the same packed weights
+    (same accumulation order) finished in torch it is bit-identical up to the sigmoid's
+    rounding (torch's exp vs. CUDA's expf: one bf16 ulp, rarely).  The plain outputs
+    themselves are held to the fp32 reference above."""
+    from kvcacheboundaryprotection_b200.engine import deinterleave_gate_up
+
     g = torch.Generator(device="cuda").manual_seed(M + F)
     x = torch.randn(M, K, generator=g, device="cuda").to(torch.bfloat16)
     wg = (torch.randn(F, K, generator=g, device="cuda") * 0.05).to(torch.bfloat16)
     wu = (torch.randn(F, K, generator=g, device="cuda") * 0.05).to(torch.bfloat16)
     wp = pack_weight(interleave_gate_up(wg, wu))
     out = _run(2, x, wp, 2 * F, F)
-    gate = (x.float() @ wg.float().t()).to(torch.bfloat16).float()
-    up = (x.float() @ wu.float().t()).to(torch.bfloat16).float()
+    gu = deinterleave_gate_up(_run(0, x, wp, 2 * F, 2 * F)).float()
+    gate, up = gu[:, :F], gu[:, F:]
+    _check(torch.cat([gate, up], 1).to(torch.bfloat16),
+           torch.cat([x.float() @ wg.float().t(), x.float() @ wu.float().t()], 1).to(torch.bfloat16))
     sig = (1.0 / (1.0 + torch.exp(-gate))).to(torch.bfloat16).float()
-    want = ((gate * sig).to(torch.bfloat16).float() * up).to(torch.bfloat16)
-    # a 1-ulp difference of g or u moves the product by about an ulp: the same budget
-    _check(out, want)
+    want = ((gate * sig).to(torch.bfloat16).float() * up).to(torch.bfloat16).float()
+    d = (out.float() - want).abs()
+    assert (d == 0).float().mean().item() >= 0.999
+    assert (d <= torch.finfo(torch.bfloat16).eps * want.abs() * 2 + 1e-6).all(), d.max().item()
 
 
 def test_prefill_gemm_rejects_bad_shapes():
