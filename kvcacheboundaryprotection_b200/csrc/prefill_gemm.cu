@@ -100,7 +100,6 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
   const int m0 = tm * kBM;
   const int kc = a.K / 128;      // packed k-blocks
   const int nk = a.K / kBK;      // 64-wide stages
-  const int nblk = a.N / 128;
 
   if (tid == 0) {
     for (int s = 0; s < kStages; ++s) {
