@@ -86,6 +86,8 @@ def parse():
                     help="run only the decode attention microbench at the workload's shape and exit")
     ap.add_argument("--micro-prefill", type=int, default=None, metavar="PROMPT_LEN",
                     help="run only the tcgen05 prefill attention microbench at this prompt length and exit")
+    ap.add_argument("--micro-prefill-gemm", type=int, default=None, metavar="ROWS",
+                    help="run only the tcgen05 prefill projection GEMM microbench over this many prompt rows and exit")
     ap.add_argument("--micro-gemm", action="store_true",
                     help="run only the decode GEMM microbench (one layer's projections + lm_head) and exit")
     return ap.parse_args()
@@ -916,6 +918,67 @@ def run_prefill_microbench(preset="qwen2.5-7b", P=8192, iters=3):
             "frac_executed": round(2 * alg / (ms * 1e-3) / 1e12 / tf, 4)}
 
 
+def run_prefill_gemm_microbench(preset="qwen2.5-7b", R=16384, iters=5):
+    """Operator microbench of kvbp_prefill_gemm (tcgen05) on one decoder layer's prefill
+    projections of ``preset`` over R prompt rows: q/k/v, o, gate/up (SwiGLU epilogue) and
+    down, each as 3 warm-up + ``iters`` timed launches (CUDA events, median), then the same
+    product through torch.mm (cuBLAS, row-major weights, plain output) for context.  The
+    launch order is fixed (per shape: own launches, then cuBLAS), so an ncu capture can
+    select a shape by its launch index."""
+    import torch
+
+    from kvcacheboundaryprotection_b200 import capi
+    from kvcacheboundaryprotection_b200.config import get_config
+    from kvcacheboundaryprotection_b200.engine import pack_weight
+
+    L = capi.lib()
+    cfg = get_config(preset)
+    dev = torch.device("cuda")
+    _, bf16_peak, _ = peaks()
+    H, F = cfg.hidden, cfg.ffn
+    qkv_n = (cfg.n_heads + 2 * cfg.n_kv_heads) * cfg.head_dim
+    shapes = (("qkv", qkv_n, H, 0), ("o", H, cfg.n_heads * cfg.head_dim, 0), ("gate_up", 2 * F, H, 2), ("down", H, F, 0))
+    g = torch.Generator(device=dev).manual_seed(0)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    rows = []
+    for name, N, K, epi in shapes:
+        x = torch.randn(R, K, generator=g, device=dev).to(torch.bfloat16)
+        w = (torch.randn(N, K, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        wp = pack_weight(w)
+        oc = N // 2 if epi == 2 else N
+        out = torch.empty(R, oc, dtype=torch.bfloat16, device=dev)
+        ref = torch.empty(R, N, dtype=torch.bfloat16, device=dev)
+
+        def own():
+            capi.check(L.kvbp_prefill_gemm(torch.cuda.current_stream().cuda_stream, epi, R, N, K, wp.data_ptr(),
+                                           x.data_ptr(), K, out.data_ptr(), oc, err.data_ptr()), "prefill_gemm")
+
+        def cublas():
+            torch.mm(x, w.t(), out=ref)
+
+        row = {"shape": name, "N": N, "K": K, "epilogue": "swiglu" if epi == 2 else "plain"}
+        for tag, fn in (("own", own), ("cublas", cublas)):
+            for _ in range(3):
+                fn()
+            torch.cuda.synchronize()
+            ts = []
+            for _ in range(iters):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                fn()
+                e1.record()
+                torch.cuda.synchronize()
+                ts.append(e0.elapsed_time(e1) * 1000)
+            us = sorted(ts)[len(ts) // 2]
+            tf = 2 * R * N * K / us / 1e6
+            row[tag] = {"us": round(us, 1), "tflops": round(tf, 1), "frac": round(tf / bf16_peak, 4)}
+        if int(err.item()):
+            raise RuntimeError("device error in prefill GEMM microbench: " + str(capi.decode_dev_errors(int(err.item()))))
+        rows.append(row)
+        del x, w, wp, out, ref
+    return {"rows_R": R, "peak_tflops": bf16_peak, "rows": rows}
+
+
 def run_gemm_microbench(preset="qwen2.5-7b", M=16, iters=10, sweep=False):
     """Operator microbench of kvbp_decode_gemm on one decoder layer's projections (and the
     lm_head) of ``preset``: M activation rows against bf16 weights streamed from HBM, each
@@ -1211,6 +1274,12 @@ def main():
 
         kbuild.build()
         print(json.dumps(run_prefill_microbench(WORKLOADS[a.workload][0], a.micro_prefill)), flush=True)
+        return
+    if a.micro_prefill_gemm is not None:
+        from kvcacheboundaryprotection_b200 import build as kbuild
+
+        kbuild.build()
+        print(json.dumps(run_prefill_gemm_microbench(WORKLOADS[a.workload][0], a.micro_prefill_gemm)), flush=True)
         return
     if a.micro_gemm:
         from kvcacheboundaryprotection_b200 import build as kbuild
