@@ -463,10 +463,11 @@ def tp_check(a, workload, rank, world, local_rank, eng, steps=8):
 
 
 def launches_per_step(cfg, tp: bool = False) -> int:
-    # own kernels: append_evict, embed, row_sumsq, per layer (q/k/v GEMM, attention, o GEMM,
-    # gate/up GEMM, down GEMM), lm_head GEMM, argmax (tensor parallel: argmax_key +
-    # key_to_token), score_update; NCCL's own kernels are not counted
-    return 1 + 1 + 1 + cfg.n_layers * 5 + 1 + (2 if tp else 1) + 1
+    # own kernels: update_append_evict (the previous step's score update runs in it), embed,
+    # row_sumsq, per layer (q/k/v GEMM, attention, o GEMM, gate/up GEMM, down GEMM),
+    # lm_head GEMM, argmax; tensor parallel: append_evict, argmax_key + key_to_token and a
+    # separate score_update; NCCL's own kernels are not counted
+    return 1 + 1 + 1 + cfg.n_layers * 5 + 1 + (2 if tp else 1) + (1 if tp else 0)
 
 
 def algorithmic_attn_bytes(B, Hq, Hkv, valid_slots):
@@ -603,15 +604,16 @@ NCU_TRAFFIC = {
 
 
 # ------------------------------------------------------------------------ microbench
-def run_microbench(cap_list=(256, 1024, 4096), policies=("lru", "attention-mass"), fracs=(0.10, 0.05), iters=20):
+def run_microbench(cap_list=(256, 1024, 4096), policies=("lru", "attention-mass"), fracs=(0.10, 0.05), iters=16):
     """Operator microbench: one fused decode attention + eviction step for 64 sequences,
-    8 kv heads x group 4, head_dim 128.  The step is two launches: kvbp_append_evict (slot
-    append + cadence protection / top-k / hard cap) and kvbp_decode_attn_score_update
-    (scatter of the new K/V row into its slot, attention + per-slot score, and the score
-    update by the last CTA of each sequence); q and the new K/V rows are the operator's
-    inputs.  "unfused_step_us" times the same step as four launches (append, q/k RoPE +
-    K/V scatter, attention, score update).  Each timed step is preceded by an L2 flush (a
-    512 MB read, which leaves no dirty lines behind) outside the CUDA-event pair."""
+    8 kv heads x group 4, head_dim 128.  The step is two launches: kvbp_update_append_evict
+    (the previous step's score update, then slot append + cadence protection / top-k / hard
+    cap) and kvbp_decode_attn_score_update without state (scatter of the new K/V row into
+    its slot, attention + per-slot score); q and the new K/V rows are the operator's inputs,
+    and every step applies the previous step's scores (steady state).  "unfused_step_us"
+    times the same step as four launches (append, q/k RoPE + K/V scatter, attention, score
+    update).  Each timed step is preceded by an L2 flush (a 512 MB read, which leaves no
+    dirty lines behind) outside the CUDA-event pair."""
     import ctypes as C_
 
     import torch
@@ -646,12 +648,12 @@ def run_microbench(cap_list=(256, 1024, 4096), policies=("lru", "attention-mass"
                 qf = (torch.randn(B, Hq, D, generator=g, device=dev) / math.sqrt(D)).to(torch.bfloat16)
                 knew = torch.randn(B, Hkv, D, generator=g, device=dev).to(torch.bfloat16)
                 vnew = torch.randn(B, Hkv, D, generator=g, device=dev).to(torch.bfloat16)
-                counter = torch.zeros(B, dtype=torch.int32, device=dev)
+                pending = torch.ones(B, dtype=torch.int32, device=dev)
 
                 def fused_step():
                     s = torch.cuda.current_stream().cuda_stream
-                    check(L.kvbp_append_evict(s, C_.byref(st["state"]), C_.byref(cfg), st["seq_step"].data_ptr(), st["next_pos"].data_ptr(), st["cur_pos"].data_ptr(), st["write_slot"].data_ptr(), None, None, 0, st["evlog"].data_ptr(), st["evcount"].data_ptr(), st["evcap"], None, err.data_ptr()), "append")
-                    check(L.kvbp_decode_attn_score_update(s, B, Hq, Hkv, D, S, qf.data_ptr(), knew.data_ptr(), vnew.data_ptr(), kc.data_ptr(), vc.data_ptr(), st["slot_pos"].data_ptr(), st["write_slot"].data_ptr(), attn_out.data_ptr(), st["step_score"].data_ptr(), C_.byref(st["state"]), st["seq_step"].data_ptr(), counter.data_ptr(), err.data_ptr()), "attn_update")
+                    check(L.kvbp_update_append_evict(s, C_.byref(st["state"]), C_.byref(cfg), st["seq_step"].data_ptr(), st["next_pos"].data_ptr(), st["cur_pos"].data_ptr(), st["write_slot"].data_ptr(), None, None, 0, st["evlog"].data_ptr(), st["evcount"].data_ptr(), st["evcap"], None, st["step_score"].data_ptr(), pending.data_ptr(), err.data_ptr()), "update_append")
+                    check(L.kvbp_decode_attn_score_update(s, B, Hq, Hkv, D, S, qf.data_ptr(), knew.data_ptr(), vnew.data_ptr(), kc.data_ptr(), vc.data_ptr(), st["slot_pos"].data_ptr(), st["write_slot"].data_ptr(), attn_out.data_ptr(), st["step_score"].data_ptr(), None, None, None, err.data_ptr()), "attn_scatter")
 
                 def step(ev=None):
                     s = torch.cuda.current_stream().cuda_stream
@@ -679,6 +681,8 @@ def run_microbench(cap_list=(256, 1024, 4096), policies=("lru", "attention-mass"
                     return gr_
 
                 def timed_replays(gr_):
+                    gr_.replay()  # the first replay of a graph pays its upload: not a step's time
+                    torch.cuda.synchronize()
                     t = 0.0
                     for it in range(iters):
                         flush.sum()
@@ -695,17 +699,14 @@ def run_microbench(cap_list=(256, 1024, 4096), policies=("lru", "attention-mass"
                 del gr
                 gr = graph_of(step)
                 tot_unfused = timed_replays(gr)
-                attn_only = 0.0
-                # attention kernel alone (same L2 discipline)
-                s_ = torch.cuda.current_stream().cuda_stream
-                for it in range(iters):
-                    flush.sum()
-                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                    e0.record()
-                    check(L.kvbp_decode_attn_score(s_, B, Hq, Hkv, D, S, q.data_ptr(), kc.data_ptr(), vc.data_ptr(), st["slot_pos"].data_ptr(), st["write_slot"].data_ptr(), attn_out.data_ptr(), st["step_score"].data_ptr(), err.data_ptr()), "attn")
-                    e1.record()
-                    torch.cuda.synchronize()
-                    attn_only += e0.elapsed_time(e1)
+                del gr
+
+                def attn_alone():
+                    check(L.kvbp_decode_attn_score(torch.cuda.current_stream().cuda_stream, B, Hq, Hkv, D, S, q.data_ptr(), kc.data_ptr(), vc.data_ptr(), st["slot_pos"].data_ptr(), st["write_slot"].data_ptr(), attn_out.data_ptr(), st["step_score"].data_ptr(), err.data_ptr()), "attn")
+
+                # attention kernel alone (a one-launch graph, same L2 discipline)
+                gr = graph_of(attn_alone)
+                attn_only = timed_replays(gr)
                 # the step's kernels one by one (eager, events between launches), over one
                 # eviction cycle of E steps
                 per = [0.0] * 4
@@ -1260,7 +1261,7 @@ def main():
         from kvcacheboundaryprotection_b200 import build as kbuild
 
         kbuild.build()
-        print(json.dumps(run_microbench(cap_list=(a.micro_only,), policies=("lru",), fracs=(0.10,), iters=5)), flush=True)
+        print(json.dumps(run_microbench(cap_list=(a.micro_only,), policies=("lru",), fracs=(0.10,), iters=16)), flush=True)
         return
     if a.micro_attn:
         from kvcacheboundaryprotection_b200 import build as kbuild

@@ -121,7 +121,9 @@ int kvbp_decode_attn_score(kvbp_stream_t stream, int32_t B, int32_t Hq, int32_t 
  *    attn / max_attn / cumul / last_access / access_count of its valid slots from the
  *    completed step_score (pass the layer that completes the max over layers: the last)
  *    and clears step_score, as kvbp_score_update does;
- *  - seq_counter [B] int32, all zero before the first call; the kernel leaves it zero. */
+ *  - seq_counter [B] int32, all zero before the first call; the kernel leaves it zero.
+ * st == NULL (seq_step, seq_counter ignored): attention + scatter only, for callers that
+ * run the score update at the start of the next step (kvbp_update_append_evict). */
 int kvbp_decode_attn_score_update(kvbp_stream_t stream, int32_t B, int32_t Hq, int32_t Hkv, int32_t head_dim,
                                   int32_t S, const void* q, const void* k_new, const void* v_new, void* kcache,
                                   void* vcache, const int32_t* slot_pos, const int32_t* write_slot, void* out,
@@ -172,6 +174,20 @@ int kvbp_append_evict(kvbp_stream_t stream, const kvbp_state* st, const kvbp_evi
                       int32_t* next_pos, int32_t* cur_pos, int32_t* write_slot, const int32_t* tokens,
                       int32_t* token_log, int32_t log_steps, int32_t* evlog, int32_t* evcount, int32_t evcap,
                       int32_t* retained_log, int32_t* dev_err);
+
+/* K2 + K3 in one launch: the previous step's score update (as kvbp_score_update, with
+ * last_access = that step, seq_step[b] on entry) runs first, then this step's
+ * kvbp_append_evict -- the reference's order (kv_coupled_generator.py:504-516 at the end
+ * of step t, then :350-364 and _maybe_evict :549-604 of step t + 1).  step_score [B][S]
+ * holds the scores the previous step's layers max-accumulated; the kernel applies them
+ * where pending[b] != 0, clears step_score for this step's layers and sets pending[b] = 1.
+ * pending [B] int32 is 0 before the first decode step after prefill (no scores yet); after
+ * the last step, kvbp_score_update applies the scores still pending. */
+int kvbp_update_append_evict(kvbp_stream_t stream, const kvbp_state* st, const kvbp_evict_cfg* cfg,
+                             int32_t* seq_step, int32_t* next_pos, int32_t* cur_pos, int32_t* write_slot,
+                             const int32_t* tokens, int32_t* token_log, int32_t log_steps, int32_t* evlog,
+                             int32_t* evcount, int32_t evcap, int32_t* retained_log, float* step_score,
+                             int32_t* pending, int32_t* dev_err);
 
 /* K3 with the victims chosen on the host -- the random policy's path.
  * RandomEvictionPolicy (src/counterfact_kv_eviction/policies.py:1553-1582) draws its

@@ -91,6 +91,10 @@ SIGNATURES = {
         C.c_int,
         [P, C.POINTER(State), C.POINTER(EvictCfg), P, P, P, P, P, P, I32, P, P, I32, P, P],
     ),
+    "kvbp_update_append_evict": (
+        C.c_int,
+        [P, C.POINTER(State), C.POINTER(EvictCfg), P, P, P, P, P, P, I32, P, P, I32, P, P, P, P],
+    ),
     "kvbp_append_evict_listed": (
         C.c_int,
         [P, C.POINTER(State), C.POINTER(EvictCfg), P, P, P, P, P, P, I32, P, P, I32, P, P, P, I32, I32, P],
@@ -131,6 +135,7 @@ SIGNATURES = {
 }
 EXTRA_SIGNATURES = {
     "kvbp_decode_attn_score_cs": (C.c_int, [P, I32, I32, I32, I32, I32, P, P, P, P, P, P, P, P, I32]),
+    "kvbp_decode_attn_score_cfg": (C.c_int, [P, I32, I32, I32, I32, I32, P, P, P, P, P, P, P, P, I32, I32]),
 }
 
 _LIB: Optional[C.CDLL] = None

@@ -329,6 +329,11 @@ struct AppendArgs {
   const int* ext_n;
   int ext_stride;
   int no_hardcap;  // listed victims only: skip the hard-capacity guardrail (per-head mode has none)
+  // previous step's score update run first (null upd_score: none): the scores the layers of
+  // that step max-accumulated into upd_score [B][S]; upd_pending [B] = 1 once a step's
+  // scores are pending (the kernel sets it, the first decode step after prefill has 0)
+  float* upd_score;
+  int* upd_pending;
 };
 
 __device__ void log_victim(const AppendArgs& a, int b, int pos) {
@@ -357,6 +362,70 @@ __global__ void __launch_bounds__(kEvictThreads) append_evict_kernel(AppendArgs 
   __syncthreads();
   const int step = sh[0], pos = sh[1];
 
+  if (a.upd_score) {
+    // ---- the previous step's score update (kv_coupled_generator.py:504-516) over the
+    // slots that step attended, before this step's append and eviction, as the reference
+    // orders them; the same arithmetic as score_update_kernel --------------------------
+    // (kU slots per thread with their loads in flight together: one block per sequence
+    // walks S slots, and a loop of dependent loads would pay the memory latency per slot)
+    constexpr int kU = 8;
+    float* sc = a.upd_score + static_cast<size_t>(b) * S;
+    if (a.upd_pending[b]) {
+      __shared__ float red_f[32];
+      float mx = 0.f;
+      for (int i0 = tid; i0 < S; i0 += kU * kEvictThreads) {
+        float v[kU];
+        int ps[kU];
+#pragma unroll
+        for (int k = 0; k < kU; ++k) {
+          const int i = i0 + k * kEvictThreads;
+          ps[k] = i < S ? s.slot_pos[i] : -1;
+          v[k] = i < S ? sc[i] : 0.f;
+        }
+#pragma unroll
+        for (int k = 0; k < kU; ++k)
+          if (ps[k] >= 0) mx = fmaxf(mx, v[k]);
+      }
+      mx = block_max_float(mx, red_f);
+      const float thr = static_cast<float>(0.05 * static_cast<double>(mx));
+      const int prev = step - 1;
+      for (int i0 = tid; i0 < S; i0 += kU * kEvictThreads) {
+        float ks[kU], ma[kU];
+        double cu[kU];
+        int ps[kU], cn[kU];
+#pragma unroll
+        for (int k = 0; k < kU; ++k) {
+          const int i = i0 + k * kEvictThreads;
+          const bool in = i < S;
+          ps[k] = in ? s.slot_pos[i] : -1;
+          ks[k] = in ? sc[i] : 0.f;
+          ma[k] = in ? s.max_attn[i] : 0.f;
+          cu[k] = in ? s.cumul[i] : 0.0;
+          cn[k] = in ? s.access_count[i] : 0;
+        }
+#pragma unroll
+        for (int k = 0; k < kU; ++k) {
+          const int i = i0 + k * kEvictThreads;
+          if (i >= S) continue;
+          if (ps[k] >= 0) {
+            if (ks[k] != ks[k]) set_err(a.err, kErrNanScore);
+            s.attn[i] = ks[k];
+            s.max_attn[i] = fmaxf(ma[k], ks[k]);
+            s.cumul[i] = __dadd_rn(cu[k], static_cast<double>(ks[k]));
+            if (ks[k] > thr) {
+              s.last_access[i] = prev;
+              s.access_count[i] = cn[k] + 1;
+            }
+          }
+          sc[i] = 0.f;  // this step's layers accumulate from zero
+        }
+      }
+    } else {
+      for (int i = tid; i < S; i += kEvictThreads) sc[i] = 0.f;
+    }
+    __syncthreads();
+  }
+
   // lowest free slot
   int mine = 0x7fffffff;
   for (int i = tid; i < S; i += kEvictThreads)
@@ -372,6 +441,7 @@ __global__ void __launch_bounds__(kEvictThreads) append_evict_kernel(AppendArgs 
       a.cur_pos[b] = pos;
       a.seq_step[b] = step;
       a.next_pos[b] = pos + 1;
+      if (a.upd_score) a.upd_pending[b] = 1;
     }
     return;
   }
@@ -558,6 +628,7 @@ __global__ void __launch_bounds__(kEvictThreads) append_evict_kernel(AppendArgs 
   }
   __syncthreads();
   if (tid == 0) a.write_slot[b] = (s.slot_pos[slot] == pos) ? slot : -1;
+  if (tid == 0 && a.upd_score) a.upd_pending[b] = 1;  // this step's scores are applied by the next call
 }
 
 // ------------------------------------------------------------------------------------
@@ -803,6 +874,7 @@ int append_evict(cudaStream_t stream, const AppendArgs& a) {
   if (a.st.S > kEvictThreads * kMaxPerThread)
     return fail(kStatusUnsupported, "append_evict: %d slots exceed %d", a.st.S, kEvictThreads * kMaxPerThread);
   if (a.n_prefix < 0 || a.n_suffix < 0) return fail(kStatusArg, "append_evict: negative protection size");
+  if (a.upd_score && !a.upd_pending) return fail(kStatusArg, "update_append_evict: pending flags are required");
   const int smem = a.st.S * 4;
   static int configured = 0;
   if (smem > 48 * 1024 && smem > configured) {
@@ -885,9 +957,11 @@ static int append_evict_common(kvbp_stream_t stream, const kvbp_state* st, const
                                const int32_t* tokens, int32_t* token_log, int32_t log_steps, int32_t* evlog,
                                int32_t* evcount, int32_t evcap, int32_t* retained_log, const int32_t* victim_pos,
                                const int32_t* victim_count, int32_t victim_stride, int32_t flags,
-                               int32_t* dev_err) {
+                               int32_t* dev_err, float* step_score = nullptr, int32_t* pending = nullptr) {
   if (!st || !cfg) return kvbp::fail(kvbp::kStatusArg, "append_evict: null state/config");
   kvbp::AppendArgs a{};
+  a.upd_score = step_score;
+  a.upd_pending = pending;
   a.ext_pos = victim_pos;
   a.ext_n = victim_count;
   a.ext_stride = victim_stride;
@@ -921,6 +995,18 @@ int kvbp_append_evict(kvbp_stream_t stream, const kvbp_state* st, const kvbp_evi
                       int32_t* retained_log, int32_t* dev_err) {
   return append_evict_common(stream, st, cfg, seq_step, next_pos, cur_pos, write_slot, tokens, token_log, log_steps,
                              evlog, evcount, evcap, retained_log, nullptr, nullptr, 0, 0, dev_err);
+}
+
+int kvbp_update_append_evict(kvbp_stream_t stream, const kvbp_state* st, const kvbp_evict_cfg* cfg,
+                             int32_t* seq_step, int32_t* next_pos, int32_t* cur_pos, int32_t* write_slot,
+                             const int32_t* tokens, int32_t* token_log, int32_t log_steps, int32_t* evlog,
+                             int32_t* evcount, int32_t evcap, int32_t* retained_log, float* step_score,
+                             int32_t* pending, int32_t* dev_err) {
+  if (!step_score || !pending)
+    return kvbp::fail(kvbp::kStatusArg, "update_append_evict: step_score and pending are required");
+  return append_evict_common(stream, st, cfg, seq_step, next_pos, cur_pos, write_slot, tokens, token_log, log_steps,
+                             evlog, evcount, evcap, retained_log, nullptr, nullptr, 0, 0, dev_err, step_score,
+                             pending);
 }
 
 int kvbp_append_evict_listed(kvbp_stream_t stream, const kvbp_state* st, const kvbp_evict_cfg* cfg,

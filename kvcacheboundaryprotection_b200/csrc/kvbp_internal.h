@@ -64,7 +64,7 @@ struct AttnExtra {
 };
 int decode_attn_score(cudaStream_t stream, int B, int Hq, int Hkv, int D, int S, const void* q, const void* kcache,
                       const void* vcache, const int* slot_pos, const int* write_slot, void* out, float* step_score,
-                      int* err, int cluster_override, const AttnExtra& extra);
+                      int* err, int cluster_override, const AttnExtra& extra, int persist_override = 0);
 
 int demote_int8(cudaStream_t st, void* kc, void* vc, int layers, int B, int Hkv, int S, const int* slots, int stride,
                 const int* counts, int* err);

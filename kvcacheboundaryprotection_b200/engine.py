@@ -10,7 +10,8 @@
 
 One decode step is::
 
-    kvbp_append_evict   new position -> lowest free slot; cadence eviction
+    kvbp_update_append_evict   the previous step's score update, then the new position
+                               -> lowest free slot; cadence eviction
     kvbp_embed
     kvbp_row_sumsq
     L x [ kvbp_decode_qkv_gemm   (RMSNorm prologue; bias, q/k norm, RoPE, K/V slot store)
@@ -19,14 +20,15 @@ One decode step is::
           kvbp_decode_gemm gu    (RMSNorm prologue, SwiGLU epilogue)
           kvbp_decode_gemm down  (residual epilogue) ]
     kvbp_decode_gemm lm_head (final RMSNorm prologue), kvbp_argmax
-    kvbp_score_update
 
+(the host-selected and per-KV-head policies and the tensor-parallel engine append with
+their own kernels and end the step with kvbp_score_update instead).
 Every step-dependent value (step counter, positions, slots) lives on the device, so
 one captured CUDA graph replays every step.  The decode GEMMs are this package's
 weight-streaming sm_100a kernels over packed weights (``gemm="kvbp"``, the default);
 ``gemm="cublas"`` runs them as torch.mm with bf16 output and float32 accumulation,
-with standalone norm / RoPE / SwiGLU kernels around them.  The prefill projections are
-cuBLAS either way.
+with standalone norm / RoPE / SwiGLU kernels around them.  The prefill projections run
+on the tcgen05 prefill GEMM (``gemm="kvbp"``) or cuBLAS.
 
 The reference computes the same step in ``KVCoupledQwen35Generator`` (host loop,
 ``src/counterfact_kv_eviction/kv_coupled_generator.py:336-516``) around
@@ -284,6 +286,8 @@ class CappedKVEngine:
         self.posmap = z(B, self.W, dt=torch.int32)
         self.step_score = z(B, S, dt=f32)
         self.seq_counter = z(B)  # arrivals per sequence of the fused score update (zero between launches)
+        self.upd_pending = z(B)  # 1 while a forwarded step's scores await the next append's update
+        self._forwarded = False  # the last launched step forwarded (its scores are pending)
         self.seq_step = z(B)
         self.next_pos = z(B)
         self.cur_pos = z(B)
@@ -580,6 +584,8 @@ class CappedKVEngine:
             )
         self.gather_src = torch.empty(self.B, self.S, dtype=torch.int32, device=self.dev)
         self.retained_log.zero_()
+        self.upd_pending.zero_()  # no forwarded decode step yet
+        self._forwarded = False
         check(
             L.kvbp_prefill_compact(
                 st, capi.C.byref(self._state), P, self.ev.capacity, nvict.value, _ptr(victim), _ptr(scores),
@@ -622,11 +628,23 @@ class CappedKVEngine:
 
     # ------------------------------------------------------------------ decode
     def _append_evict(self) -> None:
+        self._forwarded = False  # the update kernel consumes the pending scores (deferred mode)
         if self.per_head:
             self._append_evict_per_head()
             return
         if self.host_policy is not None:
             self._append_evict_listed()
+            return
+        if self.deferred_score_update:
+            check(
+                lib().kvbp_update_append_evict(
+                    self.stream, capi.C.byref(self._state), capi.C.byref(self._cfg), _ptr(self.seq_step),
+                    _ptr(self.next_pos), _ptr(self.cur_pos), _ptr(self.write_slot), _ptr(self.tokens),
+                    _ptr(self.token_log), self.max_new, _ptr(self.evlog), _ptr(self.evcount), self.evcap,
+                    _ptr(self.retained_log), _ptr(self.step_score), _ptr(self.upd_pending), _ptr(self.dev_err),
+                ),
+                "update_append_evict",
+            )
             return
         check(
             lib().kvbp_append_evict(
@@ -793,6 +811,7 @@ class CappedKVEngine:
             self._forward_kvbp()
         else:
             self._forward_cublas()
+        self._forwarded = True
 
     def _forward_kvbp(self) -> None:
         """Forward with the own decode GEMMs: the RMSNorms ride in the GEMM prologues; the
@@ -822,23 +841,24 @@ class CappedKVEngine:
         self._gemm("lm", 0, c.vocab, H, self.lm_w, self.h, H, self.logits, c.vocab, self.final_norm, ss_in, n_in)
 
     @property
-    def fused_score_update(self) -> bool:
-        """The last layer's attention runs the per-step score update (no separate launch)."""
-        return not self.per_head and type(self) is CappedKVEngine
+    def deferred_score_update(self) -> bool:
+        """A step's score update runs at the start of the next step's append kernel
+        (kvbp_update_append_evict), so the step needs no launch of its own for it; the
+        scores of the last forwarded step stay in step_score until then
+        (``apply_pending_scores`` applies them without appending)."""
+        return not self.per_head and self.host_policy is None and type(self) is CappedKVEngine
+
+    def apply_pending_scores(self) -> None:
+        """Apply a forwarded step's scores that no append has consumed yet (deferred mode)."""
+        if not self.deferred_score_update or not self._forwarded:
+            return
+        check(lib().kvbp_score_update(self.stream, capi.C.byref(self._state), _ptr(self.seq_step),
+                                      _ptr(self.step_score), _ptr(self.dev_err)), "score_update")
+        self.upd_pending.zero_()
+        self._forwarded = False
 
     def _attention(self, li: int) -> None:
         c, L = self.cfg, lib()
-        if li == c.n_layers - 1 and self.fused_score_update:
-            check(
-                L.kvbp_decode_attn_score_update(
-                    self.stream, self.B, c.n_heads, c.n_kv_heads, c.head_dim, self.S, _ptr(self.q), None, None,
-                    _ptr(self.kc[li]), _ptr(self.vc[li]), _ptr(self.slot_pos), _ptr(self.write_slot),
-                    _ptr(self.attn_out), _ptr(self.step_score), capi.C.byref(self._state), _ptr(self.seq_step),
-                    _ptr(self.seq_counter), _ptr(self.dev_err),
-                ),
-                "decode_attn_score_update",
-            )
-            return
         if self.per_head:
             check(
                 L.kvbp_decode_attn_score_heads(
@@ -888,7 +908,7 @@ class CappedKVEngine:
     def _sample_and_score(self) -> None:
         L, st, c = lib(), self.stream, self.cfg
         check(L.kvbp_argmax(st, self.B, c.vocab, c.vocab, _ptr(self.logits), _ptr(self.tokens)), "argmax")
-        if not self.fused_score_update:
+        if not self.deferred_score_update:
             check(L.kvbp_score_update(st, capi.C.byref(self._state), _ptr(self.seq_step), _ptr(self.step_score), _ptr(self.dev_err)), "score_update")
         self._head_signal_update()
 
@@ -907,7 +927,7 @@ class CappedKVEngine:
             if sample:
                 self._sample_and_score()
             else:
-                if not self.fused_score_update:
+                if not self.deferred_score_update:
                     check(lib().kvbp_score_update(self.stream, capi.C.byref(self._state), _ptr(self.seq_step), _ptr(self.step_score), _ptr(self.dev_err)), "score_update")
                 self._head_signal_update()
 
@@ -937,6 +957,7 @@ class CappedKVEngine:
         """One decode step for steps 1..max_new-1 (append/evict, forward, sample, score)."""
         if use_graph and self.graph is not None:
             self.graph.replay()
+            self._forwarded = True
         else:
             self.decode_step_launches()
         self.step += 1

@@ -44,7 +44,7 @@ def torch_reference(q, kc, vc, slot_pos):
     return out, score
 
 
-def run_kernel(q, kc, vc, slot_pos, score_init=None, cluster=0):
+def run_kernel(q, kc, vc, slot_pos, score_init=None, cluster=0, persist=None):
     L = capi.lib()
     B, Hq, D = q.shape
     Hkv, S = kc.shape[1], kc.shape[2]
@@ -54,7 +54,9 @@ def run_kernel(q, kc, vc, slot_pos, score_init=None, cluster=0):
     st = torch.cuda.current_stream().cuda_stream
     args = (st, B, Hq, Hkv, D, S, q.data_ptr(), kc.data_ptr(), vc.data_ptr(), slot_pos.data_ptr(), None,
             out.data_ptr(), score.data_ptr(), err.data_ptr())
-    if cluster:
+    if persist is not None:
+        capi.check(L.kvbp_decode_attn_score_cfg(*args, cluster, persist), "attn")
+    elif cluster:
         capi.check(L.kvbp_decode_attn_score_cs(*args, cluster), "attn")
     else:
         capi.check(L.kvbp_decode_attn_score(*args), "attn")
@@ -254,3 +256,68 @@ def test_fused_scatter_and_score_update_equal_separate_launches(B, Hq, Hkv, S):
         assert not counter.any()
         knew, vnew = vnew, knew  # second call: other rows
         seq_step += 1
+
+
+# more (sequence, kv head) pairs than one wave of two CTAs per SM holds: the persistent
+# kernel (a single wave of clusters walking the pairs round-robin) is chosen by default; it
+# must be bit-identical to one cluster per pair at the same cluster size
+PERSIST_CASES = [
+    # B, Hq, Hkv, S, free fraction, cluster size
+    (64, 32, 8, 1032, 0.01, 1),  # operator microbench, capacity 1024
+    (64, 32, 8, 1032, 0.01, 4),
+    (64, 32, 8, 264, 0.05, 1),  # capacity 256 (one consumer group)
+    (64, 32, 8, 4104, 0.002, 4),  # capacity 4096
+    (64, 32, 8, 4104, 0.002, 3),  # uneven tile split over the cluster
+    (40, 16, 8, 520, 0.1, 2),  # group of 2
+    (75, 12, 4, 300, 0.1, 1),  # group of 3, 4 kv heads
+]
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,S,free,cs", PERSIST_CASES)
+def test_persistent_kernel_bit_identical_to_one_cluster_per_pair(B, Hq, Hkv, S, free, cs):
+    q, kc, vc, pos = make_case(B, Hq, Hkv, S, free, seed=S + B + cs)
+    init = torch.rand(B, S, device="cuda") * 1e-3  # step_score already holds earlier layers' maxima
+    init[pos < 0] = 0
+    out_p, score_p = run_kernel(q, kc, vc, pos, score_init=init, cluster=cs, persist=0)
+    out_1, score_1 = run_kernel(q, kc, vc, pos, score_init=init, cluster=cs, persist=-1)
+    assert torch.equal(out_p, out_1)
+    assert torch.equal(score_p, score_1)
+    # fewer clusters than one wave holds (each walks more pairs) gives the same results
+    out_f, score_f = run_kernel(q, kc, vc, pos, score_init=init, cluster=cs, persist=7)
+    assert torch.equal(out_f, out_1)
+    assert torch.equal(score_f, score_1)
+    if B <= 40:  # the fp32 reference loop is slow: check the smaller cases against it too
+        out0, score0 = run_kernel(q, kc, vc, pos)
+        ref_out, ref_score = torch_reference(q, kc, vc, pos)
+        assert_close(out0, score0, ref_out, ref_score, pos >= 0)
+
+
+def test_persistent_kernel_fused_scatter():
+    """The new K/V row stored by the persistent kernel (st == NULL: scatter only) equals the
+    row copied into the cache first and the plain kernel run on it."""
+    B, Hq, Hkv, S = 64, 32, 8, 1032
+    q, kc, vc, pos = make_case(B, Hq, Hkv, S, 0.01, seed=5)
+    g = torch.Generator(device="cuda").manual_seed(6)
+    knew = torch.randn(B, Hkv, 128, generator=g, device="cuda").to(torch.bfloat16)
+    vnew = torch.randn(B, Hkv, 128, generator=g, device="cuda").to(torch.bfloat16)
+    ws = torch.randint(0, S, (B,), generator=g, device="cuda").to(torch.int32)
+    bi = torch.arange(B, device="cuda")
+    pos[bi, ws.long()] = 10 ** 6 + bi.to(torch.int32)
+    kc_a, vc_a = kc.clone(), vc.clone()
+    kc_b, vc_b = kc.clone(), vc.clone()
+    kc_b[bi, :, ws.long()] = knew
+    vc_b[bi, :, ws.long()] = vnew
+    L = capi.lib()
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    out_a, sc_a = torch.empty_like(q), torch.zeros(B, S, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    capi.check(L.kvbp_decode_attn_score_update(st, B, Hq, Hkv, 128, S, q.data_ptr(), knew.data_ptr(), vnew.data_ptr(),
+                                               kc_a.data_ptr(), vc_a.data_ptr(), pos.data_ptr(), ws.data_ptr(),
+                                               out_a.data_ptr(), sc_a.data_ptr(), None, None, None, err.data_ptr()),
+               "attn_scatter")
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    out_b, sc_b = run_kernel(q, kc_b, vc_b, pos, cluster=1, persist=-1)
+    assert torch.equal(kc_a, kc_b) and torch.equal(vc_a, vc_b)
+    assert torch.equal(out_a.float(), out_b)
+    assert torch.equal(sc_a, sc_b)

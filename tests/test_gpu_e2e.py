@@ -91,9 +91,8 @@ def _run_forced(preset, policy, P, cap, N, max_new, seed=0):
             break
         eng._forward()
         sp = eng.slot_pos[0].cpu().numpy()
-        # the last layer's attention folds the score update in: the step's scores are then
-        # the slots' latest attention score (attn = ks for every retained slot)
-        got = (eng.attn_s if eng.fused_score_update else eng.step_score)[0].cpu().numpy()[sp >= 0]
+        # the step's per-slot scores (max over heads and layers), before any update applies them
+        got = eng.step_score[0].cpu().numpy()[sp >= 0]
         want = o.step_scores[s - 1][sp[sp >= 0]]
         stats["score_rel"].append(np.abs(got - want) / np.maximum(want, 1e-30))
         stats.setdefault("score_ok", []).append(bool((np.abs(got - want) <= 0.08 * want + 1e-3 * want.max()).all()))

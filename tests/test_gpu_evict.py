@@ -94,6 +94,12 @@ class Driver:
     def score_update(self):
         capi.check(self.L.kvbp_score_update(self.st, C.byref(self.state), self.seq_step.data_ptr(), self.step_score.data_ptr(), self.err.data_ptr()), "score_update")
 
+    def update_append_evict(self, pending):
+        capi.check(self.L.kvbp_update_append_evict(self.st, C.byref(self.state), C.byref(self.cfg), self.seq_step.data_ptr(), self.next_pos.data_ptr(), self.cur_pos.data_ptr(), self.write_slot.data_ptr(), self.tokens.data_ptr(), self.token_log.data_ptr(), self.max_new, self.evlog.data_ptr(), self.evcount.data_ptr(), self.evcap, self.retained_log.data_ptr(), self.step_score.data_ptr(), pending.data_ptr(), self.err.data_ptr()), "update_append_evict")
+
+    def metadata(self):
+        return [t.clone() for t in (self.slot_pos, self.ins, self.last, self.cnt, self.attn, self.maxa, self.cumul, self.pre, self.posmap, self.seq_step, self.next_pos, self.cur_pos, self.write_slot, self.evcount, self.evlog)]
+
 
 @pytest.fixture(scope="module", autouse=True)
 def _lib():
@@ -147,6 +153,49 @@ def test_eviction_kernels_match_reference_trace(case):
     n = int(D.evcount[0].item())
     assert D.evlog[0, :n].cpu().numpy().tolist() == case["positions_evicted"]
     assert [P] + D.retained_log[0].cpu().numpy().tolist() == case["retained_counts_by_step"]
+
+
+DEFERRED_CASES = [c for c in GLOBAL_CASES if c["policy"] != "random"]
+
+
+@pytest.mark.parametrize("case", DEFERRED_CASES, ids=[c["name"] for c in DEFERRED_CASES])
+def test_update_append_evict_equals_separate_update_then_append(case):
+    """kvbp_update_append_evict (the previous step's score update run at the start of the
+    next append) against the reference trace, and against kvbp_score_update at the end of
+    each step + kvbp_append_evict: every metadata array bit-identical after every step."""
+    P, cap, E, max_new = case["n_prompt"], case["capacity"], case["evict_every"], case["max_new_tokens"]
+    model = StubScoreModel(vocab=97, n_heads=4, n_kv_heads=2, n_layers=2, max_cache_len=P + max_new + 8, seed=case["seed"])
+    o = generate(model, _spec(case), case["prompt"], max_new, evict_every=E, n_kv_heads=case["n_kv_heads"], regime=case["regime"])
+    n_pre, n_suf = capi.protection_sizes(cap, *(case["protect"] or (0.0, 0.0))) if case["protect"] else (0, 0)
+    cfg = capi.EvictCfg(cap, E, capi.policy_id(case["policy"]), int(case["protect"] is not None), n_pre, n_suf, int(case["regime"] == "decode"))
+    S = slot_count(cap, E, max_new, case["regime"])
+    args = (1, S, (P + max_new + 2 + 31) // 32, P + max_new + 2, max_new, cfg)
+    A, Bd = Driver(*args), Driver(*args)  # A: deferred update; Bd: separate launches
+    pending = torch.zeros(1, dtype=torch.int32, device="cuda")
+    pre = o.meta.prefill[:P] if case["policy"] != "lru" else None
+    A.prefill(P, pre)
+    Bd.prefill(P, pre)
+    for s in range(1, max_new + 1):
+        A.update_append_evict(pending)
+        Bd.append_evict()
+        assert A.slot_pos[0].cpu().numpy().tolist() == o.slot_tables[s].tolist(), f"slot table after step {s}"
+        for x, y in zip(A.metadata(), Bd.metadata()):
+            assert torch.equal(x, y), f"state differs after step {s}"
+        assert int(pending.item()) == 1
+        if s == max_new:
+            break
+        ks = o.step_scores[s - 1]
+        sp = A.slot_pos[0].cpu().numpy()
+        sc = np.zeros(S, np.float32)
+        sc[sp >= 0] = ks[sp[sp >= 0]]
+        A.step_score[0].copy_(torch.from_numpy(sc))
+        Bd.step_score[0].copy_(torch.from_numpy(sc))
+        Bd.score_update()
+    torch.cuda.synchronize()
+    assert int(A.err.item()) == 0 and int(Bd.err.item()) == 0
+    n = int(A.evcount[0].item())
+    assert A.evlog[0, :n].cpu().numpy().tolist() == case["positions_evicted"]
+    assert [P] + A.retained_log[0].cpu().numpy().tolist() == case["retained_counts_by_step"]
 
 
 def test_step0_lru_string_order_at_1024():
