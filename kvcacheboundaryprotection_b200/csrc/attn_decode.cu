@@ -116,8 +116,9 @@ struct AttnArgs {
   float scale;     // bfloat16(1/sqrt(D)) as float
 };
 
-// X: the optional parts (per-head keep masks and scores, fused scatter, fused score
-// update) are compiled in; the plain kernel (X = false) carries none of their code.
+// X: the heavier optional parts (per-head keep masks and scores, fused score update) are
+// compiled in; the plain kernel (X = false) carries none of their code.  The fused scatter
+// (knew / vnew) is a runtime branch of both.
 template <int G, int GR, bool X>
 __global__ void __launch_bounds__(attn_threads(GR), kMinBlocks) decode_attn_score_kernel(const __grid_constant__ CUtensorMap kmap,
                                                                      const __grid_constant__ CUtensorMap vmap,
@@ -257,13 +258,19 @@ __global__ void __launch_bounds__(attn_threads(GR), kMinBlocks) decode_attn_scor
   const int wslot = early ? p.write_slot[b] : -1;  // row of this step's K/V (read after the wait)
 
   const int* spos_g = p.slot_pos + static_cast<size_t>(b) * S;
+  // slot positions of the warp's rows g and g + 8 of a tile (< 0: free slot), read one
+  // tile of the group ahead so that their latency overlaps the previous tile's math;
+  // lanes t == 0 keep them for the score pass
+  auto slot_of = [&](int uu, int r) { return t0 * kTile + uu * kTile + r0 + g + r < S ? spos_g[t0 * kTile + uu * kTile + r0 + g + r] : -1; };
+  int pa_next = grp < nt ? slot_of(grp, 0) : -1, pb_next = grp < nt ? slot_of(grp, 8) : -1;
   for (int u = grp; u < nt; u += GR) {
     const int st = u % kStages;
-    // slot positions of the warp's rows g and g + 8 of this tile (< 0: free slot), read
-    // while the tile is in flight; lanes t == 0 keep them for the score pass
     const int lta = u * kTile + r0 + g, ltb = lta + 8;
-    int pa = t0 * kTile + lta < S ? spos_g[t0 * kTile + lta] : -1;
-    int pb = t0 * kTile + ltb < S ? spos_g[t0 * kTile + ltb] : -1;
+    int pa = pa_next, pb = pb_next;
+    if (u + GR < nt) {
+      pa_next = slot_of(u + GR, 0);
+      pb_next = slot_of(u + GR, 8);
+    }
     if (X && p.head_keep) {  // a slot this kv head does not retain counts as free for it
       const uint8_t* hk = p.head_keep + static_cast<size_t>(pair) * S + t0 * kTile;
       if (pa >= 0 && !hk[lta]) pa = -1;
@@ -276,7 +283,7 @@ __global__ void __launch_bounds__(attn_threads(GR), kMinBlocks) decode_attn_scor
       ok_tile = false;
     }
     ok_tile = __all_sync(0xffffffffu, ok_tile);  // warp-uniform: the tile's mma/ldmatrix are warp-wide
-    if (ok_tile && (u < n_first || (X && p.knew)) && wslot >= 0 && wslot < S) {
+    if (ok_tile && (u < n_first || p.knew) && wslot >= 0 && wslot < S) {
       // a tile staged before the wait may hold a stale copy of this step's row (and with a
       // fused scatter every tile may): the warp that owns the row (rows r0..r0+15 of the
       // tile) writes it into the staged tile, K by lanes 0-15 and V by lanes 16-31, one
@@ -287,7 +294,7 @@ __global__ void __launch_bounds__(attn_threads(GR), kMinBlocks) decode_attn_scor
         const int half = lane >> 4, ch = lane & 15, box = ch >> 3, c = ch & 7;
         __nv_bfloat16* crow = const_cast<__nv_bfloat16*>(half ? p.vc : p.kc) + (static_cast<size_t>(pair) * S + wslot) * kD + ch * 8;
         uint4 v;
-        if (X && p.knew) {
+        if (p.knew) {
           v = __ldg(reinterpret_cast<const uint4*>((half ? p.vnew : p.knew) + static_cast<size_t>(pair) * kD + ch * 8));
           *reinterpret_cast<uint4*>(crow) = v;
         } else {
@@ -809,12 +816,18 @@ __global__ void __launch_bounds__(attn_threads(GR), kMinBlocks) decode_attn_pers
 #pragma unroll
     for (int m = 0; m < 8; ++m) oacc[m][0] = oacc[m][1] = oacc[m][2] = oacc[m][3] = 0.f;
 
+    // slot positions read one tile of the group ahead (their latency overlaps the math)
+    auto slot_of = [&](int uu, int r) { return t0 * kTile + uu * kTile + r0 + g + r < S ? spos_g[t0 * kTile + uu * kTile + r0 + g + r] : -1; };
+    int pa_next = grp < nt ? slot_of(grp, 0) : -1, pb_next = grp < nt ? slot_of(grp, 8) : -1;
     for (int u = grp; u < nt; u += GR) {
       const int gi = j * nt + u;
       const int st = gi % kStages;
       const int lta = u * kTile + r0 + g, ltb = lta + 8;  // local slot index within this CTA's range
-      const int pa = t0 * kTile + lta < S ? spos_g[t0 * kTile + lta] : -1;
-      const int pb = t0 * kTile + ltb < S ? spos_g[t0 * kTile + ltb] : -1;
+      const int pa = pa_next, pb = pb_next;
+      if (u + GR < nt) {
+        pa_next = slot_of(u + GR, 0);
+        pb_next = slot_of(u + GR, 8);
+      }
       bool ok_tile = !(*reinterpret_cast<volatile int*>(bad_flag));
       if (ok_tile && !mbar_wait_bounded(&full[st], (gi / kStages) & 1)) {
         set_err(p.err, kErrWaitTimeout);
@@ -1201,7 +1214,9 @@ static int choose_persist(int B, int Hkv, int G, int cs, int nloc_tiles, int gro
 template <int G, int GR>
 static cudaError_t launch_g(cudaStream_t stream, const CUtensorMap& km, const CUtensorMap& vm, const AttnArgs& a,
                             int smem) {
-  const bool x = a.head_keep || a.head_score || a.knew || a.upd_last;
+  // the fused scatter (knew / vnew) is a small runtime branch in both kernels; the heavier
+  // options (per-head retention, in-kernel score update) select the second kernel
+  const bool x = a.head_keep || a.head_score || a.upd_last;
   auto kern = x ? decode_attn_score_kernel<G, GR, true> : decode_attn_score_kernel<G, GR, false>;
   static int configured_smem[2] = {0, 0};  // per kernel (plain, with the optional parts)
   if (smem > configured_smem[x]) {

@@ -246,16 +246,20 @@ __device__ __forceinline__ uint32_t ord_i32(int v) { return static_cast<uint32_t
 // prefix sorts first).  Digits map to 1..10 in base 11, right-padded with 0 to
 // ten places; 11^10 < 2^35.
 __device__ __forceinline__ uint64_t lex_code(int pos) {
+  // the n decimal digits, most significant first, as base-11 digits (digit + 1) of a
+  // 10-digit number padded with zeros: sum_j (d_j + 1) * 11^(10 - n + j) over the digits
+  // d_j counted from the least significant -- formed without an indexed array (which
+  // lives in local memory)
   uint32_t v = static_cast<uint32_t>(pos);
-  int digits[10];
+  uint64_t code = 0, m = 1;
   int n = 0;
   do {
-    digits[n++] = static_cast<int>(v % 10u);
+    code += static_cast<uint64_t>(v % 10u + 1u) * m;
+    m *= 11ull;
     v /= 10u;
+    ++n;
   } while (v && n < 10);
-  uint64_t code = 0;
-#pragma unroll
-  for (int i = 0; i < 10; ++i) code = code * 11ull + (i < n ? static_cast<uint64_t>(digits[n - 1 - i] + 1) : 0ull);
+  for (int i = n; i < 10; ++i) code *= 11ull;
   return code;
 }
 

@@ -334,7 +334,8 @@ struct AppendArgs {
   // scores are pending (the kernel sets it, the first decode step after prefill has 0)
   float* upd_score;
   int* upd_pending;
-  int pm_smem;  // the position bitmap fits in shared memory after the victim list
+  int pm_smem;   // the position bitmap fits in shared memory after the victim list
+  int key_smem;  // byte offset of the [S] composite keys in shared memory (0: local memory)
 };
 
 __device__ void log_victim(const AppendArgs& a, int b, int pos) {
@@ -365,7 +366,7 @@ __global__ void __launch_bounds__(kEvictThreads) append_evict_kernel(AppendArgs 
   // together: one block per sequence walks S slots, and a loop of dependent loads would pay
   // the memory latency per slot) finds the lowest free slot and, for a pending score
   // update, the maximum of the previous step's scores over the retained slots
-  constexpr int kU = 8;
+  constexpr int kU = 10;  // one iteration per pass up to 5120 slots
   float* sc = a.upd_score ? a.upd_score + static_cast<size_t>(b) * S : nullptr;
   int mine = 0x7fffffff;
   float mx = 0.f;
@@ -593,36 +594,47 @@ __global__ void __launch_bounds__(kEvictThreads) append_evict_kernel(AppendArgs 
         }
       } else if (k > 0) {
         // k rounds of block argmin.  Each thread forms the keys of its slots once (the loads
-        // of four slots in flight together) and keeps them in local memory; a thread's
-        // minimum changes only when it owned a round's winner, and then it rescans its
-        // cached keys -- a rescan from global memory put every round's latency on the
-        // critical path (4.7 us per round at 4104 slots)
-        Key3 kc[kMaxPerThread];
+        // of kQ slots in flight together) and keeps them -- in shared memory when they fit
+        // (a local array of 512 threads does not stay in L1); a thread's minimum changes only
+        // when it owned a round's winner, and then it rescans its cached keys (a rescan from
+        // global memory put every round's latency on the critical path: 4.7 us per round at
+        // 4104 slots).  A warp-first top-k (each warp its k smallest, then one warp over the
+        // 16 x k candidates) measured slower than these block rounds.
+        Key3* kcs = a.key_smem ? reinterpret_cast<Key3*>(reinterpret_cast<uint8_t*>(s_vict) + a.key_smem) : nullptr;
+        Key3 kc_local[kMaxPerThread];
+        auto kc = [&](int j) -> Key3& { return kcs ? kcs[tid + j * kEvictThreads] : kc_local[j]; };
         uint32_t skip = 0;  // bit j: slot tid + j * kEvictThreads ineligible or already taken
         const int nj = tid < S ? (S - tid + kEvictThreads - 1) / kEvictThreads : 0;
-        for (int j0 = 0; j0 < nj; j0 += 4) {
-          int pp[4], ins[4], lst[4];
-          float at[4], ma[4], pr[4];
-          double cu[4];
+        // only the fields the policy's key reads are loaded
+        const int pol = a.policy;
+        const bool need_cu = pol == kPolicyH2OFaithful || pol == kPolicyH2O || pol == kPolicySnapKV || pol == kPolicyAdaKV;
+        const bool need_at = pol == kPolicyH2O || pol == kPolicySnapKV || pol == kPolicyQuest;
+        const bool need_ma = pol == kPolicyH2O || pol == kPolicySnapKV || pol == kPolicyAdaKV;
+        const bool need_pr = pol == kPolicySnapKVFaithful;
+        constexpr int kQ = 4;  // slots per batch of loads
+        for (int j0 = 0; j0 < nj; j0 += kQ) {
+          int pp[kQ], ins[kQ], lst[kQ];
+          float at[kQ], ma[kQ], pr[kQ];
+          double cu[kQ];
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
+          for (int q = 0; q < kQ; ++q) {
             const int j = j0 + q, i = tid + j * kEvictThreads;
             const bool in = j < nj;
             pp[q] = in ? s.slot_pos[i] : -1;
             ins[q] = in ? s.insert_step[i] : 0;
             lst[q] = in ? s.last_access[i] : 0;
-            at[q] = in ? s.attn[i] : 0.f;
-            ma[q] = in ? s.max_attn[i] : 0.f;
-            pr[q] = in ? s.prefill[i] : 0.f;
-            cu[q] = in ? s.cumul[i] : 0.0;
+            at[q] = (in && need_at) ? s.attn[i] : 0.f;
+            ma[q] = (in && need_ma) ? s.max_attn[i] : 0.f;
+            pr[q] = (in && need_pr) ? s.prefill[i] : 0.f;
+            cu[q] = (in && need_cu) ? s.cumul[i] : 0.0;
           }
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
+          for (int q = 0; q < kQ; ++q) {
             const int j = j0 + q;
             if (j >= nj) break;
             const bool e = pp[q] >= 0 && pp[q] >= thr_lo && pp[q] < thr_hi;
             if (e)
-              kc[j] = policy_key(a.policy, step, pp[q], ins[q], lst[q], at[q], ma[q], cu[q], pr[q], a.err);
+              kc(j) = policy_key(a.policy, step, pp[q], ins[q], lst[q], at[q], ma[q], cu[q], pr[q], a.err);
             else
               skip |= 1u << j;
           }
@@ -631,7 +643,7 @@ __global__ void __launch_bounds__(kEvictThreads) append_evict_kernel(AppendArgs 
           KeySlot best{key_max(), 0x7fffffff};
           for (int j = 0; j < nj; ++j) {
             if ((skip >> j) & 1u) continue;
-            const KeySlot c{kc[j], tid + j * kEvictThreads};
+            const KeySlot c{kc(j), tid + j * kEvictThreads};
             if (ks_less(c, best)) best = c;
           }
           return best;
@@ -942,6 +954,12 @@ int append_evict(cudaStream_t stream, const AppendArgs& a) {
   int smem = a.st.S * 4;
   aa.pm_smem = (a.st.S + a.st.W) * 4 <= 160 * 1024;
   if (aa.pm_smem) smem = (a.st.S + a.st.W) * 4;
+  aa.key_smem = 0;
+  const int key_off = (smem + 15) / 16 * 16;
+  if (key_off + a.st.S * static_cast<int>(sizeof(Key3)) <= 200 * 1024) {
+    aa.key_smem = key_off;
+    smem = key_off + a.st.S * static_cast<int>(sizeof(Key3));
+  }
   static int configured = 0;
   if (smem > 48 * 1024 && smem > configured) {
     cudaError_t e = cudaFuncSetAttribute(append_evict_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);

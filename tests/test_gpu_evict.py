@@ -333,3 +333,39 @@ def test_per_head_policies_match_reference_trace(case):
     ok = sp >= 0
     keep = eng.head_keep[0].cpu().numpy()[:, ok].astype(bool)
     assert (keep == o.head_keep[:, sp[ok]]).all()
+
+
+@pytest.mark.parametrize("policy,E", [("lru", 24), ("h2o_faithful", 24), ("adakv", 12), ("snapkv", 20)])
+def test_eviction_kernels_large_cadence_against_oracle(policy, E):
+    """Cadences that evict more than the warp-first top-k selects at once (k > 16) go
+    through the block-round selection; both must reproduce the oracle's victims (the
+    oracle generator is pinned to the reference's traces on the other cases)."""
+    P, cap, max_new, seed = 200, 48, 60, 3
+    rng = np.random.default_rng(seed)
+    prompt = rng.integers(0, 97, P).tolist()
+    model = StubScoreModel(vocab=97, n_heads=4, n_kv_heads=2, n_layers=2, max_cache_len=P + max_new + 8, seed=seed)
+    spec = PolicySpec(policy, cap, True, 0.1, 0.1)
+    o = generate(model, spec, prompt, max_new, evict_every=E, n_kv_heads=2, regime="decode")
+    n_pre, n_suf = capi.protection_sizes(cap, 0.1, 0.1)
+    cfg = capi.EvictCfg(cap, E, capi.policy_id(policy), 1, n_pre, n_suf, 1)
+    S = slot_count(cap, E, max_new, "decode")
+    for deferred in (False, True):
+        D = Driver(1, S, (P + max_new + 2 + 31) // 32, P + max_new + 2, max_new, cfg)
+        pending = torch.zeros(1, dtype=torch.int32, device="cuda")
+        D.prefill(P, o.meta.prefill[:P] if policy != "lru" else None)
+        for s in range(1, max_new + 1):
+            D.update_append_evict(pending) if deferred else D.append_evict()
+            assert D.slot_pos[0].cpu().numpy().tolist() == o.slot_tables[s].tolist(), f"slot table after step {s}"
+            if s == max_new:
+                break
+            ks = o.step_scores[s - 1]
+            sp = D.slot_pos[0].cpu().numpy()
+            sc = np.zeros(S, np.float32)
+            sc[sp >= 0] = ks[sp[sp >= 0]]
+            D.step_score[0].copy_(torch.from_numpy(sc))
+            if not deferred:
+                D.score_update()
+        torch.cuda.synchronize()
+        assert int(D.err.item()) == 0
+        n = int(D.evcount[0].item())
+        assert D.evlog[0, :n].cpu().numpy().tolist() == o.positions_evicted
