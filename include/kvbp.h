@@ -350,7 +350,9 @@ int kvbp_decode_gemm_allreduce(kvbp_stream_t stream, int32_t M, int32_t N, int32
  * aligned); bf16 output rounded from fp32 accumulators.  Epilogue 0: out [M][ldo] =
  * bf16(acc).  Epilogue 2 (SwiGLU, gate/up interleaved in blocks of 64 rows as for
  * kvbp_decode_gemm): out [M][ldo] holds the N/2 features bf16(bf16(g * bf16(sigmoid(g)))
- * * u) (jax_inference.py:702-704,1103-1107).  N, K multiples of 128. */
+ * * u) (jax_inference.py:702-704,1103-1107).  Epilogue 3: out float [M][ldo] = acc (the
+ * row-parallel partial sums of tensor parallelism, rounded after the reduction over the
+ * ranks).  N, K multiples of 128. */
 int kvbp_prefill_gemm(kvbp_stream_t stream, int32_t epilogue, int32_t M, int32_t N, int32_t K, const void* w_packed,
                       const void* x, int32_t ldx, void* out, int32_t ldo, int32_t* dev_err);
 

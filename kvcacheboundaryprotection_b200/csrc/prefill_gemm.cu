@@ -18,7 +18,9 @@
 //           each stage back to the producer and each finished tile to the epilogue;
 //   warps 2-5  epilogue: TMEM -> registers (each warp its 32-lane quarter) -> bf16, then
 //           the accumulator goes back to the MMA warp, which meanwhile fills the other.
-// Epilogues: plain (out = bf16(acc)), and SwiGLU for the interleaved gate/up weights
+// Epilogues: plain (out = bf16(acc)), fp32 (out = acc: the row-parallel partial sums of
+// tensor parallelism, reduced over the ranks before rounding), and SwiGLU for the
+// interleaved gate/up weights
 // (rows 64t..64t+63 of block t are gate features, the next 64 the matching up ones):
 // act = bf16(bf16(g * bf16(sigmoid(g))) * u) with g, u the bf16 GEMM outputs
 // (jax_inference.py:702-704,1103-1107), so the 2F-wide gate/up product never reaches HBM.
@@ -79,10 +81,11 @@ __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::
 
 struct Args {
   const __nv_bfloat16* w;  // packed [N/128][K/128][2][128][64]
-  __nv_bfloat16* out;      // plain: [M][ldo] (columns n); SwiGLU: [M][ldo] (features n / 2)
+  void* out;               // plain: bf16 [M][ldo] (columns n); SwiGLU: bf16 [M][ldo] (features n / 2);
+                           // fp32: float [M][ldo] (columns n)
   int ldo;
   int M, N, K;
-  int swiglu;
+  int epi;  // 0 plain bf16, 2 SwiGLU, 3 fp32 accumulators (row-parallel partial sums)
   int* err;
 };
 
@@ -226,14 +229,26 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
       tc_fence_after();
       if (!__all_sync(0xffffffffu, ok && healthy())) break;
       const uint32_t acc = tmem + lane_base + static_cast<uint32_t>(buf * BN);
-      if (!a.swiglu) {
+      if (a.epi == 3) {
 #pragma unroll 1
         for (int c = 0; c < BN; c += 32) {
           float v[32];
           tmem_ld32(acc + c, v);
           const int n = tn * BN + c;
           if (row < a.M && n < a.N) {
-            uint4* dst = reinterpret_cast<uint4*>(a.out + static_cast<size_t>(row) * a.ldo + n);
+            float4* dst = reinterpret_cast<float4*>(static_cast<float*>(a.out) + static_cast<size_t>(row) * a.ldo + n);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) dst[k] = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+          }
+        }
+      } else if (a.epi == 0) {
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          float v[32];
+          tmem_ld32(acc + c, v);
+          const int n = tn * BN + c;
+          if (row < a.M && n < a.N) {
+            uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.out) + static_cast<size_t>(row) * a.ldo + n);
 #pragma unroll
             for (int k = 0; k < 4; ++k)
               dst[k] = make_uint4(pack_bf16(v[8 * k], v[8 * k + 1]), pack_bf16(v[8 * k + 2], v[8 * k + 3]),
@@ -263,7 +278,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
                 }
                 pk[k / 2] = pack_bf16(r2[0], r2[1]);
               }
-              uint4* dst = reinterpret_cast<uint4*>(a.out + static_cast<size_t>(row) * a.ldo + f);
+              uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.out) + static_cast<size_t>(row) * a.ldo + f);
 #pragma unroll
               for (int k = 0; k < 4; ++k) dst[k] = make_uint4(pk[4 * k], pk[4 * k + 1], pk[4 * k + 2], pk[4 * k + 3]);
             }
@@ -325,7 +340,8 @@ static cudaError_t launch_pg(cudaStream_t stream, const CUtensorMap& xm, const p
 int prefill_gemm(cudaStream_t stream, int epilogue, int M, int N, int K, const void* w, const void* x, int ldx,
                  void* out, int ldo, int* err) {
   if (!w || !x || !out) return fail(kStatusArg, "prefill_gemm: null pointer");
-  if (epilogue != 0 && epilogue != 2) return fail(kStatusUnsupported, "prefill_gemm: epilogue %d (plain 0, SwiGLU 2)", epilogue);
+  if (epilogue != 0 && epilogue != 2 && epilogue != 3)
+    return fail(kStatusUnsupported, "prefill_gemm: epilogue %d (plain 0, SwiGLU 2, fp32 3)", epilogue);
   if (M <= 0 || N <= 0 || K <= 0 || N % 128 || K % 128) return fail(kStatusArg, "prefill_gemm: bad size");
   if (static_cast<long long>((M + pg::kBM - 1) / pg::kBM) * (N / 128) >= (1ll << 31))
     return fail(kStatusArg, "prefill_gemm: too many tiles");
@@ -346,12 +362,12 @@ int prefill_gemm(cudaStream_t stream, int epilogue, int M, int N, int K, const v
   if (r != CUDA_SUCCESS) return fail(kStatusCuda, "prefill_gemm: tensor map failed (%d)", static_cast<int>(r));
   pg::Args a;
   a.w = static_cast<const __nv_bfloat16*>(w);
-  a.out = static_cast<__nv_bfloat16*>(out);
+  a.out = out;
   a.ldo = ldo;
   a.M = M;
   a.N = N;
   a.K = K;
-  a.swiglu = epilogue == 2;
+  a.epi = epilogue;
   a.err = err;
   const bool wide = (N / 128) % 2 == 0;
   cudaError_t e = wide ? launch_pg<256>(stream, xm, a, N / 256) : launch_pg<128>(stream, xm, a, N / 128);

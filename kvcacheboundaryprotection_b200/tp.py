@@ -325,7 +325,10 @@ class TPEngine(CappedKVEngine):
     def prefill_phases(self, input_ids: torch.Tensor) -> Iterator[Phase]:
         """Step 0 (prompt forward, scores, forced eviction, compaction, first token) with
         this rank's shards; the o/down partial sums, the per-key score and the argmax key
-        are the reduction points.  GEMMs are cuBLAS in fp32 for the row-parallel partials."""
+        are the reduction points.  With the own GEMMs (gemm="kvbp") every projection runs on
+        the tcgen05 prefill GEMM from the packed shards: q/k/v plain, gate/up with the
+        SwiGLU epilogue, o/down as fp32 partial sums (reduced over the ranks, then rounded);
+        with gemm="cublas", torch.mm (fp32 for the row-parallel partials)."""
         c, fc, d, st = self.cfg, self.full_cfg, self.dev, self.stream
         L = lib()
         ids = input_ids.to(device=d, dtype=torch.int32).contiguous()
@@ -341,6 +344,12 @@ class TPEngine(CappedKVEngine):
         scores = torch.zeros(B, P, dtype=torch.float32, device=d) if need_scores else None
         positions = torch.arange(P, dtype=torch.int32, device=d)
         fw = self.fw
+        own = self.gemm == "kvbp"
+
+        def pgemm(epi, N, K, w, xin, out):
+            check(L.kvbp_prefill_gemm(st, epi, P, N, K, _ptr(w), _ptr(xin), xin.stride(0), _ptr(out), out.stride(0),
+                                      _ptr(self.dev_err)), "prefill_gemm")
+
         for b in range(B):
             h = torch.empty(P, H, dtype=torch.bfloat16, device=d)
             check(L.kvbp_embed(st, P, fc.vocab, H, _ptr(self.embed_w), _ptr(ids[b]), _ptr(h), _ptr(self.dev_err)),
@@ -351,7 +360,11 @@ class TPEngine(CappedKVEngine):
             for li, Lw in enumerate(self.layers):
                 check(L.kvbp_add_rmsnorm(st, P, H, _ptr(h), _ptr(delta), _ptr(Lw["in_norm"]), _ptr(x), c.eps),
                       "rmsnorm")
-                qkv = torch.mm(x, fw.rowmajor(Lw["w_qkv"]).t())
+                if own:
+                    qkv = torch.empty(P, c.qkv_dim, dtype=torch.bfloat16, device=d)
+                    pgemm(0, c.qkv_dim, H, Lw["w_qkv"], x, qkv)
+                else:
+                    qkv = torch.mm(x, fw.rowmajor(Lw["w_qkv"]).t())
                 q = torch.empty(P, c.n_heads, D, dtype=torch.bfloat16, device=d)
                 kb, vb = pre_k[li, b], pre_v[li, b]
                 check(
@@ -366,18 +379,30 @@ class TPEngine(CappedKVEngine):
                 att = self._prefill_attention(q, kb, vb, need_scores, lcol)
                 if need_scores:
                     torch.maximum(colmax, lcol, out=colmax)
-                part = att.float() @ fw.rowmajor(Lw["w_o"]).float().t()
+                if own:
+                    part = torch.empty(P, H, dtype=torch.float32, device=d)
+                    pgemm(3, H, c.n_heads * D, Lw["w_o"], att, part)
+                else:
+                    part = att.float() @ fw.rowmajor(Lw["w_o"]).float().t()
                 yield ("sum", part)
                 o = part.to(torch.bfloat16)
                 check(L.kvbp_add_rmsnorm(st, P, H, _ptr(h), _ptr(o), _ptr(Lw["post_norm"]), _ptr(x), c.eps),
                       "rmsnorm")
-                gu = deinterleave_gate_up(torch.mm(x, fw.rowmajor(Lw["w_gu"]).t()))
                 act = torch.empty(P, c.ffn, dtype=torch.bfloat16, device=d)
-                check(L.kvbp_silu_mul(st, P, c.ffn, _ptr(gu), _ptr(act)), "silu_mul")
-                part = act.float() @ fw.rowmajor(Lw["w_down"]).float().t()
+                if own:
+                    pgemm(2, 2 * c.ffn, H, Lw["w_gu"], x, act)
+                else:
+                    gu = deinterleave_gate_up(torch.mm(x, fw.rowmajor(Lw["w_gu"]).t()))
+                    check(L.kvbp_silu_mul(st, P, c.ffn, _ptr(gu), _ptr(act)), "silu_mul")
+                    del gu
+                if own:
+                    part = torch.empty(P, H, dtype=torch.float32, device=d)
+                    pgemm(3, H, c.ffn, Lw["w_down"], act, part)
+                else:
+                    part = act.float() @ fw.rowmajor(Lw["w_down"]).float().t()
                 yield ("sum", part)
                 delta = part.to(torch.bfloat16)
-                del gu, act, qkv, q, part
+                del act, qkv, q, part
             hl = h[P - 1 : P].contiguous()
             dl = delta[P - 1 : P].contiguous()
             xl = torch.empty_like(hl)

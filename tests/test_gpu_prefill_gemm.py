@@ -88,3 +88,26 @@ def test_prefill_gemm_rejects_bad_shapes():
     out = torch.zeros(4, 128, dtype=torch.bfloat16, device="cuda")
     assert L.kvbp_prefill_gemm(st, 0, 4, 100, 128, w.data_ptr(), x.data_ptr(), 128, out.data_ptr(), 128, None) != 0
     assert L.kvbp_prefill_gemm(st, 1, 4, 128, 128, w.data_ptr(), x.data_ptr(), 128, out.data_ptr(), 128, None) != 0
+
+
+@pytest.mark.parametrize("M,N,K", [(300, 1152, 896), (1024, 3584, 4736), (513, 2048, 1024)])
+def test_prefill_gemm_fp32_partials(M, N, K):
+    """Epilogue 3 writes the fp32 accumulators (the row-parallel partial sums of tensor
+    parallelism): within fp32 rounding of the fp32 reference product (the K-step order
+    differs), and rounding them to bf16 gives the plain epilogue's output."""
+    g = torch.Generator(device="cuda").manual_seed(M + K)
+    x = torch.randn(M, K, generator=g, device="cuda").to(torch.bfloat16)
+    w = (torch.randn(N, K, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+    wp = pack_weight(w)
+    out = torch.full((M, N), float("nan"), dtype=torch.float32, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    capi.check(capi.lib().kvbp_prefill_gemm(torch.cuda.current_stream().cuda_stream, 3, M, N, K, wp.data_ptr(),
+                                            x.data_ptr(), x.stride(0), out.data_ptr(), out.stride(0), err.data_ptr()),
+               "prefill_gemm")
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    ref = x.float() @ w.float().t()
+    scale = (x.float().abs() @ w.float().abs().t())  # bound of the terms' magnitudes
+    assert ((out - ref).abs() <= 1e-4 * scale + 1e-6).all()
+    plain = _run(0, x, wp, N, N)
+    assert torch.equal(out.to(torch.bfloat16), plain)
