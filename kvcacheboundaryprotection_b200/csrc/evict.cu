@@ -368,16 +368,25 @@ __global__ void __launch_bounds__(kEvictThreads) append_evict_kernel(AppendArgs 
   // update, the maximum of the previous step's scores over the retained slots
   constexpr int kU = 10;  // one iteration per pass up to 5120 slots
   float* sc = a.upd_score ? a.upd_score + static_cast<size_t>(b) * S : nullptr;
+  // up to kU * kEvictThreads slots the update's other inputs are loaded in the same pass
+  // and kept in registers, so the update itself needs no second round trip
+  const bool one_pass = S <= kU * kEvictThreads;
   int mine = 0x7fffffff;
   float mx = 0.f;
+  float v[kU], ma[kU];
+  double cu[kU];
+  int ps[kU], cn[kU];
   for (int i0 = tid; i0 < S; i0 += kU * kEvictThreads) {
-    float v[kU];
-    int ps[kU];
+    const bool keep = sc && one_pass;
 #pragma unroll
     for (int k = 0; k < kU; ++k) {
       const int i = i0 + k * kEvictThreads;
-      ps[k] = i < S ? s.slot_pos[i] : 0;
-      v[k] = (sc && i < S) ? sc[i] : 0.f;
+      const bool in = i < S;
+      ps[k] = in ? s.slot_pos[i] : 0;
+      v[k] = (sc && in) ? sc[i] : 0.f;
+      ma[k] = (keep && in) ? s.max_attn[i] : 0.f;
+      cu[k] = (keep && in) ? s.cumul[i] : 0.0;
+      cn[k] = (keep && in) ? s.access_count[i] : 0;
     }
 #pragma unroll
     for (int k = 0; k < kU; ++k) {
@@ -401,35 +410,45 @@ __global__ void __launch_bounds__(kEvictThreads) append_evict_kernel(AppendArgs 
       mx = block_max_float(mx, red_f);
       const float thr = static_cast<float>(0.05 * static_cast<double>(mx));
       const int prev = step - 1;
-      for (int i0 = tid; i0 < S; i0 += kU * kEvictThreads) {
-        float ks[kU], ma[kU];
-        double cu[kU];
-        int ps[kU], cn[kU];
-#pragma unroll
-        for (int k = 0; k < kU; ++k) {
-          const int i = i0 + k * kEvictThreads;
-          const bool in = i < S;
-          ps[k] = in ? s.slot_pos[i] : -1;
-          ks[k] = in ? sc[i] : 0.f;
-          ma[k] = in ? s.max_attn[i] : 0.f;
-          cu[k] = in ? s.cumul[i] : 0.0;
-          cn[k] = in ? s.access_count[i] : 0;
-        }
-#pragma unroll
-        for (int k = 0; k < kU; ++k) {
-          const int i = i0 + k * kEvictThreads;
-          if (i >= S) continue;
-          if (ps[k] >= 0) {
-            if (ks[k] != ks[k]) set_err(a.err, kErrNanScore);
-            s.attn[i] = ks[k];
-            s.max_attn[i] = fmaxf(ma[k], ks[k]);
-            s.cumul[i] = __dadd_rn(cu[k], static_cast<double>(ks[k]));
-            if (ks[k] > thr) {
-              s.last_access[i] = prev;
-              s.access_count[i] = cn[k] + 1;
-            }
+      auto update = [&](int i, int p_i, float ks, float ma_i, double cu_i, int cn_i) {
+        if (p_i >= 0) {
+          if (ks != ks) set_err(a.err, kErrNanScore);
+          s.attn[i] = ks;
+          s.max_attn[i] = fmaxf(ma_i, ks);
+          s.cumul[i] = __dadd_rn(cu_i, static_cast<double>(ks));
+          if (ks > thr) {
+            s.last_access[i] = prev;
+            s.access_count[i] = cn_i + 1;
           }
-          sc[i] = 0.f;  // this step's layers accumulate from zero
+        }
+        sc[i] = 0.f;  // this step's layers accumulate from zero
+      };
+      if (one_pass) {
+#pragma unroll
+        for (int k = 0; k < kU; ++k) {
+          const int i = tid + k * kEvictThreads;
+          if (i < S) update(i, ps[k], v[k], ma[k], cu[k], cn[k]);
+        }
+      } else {
+        for (int i0 = tid; i0 < S; i0 += kU * kEvictThreads) {
+          float ks2[kU], ma2[kU];
+          double cu2[kU];
+          int ps2[kU], cn2[kU];
+#pragma unroll
+          for (int k = 0; k < kU; ++k) {
+            const int i = i0 + k * kEvictThreads;
+            const bool in = i < S;
+            ps2[k] = in ? s.slot_pos[i] : -1;
+            ks2[k] = in ? sc[i] : 0.f;
+            ma2[k] = in ? s.max_attn[i] : 0.f;
+            cu2[k] = in ? s.cumul[i] : 0.0;
+            cn2[k] = in ? s.access_count[i] : 0;
+          }
+#pragma unroll
+          for (int k = 0; k < kU; ++k) {
+            const int i = i0 + k * kEvictThreads;
+            if (i < S) update(i, ps2[k], ks2[k], ma2[k], cu2[k], cn2[k]);
+          }
         }
       }
     } else {

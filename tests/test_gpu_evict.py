@@ -369,3 +369,32 @@ def test_eviction_kernels_large_cadence_against_oracle(policy, E):
         assert int(D.err.item()) == 0
         n = int(D.evcount[0].item())
         assert D.evlog[0, :n].cpu().numpy().tolist() == o.positions_evicted
+
+
+def test_update_append_evict_more_slots_than_one_pass():
+    """Above 5120 slots the score update reloads its inputs in a second pass: still bit-
+    identical to the separate launches (random prefill scores and step scores)."""
+    P, C, E, max_new = 7000, 6000, 8, 20
+    cfg = capi.EvictCfg(C, E, capi.policy_id("h2o_faithful"), 1, *capi.protection_sizes(C, 0.1, 0.1), 1)
+    S = slot_count(C, E, max_new, "decode")
+    assert S > 5120
+    args = (2, S, (P + max_new + 2 + 31) // 32, P + max_new + 2, max_new, cfg)
+    A, Bd = Driver(*args), Driver(*args)
+    pending = torch.zeros(2, dtype=torch.int32, device="cuda")
+    rng = np.random.default_rng(7)
+    pre = rng.random((2, P)).astype(np.float32)
+    A.prefill(P, pre)
+    Bd.prefill(P, pre)
+    for s in range(1, max_new + 1):
+        A.update_append_evict(pending)
+        Bd.append_evict()
+        for x, y in zip(A.metadata(), Bd.metadata()):
+            assert torch.equal(x, y), f"state differs after step {s}"
+        sc = torch.from_numpy(rng.random((2, S)).astype(np.float32)).cuda()
+        sc[A.slot_pos < 0] = 0
+        A.step_score.copy_(sc)
+        Bd.step_score.copy_(sc)
+        Bd.score_update()
+    torch.cuda.synchronize()
+    assert int(A.err.item()) == 0 and int(Bd.err.item()) == 0
+    assert int(A.evcount[0].item()) > P - C  # the cadence steps evicted
