@@ -228,3 +228,32 @@ def test_tiny_qwen2_free_running_against_reference_trace():
     calls_before = [c for c in ref["policy_call_steps"] if 0 < c <= first + 1]
     n_same = (ref["n_prompt"] - ref["capacity"]) + 8 * len(calls_before)
     assert res.positions_evicted[:n_same] == ref["positions_evicted"][:n_same]
+
+
+def test_pending_scores_applied_without_append_equal_the_appends_update():
+    """The engine defers each step's score update to the next append kernel; after a forward
+    with no append to follow, apply_pending_scores runs the same update: the metadata of the
+    retained slots equals what the next append's update writes (bit for bit)."""
+    cfg = get_config("parity-qwen2")
+    w = init_weights(cfg, seed=0)
+    prompt = torch.tensor([[int(x) for x in np.random.default_rng(5).integers(0, cfg.vocab, 120)]], dtype=torch.int32)
+    engs = []
+    for _ in range(2):
+        e = CappedKVEngine(cfg, w, batch=1, evict=EvictionSpec("h2o_faithful", 48, 8, True, 0.10, 0.10),
+                           max_prompt_len=120, max_new_tokens=12)
+        assert e.deferred_score_update
+        e.prefill(prompt)
+        for _ in range(5):
+            e.run_step(use_graph=False)
+        engs.append(e)
+    a, b = engs
+    a.apply_pending_scores()
+    b._append_evict()  # applies the pending update, then appends step 6's position
+    torch.cuda.synchronize()
+    keep = (a.slot_pos >= 0) & (b.slot_pos == a.slot_pos)
+    assert int(keep.sum()) >= 40
+    for name in ("attn_s", "max_attn", "cumul", "last_access", "access_count"):
+        assert torch.equal(getattr(a, name)[keep], getattr(b, name)[keep]), name
+    assert int(a.step_score.abs().sum().item()) == 0 and int(a.upd_pending.sum().item()) == 0
+    a.check_device_errors()
+    b.check_device_errors()
