@@ -66,3 +66,22 @@ def test_host_validation_rejects_bad_arguments(L):
     assert L.kvbp_prefill_select(None, 1, 100, C.byref(cfg), None, 16, 16, 10, C.byref(n), None) == 1
     with pytest.raises(capi.KVBPError):
         capi.check(L.kvbp_embed(None, 1, 10, 12, 16, 16, 16, None), "embed")
+
+
+def test_host_validation_of_the_operator_step_and_prefill_gemm_entries(L):
+    # kvbp_update_append_evict needs its step scores and pending flags
+    st_ = capi.State(1, 64, 4, *([16] * 9))
+    cfg = capi.EvictCfg(32, 8, 0, 1, 4, 4, 1)
+    args = (None, C.byref(st_), C.byref(cfg), 16, 16, 16, 16, None, None, 0, 16, 16, 8, None)
+    assert L.kvbp_update_append_evict(*args, None, 16, None) == 1
+    assert b"step_score and pending" in L.kvbp_last_error()
+    assert L.kvbp_update_append_evict(*args, 16, None, None) == 1
+    # attention + scatter without state needs the new row
+    st = L.kvbp_decode_attn_score_update(None, 1, 4, 1, 128, 64, 16, None, None, 16, 16, 16, 16, 16, 16, None, None,
+                                         None, None)
+    assert st == 1 and b"nothing to fuse" in L.kvbp_last_error()
+    # prefill GEMM: epilogues 0 (plain), 2 (SwiGLU) and 3 (fp32) only; sizes multiples of 128
+    assert L.kvbp_prefill_gemm(None, 1, 128, 128, 128, 16, 16, 128, 16, 128, None) == 2
+    assert L.kvbp_prefill_gemm(None, 0, 128, 100, 128, 16, 16, 128, 16, 128, None) == 1
+    assert L.kvbp_prefill_gemm(None, 2, 128, 256, 128, 16, 16, 128, 16, 64, None) == 1  # SwiGLU: ldo 64 < N/2
+    assert L.kvbp_prefill_gemm(None, 0, 128, 128, 128, None, 16, 128, 16, 128, None) == 1  # null weights
