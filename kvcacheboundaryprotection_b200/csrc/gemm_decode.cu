@@ -56,9 +56,12 @@ __host__ __device__ constexpr int stages_for(int MT) { return MT == 1 ? kStagesM
 #ifndef KVBP_GEMM_EARLY
 #define KVBP_GEMM_EARLY 3  // weight stages issued before the wait on the previous kernel
 #endif
-constexpr int kConsumerWarps = 4;  // 32 features each
-constexpr int kConsumers = kConsumerWarps * 32;
-constexpr int kThreads = kConsumers + 32;
+// Consumer warps: four feature groups of 32 features, one warp per (group, 16-row m-tile)
+// -- with 32 activation rows two warps share a feature group, so each warp's dependent
+// ldmatrix / norm / mma chain covers one m-tile (with four warps doing both m-tiles the
+// kernel was issue-latency bound: 24 % HMMA-pipe activity, 43 % issue slots busy)
+__host__ __device__ constexpr int consumer_warps(int MT) { return 4 * MT; }
+__host__ __device__ constexpr int gemm_threads(int MT) { return consumer_warps(MT) * 32 + 32; }
 constexpr int kWBytes = BN * BK * 2;  // 32 KiB: two 128 x 64 halves
 constexpr int kWBox = kWBytes / 2;
 constexpr int kBlockElems = BN * BK;  // one packed block
@@ -119,8 +122,10 @@ __device__ __forceinline__ uint4 ld_relaxed_sys_v4(const uint4* p) {
 }
 
 template <int MT, int EPI, bool NORM>
-__global__ void __launch_bounds__(kThreads) decode_gemm_kernel(const __grid_constant__ CUtensorMap xmap,
-                                                               const Args a) {
+__global__ void __launch_bounds__(gemm_threads(MT)) decode_gemm_kernel(const __grid_constant__ CUtensorMap xmap,
+                                                                       const Args a) {
+  constexpr int kConsumerWarps = consumer_warps(MT);
+  constexpr int kConsumers = kConsumerWarps * 32;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   constexpr int kStages = stages_for(MT);
@@ -254,17 +259,13 @@ __global__ void __launch_bounds__(kThreads) decode_gemm_kernel(const __grid_cons
     }
   }
   const int g = lane >> 2, t = lane & 3;
-  float acc[MT][4][4];
+  const int fgrp = warp & 3;  // features fgrp * 32 .. + 31 of the tile
+  const int mtw = warp >> 2;  // this warp's 16-row m-tile
+  float acc[4][4];
 #pragma unroll
-  for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-    for (int j = 0; j < 4; ++j) acc[mt][j][0] = acc[mt][j][1] = acc[mt][j][2] = acc[mt][j][3] = 0.f;
-  float inv_lo[MT], inv_hi[MT];
-#pragma unroll
-  for (int mt = 0; mt < MT; ++mt) {
-    inv_lo[mt] = NORM ? inv_rms[mt * 16 + g] : 1.f;
-    inv_hi[mt] = NORM ? inv_rms[mt * 16 + g + 8] : 1.f;
-  }
+  for (int j = 0; j < 4; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+  const float inv_lo = NORM ? inv_rms[mtw * 16 + g] : 1.f;
+  const float inv_hi = NORM ? inv_rms[mtw * 16 + g + 8] : 1.f;
   for (int u = 0; u < nch; ++u) {
     const int st = u % kStages;
     bool go = !*reinterpret_cast<volatile int*>(flag);
@@ -280,39 +281,34 @@ __global__ void __launch_bounds__(kThreads) decode_gemm_kernel(const __grid_cons
     for (int kk = 0; kk < BK / 16; ++kk) {
       const int col = kk * 16;
       const int box = col >> 6, cb = (col & 63) >> 3;
-      // A fragments (activations): rows 16*mt .. +15, k col .. col+15
-      uint32_t af[MT][4];
-#pragma unroll
-      for (int mt = 0; mt < MT; ++mt) {
-        const int row = mt * 16 + (lane & 15);
+      // A fragments (activations): rows 16*mtw .. +15, k col .. col+15
+      uint32_t af[4];
+      {
+        const int row = mtw * 16 + (lane & 15);
         const int chunk = cb + (lane >> 4);
-        ldmatrix_x4(smem_u32(ab + box * kABox + row * 128 + ((chunk ^ (row & 7)) << 4)), af[mt][0], af[mt][1],
-                    af[mt][2], af[mt][3]);
+        ldmatrix_x4(smem_u32(ab + box * kABox + row * 128 + ((chunk ^ (row & 7)) << 4)), af[0], af[1], af[2], af[3]);
         if (NORM) {
           // x = bf16((h * inv_rms[row]) * w_norm[k]) on the fragment (k = col + 2t, +1, +8, +9)
           const int kl = st * BK + col + 2 * t;
           const uint32_t w01 = *reinterpret_cast<const uint32_t*>(wn_s + kl);
           const uint32_t w89 = *reinterpret_cast<const uint32_t*>(wn_s + kl + 8);
           const float wa = bf16lo(w01), wb2 = bf16hi(w01), wc = bf16lo(w89), wd = bf16hi(w89);
-          af[mt][0] = pack_bf16((bf16lo(af[mt][0]) * inv_lo[mt]) * wa, (bf16hi(af[mt][0]) * inv_lo[mt]) * wb2);
-          af[mt][1] = pack_bf16((bf16lo(af[mt][1]) * inv_hi[mt]) * wa, (bf16hi(af[mt][1]) * inv_hi[mt]) * wb2);
-          af[mt][2] = pack_bf16((bf16lo(af[mt][2]) * inv_lo[mt]) * wc, (bf16hi(af[mt][2]) * inv_lo[mt]) * wd);
-          af[mt][3] = pack_bf16((bf16lo(af[mt][3]) * inv_hi[mt]) * wc, (bf16hi(af[mt][3]) * inv_hi[mt]) * wd);
+          af[0] = pack_bf16((bf16lo(af[0]) * inv_lo) * wa, (bf16hi(af[0]) * inv_lo) * wb2);
+          af[1] = pack_bf16((bf16lo(af[1]) * inv_hi) * wa, (bf16hi(af[1]) * inv_hi) * wb2);
+          af[2] = pack_bf16((bf16lo(af[2]) * inv_lo) * wc, (bf16hi(af[2]) * inv_lo) * wd);
+          af[3] = pack_bf16((bf16lo(af[3]) * inv_hi) * wc, (bf16hi(af[3]) * inv_hi) * wd);
         }
       }
-      // B fragments (weights): features warp*32 .. +31, two x4 loads of 16 features each
+      // B fragments (weights): features fgrp*32 .. +31, two x4 loads of 16 features each
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const int j = lane >> 3;
-        const int frow = warp * 32 + h * 16 + (lane & 7) + ((j >> 1) << 3);
+        const int frow = fgrp * 32 + h * 16 + (lane & 7) + ((j >> 1) << 3);
         const int chunk = cb + (j & 1);
         uint32_t b0, b1, b2, b3;
         ldmatrix_x4(smem_u32(wb + box * kWBox + frow * 128 + ((chunk ^ (frow & 7)) << 4)), b0, b1, b2, b3);
-#pragma unroll
-        for (int mt = 0; mt < MT; ++mt) {
-          mma_bf16_16816(acc[mt][2 * h], af[mt][0], af[mt][1], af[mt][2], af[mt][3], b0, b1);
-          mma_bf16_16816(acc[mt][2 * h + 1], af[mt][0], af[mt][1], af[mt][2], af[mt][3], b2, b3);
-        }
+        mma_bf16_16816(acc[2 * h], af[0], af[1], af[2], af[3], b0, b1);
+        mma_bf16_16816(acc[2 * h + 1], af[0], af[1], af[2], af[3], b2, b3);
       }
     }
     __syncwarp();
@@ -321,21 +317,19 @@ __global__ void __launch_bounds__(kThreads) decode_gemm_kernel(const __grid_cons
   if (KVBP_PDL_LATE) pdl_launch_dependents();  // the next kernel may start its weight stream
 
   // ---- partial tile -> this CTA's shared memory (the ring is idle once every warp is done)
-  // acc[mt][j]: rows 16mt+g (c0,c1) and 16mt+g+8 (c2,c3); columns warp*32 + 8j + 2t (+1)
+  // acc[j]: rows 16mtw+g (c0,c1) and 16mtw+g+8 (c2,c3); columns fgrp*32 + 8j + 2t (+1)
   named_bar(1, kConsumers);
   if (tid == 0) flag[1] = *reinterpret_cast<volatile int*>(flag);  // one snapshot for every consumer
   named_bar(1, kConsumers);
   const bool ok = !flag[1];
   if (ok) {
 #pragma unroll
-    for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int c = warp * 32 + 8 * j + 2 * t;
-        const int r0 = mt * 16 + g;
-        *reinterpret_cast<float2*>(&rtile[r0 * kRedStride + c]) = make_float2(acc[mt][j][0], acc[mt][j][1]);
-        *reinterpret_cast<float2*>(&rtile[(r0 + 8) * kRedStride + c]) = make_float2(acc[mt][j][2], acc[mt][j][3]);
-      }
+    for (int j = 0; j < 4; ++j) {
+      const int c = fgrp * 32 + 8 * j + 2 * t;
+      const int r0 = mtw * 16 + g;
+      *reinterpret_cast<float2*>(&rtile[r0 * kRedStride + c]) = make_float2(acc[j][0], acc[j][1]);
+      *reinterpret_cast<float2*>(&rtile[(r0 + 8) * kRedStride + c]) = make_float2(acc[j][2], acc[j][3]);
+    }
   }
   if (cs > 1) cluster_sync_all();  // every partial tile of the cluster is complete
   else named_bar(1, kConsumers);
@@ -634,7 +628,7 @@ static cudaError_t launch_gemm(cudaStream_t stream, const CUtensorMap& xmap, con
     configured = true;
   }
   dim3 grid(a.N / gemm::BN, a.splits);
-  return launch_pdl(kern, grid, dim3(gemm::kThreads), smem, stream, a.splits > 1 ? dim3(1, a.splits, 1) : dim3(0),
+  return launch_pdl(kern, grid, dim3(gemm::gemm_threads(MT)), smem, stream, a.splits > 1 ? dim3(1, a.splits, 1) : dim3(0),
                     xmap, a);
 }
 
@@ -726,7 +720,7 @@ int decode_gemm_allreduce(cudaStream_t stream, int M, int N, int K, const void* 
     if (e != cudaSuccess) return fail(kStatusCuda, "decode_gemm_allreduce: %s", cudaGetErrorString(e));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(N / BN, splits);
-    cfg.blockDim = dim3(kThreads);
+    cfg.blockDim = dim3(gemm_threads(MT));
     cfg.dynamicSmemBytes = smem;
     cudaLaunchAttribute attr;
     attr.id = cudaLaunchAttributeClusterDimension;
