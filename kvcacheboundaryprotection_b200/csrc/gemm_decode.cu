@@ -11,6 +11,14 @@
 // DRAM pages, no tensor map, no per-row 128-byte fragments.  A producer warp feeds a
 // 3-stage ring; four consumer warps run mma.sync m16n8k16 with the activations as the
 // M operand (16 rows per m-tile, loaded by 2-D TMA) and 32 output features per warp.
+// For 17..32 rows the main loop runs on the tcgen05 tensor cores instead, operands
+// swapped: the packed weight block is the M = 128 operand (already the 128-byte-swizzled
+// K-major image the MMA reads), the activation chunk the N = 32 operand, and the fp32
+// accumulator lives in 32 TMEM columns; one thread issues the MMAs and commits each stage
+// back to the producer, so the consumer warps only apply the RMSNorm prologue to the
+// staged activations and read the accumulator out at the end.  Both main loops leave the
+// same fp32 partial tile in shared memory, so the split-K reduction and every epilogue
+// below are shared.
 //
 // Split-K: the `splits` CTAs of one column tile form a thread-block cluster.  Each CTA
 // leaves its fp32 partial tile in its own shared memory; after a cluster barrier CTA r
@@ -62,6 +70,11 @@ __host__ __device__ constexpr int stages_for(int MT) { return MT == 1 ? kStagesM
 // kernel was issue-latency bound: 24 % HMMA-pipe activity, 43 % issue slots busy)
 __host__ __device__ constexpr int consumer_warps(int MT) { return 4 * MT; }
 __host__ __device__ constexpr int gemm_threads(int MT) { return consumer_warps(MT) * 32 + 32; }
+#ifndef KVBP_GEMM_TC_MIN_MT
+#define KVBP_GEMM_TC_MIN_MT 2  // m-tiles from which the main loop runs on tcgen05
+#endif
+__host__ __device__ constexpr bool use_tc(int MT) { return MT >= KVBP_GEMM_TC_MIN_MT; }
+constexpr int kTmemCols = 32;  // accumulator: 128 lanes (features) x 16*MT columns (rows)
 constexpr int kWBytes = BN * BK * 2;  // 32 KiB: two 128 x 64 halves
 constexpr int kWBox = kWBytes / 2;
 constexpr int kBlockElems = BN * BK;  // one packed block
@@ -121,7 +134,60 @@ __device__ __forceinline__ uint4 ld_relaxed_sys_v4(const uint4* p) {
   return v;
 }
 
-template <int MT, int EPI, bool NORM>
+// ---- tcgen05 helpers (kind::f16, one CTA) ---------------------------------------------
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row core groups 1024 B
+// apart (SBO), LBO unused for this layout, descriptor version 1.
+__device__ __forceinline__ uint64_t tc_sdesc(uint32_t saddr) {
+  return static_cast<uint64_t>((saddr >> 4) & 0x3FFF) | (static_cast<uint64_t>(1) << 16) |
+         (static_cast<uint64_t>(1024 >> 4) << 32) | (static_cast<uint64_t>(1) << 46) | (static_cast<uint64_t>(2) << 61);
+}
+// instruction descriptor: D f32, A and B bf16, both K-major, M x N
+__host__ __device__ constexpr uint32_t tc_idesc(int M, int N) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(N >> 3) << 17) |
+         (static_cast<uint32_t>(M >> 4) << 24);
+}
+__device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t id, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+      "l"(da), "l"(db), "r"(id), "r"(acc));
+}
+// arrives once on bar when every tcgen05 operation this thread issued so far is complete
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tc_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+// 16 consecutive TMEM columns of this warp's 32 lanes (one lane per thread)
+__device__ __forceinline__ void tc_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
+}
+// named barrier that also ORs a predicate over the participating threads (the same
+// result in every thread)
+__device__ __forceinline__ int bar_any(int id, int nthreads, int pred) {
+  int r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.s32 p, %1, 0;\n\tbar.red.or.pred q, %2, %3, p;\n\tselp.s32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(pred), "r"(id), "r"(nthreads)
+      : "memory");
+  return r;
+}
+// RMSNorm prologue on a packed bf16 pair: bf16((x * inv) * w), the mma.sync path's order
+__device__ __forceinline__ uint32_t norm_pair(uint32_t x, uint32_t w, float inv) {
+  return pack_bf16((bf16lo(x) * inv) * bf16lo(w), (bf16hi(x) * inv) * bf16hi(w));
+}
+
+template <int MT, int EPI, bool NORM, bool TC>
 __global__ void __launch_bounds__(gemm_threads(MT)) decode_gemm_kernel(const __grid_constant__ CUtensorMap xmap,
                                                                        const Args a) {
   constexpr int kConsumerWarps = consumer_warps(MT);
@@ -143,6 +209,8 @@ __global__ void __launch_bounds__(gemm_threads(MT)) decode_gemm_kernel(const __g
   int* flag = reinterpret_cast<int*>(red + 2 * 32);  // [0] bad, [1] its snapshot after the main loop
   uint64_t* full = reinterpret_cast<uint64_t*>(flag + 4);
   uint64_t* empty = full + kStages;
+  uint64_t* accbar = empty + kStages;                         // TC: every MMA of the CTA complete
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(accbar + 1);  // TC: TMEM base address
   float* rtile = reinterpret_cast<float*>(ring);  // [16*MT][kRedStride] partial tile, after the main loop
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -171,12 +239,21 @@ __global__ void __launch_bounds__(gemm_threads(MT)) decode_gemm_kernel(const __g
     prefetch_tmap(&xmap);
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 2);
-      mbar_init(&empty[s], kConsumerWarps);
+      mbar_init(&empty[s], TC ? 1 : kConsumerWarps);  // TC: the MMA commit frees a stage
     }
+    if (TC) mbar_init(accbar, 1);
     flag[0] = 0;
     fence_barrier_init();
   }
+  if (TC && warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tslot)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
+  }
+  if (TC) tc_before();
   __syncthreads();
+  if (TC) tc_after();
+  const uint32_t tmem = TC ? *tslot : 0u;
   if (!KVBP_PDL_LATE) pdl_launch_dependents();
 
   // ================================ producer warp =================================
@@ -258,81 +335,163 @@ __global__ void __launch_bounds__(gemm_threads(MT)) decode_gemm_kernel(const __g
       }
     }
   }
-  const int g = lane >> 2, t = lane & 3;
-  const int fgrp = warp & 3;  // features fgrp * 32 .. + 31 of the tile
-  const int mtw = warp >> 2;  // this warp's 16-row m-tile
-  float acc[4][4];
-#pragma unroll
-  for (int j = 0; j < 4; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
-  const float inv_lo = NORM ? inv_rms[mtw * 16 + g] : 1.f;
-  const float inv_hi = NORM ? inv_rms[mtw * 16 + g + 8] : 1.f;
-  for (int u = 0; u < nch; ++u) {
-    const int st = u % kStages;
-    bool go = !*reinterpret_cast<volatile int*>(flag);
-    if (go && !mbar_wait_bounded(&full[st], (u / kStages) & 1)) {
-      set_err(a.err, kErrWaitTimeout);
-      atomicExch(flag, 1);
-      go = false;
-    }
-    if (!__all_sync(0xffffffffu, go)) break;  // the warp leaves together (ldmatrix/mma are warp-wide)
-    const uint8_t* wb = ring + st * kStageBytes;
-    const uint8_t* ab = wb + kWBytes;
-#pragma unroll
-    for (int kk = 0; kk < BK / 16; ++kk) {
-      const int col = kk * 16;
-      const int box = col >> 6, cb = (col & 63) >> 3;
-      // A fragments (activations): rows 16*mtw .. +15, k col .. col+15
-      uint32_t af[4];
-      {
-        const int row = mtw * 16 + (lane & 15);
-        const int chunk = cb + (lane >> 4);
-        ldmatrix_x4(smem_u32(ab + box * kABox + row * 128 + ((chunk ^ (row & 7)) << 4)), af[0], af[1], af[2], af[3]);
+  // one snapshot of the error flag for every consumer, taken after the main loop
+  auto snapshot_flag = [&]() {
+    named_bar(1, kConsumers);
+    if (tid == 0) flag[1] = *reinterpret_cast<volatile int*>(flag);
+    named_bar(1, kConsumers);
+    return !flag[1];
+  };
+  bool ok;
+  if constexpr (TC) {
+    // ---- tcgen05 main loop: D[128 features][16*MT rows] += W[128][16] . X^T[16][16*MT],
+    // eight MMAs per 128-wide stage issued by thread 0, the stage freed by their commit.
+    // With the norm prologue every consumer first rewrites the staged activations in place
+    // (x -> bf16((x * inv_rms[row]) * w_norm[k])) and the MMAs wait for all of them.
+    constexpr uint32_t kId = tc_idesc(128, 16 * MT);
+    constexpr int kChunks = 2 * MT * 16 * 8;  // 16-byte chunks of one stage's activation boxes
+    if (NORM || tid == 0) {
+      for (int u = 0; u < nch; ++u) {
+        const int st = u % kStages;
+        int bad = *reinterpret_cast<volatile int*>(flag) != 0;
+        if (!bad && !mbar_wait_bounded(&full[st], (u / kStages) & 1)) {
+          set_err(a.err, kErrWaitTimeout);
+          atomicExch(flag, 1);
+          bad = 1;
+        }
+        uint8_t* ab = ring + st * kStageBytes + kWBytes;
         if (NORM) {
-          // x = bf16((h * inv_rms[row]) * w_norm[k]) on the fragment (k = col + 2t, +1, +8, +9)
-          const int kl = st * BK + col + 2 * t;
-          const uint32_t w01 = *reinterpret_cast<const uint32_t*>(wn_s + kl);
-          const uint32_t w89 = *reinterpret_cast<const uint32_t*>(wn_s + kl + 8);
-          const float wa = bf16lo(w01), wb2 = bf16hi(w01), wc = bf16lo(w89), wd = bf16hi(w89);
-          af[0] = pack_bf16((bf16lo(af[0]) * inv_lo) * wa, (bf16hi(af[0]) * inv_lo) * wb2);
-          af[1] = pack_bf16((bf16lo(af[1]) * inv_hi) * wa, (bf16hi(af[1]) * inv_hi) * wb2);
-          af[2] = pack_bf16((bf16lo(af[2]) * inv_lo) * wc, (bf16hi(af[2]) * inv_lo) * wd);
-          af[3] = pack_bf16((bf16lo(af[3]) * inv_hi) * wc, (bf16hi(af[3]) * inv_hi) * wd);
+          if (!bad) {
+#pragma unroll
+            for (int q = tid; q < kChunks; q += kConsumers) {
+              const int box = q / (MT * 16 * 8);
+              const int row = (q >> 3) % (MT * 16);
+              const int pc = q & 7;            // stored chunk within the 128-byte row
+              const int c = pc ^ (row & 7);    // logical chunk (128-byte swizzle)
+              uint4* px = reinterpret_cast<uint4*>(ab + box * kABox + row * 128 + pc * 16);
+              const uint4 wv = *reinterpret_cast<const uint4*>(wn_s + st * BK + box * 64 + c * 8);
+              const float inv = inv_rms[row];
+              uint4 xv = *px;
+              xv.x = norm_pair(xv.x, wv.x, inv);
+              xv.y = norm_pair(xv.y, wv.y, inv);
+              xv.z = norm_pair(xv.z, wv.z, inv);
+              xv.w = norm_pair(xv.w, wv.w, inv);
+              *px = xv;
+            }
+            fence_proxy_async_smem();  // the tensor cores read the rewritten tile next
+          }
+          if (bar_any(1, kConsumers, bad)) break;  // every consumer leaves together
+        } else if (bad) {
+          break;
+        }
+        if (tid == 0) {
+          tc_after();
+          const uint32_t wa = smem_u32(ring + st * kStageBytes), xa = smem_u32(ab);
+#pragma unroll
+          for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks)
+              tc_mma(tmem, tc_sdesc(wa + h * kWBox + ks * 32), tc_sdesc(xa + h * kABox + ks * 32), kId,
+                     (u > 0 || h > 0 || ks > 0) ? 1u : 0u);
+          tc_commit(&empty[st]);
         }
       }
-      // B fragments (weights): features fgrp*32 .. +31, two x4 loads of 16 features each
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int j = lane >> 3;
-        const int frow = fgrp * 32 + h * 16 + (lane & 7) + ((j >> 1) << 3);
-        const int chunk = cb + (j & 1);
-        uint32_t b0, b1, b2, b3;
-        ldmatrix_x4(smem_u32(wb + box * kWBox + frow * 128 + ((chunk ^ (frow & 7)) << 4)), b0, b1, b2, b3);
-        mma_bf16_16816(acc[2 * h], af[0], af[1], af[2], af[3], b0, b1);
-        mma_bf16_16816(acc[2 * h + 1], af[0], af[1], af[2], af[3], b2, b3);
-      }
+      if (tid == 0) tc_commit(accbar);  // also when the loop ended early: nothing stays in flight
     }
     __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[st]);
-  }
-  if (KVBP_PDL_LATE) pdl_launch_dependents();  // the next kernel may start its weight stream
-
-  // ---- partial tile -> this CTA's shared memory (the ring is idle once every warp is done)
-  // acc[j]: rows 16mtw+g (c0,c1) and 16mtw+g+8 (c2,c3); columns fgrp*32 + 8j + 2t (+1)
-  named_bar(1, kConsumers);
-  if (tid == 0) flag[1] = *reinterpret_cast<volatile int*>(flag);  // one snapshot for every consumer
-  named_bar(1, kConsumers);
-  const bool ok = !flag[1];
-  if (ok) {
+    if (!mbar_wait_bounded(accbar, 0)) {
+      set_err(a.err, kErrWaitTimeout);
+      atomicExch(flag, 1);
+    }
+    tc_after();
+    if (KVBP_PDL_LATE) pdl_launch_dependents();  // the next kernel may start its weight stream
+    ok = snapshot_flag();
+    // ---- accumulator -> partial tile: warp w reads features 32(w%4) .. +31 (its TMEM lane
+    // quarter), rows 16(w/4) .. +15 (columns)
+    if (ok) {
+      const int quarter = warp & 3, half = warp >> 2;
+      float v[16];
+      tc_ld16(tmem + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(half * 16), v);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int c = fgrp * 32 + 8 * j + 2 * t;
-      const int r0 = mtw * 16 + g;
-      *reinterpret_cast<float2*>(&rtile[r0 * kRedStride + c]) = make_float2(acc[j][0], acc[j][1]);
-      *reinterpret_cast<float2*>(&rtile[(r0 + 8) * kRedStride + c]) = make_float2(acc[j][2], acc[j][3]);
+      for (int j = 0; j < 16; ++j) rtile[(half * 16 + j) * kRedStride + quarter * 32 + lane] = v[j];
+    }
+    tc_before();
+  } else {
+    const int g = lane >> 2, t = lane & 3;
+    const int fgrp = warp & 3;  // features fgrp * 32 .. + 31 of the tile
+    const int mtw = warp >> 2;  // this warp's 16-row m-tile
+    float acc[4][4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+    const float inv_lo = NORM ? inv_rms[mtw * 16 + g] : 1.f;
+    const float inv_hi = NORM ? inv_rms[mtw * 16 + g + 8] : 1.f;
+    for (int u = 0; u < nch; ++u) {
+      const int st = u % kStages;
+      bool go = !*reinterpret_cast<volatile int*>(flag);
+      if (go && !mbar_wait_bounded(&full[st], (u / kStages) & 1)) {
+        set_err(a.err, kErrWaitTimeout);
+        atomicExch(flag, 1);
+        go = false;
+      }
+      if (!__all_sync(0xffffffffu, go)) break;  // the warp leaves together (ldmatrix/mma are warp-wide)
+      const uint8_t* wb = ring + st * kStageBytes;
+      const uint8_t* ab = wb + kWBytes;
+#pragma unroll
+      for (int kk = 0; kk < BK / 16; ++kk) {
+        const int col = kk * 16;
+        const int box = col >> 6, cb = (col & 63) >> 3;
+        // A fragments (activations): rows 16*mtw .. +15, k col .. col+15
+        uint32_t af[4];
+        {
+          const int row = mtw * 16 + (lane & 15);
+          const int chunk = cb + (lane >> 4);
+          ldmatrix_x4(smem_u32(ab + box * kABox + row * 128 + ((chunk ^ (row & 7)) << 4)), af[0], af[1], af[2], af[3]);
+          if (NORM) {
+            // x = bf16((h * inv_rms[row]) * w_norm[k]) on the fragment (k = col + 2t, +1, +8, +9)
+            const int kl = st * BK + col + 2 * t;
+            const uint32_t w01 = *reinterpret_cast<const uint32_t*>(wn_s + kl);
+            const uint32_t w89 = *reinterpret_cast<const uint32_t*>(wn_s + kl + 8);
+            const float wa = bf16lo(w01), wb2 = bf16hi(w01), wc = bf16lo(w89), wd = bf16hi(w89);
+            af[0] = pack_bf16((bf16lo(af[0]) * inv_lo) * wa, (bf16hi(af[0]) * inv_lo) * wb2);
+            af[1] = pack_bf16((bf16lo(af[1]) * inv_hi) * wa, (bf16hi(af[1]) * inv_hi) * wb2);
+            af[2] = pack_bf16((bf16lo(af[2]) * inv_lo) * wc, (bf16hi(af[2]) * inv_lo) * wd);
+            af[3] = pack_bf16((bf16lo(af[3]) * inv_hi) * wc, (bf16hi(af[3]) * inv_hi) * wd);
+          }
+        }
+        // B fragments (weights): features fgrp*32 .. +31, two x4 loads of 16 features each
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int j = lane >> 3;
+          const int frow = fgrp * 32 + h * 16 + (lane & 7) + ((j >> 1) << 3);
+          const int chunk = cb + (j & 1);
+          uint32_t b0, b1, b2, b3;
+          ldmatrix_x4(smem_u32(wb + box * kWBox + frow * 128 + ((chunk ^ (frow & 7)) << 4)), b0, b1, b2, b3);
+          mma_bf16_16816(acc[2 * h], af[0], af[1], af[2], af[3], b0, b1);
+          mma_bf16_16816(acc[2 * h + 1], af[0], af[1], af[2], af[3], b2, b3);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[st]);
+    }
+    if (KVBP_PDL_LATE) pdl_launch_dependents();  // the next kernel may start its weight stream
+
+    // ---- partial tile -> this CTA's shared memory (the ring is idle once every warp is done)
+    // acc[j]: rows 16mtw+g (c0,c1) and 16mtw+g+8 (c2,c3); columns fgrp*32 + 8j + 2t (+1)
+    ok = snapshot_flag();
+    if (ok) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int c = fgrp * 32 + 8 * j + 2 * t;
+        const int r0 = mtw * 16 + g;
+        *reinterpret_cast<float2*>(&rtile[r0 * kRedStride + c]) = make_float2(acc[j][0], acc[j][1]);
+        *reinterpret_cast<float2*>(&rtile[(r0 + 8) * kRedStride + c]) = make_float2(acc[j][2], acc[j][3]);
+      }
     }
   }
   if (cs > 1) cluster_sync_all();  // every partial tile of the cluster is complete
   else named_bar(1, kConsumers);
+  if (TC && warp == 0)  // every TMEM read and MMA of the CTA is complete
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
 
   // ---- reduce this CTA's row slice over the cluster (rank order) and run the epilogue
   const uint32_t rt_local = smem_u32(rtile);
@@ -613,12 +772,13 @@ static EncodeTiledFnG encode_fn_g() {
 static int gemm_smem_bytes(int MT) {
   using namespace gemm;
   const int kStages = stages_for(MT);
-  return kStages * (kWBytes + MT * 16 * BK * 2) + kStages * BK * 2 + (32 + 2 * 32) * 4 + 16 + 2 * kStages * 8 + 1024;
+  return kStages * (kWBytes + MT * 16 * BK * 2) + kStages * BK * 2 + (32 + 2 * 32) * 4 + 16 + 2 * kStages * 8 + 16 +
+         1024;
 }
 
 template <int MT, int EPI, bool NORM>
 static cudaError_t launch_gemm(cudaStream_t stream, const CUtensorMap& xmap, const gemm::Args& a) {
-  auto kern = gemm::decode_gemm_kernel<MT, EPI, NORM>;
+  auto kern = gemm::decode_gemm_kernel<MT, EPI, NORM, gemm::use_tc(MT)>;
   const int smem = gemm_smem_bytes(MT);
   static bool configured = false;
   if (!configured) {
@@ -714,7 +874,8 @@ int decode_gemm_allreduce(cudaStream_t stream, int M, int N, int K, const void* 
     // the ranks' CTAs wait on each other: every CTA of the grid must be resident at once
     const int MT = M > 16 ? 2 : 1;
     const int smem = gemm_smem_bytes(MT);
-    auto kern = MT == 2 ? decode_gemm_kernel<2, kResidAR, false> : decode_gemm_kernel<1, kResidAR, false>;
+    auto kern = MT == 2 ? decode_gemm_kernel<2, kResidAR, false, use_tc(2)>
+                        : decode_gemm_kernel<1, kResidAR, false, use_tc(1)>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e == cudaSuccess) e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     if (e != cudaSuccess) return fail(kStatusCuda, "decode_gemm_allreduce: %s", cudaGetErrorString(e));
