@@ -11,10 +11,11 @@
 // DRAM pages, no tensor map, no per-row 128-byte fragments.  A producer warp feeds a
 // 3-stage ring; four consumer warps run mma.sync m16n8k16 with the activations as the
 // M operand (16 rows per m-tile, loaded by 2-D TMA) and 32 output features per warp.
-// For 17..32 rows the main loop runs on the tcgen05 tensor cores instead, operands
-// swapped: the packed weight block is the M = 128 operand (already the 128-byte-swizzled
-// K-major image the MMA reads), the activation chunk the N = 32 operand, and the fp32
-// accumulator lives in 32 TMEM columns; one thread issues the MMAs and commits each stage
+// For 17..32 rows, and whenever the RMSNorm prologue is fused, the main loop runs on the
+// tcgen05 tensor cores instead, operands swapped: the packed weight block is the M = 128
+// operand (already the 128-byte-swizzled K-major image the MMA reads), the activation
+// chunk the N = 16 or 32 operand, and the fp32 accumulator lives in 32 TMEM columns; one
+// thread issues the MMAs and commits each stage
 // back to the producer, so the consumer warps only apply the RMSNorm prologue to the
 // staged activations and read the accumulator out at the end.  Both main loops leave the
 // same fp32 partial tile in shared memory, so the split-K reduction and every epilogue
@@ -70,10 +71,12 @@ __host__ __device__ constexpr int stages_for(int MT) { return MT == 1 ? kStagesM
 // kernel was issue-latency bound: 24 % HMMA-pipe activity, 43 % issue slots busy)
 __host__ __device__ constexpr int consumer_warps(int MT) { return 4 * MT; }
 __host__ __device__ constexpr int gemm_threads(int MT) { return consumer_warps(MT) * 32 + 32; }
-#ifndef KVBP_GEMM_TC_MIN_MT
-#define KVBP_GEMM_TC_MIN_MT 2  // m-tiles from which the main loop runs on tcgen05
-#endif
-__host__ __device__ constexpr bool use_tc(int MT) { return MT >= KVBP_GEMM_TC_MIN_MT; }
+// Main loop per kernel instance: tcgen05 for 17..32 rows, and for any row count when the
+// RMSNorm prologue is fused (the mma.sync loop re-forms the same normalised fragments in
+// each of the four warps that share them; the tcgen05 loop rewrites each staged chunk
+// once).  Without the prologue and with <= 16 rows the mma.sync loop is faster (shorter
+// set-up and drain per CTA): measured on B200 for the 1-, 16- and 32-row decode shapes.
+__host__ __device__ constexpr bool use_tc(int MT, bool norm) { return MT >= 2 || norm; }
 constexpr int kTmemCols = 32;  // accumulator: 128 lanes (features) x 16*MT columns (rows)
 constexpr int kWBytes = BN * BK * 2;  // 32 KiB: two 128 x 64 halves
 constexpr int kWBox = kWBytes / 2;
@@ -778,7 +781,7 @@ static int gemm_smem_bytes(int MT) {
 
 template <int MT, int EPI, bool NORM>
 static cudaError_t launch_gemm(cudaStream_t stream, const CUtensorMap& xmap, const gemm::Args& a) {
-  auto kern = gemm::decode_gemm_kernel<MT, EPI, NORM, gemm::use_tc(MT)>;
+  auto kern = gemm::decode_gemm_kernel<MT, EPI, NORM, gemm::use_tc(MT, NORM)>;
   const int smem = gemm_smem_bytes(MT);
   static bool configured = false;
   if (!configured) {
@@ -874,8 +877,8 @@ int decode_gemm_allreduce(cudaStream_t stream, int M, int N, int K, const void* 
     // the ranks' CTAs wait on each other: every CTA of the grid must be resident at once
     const int MT = M > 16 ? 2 : 1;
     const int smem = gemm_smem_bytes(MT);
-    auto kern = MT == 2 ? decode_gemm_kernel<2, kResidAR, false, use_tc(2)>
-                        : decode_gemm_kernel<1, kResidAR, false, use_tc(1)>;
+    auto kern = MT == 2 ? decode_gemm_kernel<2, kResidAR, false, use_tc(2, false)>
+                        : decode_gemm_kernel<1, kResidAR, false, use_tc(1, false)>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e == cudaSuccess) e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     if (e != cudaSuccess) return fail(kStatusCuda, "decode_gemm_allreduce: %s", cudaGetErrorString(e));
