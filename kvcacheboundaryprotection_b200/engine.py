@@ -344,18 +344,20 @@ class CappedKVEngine:
     def _pick_splits(N: int, K: int, sms: int = 148) -> int:
         """Split-K factor (CTAs per 128-column tile, one thread-block cluster) of a decode
         GEMM with N / 128 column tiles and K / 128 k-blocks, from a burst sweep of every
-        per-rank shape of the 7B and Qwen3-4B decoders at 1, 2, 4 and 8 GPUs on B200:
-        * >= 2 tiles per SM: no split (the grid already fills two CTAs per SM);
+        per-rank shape of the 7B, Qwen2.5-3B and Qwen3-4B decoders at 1, 2, 4 and 8 GPUs on
+        B200 (and of 149 .. 240-tile shapes at 1, 16 and 32 rows):
+        * more tiles than SMs: no split -- a split only adds a second wave (172 tiles of
+          the 3B gate/up: 29.7 us unsplit against 33.8 us with 3 splits; 149, 152, 160 and
+          200 tiles alike);
         * >= ~2/3 tile per SM: the split whose whole waves of 2 CTAs per SM carry the most
-          work per wave -- a grid a few CTAs past a whole wave leaves them as a slow tail
-          (149 tiles: 3 splits, not 2);
+          work per wave (148 tiles: 2 splits, one full wave);
         * 24.. tiles: about 256 CTAs, at most 8 per cluster (the single-GPU 7B q/k/v, o and
           down shapes, re-swept inside the decode step: 7, 8, 8);
         * fewer tiles: about 210 CTAs in all, at most 16 per cluster."""
         tiles = max(1, N // 128)
         kc = max(1, K // 128)
         slots = 2 * sms
-        if tiles >= slots:
+        if tiles > sms:
             return 1
         if tiles * 3 >= slots:
             cands = range(1, min(4, kc) + 1)
