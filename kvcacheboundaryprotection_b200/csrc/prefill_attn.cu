@@ -61,46 +61,6 @@ constexpr int kOffBars = kOffStat + 4 * kRows * 8;    // 12 mbarriers
 constexpr int kOffMisc = kOffBars + 128;              // tmem address, flags
 constexpr int kSmem = kOffMisc + 64 + 1024;
 
-// Shared-memory matrix descriptor: 128-byte swizzle, version 1 (tcgen05).
-__device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
-  return static_cast<uint64_t>((saddr >> 4) & 0x3FFF) | (static_cast<uint64_t>((lbo >> 4) & 0x3FFF) << 16) |
-         (static_cast<uint64_t>((sbo >> 4) & 0x3FFF) << 32) | (static_cast<uint64_t>(1) << 46) |
-         (static_cast<uint64_t>(2) << 61);
-}
-
-// kind::f16 instruction descriptor: D f32, A/B bf16, A K-major, B K- or MN-major, M x N
-__host__ __device__ constexpr uint32_t idesc(int M, int N, int b_mn_major) {
-  return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(b_mn_major) << 16) |
-         (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
-}
-
-__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t id, uint32_t acc) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
-      "l"(da), "l"(db), "r"(id), "r"(acc));
-}
-
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
-  uint32_t r[32];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-}
-
 // 2^x (the hardware approximation; -inf gives +0)
 __device__ __forceinline__ float ex2(float x) {
   float y;
@@ -124,8 +84,6 @@ __device__ __forceinline__ void rnd_scaled_pair(float& a, float& b, uint32_t sca
   b = __uint_as_float(w & 0xFFFF0000u);
 }
 
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
 struct Args {
   int P, Hq, Hkv, G;
@@ -178,9 +136,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(const __grid_
                  "r"(kTmemCols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
   }
-  tc_fence_before();
+  tc_before();
   __syncthreads();
-  tc_fence_after();
+  tc_after();
   const uint32_t tmem = *tslot;
   const uint32_t tO = tmem + 256;
   uint8_t* sQ = base + kOffQ;
@@ -199,7 +157,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(const __grid_
   // =============================== control warp =====================================
   if (warp == kCWarps) {
     if (lane == 0) {
-      const uint32_t idS = idesc(128, 128, 0), idO = idesc(128, 128, 1);
+      const uint32_t idS = tc_idesc(128, 128, 0), idO = tc_idesc(128, 128, 1);
       auto key_tile = [&](int j) { return j < nkt ? j : j - nkt; };
       auto issue_k = [&](int j) {  // K tile of S-tile j into buffer j & 1
         const int b = j & 1;
@@ -212,14 +170,14 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(const __grid_
         const int b = j & 1;
         wait_or_fail(&kfull[b], (j >> 1) & 1);
         if (j >= 2) wait_or_fail(&sfree[b], ((j >> 1) - 1) & 1);
-        tc_fence_after();
+        tc_after();
         for (int ks = 0; ks < 8; ++ks) {
           const uint32_t off = (ks >> 2) * kHalf + (ks & 3) * 32;
-          mma_bf16(tmem + b * 128, sdesc(smem_u32(sQ) + off, 16, 1024), sdesc(smem_u32(kbuf(b)) + off, 16, 1024),
+          tc_mma(tmem + b * 128, tc_sdesc(smem_u32(sQ) + off, 16, 1024), tc_sdesc(smem_u32(kbuf(b)) + off, 16, 1024),
                    idS, ks > 0);
         }
-        mma_commit(&sfull[b]);
-        mma_commit(&kfree[b]);
+        tc_commit(&sfull[b]);
+        tc_commit(&kfree[b]);
       };
       mbar_expect_tx(qfull, kTile);
       tma_load_3d(sQ, &qmap, qfull, 0, h, q0);
@@ -239,14 +197,14 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(const __grid_
           tma_load_3d(sV + kHalf, &vmap, vfull, 64, kt * kKeys, g);
           wait_or_fail(pfull, kt & 1);
           wait_or_fail(vfull, kt & 1);
-          tc_fence_after();
+          tc_after();
           for (int ks = 0; ks < 8; ++ks) {  // K = 128 keys in steps of 16
             const uint32_t aoff = (ks >> 2) * kHalf + (ks & 3) * 32;
-            const uint64_t dv = sdesc(smem_u32(sV) + ks * 16 * 128, kHalf, 1024);  // MN-major V
-            mma_bf16(tO, sdesc(smem_u32(sPh) + aoff, 16, 1024), dv, idO, (kt > 0 || ks > 0));
-            mma_bf16(tO, sdesc(smem_u32(sPl) + aoff, 16, 1024), dv, idO, 1);
+            const uint64_t dv = tc_sdesc(smem_u32(sV) + ks * 16 * 128, kHalf, 1024);  // MN-major V
+            tc_mma(tO, tc_sdesc(smem_u32(sPh) + aoff, 16, 1024), dv, idO, (kt > 0 || ks > 0));
+            tc_mma(tO, tc_sdesc(smem_u32(sPl) + aoff, 16, 1024), dv, idO, 1);
           }
-          mma_commit(pvdone);
+          tc_commit(pvdone);
         }
       }
     }
@@ -266,11 +224,11 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(const __grid_
     for (int j = 0; j < nkt; ++j) {
       const int b = j & 1;
       wait_or_fail(&sfull[b], (j >> 1) & 1);
-      tc_fence_after();
+      tc_after();
       float s[32];
       const bool ok = __all_sync(0xffffffffu, healthy());
-      if (ok) tmem_ld32(tmem + b * 128 + lane_base + cg * 32, s);
-      tc_fence_before();
+      if (ok) tc_ld32(tmem + b * 128 + lane_base + cg * 32, s);
+      tc_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&sfree[b]);
       if (ok) {
@@ -321,11 +279,11 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(const __grid_
     for (int kt = 0; kt < nkt; ++kt) {
       const int j = nkt + kt, b = j & 1;
       wait_or_fail(&sfull[b], (j >> 1) & 1);
-      tc_fence_after();
+      tc_after();
       float s[32];
       const bool ok = __all_sync(0xffffffffu, healthy());
-      if (ok) tmem_ld32(tmem + b * 128 + lane_base + cg * 32, s);
-      tc_fence_before();
+      if (ok) tc_ld32(tmem + b * 128 + lane_base + cg * 32, s);
+      tc_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&sfree[b]);
 #pragma unroll
@@ -387,10 +345,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(const __grid_
     }
     // ---- O -> bf16 output (this warp's 32 of the 128 dims)
     wait_or_fail(pvdone, (nkt - 1) & 1);
-    tc_fence_after();
+    tc_after();
     if (__all_sync(0xffffffffu, healthy())) {
       float o[32];
-      tmem_ld32(tO + lane_base + cg * 32, o);
+      tc_ld32(tO + lane_base + cg * 32, o);
       if (row < a.P) {
         uint32_t w[16];
 #pragma unroll
@@ -401,7 +359,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(const __grid_
       }
     }
   }
-  tc_fence_before();
+  tc_before();
   __syncthreads();
   if (warp == kCWarps) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
 }

@@ -37,48 +37,6 @@ constexpr int kHalf = 128 * 128;  // bytes of one 128 x 64 bf16 tile (16 KiB)
 constexpr int kThreads = 6 * 32;
 constexpr int kGroupM = 8;  // row tiles per raster band
 
-__device__ __forceinline__ uint64_t sdesc(uint32_t saddr) {
-  // K-major, 128-byte swizzle: 8-row core groups 1024 B apart (SBO), LBO unused (16 B)
-  return static_cast<uint64_t>((saddr >> 4) & 0x3FFF) | (static_cast<uint64_t>(1) << 16) |
-         (static_cast<uint64_t>(1024 >> 4) << 32) | (static_cast<uint64_t>(1) << 46) | (static_cast<uint64_t>(2) << 61);
-}
-
-// kind::f16 instruction descriptor: D f32, A/B bf16, both K-major, M x N
-__host__ __device__ constexpr uint32_t idesc(int M, int N) {
-  return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(N >> 3) << 17) |
-         (static_cast<uint32_t>(M >> 4) << 24);
-}
-
-__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t id, uint32_t acc) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
-      "l"(da), "l"(db), "r"(id), "r"(acc));
-}
-
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
-  uint32_t r[32];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-}
-
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
 struct Args {
   const __nv_bfloat16* w;  // packed [N/128][K/128][2][128][64]
   void* out;               // plain: bf16 [M][ldo] (columns n); SwiGLU: bf16 [M][ldo] (features n / 2);
@@ -140,9 +98,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
                  "r"(2 * BN));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
   }
-  tc_fence_before();
+  tc_before();
   __syncthreads();
-  tc_fence_after();
+  tc_after();
   const uint32_t tmem = *tslot;
   auto healthy = [&]() { return !*reinterpret_cast<volatile int*>(bad); };
   auto wait_or_fail = [&](uint64_t* bar, uint32_t ph) {
@@ -186,14 +144,14 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
   } else if (warp == 1) {
     // =========================== MMA issue ============================================
     if (lane == 0) {
-      constexpr uint32_t id = idesc(kBM, BN);
+      constexpr uint32_t id = tc_idesc(kBM, BN);
       long long g = 0;
       int i = 0;  // tiles of this CTA so far
       for (int t = blockIdx.x; t < n_tiles && healthy(); t += gridDim.x, ++i) {
         const int buf = i & 1;
         // the epilogue has drained this buffer's previous tile (tile i - 2)
         if (i >= 2 && !wait_or_fail(&accempty[buf], static_cast<uint32_t>((i >> 1) - 1) & 1)) break;
-        tc_fence_after();
+        tc_after();
         const uint32_t acc = tmem + static_cast<uint32_t>(buf * BN);
         bool ok = true;
         for (int u = 0; u < nk; ++u, ++g) {
@@ -202,16 +160,16 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
             ok = false;
             break;
           }
-          tc_fence_after();
+          tc_after();
           const uint32_t sA = smem_u32(base + st * kStage);
           const uint32_t sB = sA + kHalf;
 #pragma unroll
           for (int ks = 0; ks < kBK / 16; ++ks)
-            mma_bf16(acc, sdesc(sA + ks * 32), sdesc(sB + ks * 32), id, (u > 0 || ks > 0) ? 1u : 0u);
-          mma_commit(&empty[st]);
+            tc_mma(acc, tc_sdesc(sA + ks * 32), tc_sdesc(sB + ks * 32), id, (u > 0 || ks > 0) ? 1u : 0u);
+          tc_commit(&empty[st]);
         }
         if (!ok) break;
-        mma_commit(&accfull[buf]);  // arrives when every MMA issued so far is complete
+        tc_commit(&accfull[buf]);  // arrives when every MMA issued so far is complete
       }
     }
     __syncwarp();
@@ -226,14 +184,14 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
       tile_of(t, n_tn, n_tm, tm, tn);
       const int row = tm * kBM + q * 32 + lane;
       const bool ok = wait_or_fail(&accfull[buf], static_cast<uint32_t>(i >> 1) & 1);
-      tc_fence_after();
+      tc_after();
       if (!__all_sync(0xffffffffu, ok && healthy())) break;
       const uint32_t acc = tmem + lane_base + static_cast<uint32_t>(buf * BN);
       if (a.epi == 3) {
 #pragma unroll 1
         for (int c = 0; c < BN; c += 32) {
           float v[32];
-          tmem_ld32(acc + c, v);
+          tc_ld32(acc + c, v);
           const int n = tn * BN + c;
           if (row < a.M && n < a.N) {
             float4* dst = reinterpret_cast<float4*>(static_cast<float*>(a.out) + static_cast<size_t>(row) * a.ldo + n);
@@ -245,7 +203,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
 #pragma unroll 1
         for (int c = 0; c < BN; c += 32) {
           float v[32];
-          tmem_ld32(acc + c, v);
+          tc_ld32(acc + c, v);
           const int n = tn * BN + c;
           if (row < a.M && n < a.N) {
             uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.out) + static_cast<size_t>(row) * a.ldo + n);
@@ -261,8 +219,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
 #pragma unroll 1
           for (int j = 0; j < 64; j += 32) {  // 32 gate columns and the matching 32 up columns
             float gv[32], uv[32];
-            tmem_ld32(acc + b * 128 + j, gv);
-            tmem_ld32(acc + b * 128 + 64 + j, uv);
+            tc_ld32(acc + b * 128 + j, gv);
+            tc_ld32(acc + b * 128 + 64 + j, uv);
             const int f = (tn * kNB + b) * 64 + j;  // feature index
             if (row < a.M) {
               uint32_t pk[16];
@@ -286,12 +244,12 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
         }
       }
       // this warp's TMEM reads are complete: hand the buffer back to the MMA warp
-      tc_fence_before();
+      tc_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&accempty[buf]);
     }
   }
-  tc_fence_before();
+  tc_before();
   __syncthreads();
   if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * BN));
 }

@@ -152,11 +152,12 @@ def test_residual_add_matches_torch():
     assert (ss[:, M:] == 0).all()
 
 
-def test_gemm_fp32_epilogue_is_the_unrounded_sum():
+@pytest.mark.parametrize("M", [16, 32])  # 32 rows: the tcgen05 main loop
+def test_gemm_fp32_epilogue_is_the_unrounded_sum(M):
     from kvcacheboundaryprotection_b200.engine import pack_weight
 
     g = torch.Generator(device="cuda").manual_seed(4)
-    M, N, K = 16, 512, 1024
+    N, K = 512, 1024
     W = (torch.randn(N, K, generator=g, device="cuda") * 0.05).to(torch.bfloat16)
     x = torch.randn(M, K, generator=g, device="cuda").to(torch.bfloat16)
     for splits in (1, 4):
@@ -167,3 +168,37 @@ def test_gemm_fp32_epilogue_is_the_unrounded_sum():
         torch.cuda.synchronize()
         ref = x.float() @ W.float().t()
         assert torch.allclose(out, ref, rtol=1e-4, atol=1e-4)
+
+
+@pytest.mark.parametrize("M,splits", [(5, 1), (16, 4), (32, 2)])  # 32 rows: the tcgen05 main loop
+def test_fused_allreduce_gemm_single_rank_equals_residual_gemm(M, splits):
+    """kvbp_decode_gemm_allreduce with one rank (its own symmetric buffer the only peer) is
+    the residual GEMM: h = bf16(h + bf16(acc)) bit for bit and the same per-tile sums of
+    squares of the new h -- the allreduce epilogue's push, tag wait and rank-order sum
+    reduce to the identity."""
+    from kvcacheboundaryprotection_b200.engine import pack_weight
+
+    g = torch.Generator(device="cuda").manual_seed(11)
+    N, K = 1024, 2048
+    W = (torch.randn(N, K, generator=g, device="cuda") * 0.03).to(torch.bfloat16)
+    x = torch.randn(M, K, generator=g, device="cuda").to(torch.bfloat16)
+    h0 = torch.randn(M, N, generator=g, device="cuda").to(torch.bfloat16)
+    Wp = pack_weight(W)
+    L = capi.lib()
+    st = torch.cuda.current_stream().cuda_stream
+    h_ref, ss_ref = h0.clone(), torch.zeros(N // 128, 32, device="cuda")
+    capi.check(L.kvbp_decode_gemm(st, 1, M, N, K, Wp.data_ptr(), x.data_ptr(), K, None, 0, None, 1e-6,
+                                  h_ref.data_ptr(), N, ss_ref.data_ptr(), splits, None), "residual gemm")
+    buf_bytes = 2 * 1 * M * N * 8
+    buf = torch.zeros(buf_bytes // 4, dtype=torch.int32, device="cuda")
+    peers = torch.tensor([buf.data_ptr()], dtype=torch.int64, device="cuda")
+    epoch = torch.ones(1, dtype=torch.int32, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    h, ss = h0.clone(), torch.zeros(N // 128, 32, device="cuda")
+    capi.check(L.kvbp_decode_gemm_allreduce(st, M, N, K, Wp.data_ptr(), x.data_ptr(), K, h.data_ptr(), ss.data_ptr(),
+                                            splits, peers.data_ptr(), 1, 0, 0, epoch.data_ptr(), buf_bytes,
+                                            err.data_ptr()), "allreduce gemm")
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    assert torch.equal(h, h_ref)
+    assert torch.allclose(ss[:, :M], ss_ref[:, :M], rtol=1e-5, atol=0)
