@@ -70,8 +70,8 @@ __host__ __device__ inline int align_up(int x, int a) { return (x + a - 1) / a *
 __host__ __device__ inline AttnSmem attn_smem_layout(int nloc_tiles, int consumer_warps) {
   AttnSmem L;
   const int nloc = nloc_tiles * kTile;
-  L.logits = kStages * kStageBytes;  // [nloc][8] rounded logits
-  L.escr = L.logits + nloc * 8 * 4;  // [warp][16 rows][8] softmax weights of the current tile
+  L.logits = kStages * kStageBytes;  // [nloc][8] rounded logits (bf16: they are bf16 values)
+  L.escr = L.logits + nloc * 8 * 2;  // [warp][16 rows][8] softmax weights of the current tile
   L.spos = L.escr + consumer_warps * 16 * 8 * 4;
   L.orecv = align_up(L.spos + nloc * 4, 16);  // [CS][per] received O slices
   L.srecv = L.orecv + (8 * kD + kMaxCluster) * 4;  // [CS][16] received (max, sum)
@@ -129,7 +129,7 @@ __global__ void __launch_bounds__(attn_threads(GR), kMinBlocks) decode_attn_scor
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const AttnSmem L = attn_smem_layout(p.nloc_tiles, kConsumerWarps);
   uint8_t* ring = base;
-  float* logits = reinterpret_cast<float*>(base + L.logits);
+  __nv_bfloat16* logits = reinterpret_cast<__nv_bfloat16*>(base + L.logits);
   float* escr = reinterpret_cast<float*>(base + L.escr);
   int* spos_s = reinterpret_cast<int*>(base + L.spos);
   float* orecv = reinterpret_cast<float*>(base + L.orecv);
@@ -335,8 +335,8 @@ __global__ void __launch_bounds__(attn_threads(GR), kMinBlocks) decode_attn_scor
       float sa1 = va ? bf16r(bf16r(a0c[1] + a1c[1]) * p.scale) : NEG_INF;
       float sb0 = vb ? bf16r(bf16r(a0c[2] + a1c[2]) * p.scale) : NEG_INF;
       float sb1 = vb ? bf16r(bf16r(a0c[3] + a1c[3]) * p.scale) : NEG_INF;
-      *reinterpret_cast<float2*>(&logits[lta * 8 + 2 * t]) = make_float2(sa0, sa1);
-      *reinterpret_cast<float2*>(&logits[ltb * 8 + 2 * t]) = make_float2(sb0, sb1);
+      *reinterpret_cast<uint32_t*>(&logits[lta * 8 + 2 * t]) = pack_bf16(sa0, sa1);  // exact: bf16 values
+      *reinterpret_cast<uint32_t*>(&logits[ltb * 8 + 2 * t]) = pack_bf16(sb0, sb1);
       // ---- online softmax over the warp's 16 rows -----------------------------------
       float tm0 = fmaxf(sa0, sb0), tm1 = fmaxf(sa1, sb1);
 #pragma unroll
@@ -523,7 +523,7 @@ __global__ void __launch_bounds__(attn_threads(GR), kMinBlocks) decode_attn_scor
         float mx = 0.f;
 #pragma unroll
         for (int h = 0; h < G; ++h) {
-          const float pr = iLh[h] > 0.f ? expf(logits[i * 8 + h] - Mh[h]) * iLh[h] : 0.f;
+          const float pr = iLh[h] > 0.f ? expf(__bfloat162float(logits[i * 8 + h]) - Mh[h]) * iLh[h] : 0.f;
           mx = fmaxf(mx, pr);
         }
         if (mx != mx) set_err(p.err, kErrNanScore);
@@ -537,7 +537,7 @@ __global__ void __launch_bounds__(attn_threads(GR), kMinBlocks) decode_attn_scor
         float mx = 0.f;
 #pragma unroll
         for (int h = 0; h < G; ++h) {
-          const float pr = iLh[h] > 0.f ? expf(logits[i * 8 + h] - Mh[h]) * iLh[h] : 0.f;
+          const float pr = iLh[h] > 0.f ? expf(__bfloat162float(logits[i * 8 + h]) - Mh[h]) * iLh[h] : 0.f;
           mx = fmaxf(mx, pr);
           if (kvh * G + h < p.Hkv)
             atomicMax(reinterpret_cast<int*>(&hrow[static_cast<size_t>(h) * S + t0 * kTile + i]), __float_as_int(pr));
@@ -656,8 +656,8 @@ __host__ __device__ inline PersistSmem persist_smem_layout(int nloc_tiles, int c
   PersistSmem L;
   const int nloc = nloc_tiles * kTile;
   L.opart = kStages * kStageBytes;                    // [warp][hp][128] partial outputs
-  L.logits = L.opart + consumer_warps * hp * kD * 4;  // [nloc][hp] rounded logits
-  L.escr = L.logits + nloc * hp * 4;                  // [warp][16][8] softmax weights of a tile
+  L.logits = L.opart + consumer_warps * hp * kD * 4;  // [nloc][hp] rounded logits (bf16 values)
+  L.escr = L.logits + nloc * hp * 2;                  // [warp][16][8] softmax weights of a tile
   L.spos = L.escr + consumer_warps * 16 * 8 * 4;      // [nloc] slot positions
   L.orecv = align_up(L.spos + nloc * 4, 16);          // received O slices
   L.srecv = L.orecv + (8 * kD + kMaxCluster) * 4;     // [CS][16] received (max, sum)
@@ -679,7 +679,7 @@ __global__ void __launch_bounds__(attn_threads(GR), kMinBlocks) decode_attn_pers
   const PersistSmem L = persist_smem_layout(p.nloc_tiles, kConsumerWarps, HP);
   uint8_t* ring = base;
   float* opart = reinterpret_cast<float*>(base + L.opart);
-  float* logits = reinterpret_cast<float*>(base + L.logits);
+  __nv_bfloat16* logits = reinterpret_cast<__nv_bfloat16*>(base + L.logits);
   float* escr = reinterpret_cast<float*>(base + L.escr);
   int* spos_s = reinterpret_cast<int*>(base + L.spos);
   float* orecv = reinterpret_cast<float*>(base + L.orecv);
@@ -884,8 +884,8 @@ __global__ void __launch_bounds__(attn_threads(GR), kMinBlocks) decode_attn_pers
         float sb0 = vb ? bf16r(bf16r(a0c[2] + a1c[2]) * p.scale) : NEG_INF;
         float sb1 = vb ? bf16r(bf16r(a0c[3] + a1c[3]) * p.scale) : NEG_INF;
         if (2 * t < HP) {
-          *reinterpret_cast<float2*>(&logits[lta * HP + 2 * t]) = make_float2(sa0, sa1);
-          *reinterpret_cast<float2*>(&logits[ltb * HP + 2 * t]) = make_float2(sb0, sb1);
+          *reinterpret_cast<uint32_t*>(&logits[lta * HP + 2 * t]) = pack_bf16(sa0, sa1);  // exact: bf16 values
+          *reinterpret_cast<uint32_t*>(&logits[ltb * HP + 2 * t]) = pack_bf16(sb0, sb1);
         }
         float tm0 = fmaxf(sa0, sb0), tm1 = fmaxf(sa1, sb1);
 #pragma unroll
@@ -1080,7 +1080,7 @@ __global__ void __launch_bounds__(attn_threads(GR), kMinBlocks) decode_attn_pers
         float mx = 0.f;
 #pragma unroll
         for (int h = 0; h < G; ++h) {
-          const float pr = iLh[h] > 0.f ? expf(logits[i * HP + h] - Mh[h]) * iLh[h] : 0.f;
+          const float pr = iLh[h] > 0.f ? expf(__bfloat162float(logits[i * HP + h]) - Mh[h]) * iLh[h] : 0.f;
           mx = fmaxf(mx, pr);
         }
         if (mx != mx) set_err(p.err, kErrNanScore);
