@@ -73,6 +73,10 @@ def parse():
                     help="sequences (per GPU under data parallelism, in total under tensor parallelism)")
     ap.add_argument("--parallel", default="auto", choices=["auto", "tp", "dp"],
                     help="multi-GPU scheme (auto: the workload's own, see WORKLOADS)")
+    ap.add_argument("--tp-size", type=int, default=None,
+                    help="tensor parallelism: ranks per tensor-parallel group (default: the reference's clamp, the "
+                         "largest size <= N dividing the query heads, KV heads and FFN width; N / size data-parallel "
+                         "groups then split the sequences)")
     ap.add_argument("--no-micro", action="store_true", help="skip the operator microbench sweep")
     ap.add_argument("--no-configs", action="store_true", help="skip the other workloads measured beside the headline")
     ap.add_argument("--no-check", action="store_true", help="skip the tensor-parallel correctness check")
@@ -158,10 +162,36 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------------ ours
-def _build_engine(workload, tp, rank, world, dev, B, n_new, seed_rank):
-    """The workload's engine on this rank: tensor-parallel (TPEngine over all ranks'
-    KV-head groups, the same synthetic post-prefill state on every rank) or one GPU's
-    independent sequences (CappedKVEngine, its own seeded state)."""
+_TP_GROUPS = {}  # tensor-parallel size -> the process groups (created once, by every rank)
+
+
+def tp_layout(a, cfg, world, rank, B):
+    """(tp size, data-parallel replicas, this rank's replica, rank in its group, group,
+    group ranks) of a tensor-parallel decode of B sequences over ``world`` ranks: the tp
+    size is --tp-size or the reference's clamp (tp.reference_tp_size); the replicas split
+    the sequences; with one replica the group is the whole world."""
+    import torch.distributed as dist
+
+    from kvcacheboundaryprotection_b200.tp import reference_tp_size, tp_groups
+
+    t = min(a.tp_size or reference_tp_size(cfg, world), world)
+    if t < 1 or world % t or B % (world // t):
+        t = world  # the sequences do not split over the replicas: one group of every rank
+    dp = world // t
+    if dp == 1:
+        return t, 1, 0, rank, None, None
+    groups = tp_groups(world, t)
+    if t not in _TP_GROUPS:
+        _TP_GROUPS[t] = [dist.new_group(r) for r in groups]  # collective: every rank, every group
+    g = rank // t
+    return t, dp, g, rank % t, _TP_GROUPS[t][g], groups[g]
+
+
+def _build_engine(a, workload, tp, rank, world, dev, B, n_new, seed_rank):
+    """The workload's engine on this rank: tensor-parallel (TPEngine over its group's
+    KV-head shards, the same synthetic post-prefill state on every rank of a group, B /
+    replicas sequences per group) or one GPU's independent sequences (CappedKVEngine, its
+    own seeded state)."""
     import torch
 
     from kvcacheboundaryprotection_b200.config import get_config
@@ -175,13 +205,15 @@ def _build_engine(workload, tp, rank, world, dev, B, n_new, seed_rank):
     if tp:
         from kvcacheboundaryprotection_b200.tp import TPEngine, local_config, shard_weights, tp_plan
 
-        plan = tp_plan(cfg, world, rank)
+        t, dp, g, trank, group, granks = tp_layout(a, cfg, world, rank, B)
+        plan = tp_plan(cfg, t, trank)
         fw = FusedWeights(local_config(cfg, plan), shard_weights(cfg, weights, plan), dev)
         del weights
         torch.cuda.empty_cache()
-        eng = TPEngine(cfg, fw, plan=plan, fused_allreduce=True, batch=B, evict=spec, max_prompt_len=P,
-                       max_new_tokens=n_new, device=dev)
-        eng.synthetic_prefill(P, seed=1234)
+        eng = TPEngine(cfg, fw, plan=plan, fused_allreduce=not a.nccl_allreduce, batch=B // dp, evict=spec,
+                       max_prompt_len=P, max_new_tokens=n_new, device=dev, group=group, group_ranks=granks)
+        eng.tp_size, eng.replicas, eng.replica = t, dp, g
+        eng.synthetic_prefill(P, seed=1234 + g)
     else:
         fw = FusedWeights(cfg, weights, dev)
         del weights
@@ -207,7 +239,8 @@ def decode_run(a, workload, par, rank, world, local_rank, *, steps, warmup, full
     B = (a.batch or B0) if workload == a.workload else B0
     K, W = steps, warmup
     n_new = W + K + (a.e2e_steps if full else 0) + 16
-    cfg, eng, fw = _build_engine(workload, tp, rank, world, dev, B, n_new, rank)
+    cfg, eng, fw = _build_engine(a, workload, tp, rank, world, dev, B, n_new, rank)
+    Br = eng.B  # this rank's sequences (a tensor-parallel group's share of the B under tp)
     eng.capture()
     for _ in range(W):
         eng.run_step()
@@ -242,8 +275,8 @@ def decode_run(a, workload, par, rank, world, local_rank, *, steps, warmup, full
     e2e = None
     if full:
         # end to end through host buffers: the host feeds each step's tokens and reads them back
-        pin_in = torch.empty(B, dtype=torch.int32, pin_memory=True)
-        pin_out = torch.empty(B, dtype=torch.int32, pin_memory=True)
+        pin_in = torch.empty(Br, dtype=torch.int32, pin_memory=True)
+        pin_out = torch.empty(Br, dtype=torch.int32, pin_memory=True)
         pin_in.copy_(eng.tokens.cpu())
         if world > 1:
             dist.barrier()
@@ -263,8 +296,8 @@ def decode_run(a, workload, par, rank, world, local_rank, *, steps, warmup, full
         e2e = {
             "value": round(seqs * a.e2e_steps / e2e_s, 2),
             "unit": "tok/s",
-            "h2d_bytes_per_step": 4 * B,
-            "d2h_bytes_per_step": 4 * B,
+            "h2d_bytes_per_step": 4 * Br,  # per rank
+            "d2h_bytes_per_step": 4 * Br,
             "how": "host copies each step's token ids in from pinned memory, replays the step, reads the sampled ids back and synchronises",
         }
 
@@ -272,7 +305,7 @@ def decode_run(a, workload, par, rank, world, local_rank, *, steps, warmup, full
     km = measure_kernels_in_step(eng, steps=2)
     hbm, tf, peak_kind = peaks()
     avg_valid = C + 3.5  # retained slots per (sequence, kv head): C .. C+E-1 over a cadence
-    kbytes = kernel_algorithmic_bytes(eng.cfg, B, avg_valid)  # this rank's shapes
+    kbytes = kernel_algorithmic_bytes(eng.cfg, Br, avg_valid)  # this rank's shapes
     per_step = {"attention": cfg.n_layers, "qkv": cfg.n_layers, "o": cfg.n_layers, "gate_up": cfg.n_layers,
                 "down": cfg.n_layers, "lm_head": 1}
     kernels = {}
@@ -296,8 +329,14 @@ def decode_run(a, workload, par, rank, world, local_rank, *, steps, warmup, full
                            d["timing"] + ": events around each eager launch"),
                 "algorithmic_bytes_per_launch": d["algorithmic_bytes_per_launch"]}
 
+    if tp:
+        tsz, reps = getattr(eng, "tp_size", world), getattr(eng, "replicas", 1)
+        tp_par = f"tp{tsz}" + (f"xdp{reps}" if reps > 1 else "")
+        tp_desc = (f"{B} sequences tensor-parallel over {world} GPUs" if reps == 1 else
+                   f"{B} sequences: {reps} data-parallel groups of {Br}, each tensor-parallel over {tsz} GPUs "
+                   f"(the reference's TP clamp for {eng.full_cfg.n_kv_heads} KV heads)")
     lc = eng.cfg
-    step_bytes = fw.streamed_bytes(B) + cfg.n_layers * algorithmic_attn_bytes(B, lc.n_heads, lc.n_kv_heads, avg_valid)
+    step_bytes = fw.streamed_bytes(Br) + cfg.n_layers * algorithmic_attn_bytes(Br, lc.n_heads, lc.n_kv_heads, avg_valid)
     step_ms = ms / K
     out = {
         "metric": METRIC,
@@ -314,14 +353,14 @@ def decode_run(a, workload, par, rank, world, local_rank, *, steps, warmup, full
         "data": "synthetic (seeded random bf16 weights N(0,0.02); decode from a synthetic post-prefill state)",
         "config": {
             "workload": f"{preset} decode, capacity {C}, {policy} eviction every 8 steps, protect-frac 0.10, "
-            + (f"{B} sequences tensor-parallel over {world} GPUs" if tp else f"{B} sequences/GPU")
+            + (tp_desc if tp else f"{B} sequences/GPU")
             + f", prompt {P}, greedy",
-            "batch_per_gpu": B,
+            "batch_per_gpu": Br,
             "global_batch": seqs,
             "capacity": C,
             "prompt_len": P,
             "policy": policy,
-            "parallelism": f"tp{world}" if tp else f"dp{world}",
+            "parallelism": tp_par if tp else f"dp{world}",
             "allreduce": "fused NVLink GEMM epilogue (o, down) + NCCL (score, argmax)" if tp else None,
             "l2": "inputs larger than L2 (all weights streamed every step)",
         },
@@ -378,12 +417,18 @@ def tp_check(a, workload, rank, world, local_rank, eng, steps=8):
     dev = torch.device("cuda", local_rank)
     names = ["token_log", "evlog", "evcount", "slot_pos", "cumul", "h", "tokens", "retained_log"]
     mine = torch.tensor([_checksum(getattr(eng, n)) for n in names], dtype=torch.int64, device=dev)
-    allv = [torch.empty_like(mine) for _ in range(world)]
-    dist.all_gather(allv, mine)
+    # the ranks of one tensor-parallel group decode the same sequences (data-parallel
+    # replicas of the group decode others)
+    allv = [torch.empty_like(mine) for _ in range(eng.plan.world)]
+    dist.all_gather(allv, mine, group=eng.group)
     differ = [names[i] for i in range(len(names)) if any(int(v[i]) != int(allv[0][i]) for v in allv)]
+    gate = torch.tensor([1 if differ else 0], dtype=torch.int32, device=dev)
+    dist.all_reduce(gate, op=dist.ReduceOp.MAX)  # any group's ranks differ
+    if int(gate.item()) and not differ:
+        differ = ["(another tensor-parallel group)"]
 
     preset, B0, C, P, policy, _ = WORKLOADS[workload]
-    B = (a.batch or B0) if workload == a.workload else B0
+    B = eng.B  # this group's sequences
     cfg = eng.full_cfg
     ref = CappedKVEngine(cfg, FusedWeights(cfg, init_weights(cfg, seed=0, device=dev), dev), batch=B,
                          evict=EvictionSpec(policy, C, 8, True, 0.10, 0.10), max_prompt_len=P,

@@ -89,6 +89,26 @@ def tp_plan(cfg: ModelConfig, world: int, rank: int) -> TPPlan:
     return TPPlan(world, rank, kv, q, rep, flo * 128, fhi * 128, vlo * 128, vhi * 128)
 
 
+def reference_tp_size(cfg: ModelConfig, devices: int) -> int:
+    """The tensor-parallel size the reference runs on ``devices`` devices: the largest
+    size <= devices that divides the query heads, the KV heads and the FFN width
+    (jax_inference.py:1846-1861 clamps a requested TP size this way; Qwen2.5-7B's 4 KV
+    heads make it 4 on 8 devices, Qwen3-4B's 8 KV heads keep 8)."""
+    t = max(1, int(devices))
+    while t > 1 and (cfg.n_heads % t or cfg.n_kv_heads % t or cfg.ffn % t):
+        t -= 1
+    return t
+
+
+def tp_groups(world: int, tp_size: int) -> List[List[int]]:
+    """Ranks of the tensor-parallel groups when ``world`` ranks run ``world // tp_size``
+    data-parallel replicas of a ``tp_size``-way tensor-parallel decode: consecutive ranks
+    form a group (on one node they share the NVSwitch fabric equally)."""
+    if tp_size < 1 or world % tp_size:
+        raise ValueError(f"tensor-parallel size {tp_size} does not divide {world} ranks")
+    return [list(range(g * tp_size, (g + 1) * tp_size)) for g in range(world // tp_size)]
+
+
 def local_config(cfg: ModelConfig, plan: TPPlan) -> ModelConfig:
     """The shapes one rank computes with (its heads, FFN share and vocabulary share)."""
     return replace(
@@ -148,9 +168,10 @@ class NcclCollective:
 class SymmetricBuffer:
     """A device buffer mapped into every rank of the process group (torch symmetric
     memory): ``peers`` is a device array of the ranks' base addresses, for the decode
-    GEMM's fused allreduce."""
+    GEMM's fused allreduce -- of ranks ``peer_ranks`` only (default: all), so that a
+    tensor-parallel group inside a larger job passes the kernel its own ranks' buffers."""
 
-    def __init__(self, nbytes: int, device: torch.device, group=None):
+    def __init__(self, nbytes: int, device: torch.device, group=None, peer_ranks: Sequence[int] = None):
         import torch.distributed as dist
         import torch.distributed._symmetric_memory as symm_mem
 
@@ -158,7 +179,10 @@ class SymmetricBuffer:
         self.nbytes = (int(nbytes) + 255) // 256 * 256
         self.buf = symm_mem.empty(self.nbytes, dtype=torch.uint8, device=device)
         self.handle = symm_mem.rendezvous(self.buf, group.group_name)
-        self.peers = torch.tensor(list(self.handle.buffer_ptrs), dtype=torch.int64, device=device)
+        ptrs = list(self.handle.buffer_ptrs)
+        if peer_ranks is not None:
+            ptrs = [ptrs[r] for r in peer_ranks]
+        self.peers = torch.tensor(ptrs, dtype=torch.int64, device=device)
         self.group = group
         self.reset()
 
@@ -198,15 +222,18 @@ class TPEngine(CappedKVEngine):
     sharded here) or this rank's prebuilt ``FusedWeights``.  ``collective`` performs the
     reductions when the step runs as one rank of a process group.  With
     ``fused_allreduce`` (one rank per GPU in a real process group) the o/down partial sums
-    are reduced inside the GEMMs over NVLink instead of by ``collective``."""
+    are reduced inside the GEMMs over NVLink instead of by ``collective``.  ``group`` /
+    ``group_ranks``: the tensor-parallel group when the process group holds several
+    (data-parallel replicas of the tensor-parallel decode); default the whole world."""
 
     def __init__(self, cfg: ModelConfig, weights, *, plan: TPPlan, collective: Callable = None,
-                 fused_allreduce: bool = False, **kw):
+                 fused_allreduce: bool = False, group=None, group_ranks: Sequence[int] = None, **kw):
         if kw.get("gemm", "kvbp") != "kvbp":
             raise ValueError("tensor parallelism runs on the own decode GEMMs")
         self.full_cfg = cfg
         self.plan = plan
-        self.coll = collective or NcclCollective()
+        self.group = group
+        self.coll = collective or NcclCollective(group)
         lcfg = local_config(cfg, plan)
         if not isinstance(weights, FusedWeights):
             dev = kw.get("device")
@@ -218,7 +245,10 @@ class TPEngine(CappedKVEngine):
         self.splits.update(allreduce_splits(cfg, plan.world, plan.rank))
         self.symm = None
         if fused_allreduce and plan.world > 1:
-            self.symm = SymmetricBuffer(allreduce_buffer_bytes(plan.world, self.B, cfg.hidden), self.dev)
+            # mapped over the whole process group (every rank makes the same call), the
+            # kernel given its own group's ranks
+            self.symm = SymmetricBuffer(allreduce_buffer_bytes(plan.world, self.B, cfg.hidden), self.dev,
+                                        peer_ranks=group_ranks)
 
     def _allreduce_gemm(self, name, K, w, x, ldx, call, ss_out) -> None:
         c = self.cfg

@@ -116,3 +116,20 @@ def test_allreduce_slots_are_independent_of_the_call():
             assert not (seen & set(offs))
             seen |= set(offs)
     assert len(seen) * 16 == size
+
+
+def test_reference_tp_clamp_and_groups():
+    """The tensor-parallel size follows the reference's clamp (jax_inference.py:1846-1861:
+    the largest size <= the requested one dividing the query heads, the KV heads and the
+    FFN width); the remaining factor of the world becomes data-parallel groups of
+    consecutive ranks."""
+    from kvcacheboundaryprotection_b200.tp import reference_tp_size, tp_groups
+
+    q7, q4, q3 = get_config("qwen2.5-7b"), get_config("qwen3-4b"), get_config("qwen2.5-3b")
+    assert [reference_tp_size(q7, n) for n in (1, 2, 4, 8)] == [1, 2, 4, 4]  # 4 KV heads
+    assert [reference_tp_size(q4, n) for n in (1, 2, 4, 8)] == [1, 2, 4, 8]  # 8 KV heads
+    assert [reference_tp_size(q3, n) for n in (1, 2, 4, 8)] == [1, 2, 2, 2]  # 2 KV heads
+    assert tp_groups(8, 4) == [[0, 1, 2, 3], [4, 5, 6, 7]]
+    assert tp_groups(4, 4) == [[0, 1, 2, 3]]
+    with pytest.raises(ValueError):
+        tp_groups(8, 3)
