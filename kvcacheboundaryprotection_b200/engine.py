@@ -346,9 +346,12 @@ class CappedKVEngine:
         GEMM with N / 128 column tiles and K / 128 k-blocks, from a burst sweep of every
         per-rank shape of the 7B, Qwen2.5-3B and Qwen3-4B decoders at 1, 2, 4 and 8 GPUs on
         B200 (and of 149 .. 240-tile shapes at 1, 16 and 32 rows):
-        * more tiles than SMs: no split -- a split only adds a second wave (172 tiles of
-          the 3B gate/up: 29.7 us unsplit against 33.8 us with 3 splits; 149, 152, 160 and
-          200 tiles alike);
+        * a few tiles past one whole wave of 2 CTAs per SM (up to 1/8 of a wave more): 2
+          splits, so the CTAs left over for a second wave carry half a k range (297 tiles,
+          the TP = 4 lm_head shard: 61.4-63.6 us against 65.5-66.4 us unsplit);
+        * otherwise more tiles than SMs: no split -- a split only adds a second wave (172
+          tiles of the 3B gate/up: 29.7 us unsplit against 33.8 us with 3 splits; 149, 152,
+          160, 200 and 594 tiles alike);
         * >= ~2/3 tile per SM: the split whose whole waves of 2 CTAs per SM carry the most
           work per wave (148 tiles: 2 splits, one full wave);
         * 24.. tiles: about 256 CTAs, at most 8 per cluster (the single-GPU 7B q/k/v, o and
@@ -357,6 +360,8 @@ class CappedKVEngine:
         tiles = max(1, N // 128)
         kc = max(1, K // 128)
         slots = 2 * sms
+        if slots < tiles <= slots + slots // 8:
+            return 2
         if tiles > sms:
             return 1
         if tiles * 3 >= slots:

@@ -87,6 +87,8 @@ def test_split_k_choices():
     assert pick(128 * 148, H) == 2       # 148 tiles: exactly two CTAs per SM
     assert pick(128 * 149, H) == 1       # 149 tiles: any split adds a second wave
     assert pick(128 * 172, 2048) == 1    # the Qwen2.5-3B gate/up (measured 29.7 vs 33.8 us at 3)
+    assert pick(128 * 297, H) == 2       # one tile past a whole wave (the TP=4 lm_head shard)
+    assert pick(128 * 594, H) == 1
     assert pick(768, H) == 16            # 6 tiles (q/k/v at TP=8)
     # tensor parallel: each rank picks for its own shard
     from kvcacheboundaryprotection_b200.tp import allreduce_splits
