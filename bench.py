@@ -16,9 +16,12 @@ Inputs are larger than L2 (15 GB of weights are streamed every step).
 
 Multi-GPU: one process per GPU.  The headline at N > 1 decodes the same 16 sequences
 tensor-parallel over KV-head groups (strong scaling; o/down allreduce fused into the
-GEMMs over NVLink, score and argmax allreduce-MAX by NCCL) and checks it ("tp_check":
-bit-identical state on every rank, and logits / victims against one GPU decoding the
-same state).  Beside it: "data_parallel" (16 independent sequences per GPU, no
+GEMMs over NVLink, score and argmax allreduce-MAX by NCCL).  The tensor-parallel size is
+the reference's clamp (the largest size <= N dividing the query heads, KV heads and FFN
+width: 2, 4, 4 for the 7B model at N = 2, 4, 8); the rest of N becomes data-parallel
+replicas of the group that split the sequences (``--tp-size`` overrides).  The run checks
+itself ("tp_check": bit-identical state on the ranks of each group, and logits / victims
+against one GPU decoding the same state).  Beside it: "data_parallel" (16 independent sequences per GPU, no
 collective, weak scaling) and "configs" -- the Qwen2.5-3B-arch workload (32 sequences
 per GPU, capacity 256, LRU, data parallel) and the Qwen3-4B-arch single 65536-token
 sequence (capacity 4096, LRU, tensor parallel over its 8 KV heads).  Time = max over
