@@ -643,11 +643,16 @@ def kernel_algorithmic_bytes(cfg, B, avg_valid):
 
 
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch, from ncu
-# captures of this file's --micro-attn / --micro-gemm runs on B200 (qwen2.5-7b shapes).
+# captures on B200 at the qwen2.5-7b shapes: the attention from this file's --micro-attn
+# run, the GEMMs from run_gemm_microbench("qwen2.5-7b", M=16) (its q/k/v launch is the
+# same main loop and weight stream as the step's, with the plain epilogue).
 NCU_TRAFFIC = {
     ("qwen2.5-7b", "attention"): 34129152,
-    ("qwen2.5-7b", "gate_up"): 271750400 + 4199424,
-    ("qwen2.5-7b", "o"): 25949952,
+    ("qwen2.5-7b", "qkv"): 33217536,
+    ("qwen2.5-7b", "o"): 25949440,
+    ("qwen2.5-7b", "gate_up"): 271760384 + 384000,
+    ("qwen2.5-7b", "down"): 136550144 + 708096,
+    ("qwen2.5-7b", "lm_head"): 1090553600 + 4642560,
 }
 
 
