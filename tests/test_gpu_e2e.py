@@ -121,6 +121,54 @@ def test_teacher_forced_parity(preset, policy):
         assert len(set(evicted) & set(o.positions_evicted)) >= 0.9 * len(evicted)
 
 
+def test_teacher_forced_parity_twenty_sequences_in_one_batch():
+    """Twenty sequences decoded in one batch: every decode GEMM then has 17..32 activation
+    rows and runs the tcgen05 main loop (the single-sequence runs above take it only for
+    the norm-prologue GEMMs).  Each sequence must match its own oracle run as those do:
+    logits within 2e-2 per step and identical LRU slot tables and victims."""
+    cfg = get_config("parity-qwen2")
+    w = init_weights(cfg, seed=0)
+    wn = {k: v.float().numpy() for k, v in w.items()}
+    B, P, cap, N, max_new = 20, 300, 64, 512, 17  # two eviction cadences
+    prompts = [[int(x) for x in np.random.default_rng(100 + b).integers(0, cfg.vocab, P)] for b in range(B)]
+    spec = PolicySpec("lru", cap, True, 0.10, 0.10)
+    orc = [generate(OracleModel(_ocfg(cfg), wn, max_cache_len=N), spec, p, max_new, evict_every=8,
+                    n_kv_heads=cfg.n_kv_heads, record_logits=True) for p in prompts]
+    forced = np.array([o.generated_token_ids[P:] for o in orc], dtype=np.int32)  # [B][max_new]
+
+    eng = CappedKVEngine(cfg, w, batch=B, evict=EvictionSpec("lru", cap, 8, True, 0.10, 0.10), max_prompt_len=P,
+                         max_new_tokens=max_new)
+    eng.prefill(torch.tensor(prompts, dtype=torch.int32))
+    torch.cuda.synchronize()
+    worst = 0.0
+
+    def check_step(s):
+        nonlocal worst
+        got = eng.logits.float().cpu().numpy()
+        for b in range(B):
+            worst = max(worst, float(np.abs(got[b] - orc[b].step_logits[s]).max()))
+
+    check_step(0)
+    for s in range(1, max_new + 1):
+        eng.tokens.copy_(torch.from_numpy(forced[:, s - 1]).to(eng.tokens.device))
+        eng._append_evict()
+        sp = eng.slot_pos.cpu().numpy()
+        for b in range(B):
+            assert sp[b].tolist() == orc[b].slot_tables[s].tolist(), f"slot table of sequence {b} at step {s}"
+        if s == max_new:
+            break
+        eng._forward()
+        check_step(s)
+        eng._sample_and_score()
+    torch.cuda.synchronize()
+    eng.check_device_errors()
+    print(f"20 sequences: max logit diff {worst:.3g}")
+    assert worst <= 2e-2, worst
+    for b in range(B):
+        n = int(eng.evcount[b].item())
+        assert eng.evlog[b, :n].cpu().numpy().tolist() == orc[b].positions_evicted
+
+
 @pytest.mark.parametrize("fixture", ["e2e_parity_qwen2.json", "e2e_parity_qwen2_h2o.json"])
 def test_free_running_against_reference_trace(fixture):
     with open(os.path.join(GOLDEN, fixture)) as f:
